@@ -1,0 +1,653 @@
+// tcgen05 / TMEM / TMA GEMM for the residual-MLP forward and backward products.
+//
+// One kernel computes, for each batch z (twin critic index),
+//     D[z][m][n] = scale * sum_k A[z][m][k] * B[z][n][k]   (+ bias[n]) (+ residual[m][n]) (+ D_old)
+// with A and B each either K-contiguous ("K-major") or M/N-contiguous
+// ("MN-major") in global memory. That covers the three products of a linear
+// layer y = x W^T that the reference issues as cuBLASLt plans
+// (src/robolearn/cuda/linear.py:179-185): forward (A=x K-major, B=W K-major),
+// input gradient dx = dy W (A=dy K-major, B=W MN-major) and weight gradient
+// dW = dy^T x (A=dy MN-major, B=x MN-major, contraction over the batch rows).
+//
+// Two operand kinds:
+//   kind 0: fp16 operands, fp32 accumulation (tcgen05.mma kind::f16);
+//   kind 1: fp32 operands through a three-product tf32 split, A = A_hi + A_lo,
+//           D = A_hi B_hi + A_hi B_lo + A_lo B_hi (tcgen05.mma kind::tf32), which
+//           keeps the products within ~1e-6 relative of fp32 (the reference's
+//           FP32 recipe uses pedantic fp32 GEMMs, kernels.cu:436-444).
+//
+// Layout: 128 x BN output tile per CTA (BN multiple of 16, <= 256), K staged
+// 128 bytes at a time through a multi-stage TMA -> smem ring with 128-byte
+// swizzle, accumulator in TMEM. Warp roles: warp 0 = TMA producer, warp 1 =
+// TMEM allocation + MMA issue (one elected thread), warps 2..5 = epilogue
+// (TMEM -> registers -> fused epilogue -> global). Every mbarrier wait is bounded
+// by wall-clock time and reports through the caller's health word.
+//
+// Epilogue extras: per-column partial moments over each 32-row group (mean and
+// sum of squared deviations) feed training-mode batch norm without another read
+// of the output.
+
+#include "common.cuh"
+#include "../../include/rl2.h"
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+
+namespace rl2 {
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kMaxSmem = 232448;
+
+struct Params {
+    int M, N, K;
+    int batch, splits, kblocks_total, kblocks_per_split;
+    int BN, a_batched, b_batched;
+    float* d;
+    long long ldd, d_bstride, d_split_stride;
+    int accumulate;
+    const float* bias;
+    long long bias_bstride;
+    const float* residual;
+    long long ldr, r_bstride;
+    float* stat_mean;
+    float* stat_m2;
+    long long stat_bstride;
+    const float* scale;
+    int* health;
+};
+
+// Wall-clock bounded mbarrier wait (4 s), so a lost arrival cannot hang the GPU.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, int* health) {
+    if (ptx::mbar_try_wait(bar, phase)) return true;
+    uint64_t start;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+    for (uint32_t i = 1;; ++i) {
+        if (ptx::mbar_try_wait(bar, phase)) return true;
+        if ((i & 1023u) == 0) {
+            uint64_t now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (now - start > 4000000000ull) {
+                if (health) atomicOr(health, kHealthTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;  // 128-byte swizzle
+    return d;
+}
+
+// Reduce-scatter of 16 per-lane values over the 32 lanes of a warp: afterwards
+// lane l holds the warp total of column (l >> 1) & 15.
+__device__ __forceinline__ float reduce_scatter16(float (&v)[16]) {
+    const int lane = threadIdx.x & 31;
+    float a[8];
+    {
+        const bool hi = lane & 16;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float keep = hi ? v[8 + j] : v[j];
+            const float send = hi ? v[j] : v[8 + j];
+            a[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+    }
+    float b[4];
+    {
+        const bool hi = lane & 8;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float keep = hi ? a[4 + j] : a[j];
+            const float send = hi ? a[j] : a[4 + j];
+            b[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+    }
+    float c[2];
+    {
+        const bool hi = lane & 4;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float keep = hi ? b[2 + j] : b[j];
+            const float send = hi ? b[j] : b[2 + j];
+            c[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+    }
+    float e;
+    {
+        const bool hi = lane & 2;
+        const float keep = hi ? c[1] : c[0];
+        const float send = hi ? c[0] : c[1];
+        e = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    return e + __shfl_xor_sync(0xffffffffu, e, 1);
+}
+
+template <int KIND, int A_MN, int B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_a_lo, const __grid_constant__ CUtensorMap tma_b_lo,
+                const Params p, const int stages) {
+    constexpr int kElem = KIND == 0 ? 2 : 4;
+    constexpr int kBK = 128 / kElem;       // K elements per stage (one 128-byte swizzle row)
+    constexpr int kUK = 32 / kElem;        // K per MMA instruction (32 bytes)
+    constexpr int kChunk = 128 / kElem;    // MN elements per 128-byte chunk (MN-major boxes)
+    constexpr int kPlanes = KIND == 0 ? 1 : 2;
+    const int BN = p.BN;
+    const uint32_t a_bytes = kBM * 128;                 // 128 rows x 128 B per plane
+    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
+    const uint32_t stage_bytes = (a_bytes + b_bytes) * kPlanes;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
+    uint64_t* empty = full + stages;
+    uint64_t* acc_full = empty + stages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_tile = blockIdx.x;
+    const int m_tile = blockIdx.y;
+    const int z = blockIdx.z / p.splits;
+    const int split = blockIdx.z % p.splits;
+    const int kb_begin = split * p.kblocks_per_split;
+    const int kb_end = min(p.kblocks_total, kb_begin + p.kblocks_per_split);
+    const int n_kb = kb_end - kb_begin;
+    const uint32_t tmem_cols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        ptx::mbar_init(acc_full, 1);
+        ptx::fence_barrier_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, tmem_cols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (ptx::elect_one()) {
+            ptx::prefetch_tensormap(&tma_a);
+            ptx::prefetch_tensormap(&tma_b);
+            const int za = p.a_batched ? z : 0;
+            const int zb = p.b_batched ? z : 0;
+            const int m0 = m_tile * kBM;
+            const int n0 = n_tile * BN;
+            int s = 0;
+            uint32_t phase = 0;
+            for (int kb = kb_begin; kb < kb_end; ++kb) {
+                if (!wait_bar(&empty[s], phase ^ 1, p.health)) break;
+                ptx::mbar_arrive_expect_tx(&full[s], stage_bytes);
+                uint8_t* sa = smem + s * stage_bytes;
+                uint8_t* sb = sa + a_bytes * kPlanes;
+                const int k0 = kb * kBK;
+                for (int plane = 0; plane < kPlanes; ++plane) {
+                    const CUtensorMap* ma = plane == 0 ? &tma_a : &tma_a_lo;
+                    const CUtensorMap* mb = plane == 0 ? &tma_b : &tma_b_lo;
+                    uint8_t* da = sa + plane * a_bytes;
+                    uint8_t* db = sb + plane * b_bytes;
+                    if (A_MN) {
+                        for (int c = 0; c < kBM / kChunk; ++c)
+                            ptx::tma_load_3d(da + c * (kBK * 128), ma, &full[s], m0 + c * kChunk, k0, za);
+                    } else {
+                        ptx::tma_load_3d(da, ma, &full[s], k0, m0, za);
+                    }
+                    if (B_MN) {
+                        for (int c = 0; c < BN / kChunk; ++c)
+                            ptx::tma_load_3d(db + c * (kBK * 128), mb, &full[s], n0 + c * kChunk, k0, zb);
+                    } else {
+                        ptx::tma_load_3d(db, mb, &full[s], k0, n0, zb);
+                    }
+                }
+                if (++s == stages) {
+                    s = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (ptx::elect_one()) {
+            const uint32_t fmt = KIND == 0 ? 0u : 2u;
+            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(A_MN) << 15) |
+                                   (static_cast<uint32_t>(B_MN) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                   (static_cast<uint32_t>(kBM >> 4) << 24);
+            // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = 8 K-rows.
+            // K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
+            const uint32_t lbo_mn = kBK * 128;
+            int s = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int i = 0; i < n_kb; ++i) {
+                if (!wait_bar(&full[s], phase, p.health)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t sa = ptx::smem_u32(smem + s * stage_bytes);
+                const uint32_t sb = sa + a_bytes * kPlanes;
+#pragma unroll
+                for (int j = 0; j < kBK / kUK; ++j) {
+                    const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
+                    const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
+                    const uint64_t da = smem_desc(sa + a_off, A_MN ? lbo_mn : 16, 1024);
+                    const uint64_t db = smem_desc(sb + b_off, B_MN ? lbo_mn : 16, 1024);
+                    const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
+                    if (KIND == 0) {
+                        ptx::mma_f16(tmem, da, db, idesc, acc);
+                    } else {
+                        const uint64_t da_lo = smem_desc(sa + a_bytes + a_off, A_MN ? lbo_mn : 16, 1024);
+                        const uint64_t db_lo = smem_desc(sb + b_bytes + b_off, B_MN ? lbo_mn : 16, 1024);
+                        ptx::mma_tf32(tmem, da_lo, db, idesc, acc);
+                        ptx::mma_tf32(tmem, da, db_lo, idesc, 1u);
+                        ptx::mma_tf32(tmem, da, db, idesc, 1u);
+                    }
+                }
+                ptx::mma_commit(&empty[s]);
+                if (++s == stages) {
+                    s = 0;
+                    phase ^= 1;
+                }
+            }
+            if (ok) ptx::mma_commit(acc_full);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row_local = q * 32 + lane;
+        const int row = m_tile * kBM + row_local;
+        const bool row_ok = row < p.M;
+        const int valid = min(max(p.M - (m_tile * kBM + q * 32), 0), 32);
+        const bool ok = wait_bar(acc_full, 0, p.health);
+        ptx::tc_fence_after();
+        if (ok && n_kb > 0) {
+            const float scale = p.scale ? *p.scale : 1.0f;
+            float* d = p.d + static_cast<long long>(z) * p.d_bstride + static_cast<long long>(split) * p.d_split_stride;
+            const float* bias = p.bias ? p.bias + static_cast<long long>(z) * p.bias_bstride : nullptr;
+            const float* res = p.residual ? p.residual + static_cast<long long>(z) * p.r_bstride : nullptr;
+            const int group = (m_tile * kBM) / 32 + q;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                ptx::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0), v);
+                const int col0 = n_tile * BN + c0;
+                if (col0 >= p.N) break;  // warp-uniform
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float x = v[i] * scale;
+                    const int col = col0 + i;
+                    if (col < p.N) {
+                        if (bias) x += bias[col];
+                        if (res && row_ok) x += res[static_cast<long long>(row) * p.ldr + col];
+                        if (p.accumulate && row_ok) x += d[static_cast<long long>(row) * p.ldd + col];
+                    }
+                    v[i] = x;
+                }
+                if (row_ok) {
+                    float* drow = d + static_cast<long long>(row) * p.ldd + col0;
+                    if (col0 + 16 <= p.N && (p.ldd & 3) == 0 && ptx::aligned16(drow)) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            *reinterpret_cast<float4*>(drow + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (col0 + i < p.N) drow[i] = v[i];
+                    }
+                }
+                if (p.stat_mean && valid > 0) {
+                    float t[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) t[i] = row_ok ? v[i] : 0.0f;
+                    const float total = reduce_scatter16(t);
+                    const float mean_mine = total / static_cast<float>(valid);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float m_i = __shfl_sync(0xffffffffu, mean_mine, 2 * i);
+                        const float dv = row_ok ? v[i] - m_i : 0.0f;
+                        t[i] = dv * dv;
+                    }
+                    const float m2 = reduce_scatter16(t);
+                    const int col = col0 + ((lane >> 1) & 15);
+                    if ((lane & 1) == 0 && col < p.N) {
+                        const long long idx = static_cast<long long>(z) * p.stat_bstride +
+                                              static_cast<long long>(group) * p.N + col;
+                        p.stat_mean[idx] = mean_mine;
+                        p.stat_m2[idx] = m2;
+                    }
+                }
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+}  // namespace gemm
+}  // namespace rl2
+
+// ===========================================================================
+// host side: tensor maps, plans, dispatch
+// ===========================================================================
+namespace rl2 {
+namespace gemm {
+namespace {
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+// 3D map {inner, outer, batch} with a 128-byte-swizzled box {box_inner, box_outer, 1}.
+bool make_map(CUtensorMap* map, const void* base, int elem, long long inner, long long outer, long long batch,
+              long long ld_elems, long long batch_stride_elems, int box_inner, int box_outer) {
+    EncodeTiled enc = encoder();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+        return false;
+    }
+    if (!aligned(base, 16)) {
+        set_error("GEMM operand base address must be 16-byte aligned");
+        return false;
+    }
+    const long long ld_bytes = ld_elems * elem;
+    if (ld_bytes % 16 != 0 || ld_bytes <= 0) {
+        set_error("GEMM operand row stride must be a positive multiple of 16 bytes (got %lld)", ld_bytes);
+        return false;
+    }
+    long long bs_bytes = batch_stride_elems * elem;
+    if (batch <= 1) {
+        batch = 1;
+        bs_bytes = ld_bytes * outer;
+        bs_bytes = (bs_bytes + 15) / 16 * 16;
+    }
+    if (bs_bytes % 16 != 0 || bs_bytes <= 0) {
+        set_error("GEMM operand batch stride must be a positive multiple of 16 bytes");
+        return false;
+    }
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld_bytes), static_cast<cuuint64_t>(bs_bytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for extents %lld x %lld x %lld", static_cast<int>(r), inner,
+                  outer, batch);
+        return false;
+    }
+    return true;
+}
+
+struct Plan {
+    CUtensorMap ta, tb, ta_lo, tb_lo;
+    Params p;
+    int kind, a_mn, b_mn, stages, smem;
+    dim3 grid;
+};
+
+typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params,
+                         const int);
+
+KernelFn pick(int kind, int a_mn, int b_mn) {
+    const int key = kind * 4 + a_mn * 2 + b_mn;
+    switch (key) {
+        case 0: return gemm_kernel<0, 0, 0>;
+        case 1: return gemm_kernel<0, 0, 1>;
+        case 2: return gemm_kernel<0, 1, 0>;
+        case 3: return gemm_kernel<0, 1, 1>;
+        case 4: return gemm_kernel<1, 0, 0>;
+        case 5: return gemm_kernel<1, 0, 1>;
+        case 6: return gemm_kernel<1, 1, 0>;
+        default: return gemm_kernel<1, 1, 1>;
+    }
+}
+
+int auto_tile_n(int n, int kind, int b_mn) {
+    const int chunk = kind == 0 ? 64 : 32;
+    const int quantum = b_mn ? chunk : 16;
+    if (n <= 256) return (n + quantum - 1) / quantum * quantum;
+    return 256;
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace rl2
+
+using rl2::gemm::Plan;
+
+extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
+    using namespace rl2;
+    using namespace rl2::gemm;
+    clear_error();
+    if (!g) {
+        set_error("null GEMM descriptor");
+        return nullptr;
+    }
+    if ((g->kind != 0 && g->kind != 1) || g->m < 1 || g->n < 1 || g->k < 1 || g->batch < 1) {
+        set_error("GEMM requires kind 0/1 and positive m, n, k, batch");
+        return nullptr;
+    }
+    if (!g->a || !g->b || !g->d || (g->kind == 1 && (!g->a_lo || !g->b_lo))) {
+        set_error("GEMM operands / output must be non-null (kind 1 also needs a_lo and b_lo)");
+        return nullptr;
+    }
+    if ((g->a_major != 0 && g->a_major != 1) || (g->b_major != 0 && g->b_major != 1)) {
+        set_error("GEMM majors must be 0 (K contiguous) or 1 (M/N contiguous)");
+        return nullptr;
+    }
+    const int splits = g->k_splits < 1 ? 1 : g->k_splits;
+    if (splits > 1 && (g->bias || g->residual || g->accumulate || g->stat_mean || g->d_split_stride <= 0)) {
+        set_error("split-K GEMMs write plain partials: no bias/residual/accumulate/stats, positive split stride");
+        return nullptr;
+    }
+    if ((g->stat_mean == nullptr) != (g->stat_m2 == nullptr)) {
+        set_error("GEMM column statistics need both stat_mean and stat_m2");
+        return nullptr;
+    }
+    const int elem = g->kind == 0 ? 2 : 4;
+    const int bk = 128 / elem;
+    const int chunk = 128 / elem;
+    int bn = g->tile_n > 0 ? g->tile_n : auto_tile_n(g->n, g->kind, g->b_major);
+    if (bn % 16 != 0 || bn < 16 || bn > 256 || (g->b_major == 1 && bn % chunk != 0)) {
+        set_error("GEMM tile_n must be a multiple of 16 in [16, 256] (and of %d for an N-contiguous B)", chunk);
+        return nullptr;
+    }
+    Plan* plan = new (std::nothrow) Plan();
+    if (!plan) {
+        set_error("out of host memory");
+        return nullptr;
+    }
+    std::memset(plan, 0, sizeof(Plan));
+    plan->kind = g->kind;
+    plan->a_mn = g->a_major;
+    plan->b_mn = g->b_major;
+    const long long a_batch = g->a_batch_stride ? g->batch : 1;
+    const long long b_batch = g->b_batch_stride ? g->batch : 1;
+    bool ok = true;
+    for (int plane = 0; plane < (g->kind == 0 ? 1 : 2) && ok; ++plane) {
+        const void* a = plane == 0 ? g->a : g->a_lo;
+        const void* b = plane == 0 ? g->b : g->b_lo;
+        CUtensorMap* ma = plane == 0 ? &plan->ta : &plan->ta_lo;
+        CUtensorMap* mb = plane == 0 ? &plan->tb : &plan->tb_lo;
+        if (g->a_major == 0)
+            ok = ok && make_map(ma, a, elem, g->k, g->m, a_batch, g->lda, g->a_batch_stride, bk, kBM);
+        else
+            ok = ok && make_map(ma, a, elem, g->m, g->k, a_batch, g->lda, g->a_batch_stride, chunk, bk);
+        if (g->b_major == 0)
+            ok = ok && make_map(mb, b, elem, g->k, g->n, b_batch, g->ldb, g->b_batch_stride, bk, bn);
+        else
+            ok = ok && make_map(mb, b, elem, g->n, g->k, b_batch, g->ldb, g->b_batch_stride, chunk, bk);
+    }
+    if (!ok) {
+        delete plan;
+        return nullptr;
+    }
+    if (g->kind == 0) {
+        plan->ta_lo = plan->ta;
+        plan->tb_lo = plan->tb;
+    }
+    Params& p = plan->p;
+    p.M = g->m;
+    p.N = g->n;
+    p.K = g->k;
+    p.batch = g->batch;
+    p.kblocks_total = (g->k + bk - 1) / bk;
+    p.splits = std::min(splits, p.kblocks_total);
+    p.kblocks_per_split = (p.kblocks_total + p.splits - 1) / p.splits;
+    p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;  // every split non-empty
+    p.BN = bn;
+    p.a_batched = g->a_batch_stride != 0;
+    p.b_batched = g->b_batch_stride != 0;
+    p.d = g->d;
+    p.ldd = g->ldd;
+    p.d_bstride = g->d_batch_stride;
+    p.d_split_stride = g->d_split_stride;
+    p.accumulate = g->accumulate;
+    p.bias = g->bias;
+    p.bias_bstride = g->bias_batch_stride;
+    p.residual = g->residual;
+    p.ldr = g->ldr;
+    p.r_bstride = g->residual_batch_stride;
+    p.stat_mean = g->stat_mean;
+    p.stat_m2 = g->stat_m2;
+    p.stat_bstride = g->stat_batch_stride;
+    p.scale = g->scale;
+    p.health = g->health;
+    const int planes = g->kind == 0 ? 1 : 2;
+    const int stage_bytes = (kBM * 128 + bn * 128) * planes;
+    const int overhead = 1024 + 256;
+    plan->stages = std::min(8, (kMaxSmem - overhead) / stage_bytes);
+    if (plan->stages < 2) {
+        set_error("GEMM tile does not fit shared memory");
+        delete plan;
+        return nullptr;
+    }
+    plan->smem = plan->stages * stage_bytes + overhead;
+    plan->grid = dim3((g->n + bn - 1) / bn, (g->m + kBM - 1) / kBM, g->batch * p.splits);
+    if (plan->grid.y > 65535 || plan->grid.z > 65535) {
+        set_error("GEMM grid exceeds launch limits");
+        delete plan;
+        return nullptr;
+    }
+    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             plan->smem) != cudaSuccess) {
+        set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", plan->smem);
+        delete plan;
+        return nullptr;
+    }
+    return plan;
+}
+
+extern "C" int rl2_gemm_run(void* opaque, void* stream) {
+    using namespace rl2;
+    using namespace rl2::gemm;
+    clear_error();
+    if (!opaque) {
+        set_error("null GEMM plan");
+        return -1;
+    }
+    Plan* plan = static_cast<Plan*>(opaque);
+    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
+    fn<<<plan->grid, kThreads, plan->smem, as_stream(stream)>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo,
+                                                               plan->p, plan->stages);
+    return launch_status("tcgen05 GEMM");
+}
+
+extern "C" int rl2_gemm_destroy(void* opaque) {
+    rl2::clear_error();
+    delete static_cast<Plan*>(opaque);
+    return 0;
+}
+
+extern "C" int rl2_gemm_tile_n(void* opaque) {
+    return opaque ? static_cast<Plan*>(opaque)->p.BN : -1;
+}
+
+// ---------------------------------------------------------------------------
+// split-K reduction (fixed summation order -> run-to-run bitwise determinism)
+// ---------------------------------------------------------------------------
+namespace rl2 {
+namespace gemm {
+__global__ void split_reduce_kernel(const float* __restrict__ part, long long stride, int splits,
+                                    float* __restrict__ out, long long count, int accumulate) {
+    const long long n4 = count / 4;
+    const bool vec = (stride % 4 == 0) && ptx::aligned16(part) && ptx::aligned16(out);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < (vec ? n4 : count);
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        if (vec) {
+            float4 acc = accumulate ? reinterpret_cast<const float4*>(out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < splits; ++s) {
+                const float4 v = reinterpret_cast<const float4*>(part + s * stride)[i];
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            reinterpret_cast<float4*>(out)[i] = acc;
+        } else {
+            float acc = accumulate ? out[i] : 0.0f;
+            for (int s = 0; s < splits; ++s) acc += part[s * stride + i];
+            out[i] = acc;
+        }
+    }
+    if (vec && blockIdx.x == 0) {
+        for (long long i = n4 * 4 + threadIdx.x; i < count; i += blockDim.x) {
+            float acc = accumulate ? out[i] : 0.0f;
+            for (int s = 0; s < splits; ++s) acc += part[s * stride + i];
+            out[i] = acc;
+        }
+    }
+}
+}  // namespace gemm
+}  // namespace rl2
+
+extern "C" int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out,
+                                long long count, int accumulate, void* stream) {
+    using namespace rl2;
+    clear_error();
+    if (!partial || !out || splits < 1 || count < 1 || split_stride < count) {
+        set_error("split reduce needs non-null buffers, splits >= 1 and split_stride >= count");
+        return -1;
+    }
+    const long long work = count / 4 + 1;
+    const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 148LL * 8));
+    gemm::split_reduce_kernel<<<blocks, 256, 0, as_stream(stream)>>>(partial, split_stride, splits, out, count,
+                                                                      accumulate);
+    return launch_status("split-K reduce");
+}

@@ -1,0 +1,108 @@
+"""Host wrapper of the tcgen05 dense-product plans (``rl2_gemm_*``).
+
+A plan binds persistent device buffers once (their TMA descriptors are encoded
+at creation) and then enqueues the product on a stream with no allocation, so
+it can be captured in a CUDA graph. This replaces the reference's
+``CudaLinear`` cuBLASLt plans (``src/robolearn/cuda/linear.py:155-375``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+FP16 = 0
+TF32X3 = 1
+
+
+def operand_ld(cols: int, kind: int) -> int:
+    """Row stride (elements) giving 16-byte aligned rows for an operand plane."""
+    q = 8 if kind == FP16 else 4
+    return (cols + q - 1) // q * q
+
+
+def tf32_split(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact split ``x = hi + lo`` with ``hi`` representable in tf32 (low 13 mantissa bits cleared)."""
+    hi = (x.contiguous().view(torch.int32) & -8192).view(torch.float32)
+    return hi, x - hi
+
+
+class DensePlan:
+    """One ``D = scale * A B^T (+ bias) (+ residual) (+ D)`` product over fixed buffers."""
+
+    def __init__(
+        self,
+        *,
+        kind: int,
+        m: int,
+        n: int,
+        k: int,
+        a: torch.Tensor,
+        b: torch.Tensor,
+        d: torch.Tensor,
+        lda: int,
+        ldb: int,
+        ldd: int,
+        a_major: int = 0,
+        b_major: int = 0,
+        batch: int = 1,
+        a_batch_stride: int = 0,
+        b_batch_stride: int = 0,
+        d_batch_stride: int = 0,
+        a_lo: torch.Tensor | None = None,
+        b_lo: torch.Tensor | None = None,
+        accumulate: bool = False,
+        bias: torch.Tensor | None = None,
+        bias_batch_stride: int = 0,
+        residual: torch.Tensor | None = None,
+        ldr: int = 0,
+        residual_batch_stride: int = 0,
+        stat_mean: torch.Tensor | None = None,
+        stat_m2: torch.Tensor | None = None,
+        stat_batch_stride: int = 0,
+        scale: torch.Tensor | None = None,
+        k_splits: int = 1,
+        d_split_stride: int = 0,
+        tile_n: int = 0,
+        health: torch.Tensor | None = None,
+    ):
+        self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health]
+        desc = N.GemmDesc(
+            kind=kind, m=m, n=n, k=k, batch=batch,
+            a=N.ptr(a), a_lo=N.ptr(a_lo), a_major=a_major, lda=lda, a_batch_stride=a_batch_stride,
+            b=N.ptr(b), b_lo=N.ptr(b_lo), b_major=b_major, ldb=ldb, b_batch_stride=b_batch_stride,
+            d=N.ptr(d), ldd=ldd, d_batch_stride=d_batch_stride, accumulate=int(accumulate),
+            bias=N.ptr(bias), bias_batch_stride=bias_batch_stride,
+            residual=N.ptr(residual), ldr=ldr, residual_batch_stride=residual_batch_stride,
+            stat_mean=N.ptr(stat_mean), stat_m2=N.ptr(stat_m2), stat_batch_stride=stat_batch_stride,
+            scale=N.ptr(scale), k_splits=k_splits, d_split_stride=d_split_stride, tile_n=tile_n,
+            health=N.ptr(health),
+        )
+        self._lib = N.load()
+        self.handle = N.created(self._lib.rl2_gemm_create(ctypes.byref(desc)), "create tcgen05 GEMM plan")
+        self.tile_n = self._lib.rl2_gemm_tile_n(self.handle)
+        self.flops = 2 * m * n * k * batch * (3 if kind == TF32X3 else 1)
+
+    def run(self, stream=None) -> None:
+        N.check(self._lib.rl2_gemm_run(self.handle, N.stream_ptr(stream)), "tcgen05 GEMM")
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.rl2_gemm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def split_reduce(partial: torch.Tensor, split_stride: int, splits: int, out: torch.Tensor, count: int,
+                 accumulate: bool = False, stream=None) -> None:
+    lib = N.load()
+    N.check(lib.rl2_split_reduce(N.ptr(partial), split_stride, splits, N.ptr(out), count, int(accumulate),
+                                 N.stream_ptr(stream)), "split-K reduce")

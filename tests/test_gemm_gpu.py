@@ -1,0 +1,132 @@
+"""tcgen05 GEMM numerics against torch fp32/fp64 references of the same product.
+
+Covers both operand kinds (fp16, tf32x3 split), all four operand-major
+combinations, ragged M/N/K tails, twin batching, shared operands, the fused
+epilogue (bias, residual, accumulate, scale, 32-row column moments) and split-K.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from robolearn_b200 import dense  # noqa: E402
+
+
+def _store(logical: torch.Tensor, major: int, kind: int) -> tuple[torch.Tensor, int]:
+    """Lay out logical [batch, rows, k] as K-contiguous (major 0) or rows-contiguous (major 1)."""
+    bsz, rows, k = logical.shape
+    src = logical if major == 0 else logical.transpose(1, 2)
+    inner = k if major == 0 else rows
+    ld = dense.operand_ld(inner, kind)
+    buf = torch.zeros(bsz, src.shape[1], ld, device="cuda", dtype=torch.float16 if kind == 0 else torch.float32)
+    buf[:, :, :inner] = src.to(buf.dtype)
+    return buf, ld
+
+
+def _run(kind, m, n, k, a_major, b_major, batch=2, shared_a=False, **epi):
+    g = torch.Generator(device="cuda").manual_seed(m * 131 + n * 7 + k)
+    A = torch.randn(1 if shared_a else batch, m, k, device="cuda", generator=g)
+    B = torch.randn(batch, n, k, device="cuda", generator=g) / k**0.5
+    if kind == 0:
+        A, B = A.half().float(), B.half().float()
+    a_st, lda = _store(A, a_major, kind)
+    b_st, ldb = _store(B, b_major, kind)
+    ldd = n + 3
+    D = torch.zeros(batch, m, ldd, device="cuda")
+    kw = {}
+    if kind == 1:
+        a_hi, a_lo = dense.tf32_split(a_st)
+        b_hi, b_lo = dense.tf32_split(b_st)
+        a_st, b_st = a_hi, b_hi
+        kw = dict(a_lo=a_lo, b_lo=b_lo)
+    ref = torch.einsum("zmk,znk->zmn", A.double().expand(batch, m, k), B.double())
+    plan = dense.DensePlan(
+        kind=kind, m=m, n=n, k=k, a=a_st, b=b_st, d=D, lda=lda, ldb=ldb, ldd=ldd, a_major=a_major,
+        b_major=b_major, batch=batch, a_batch_stride=0 if shared_a else a_st[0].numel(),
+        b_batch_stride=b_st[0].numel(), d_batch_stride=D[0].numel(), **kw, **epi,
+    )
+    return plan, D, ref
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("a_major,b_major", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (300, 200, 160), (257, 101, 123), (64, 512, 520)])
+def test_gemm_matches_reference(kind, a_major, b_major, m, n, k):
+    plan, D, ref = _run(kind, m, n, k, a_major, b_major)
+    plan.run()
+    torch.cuda.synchronize()
+    out = D[:, :, :n].double()
+    tol = 2e-3 if kind == 0 else 2e-6
+    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    assert err < tol, (err, plan.tile_n)
+
+
+def test_gemm_epilogue_bias_residual_accumulate_scale_and_shared_operand():
+    m, n, k, batch = 200, 96, 64, 2
+    bias = torch.randn(batch, n, device="cuda")
+    res = torch.randn(batch, m, n, device="cuda")
+    scale = torch.tensor([0.25], device="cuda")
+    plan, D, ref = _run(0, m, n, k, 0, 0, batch=batch, shared_a=True, bias=bias, bias_batch_stride=n,
+                        residual=res, ldr=n, residual_batch_stride=m * n, scale=scale, accumulate=True)
+    D.fill_(1.5)
+    plan.run()
+    torch.cuda.synchronize()
+    expect = 0.25 * ref + bias.double()[:, None, :] + res.double() + 1.5
+    assert (D[:, :, :n].double() - expect).abs().max().item() < 2e-3 * expect.abs().max().item()
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_gemm_column_moments(kind):
+    m, n, k, batch = 300, 80, 96, 2
+    groups = (m + 31) // 32
+    mean = torch.zeros(batch, groups, n, device="cuda")
+    m2 = torch.zeros(batch, groups, n, device="cuda")
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, stat_mean=mean, stat_m2=m2, stat_batch_stride=groups * n)
+    plan.run()
+    torch.cuda.synchronize()
+    out = D[:, :, :n].double()
+    for gidx in range(groups):
+        rows = out[:, gidx * 32:(gidx + 1) * 32]
+        mu = rows.mean(1)
+        assert torch.allclose(mean[:, gidx].double(), mu, atol=1e-4, rtol=1e-4)
+        assert torch.allclose(m2[:, gidx].double(), ((rows - mu[:, None]) ** 2).sum(1), atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_gemm_split_k_partials_reduce(kind):
+    m, n, k, batch, splits = 256, 128, 1024, 2, 4
+    stride = batch * m * (n + 3)
+    part = torch.zeros(splits, stride, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn(batch, m, k, device="cuda", generator=g)
+    B = torch.randn(batch, n, k, device="cuda", generator=g) / k**0.5
+    if kind == 0:
+        A, B = A.half().float(), B.half().float()
+    a_st, lda = _store(A, 1, kind)
+    b_st, ldb = _store(B, 1, kind)
+    kw = {}
+    if kind == 1:
+        a_st, a_lo = dense.tf32_split(a_st)
+        b_st, b_lo = dense.tf32_split(b_st)
+        kw = dict(a_lo=a_lo, b_lo=b_lo)
+    plan = dense.DensePlan(kind=kind, m=m, n=n, k=k, a=a_st, b=b_st, d=part, lda=lda, ldb=ldb, ldd=n + 3,
+                           a_major=1, b_major=1, batch=batch, a_batch_stride=a_st[0].numel(),
+                           b_batch_stride=b_st[0].numel(), d_batch_stride=m * (n + 3), k_splits=splits,
+                           d_split_stride=stride, **kw)
+    out = torch.zeros(stride, device="cuda")
+    plan.run()
+    dense.split_reduce(part, stride, splits, out, stride)
+    torch.cuda.synchronize()
+    got = out.view(batch, m, n + 3)[:, :, :n].double()
+    ref = torch.einsum("zmk,znk->zmn", A.double(), B.double())
+    tol = 2e-3 if kind == 0 else 2e-6
+    assert (got - ref).abs().max().item() < tol * ref.abs().max().item()
+
+
+def test_gemm_rejects_misaligned_stride():
+    a = torch.zeros(16, 10, device="cuda", dtype=torch.float16)
+    b = torch.zeros(16, 16, device="cuda", dtype=torch.float16)
+    d = torch.zeros(16, 16, device="cuda")
+    with pytest.raises(RuntimeError, match="16 bytes"):
+        dense.DensePlan(kind=0, m=16, n=16, k=10, a=a, b=b, d=d, lda=10, ldb=16, ldd=16)
