@@ -91,6 +91,64 @@ int rl2_gemm_tile_n(void* plan);
 int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out, long long count,
                      int accumulate, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * fused categorical critic objective: min-Q twin selection + two-hot Bellman
+ * projection onto the atom support + log-softmax cross-entropy + logits
+ * gradient + head-bias gradient, one kernel. Replaces rl_flash_categorical_target
+ * (src/robolearn/cuda/categorical_kernels.cuh:159-176) together with the
+ * rl_flash_categorical_forward/backward pair (:126-157) on the critic-loss path
+ * (reference semantics: src/robolearn/flashsac/updates.py:19-80,248-257).
+ *
+ * Rows: transition i reads target logits at row target_row_offset + i (the
+ * next-observation half of the critic batch) and online logits at row i; both
+ * carry the head bias already. Twin t lives at +t * *_twin_stride floats.
+ * loss_weight multiplies every per-row CE and gradient (1 / (2B) for the mean).
+ * min_v / max_v are the support bounds as the caller's doubles; the kernel
+ * clamps with their float32 roundings and divides by float32((max-min)/(bins-1)),
+ * the conversions Torch applies to the reference's Python scalars.
+ * Outputs (each optional): dlogits fp32, d16 fp16 operand scaled by *d16_scale,
+ * d_hi/d_lo tf32 operand planes, target_out [B][bins]. loss_out, max_entropy_out
+ * (max of alpha * next_log_pi), bias_grad_out [2][bins] are reduced in a fixed
+ * order. workspace holds rl2_categorical_workspace_floats(batch, bins) floats;
+ * counter is one zero-initialised unsigned int that the kernel leaves at zero.
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_critic_objective_args {
+    const float* target_logits;
+    long long target_row_stride, target_twin_stride;
+    int target_row_offset;
+    const float* online_logits;
+    long long online_row_stride, online_twin_stride;
+    const float* reward;
+    const float* terminated;
+    const float* discount;
+    const float* next_log_pi;
+    const float* alpha;
+    const float* support;
+    double min_v, max_v;
+    int bins, batch;
+    float loss_weight;
+    float* dlogits;
+    long long dlogits_row_stride, dlogits_twin_stride;
+    void* d16;
+    long long d16_row_stride, d16_twin_stride;
+    const float* d16_scale;
+    float* d_hi;
+    float* d_lo;
+    long long dplane_row_stride, dplane_twin_stride;
+    float* target_out;
+    long long target_out_row_stride;
+    float* workspace;
+    unsigned* counter;
+    float* loss_out;
+    float* max_entropy_out;
+    float* bias_grad_out;
+    int bias_grad_accumulate;
+    int* health;
+} rl2_critic_objective_args;
+
+int rl2_categorical_workspace_floats(int batch, int bins);
+int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,23 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class CriticObjectiveArgs(ctypes.Structure):
+    """``rl2_critic_objective_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("target_logits", P), ("target_row_stride", LL), ("target_twin_stride", LL), ("target_row_offset", I),
+        ("online_logits", P), ("online_row_stride", LL), ("online_twin_stride", LL),
+        ("reward", P), ("terminated", P), ("discount", P), ("next_log_pi", P), ("alpha", P), ("support", P),
+        ("min_v", D), ("max_v", D), ("bins", I), ("batch", I), ("loss_weight", F),
+        ("dlogits", P), ("dlogits_row_stride", LL), ("dlogits_twin_stride", LL),
+        ("d16", P), ("d16_row_stride", LL), ("d16_twin_stride", LL), ("d16_scale", P),
+        ("d_hi", P), ("d_lo", P), ("dplane_row_stride", LL), ("dplane_twin_stride", LL),
+        ("target_out", P), ("target_out_row_stride", LL),
+        ("workspace", P), ("counter", P), ("loss_out", P), ("max_entropy_out", P), ("bias_grad_out", P),
+        ("bias_grad_accumulate", I), ("health", P),
+    ]
+
+
 # name -> (argtypes, restype); every symbol here is declared in include/rl2.h
 SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_last_error": ([], ctypes.c_char_p),
@@ -51,6 +68,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_gemm_destroy": ([P], I),
     "rl2_gemm_tile_n": ([P], I),
     "rl2_split_reduce": ([P, LL, I, P, LL, I, P], I),
+    "rl2_categorical_workspace_floats": ([I, I], I),
+    "rl2_critic_objective": ([ctypes.POINTER(CriticObjectiveArgs), P], I),
 }
 
 

@@ -77,13 +77,16 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, int* hea
     }
 }
 
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor. layout 2 = 128-byte swizzle (16-byte granules,
+// 8-row atoms); layout 1 = 128-byte swizzle with 32-byte granules (4-row atoms),
+// the only form tcgen05 accepts for MN-major 32-bit (tf32) operands.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout = 2) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
     d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
-    d |= static_cast<uint64_t>(2) << 61;  // 128-byte swizzle
+    d |= static_cast<uint64_t>(layout) << 61;
     return d;
 }
 
@@ -229,9 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(A_MN) << 15) |
                                    (static_cast<uint32_t>(B_MN) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                    (static_cast<uint32_t>(kBM >> 4) << 24);
-            // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = 8 K-rows.
-            // K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
+            // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = one swizzle
+            // atom of K rows (8 rows = 1024 B for fp16; 4 rows = 512 B for the tf32 32-byte-granule
+            // swizzle). K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
             const uint32_t lbo_mn = kBK * 128;
+            const uint32_t sbo_mn = KIND == 0 ? 1024u : 512u;
+            const uint32_t lay_mn = KIND == 0 ? 2u : 1u;
             int s = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -247,14 +253,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < kBK / kUK; ++j) {
                     const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
                     const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
-                    const uint64_t da = smem_desc(sa + a_off, A_MN ? lbo_mn : 16, 1024);
-                    const uint64_t db = smem_desc(sb + b_off, B_MN ? lbo_mn : 16, 1024);
+                    const uint64_t da = A_MN ? smem_desc(sa + a_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sa + a_off, 16, 1024);
+                    const uint64_t db = B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
                     const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
                     if (KIND == 0) {
                         ptx::mma_f16(tmem, da, db, idesc, acc);
                     } else {
-                        const uint64_t da_lo = smem_desc(sa + a_bytes + a_off, A_MN ? lbo_mn : 16, 1024);
-                        const uint64_t db_lo = smem_desc(sb + b_bytes + b_off, B_MN ? lbo_mn : 16, 1024);
+                        const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
+                                                    : smem_desc(sa + a_bytes + a_off, 16, 1024);
+                        const uint64_t db_lo = B_MN ? smem_desc(sb + b_bytes + b_off, lbo_mn, sbo_mn, lay_mn)
+                                                    : smem_desc(sb + b_bytes + b_off, 16, 1024);
                         ptx::mma_tf32(tmem, da_lo, db, idesc, acc);
                         ptx::mma_tf32(tmem, da, db_lo, idesc, 1u);
                         ptx::mma_tf32(tmem, da, db, idesc, 1u);
@@ -371,7 +379,8 @@ EncodeTiled encoder() {
 
 // 3D map {inner, outer, batch} with a 128-byte-swizzled box {box_inner, box_outer, 1}.
 bool make_map(CUtensorMap* map, const void* base, int elem, long long inner, long long outer, long long batch,
-              long long ld_elems, long long batch_stride_elems, int box_inner, int box_outer) {
+              long long ld_elems, long long batch_stride_elems, int box_inner, int box_outer,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiled enc = encoder();
     if (!enc) {
         set_error("cuTensorMapEncodeTiled is unavailable from the driver");
@@ -403,7 +412,7 @@ bool make_map(CUtensorMap* map, const void* base, int elem, long long inner, lon
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = enc(map, elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (%d) for extents %lld x %lld x %lld", static_cast<int>(r), inner,
@@ -504,14 +513,16 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         const void* b = plane == 0 ? g->b : g->b_lo;
         CUtensorMap* ma = plane == 0 ? &plan->ta : &plan->ta_lo;
         CUtensorMap* mb = plane == 0 ? &plan->tb : &plan->tb_lo;
+        // MN-major tf32 tiles use the 32-byte-granule 128-byte swizzle (see smem_desc).
+        const CUtensorMapSwizzle mn_swz = g->kind == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
         if (g->a_major == 0)
             ok = ok && make_map(ma, a, elem, g->k, g->m, a_batch, g->lda, g->a_batch_stride, bk, kBM);
         else
-            ok = ok && make_map(ma, a, elem, g->m, g->k, a_batch, g->lda, g->a_batch_stride, chunk, bk);
+            ok = ok && make_map(ma, a, elem, g->m, g->k, a_batch, g->lda, g->a_batch_stride, chunk, bk, mn_swz);
         if (g->b_major == 0)
             ok = ok && make_map(mb, b, elem, g->k, g->n, b_batch, g->ldb, g->b_batch_stride, bk, bn);
         else
-            ok = ok && make_map(mb, b, elem, g->n, g->k, b_batch, g->ldb, g->b_batch_stride, chunk, bk);
+            ok = ok && make_map(mb, b, elem, g->n, g->k, b_batch, g->ldb, g->b_batch_stride, chunk, bk, mn_swz);
     }
     if (!ok) {
         delete plan;

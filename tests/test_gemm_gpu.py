@@ -57,7 +57,7 @@ def test_gemm_matches_reference(kind, a_major, b_major, m, n, k):
     plan.run()
     torch.cuda.synchronize()
     out = D[:, :, :n].double()
-    tol = 2e-3 if kind == 0 else 2e-6
+    tol = 2e-3 if kind == 0 else 2e-5
     err = (out - ref).abs().max().item() / ref.abs().max().item()
     assert err < tol, (err, plan.tile_n)
 
@@ -120,7 +120,7 @@ def test_gemm_split_k_partials_reduce(kind):
     torch.cuda.synchronize()
     got = out.view(batch, m, n + 3)[:, :, :n].double()
     ref = torch.einsum("zmk,znk->zmn", A.double(), B.double())
-    tol = 2e-3 if kind == 0 else 2e-6
+    tol = 2e-3 if kind == 0 else 2e-5
     assert (got - ref).abs().max().item() < tol * ref.abs().max().item()
 
 
