@@ -37,6 +37,20 @@ const char* rl2_last_error(void);
 int rl2_abi_version(void);
 
 /* ---------------------------------------------------------------------------
+ * operand planes: derived copies that feed the tensor-core products.
+ * Either h16 (fp16, multiplied by *scale when scale is set, overflow -> *found_inf = 1)
+ * or hi + lo (fp32 pair, hi exact in tf32, hi + lo = value). ld / twin_stride in elements.
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_plane {
+    void* h16;
+    float* hi;
+    float* lo;
+    long long ld, twin_stride;
+    const float* scale;
+    int* found_inf;
+} rl2_plane;
+
+/* ---------------------------------------------------------------------------
  * dense products (tcgen05 + TMA). Replaces the cuBLASLt dense plans
  * rl_plan_create / rl_plan_create_mixed / rl_plan_run / rl_plan_destroy
  * (src/robolearn/cuda/kernels.cu:410-731, driven by src/robolearn/cuda/linear.py:155-375)
@@ -52,6 +66,8 @@ int rl2_abi_version(void);
  *         the output, laid out [batch][ceil(m/32)][n] with stat_batch_stride.
  * k_splits > 1 writes independent partial products to d + s * d_split_stride
  *         (no bias / residual / accumulate / stats), reduced by rl2_split_reduce.
+ * out_plane (optional): operand plane copy of the final output (twin_stride per batch).
+ * d may be null when out_plane is set (plane-only output).
  * ------------------------------------------------------------------------- */
 typedef struct rl2_gemm_desc {
     int kind;
@@ -79,6 +95,7 @@ typedef struct rl2_gemm_desc {
     long long d_split_stride;
     int tile_n;
     int* health;
+    rl2_plane out_plane;
 } rl2_gemm_desc;
 
 void* rl2_gemm_create(const rl2_gemm_desc* desc);
@@ -148,6 +165,311 @@ typedef struct rl2_critic_objective_args {
 
 int rl2_categorical_workspace_floats(int batch, int bins);
 int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * batch norm over the rows of [twins][rows][cols] matrices, training or
+ * evaluation mode. Replaces rl_flash_bn_forward / rl_flash_bn_backward and their
+ * fp16 variants (src/robolearn/cuda/flash_kernels.cuh:500-609; semantics of
+ * src/robolearn/flashsac/layers.py:32-64,189-222: biased variance normalises,
+ * running variance uses rows/(rows-1), running buffers move by lerp(momentum)).
+ * Column moments travel as per-32-row-group (mean, M2) partials [twins][G][cols],
+ * G = ceil(rows / 32), merged in a fixed order (Chan et al.). A twin stride of 0
+ * shares one matrix / one set of statistics across the twins.
+ * ------------------------------------------------------------------------- */
+int rl2_colstats(const float* x, long long ldx, long long x_twin_stride, int twins, int rows, int cols,
+                 float* mean_part, float* m2_part, long long part_twin_stride, void* stream);
+
+int rl2_bn_finalize(const float* mean_part, const float* m2_part, long long part_twin_stride, int twins, int rows,
+                    int cols, float* mean, float* invstd, float* running_mean, float* running_var, float momentum,
+                    float eps, int update_running, void* stream);
+
+/* eval mode: mean = running_mean, invstd = 1 / sqrt(running_var + eps), count elements */
+int rl2_bn_eval_prepare(const float* running_mean, const float* running_var, long long count, float eps,
+                        float* mean, float* invstd, void* stream);
+
+typedef struct rl2_bn_apply_args {
+    const float* x;
+    long long ldx, x_twin_stride;
+    int twins, rows, cols;
+    const float* mean;   /* [twins][cols] */
+    const float* invstd; /* [twins][cols] */
+    const float* gamma;  /* [twins][cols] */
+    const float* beta;   /* [twins][cols] */
+    int relu;
+    const float* residual; /* optional, added after the activation */
+    long long ldr, residual_twin_stride;
+    float* y; /* optional fp32 output */
+    long long ldy, y_twin_stride;
+    rl2_plane plane; /* optional operand plane of the output */
+} rl2_bn_apply_args;
+
+int rl2_bn_apply(const rl2_bn_apply_args* args, void* stream);
+
+typedef struct rl2_bn_backward_args {
+    const float* dy; /* gradient w.r.t. the block output after the activation */
+    long long lddy, dy_twin_stride;
+    const float* x; /* pre-normalisation input */
+    long long ldx, x_twin_stride;
+    int twins, rows, cols;
+    const float* mean;
+    const float* invstd;
+    const float* gamma;
+    const float* beta;
+    int relu, training;
+    float* s1_part; /* [twins][G][cols] sums of dbn           */
+    float* s2_part; /* [twins][G][cols] sums of dbn * xhat    */
+    const float* coef1; /* [twins][cols] mean(dbn)   (apply)    */
+    const float* coef2; /* [twins][cols] mean(dbn*xhat) (apply) */
+    float* dx; /* optional fp32 input gradient */
+    long long lddx, dx_twin_stride;
+    int sum_twins; /* dx[r][c] = sum over twins (shared input) */
+    rl2_plane plane; /* optional operand plane of dx */
+} rl2_bn_backward_args;
+
+int rl2_bn_backward_reduce(const rl2_bn_backward_args* args, void* stream);
+int rl2_bn_backward_finalize(const float* s1_part, const float* s2_part, int twins, int rows, int cols,
+                             float* dgamma, float* dbeta, long long grad_twin_stride, int accumulate, float* coef1,
+                             float* coef2, void* stream);
+int rl2_bn_backward_apply(const rl2_bn_backward_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * RMS post-norm u = h / sqrt(mean(h^2) + eps) * gamma per row. Replaces
+ * rl_flash_rms_forward / rl_flash_rms_backward (flash_kernels.cuh:611-634;
+ * src/robolearn/flashsac/layers.py:67-81,225-240).
+ * ------------------------------------------------------------------------- */
+int rl2_rms_forward(const float* h, long long ldh, long long h_twin_stride, int twins, int rows, int cols,
+                    const float* gamma, float eps, float* r_out, float* u, long long ldu, long long u_twin_stride,
+                    const rl2_plane* plane, void* stream);
+
+/* dh = r * g*du - h * r^3 * sum(g*du*h) / cols; dgamma partials [twins][G][cols] of du*h*r */
+int rl2_rms_backward(const float* du, long long lddu, long long du_twin_stride, const float* h, long long ldh,
+                     long long h_twin_stride, const float* r, const float* gamma, int twins, int rows, int cols,
+                     float* dh, long long lddh, long long dh_twin_stride, float* dgamma_part, void* stream);
+
+/* out[t][c] (+)= sum_g part[t][g][c], fixed order */
+int rl2_colsum_finalize(const float* part, int twins, int groups, int cols, float* out, long long out_twin_stride,
+                        int accumulate, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * tanh-Gaussian policy head (src/robolearn/flashsac/layers.py:116-166; Warp
+ * restatement _sample_policy, src/robolearn/warp/flashsac.py:72-95).
+ * head rows hold [mean (act) | pre-tanh log-std (act)], biases already added.
+ * Sample: actions = tanh(mean + std * noise), log_pi = Gaussian log-density -
+ * tanh Jacobian (deterministic: actions = tanh(mean)). Backward: from d_action
+ * (rows < grad_rows) and d log pi (array, or one device scalar for rows <
+ * grad_rows) to d_head (fp32 and/or operand plane) and per-32-row-group bias
+ * partials [G][2*act]; optional behaviour-cloning term bc_alpha * q_abs *
+ * mean((a - replay_action)^2) (updates.py:130-134).
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_policy_args {
+    const float* head;
+    long long ld_head;
+    const float* noise;
+    long long ld_noise;
+    int rows, act;
+    float* actions;
+    long long ld_actions;
+    float* log_pi;
+    /* backward */
+    int grad_rows;
+    const float* d_action;
+    long long ld_d_action;
+    const float* d_log_pi;
+    const float* d_log_pi_value;
+    float bc_alpha;
+    const float* q_abs;
+    const float* replay_action;
+    long long ld_replay_action;
+    float* d_head;
+    long long ld_d_head;
+    rl2_plane d_plane;
+    float* bias_part;
+} rl2_policy_args;
+
+/* Replaces the actor-phase Warp kernels _sample_policy / _first_actions (warp/flashsac.py:72-102). */
+int rl2_policy_sample(const rl2_policy_args* args, int deterministic, void* stream);
+int rl2_policy_backward(const rl2_policy_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * actor objective over the frozen critic (updates.py:117-137; Warp
+ * _actor_objective / _actor_diagnostics, warp/flashsac.py:105-153): per row the
+ * twins' log-softmax and expected value, q = min(q0, q1), loss = mean(alpha *
+ * log_pi - q) (+ bc term), entropy = -mean(log_pi), mean_action, q_abs; the
+ * logits gradient of -q/B goes to d_logits (plane, twin_stride per twin) and
+ * d log pi = alpha / B to *d_log_pi_out.
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_actor_objective_args {
+    const float* logits;
+    long long logits_row_stride, logits_twin_stride;
+    const float* support;
+    int bins, batch, act;
+    const float* log_pi;
+    const float* actions;
+    long long actions_row_stride;
+    const float* replay_action;
+    long long replay_row_stride;
+    float bc_alpha;
+    const float* alpha;
+    rl2_plane d_logits;
+    float* workspace;
+    unsigned* counter;
+    float* loss_out;
+    float* entropy_out;
+    float* mean_action_out;
+    float* q_abs_out;
+    float* d_log_pi_out;
+} rl2_actor_objective_args;
+
+int rl2_actor_objective_workspace_floats(int batch);
+int rl2_actor_objective(const rl2_actor_objective_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * temperature (updates.py:297-326): loss = exp(log_temp) * (entropy - target),
+ * one torch-formula Adam step on log_temp with the warmup-cosine schedule
+ * (_utils/scheduler.py:43-65); adam_state = [step, m, v]. alpha_out receives
+ * exp(log_temp) after the step (or without a step when update = 0).
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_temperature_args {
+    float* log_temp;
+    const float* entropy;
+    float target_entropy;
+    float* adam_state;
+    float beta1, beta2, eps;
+    double lr_init, lr_peak, lr_end, warmup_steps, decay_steps;
+    int update;
+    float* value_out;
+    float* loss_out;
+    float* alpha_out;
+} rl2_temperature_args;
+
+int rl2_temperature_step(const rl2_temperature_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * fused optimizer pass over one network's flat parameter arena: Adam (+ AMP
+ * skip) -> weight-norm projection -> operand-plane refresh -> target EMA.
+ * Replaces rl_adam_create / rl_adam_step / rl_adam_set_scaler / rl_adam_unscale
+ * (src/robolearn/cuda/kernels.cu:760-907), rl_flash_projection_* and
+ * rl_flash_ema_* (src/robolearn/cuda/flash_kernels.cuh:383-498) and the fp16
+ * weight casts rl_cast_f32_f16 (kernels.cu:663-687).
+ *
+ * One segment = one projection unit, processed by one CTA:
+ *   kind 0 plain vector (no projection: head / policy biases),
+ *   kind 1 unit-linear weight row -> w / max(||w||, 1e-8),
+ *   kind 2 BN (weight at offset, bias at offset2) -> both * sqrt(C)/sqrt(sum(w^2+b^2)+1e-8),
+ *   kind 3 RMS scale -> w * sqrt(C)/sqrt(sum(w^2)+1e-8).
+ * length <= rl2_segment_max_length() per vector. plane_offset >= 0 refreshes the
+ * row's operand copy in weight_plane (and target_plane for the EMA target).
+ * formula 0 = torch Adam (lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps)),
+ * formula 1 = Warp-NN Adam (lr * m c1 / (sqrt(v c2) + eps)).
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_segment {
+    long long offset;
+    long long offset2;
+    long long plane_offset;
+    int length;
+    int kind;
+} rl2_segment;
+
+/* state: 9 floats per optimizer [attempts, steps, step_size, bc2, lr, skip, scale, growth, skipped].
+ * Schedules the learning rate (warmup-cosine over attempts or steps, or *lr_override),
+ * advances the step unless *found_inf is set (then skip), updates the dynamic loss
+ * scale when scaler = 1, and clears *found_inf. */
+typedef struct rl2_adam_prepare_args {
+    float* state;
+    int* found_inf;
+    int formula;
+    float beta1, beta2;
+    double lr_init, lr_peak, lr_end, warmup_steps, decay_steps;
+    int schedule_on_attempts;
+    const float* lr_override;
+    int scaler;
+    float growth, backoff;
+    int growth_interval;
+    float* scale_out;
+    float* inv_scale_out;
+} rl2_adam_prepare_args;
+
+typedef struct rl2_adam_args {
+    float* params;
+    const float* grads; /* null: projection / EMA only */
+    float* m;
+    float* v;
+    const rl2_segment* segments; /* device array */
+    int count;
+    const float* state;
+    int formula;
+    float beta1, beta2, eps;
+    int project;
+    rl2_plane weight_plane;
+    float* target_params;
+    float tau;
+    rl2_plane target_plane;
+} rl2_adam_args;
+
+int rl2_adam_prepare(const rl2_adam_prepare_args* args, void* stream);
+int rl2_adam_step(const rl2_adam_args* args, void* stream);
+int rl2_segment_max_length(void);
+
+/* ---------------------------------------------------------------------------
+ * replay sampling and gather. Replaces the Warp kernels _sample_indices and
+ * _gather_batch (src/robolearn/warp/_flash_replay.py:116-160) and the batch
+ * assembly kernels _actor_observations / _critic_inputs (warp/flashsac.py:53-69,
+ * 166-182); Torch counterpart TorchUniformBuffer.sample (flashsac/replay.py:179-194).
+ *
+ * rl2_replay_sample: indices[i] uniform in [0, n) by Warp's unbiased rejection
+ * rule, n = *population (device int64) or fixed_population, random words from
+ * Philox4x32-10 with key = seed and counter = (i, *epoch, round, stream).
+ * rl2_counter_advance adds `by` to a device epoch counter (graph-capturable).
+ * rl2_replay_gather copies rows bit-exactly into the network layouts and the
+ * optional raw batch arrays; with g_var set, reward_out = r / max(sqrt(g_var +
+ * norm_eps), g_r_max / g_max) (_utils/reward_normalization.py:28-38).
+ * ------------------------------------------------------------------------- */
+int rl2_replay_sample(unsigned long long seed, const unsigned long long* epoch, const long long* population,
+                      long long fixed_population, int batch, int* indices, int* health, void* stream);
+int rl2_counter_advance(unsigned long long* epoch, unsigned long long by, void* stream);
+
+typedef struct rl2_replay_gather_args {
+    const int* indices;
+    int batch;
+    const float* obs;
+    const float* next_obs;
+    long long ld_obs;
+    const float* action;
+    long long ld_action;
+    const float* reward;
+    const float* terminated;
+    const float* truncated;
+    const float* discount;
+    int obs_dim, act_dim, actor_obs_dim;
+    float* critic_x; /* [2B][ld_critic_x]: rows i = [obs | action], rows B+i = [next_obs | .] */
+    long long ld_critic_x;
+    float* actor_x; /* [2B][ld_actor_x]: rows i = obs prefix, rows B+i = next_obs prefix */
+    long long ld_actor_x;
+    float* reward_out;
+    float* terminated_out;
+    float* truncated_out;
+    float* discount_out;
+    const float* g_var;
+    const float* g_r_max;
+    float g_max, norm_eps;
+    float* batch_obs;
+    float* batch_next_obs;
+    float* batch_action;
+    float* batch_reward;
+    float* critic_x_pi; /* [B][ld_critic_x_pi]: obs rows for the actor-phase critic input */
+    long long ld_critic_x_pi;
+} rl2_replay_gather_args;
+
+int rl2_replay_gather(const rl2_replay_gather_args* args, void* stream);
+
+/* Standard normal policy noise (Box-Muller over Philox4x32-10 words; replaces the Warp
+ * _normal_noise kernel, src/robolearn/warp/flashsac.py:44-50): out[r][c], r < rows, c < cols. */
+int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols, float* out,
+                     long long ld, void* stream);
+
+/* Host-side Philox4x32-10 block (for checking device streams against the published algorithm). */
+void rl2_philox4x32(unsigned int c0, unsigned int c1, unsigned int c2, unsigned int c3, unsigned int k0,
+                    unsigned int k1, unsigned int* out4);
 
 #ifdef __cplusplus
 }

@@ -182,6 +182,34 @@ def linear(x, w):
     return np.einsum("trk,tnk->trn", x, w)
 
 
+# Operand rounding of the dense products. The FP32 recipe leaves operands as they
+# are; the FP16-operand recipe rounds every product operand to fp16 (gradient
+# operands after multiplying by the loss scale S, then divided by S), which is
+# what both the reference's autocast path and the CUDA path feed the tensor cores.
+_ROUND = {"mode": "fp32", "scale": 1.0}
+
+
+def set_operand_rounding(mode: str = "fp32", scale: float = 1.0) -> None:
+    if mode not in ("fp32", "fp16"):
+        raise ValueError(mode)
+    _ROUND["mode"], _ROUND["scale"] = mode, float(scale)
+
+
+def _rf(x):
+    """forward / weight operand"""
+    if _ROUND["mode"] == "fp16":
+        return np.asarray(x).astype(np.float16).astype(np.float64)
+    return x
+
+
+def _rg(x):
+    """gradient operand (carries the loss scale while rounded)"""
+    if _ROUND["mode"] == "fp16":
+        s = _ROUND["scale"]
+        return (np.asarray(x) * s).astype(np.float16).astype(np.float64) / s
+    return x
+
+
 def relu(x):
     return np.maximum(x, 0.0)
 
@@ -197,6 +225,24 @@ def sigmoid(x):
 # ----------------------------------------------------------------------------
 # backbone (embedder -> residual blocks -> RMS post-norm), shared by actor and critic
 # ----------------------------------------------------------------------------
+
+
+_MARGIN = [np.inf]
+
+
+def _note_margin(pre_relu) -> None:
+    """Track the smallest |pre-activation| seen by a ReLU (how close a mask decision is to the kink)."""
+    _MARGIN[0] = min(_MARGIN[0], float(np.abs(pre_relu).min()))
+
+
+def relu_margin_reset() -> None:
+    _MARGIN[0] = np.inf
+
+
+def relu_margin() -> float:
+    """Smallest |pre-ReLU| value since the last reset; a decision closer to 0 than the
+    arithmetic's rounding is not determined by fp32 evaluation order."""
+    return _MARGIN[0]
 
 
 def _stack(p: dict, key: str, twin: bool) -> np.ndarray:
@@ -219,24 +265,26 @@ def backbone_forward(p, x, blocks, training, twin, dtype):
     )
     stats["embedder.norm"] = (rm, rv)
     w_e = g(wkey)
-    h = linear(y, w_e)
+    h = linear(_rf(y), _rf(w_e))
     caches.append(("embed", y, c_bn, w_e))
     for i in range(blocks):
         suffix = ".weight" if twin else ".w.weight"
         w1 = g(f"encoder.{i}.w1{suffix}")
         w2 = g(f"encoder.{i}.w2{suffix}")
-        t1 = linear(h, w1)
+        t1 = linear(_rf(h), _rf(w1))
         n1, c1, rm1, rv1 = bn_forward(
             t1, g(f"encoder.{i}.norm1.weight"), g(f"encoder.{i}.norm1.bias"),
             g(f"encoder.{i}.norm1.running_mean"), g(f"encoder.{i}.norm1.running_var"), training,
         )
         a1 = relu(n1)
-        t2 = linear(a1, w2)
+        _note_margin(n1)
+        t2 = linear(_rf(a1), _rf(w2))
         n2, c2, rm2, rv2 = bn_forward(
             t2, g(f"encoder.{i}.norm2.weight"), g(f"encoder.{i}.norm2.bias"),
             g(f"encoder.{i}.norm2.running_mean"), g(f"encoder.{i}.norm2.running_var"), training,
         )
         a2 = relu(n2)
+        _note_margin(n2)
         stats[f"encoder.{i}.norm1"] = (rm1, rv1)
         stats[f"encoder.{i}.norm2"] = (rm2, rv2)
         caches.append(("block", h, w1, w2, c1, n1, a1, c2, n2))
@@ -255,15 +303,15 @@ def backbone_backward(du, caches, blocks, twin, need_input_grad):
         suffix = ".weight" if twin else ".w.weight"
         d_n2 = dh * (n2 > 0)
         d_t2, grads[f"encoder.{i}.norm2.weight"], grads[f"encoder.{i}.norm2.bias"] = bn_backward(d_n2, c2)
-        grads[f"encoder.{i}.w2{suffix}"] = np.einsum("trn,trk->tnk", d_t2, a1)
-        d_a1 = np.einsum("trn,tnk->trk", d_t2, w2)
+        grads[f"encoder.{i}.w2{suffix}"] = np.einsum("trn,trk->tnk", _rg(d_t2), _rf(a1))
+        d_a1 = np.einsum("trn,tnk->trk", _rg(d_t2), _rf(w2))
         d_n1 = d_a1 * (n1 > 0)
         d_t1, grads[f"encoder.{i}.norm1.weight"], grads[f"encoder.{i}.norm1.bias"] = bn_backward(d_n1, c1)
-        grads[f"encoder.{i}.w1{suffix}"] = np.einsum("trn,trk->tnk", d_t1, h_in)
-        dh = np.einsum("trn,tnk->trk", d_t1, w1) + dh
+        grads[f"encoder.{i}.w1{suffix}"] = np.einsum("trn,trk->tnk", _rg(d_t1), _rf(h_in))
+        dh = np.einsum("trn,tnk->trk", _rg(d_t1), _rf(w1)) + dh
     _, y_e, c_bn, w_e = caches[0]
-    grads["embedder.w.weight" if twin else "embedder.w.w.weight"] = np.einsum("trn,trk->tnk", dh, y_e)
-    d_y = np.einsum("trn,tnk->trk", dh, w_e)
+    grads["embedder.w.weight" if twin else "embedder.w.w.weight"] = np.einsum("trn,trk->tnk", _rg(dh), _rf(y_e))
+    d_y = np.einsum("trn,tnk->trk", _rg(dh), _rf(w_e))
     dx, grads["embedder.norm.weight"], grads["embedder.norm.bias"] = bn_backward(d_y, c_bn)
     if not twin:
         grads = {k: v[0] for k, v in grads.items()}
@@ -285,8 +333,8 @@ def actor_forward(p, d: Dims, obs, noise, training, dtype=np.float64):
     u0 = u[0]
     wm = p["predictor.mean_w.w.weight"].astype(dtype)
     ws = p["predictor.std_w.w.weight"].astype(dtype)
-    mean = u0 @ wm.T + p["predictor.mean_bias"].astype(dtype)
-    s = u0 @ ws.T + p["predictor.std_bias"].astype(dtype)
+    mean = _rf(u0) @ _rf(wm).T + p["predictor.mean_bias"].astype(dtype)
+    s = _rf(u0) @ _rf(ws).T + p["predictor.std_bias"].astype(dtype)
     ts = np.tanh(s)
     log_std = LOG_STD_MIN + (LOG_STD_MAX - LOG_STD_MIN) * 0.5 * (1.0 + ts)
     std = np.exp(log_std)
@@ -310,12 +358,12 @@ def actor_backward(cache, d: Dims, d_action, d_log_prob):
     d_s = d_log_std * (LOG_STD_MAX - LOG_STD_MIN) * 0.5 * (1.0 - ts * ts)
     u = cache["u"]
     grads = {
-        "predictor.mean_w.w.weight": d_mean.T @ u,
-        "predictor.std_w.w.weight": d_s.T @ u,
+        "predictor.mean_w.w.weight": _rg(d_mean).T @ _rf(u),
+        "predictor.std_w.w.weight": _rg(d_s).T @ _rf(u),
         "predictor.mean_bias": d_mean.sum(axis=0),
         "predictor.std_bias": d_s.sum(axis=0),
     }
-    du = d_mean @ cache["wm"] + d_s @ cache["ws"]
+    du = _rg(d_mean) @ _rf(cache["wm"]) + _rg(d_s) @ _rf(cache["ws"])
     g2, _ = backbone_backward(du[None], cache["caches"], d.actor_blocks, False, False)
     grads.update(g2)
     return grads
@@ -330,7 +378,7 @@ def critic_forward(p, d: Dims, obs, act, training, dtype=np.float64):
     x = np.broadcast_to(x[None], (2,) + x.shape)
     u, caches, stats = backbone_forward(p, x, d.critic_blocks, training, True, dtype)
     w = p["predictor.w.weight"].astype(dtype)
-    logits = linear(u, w) + p["predictor.bias"].astype(dtype)[:, None, :]
+    logits = linear(_rf(u), _rf(w)) + p["predictor.bias"].astype(dtype)[:, None, :]
     mx = logits.max(axis=-1, keepdims=True)
     lse = mx + np.log(np.exp(logits - mx).sum(axis=-1, keepdims=True))
     log_probs = logits - lse
@@ -351,10 +399,10 @@ def critic_backward(cache, d: Dims, d_log_probs=None, d_q=None, need_input_grad=
         d_logits += d_q[..., None] * probs * (z - q[..., None])
     u = cache["u"]
     grads = {
-        "predictor.w.weight": np.einsum("trn,trk->tnk", d_logits, u),
+        "predictor.w.weight": np.einsum("trn,trk->tnk", _rg(d_logits), _rf(u)),
         "predictor.bias": d_logits.sum(axis=1),
     }
-    du = np.einsum("trn,tnk->trk", d_logits, cache["w"])
+    du = np.einsum("trn,tnk->trk", _rg(d_logits), _rf(cache["w"]))
     g2, dx = backbone_backward(du, cache["caches"], d.critic_blocks, True, need_input_grad)
     grads.update(g2)
     return grads, (dx.sum(axis=0) if need_input_grad else None)
@@ -553,6 +601,7 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
     a_nobs = nobs[:, : d.obs]
     B = obs.shape[0]
     metrics = {}
+    grads_out = {}
 
     if do_actor:
         # ---- update_actor (updates.py:83-166)
@@ -578,6 +627,7 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
         d_lp = np.zeros(2 * B)
         d_lp[:B] = alpha / B
         grads = actor_backward(a_cache, d, d_act, d_lp)
+        grads_out["actor"] = grads
         entropy = -lps.mean()
         metrics["actor/loss"] = loss
         metrics["actor/entropy"] = entropy
@@ -612,6 +662,7 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
     loss, d_logits = categorical_loss_grad(p_lp[:, :B], tgt, 2 * B)
     metrics["critic/loss"] = loss
     grads, _ = _critic_backward_from_logits(c_cache, d, d_logits)
+    grads_out["critic"] = grads
     lr = warmup_cosine(opt_c.step, h.lr_init, h.lr_peak, h.lr_end, h.warmup, h.decay)
     critic = _apply_stats(critic, c_stats)
     critic = _adam_net(critic, grads, opt_c, c_names, lr, dtype)
@@ -621,17 +672,17 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
 
     new_state = dict(state)
     new_state.update(actor=actor, critic=critic, target=target, log_temp=log_temp,
-                     opt_actor=opt_a, opt_critic=opt_c, opt_temp=opt_t)
+                     opt_actor=opt_a, opt_critic=opt_c, opt_temp=opt_t, grads=grads_out)
     return new_state, metrics
 
 
 def _critic_backward_from_logits(cache, d: Dims, d_logits):
     u = cache["u"]
     grads = {
-        "predictor.w.weight": np.einsum("trn,trk->tnk", d_logits, u),
+        "predictor.w.weight": np.einsum("trn,trk->tnk", _rg(d_logits), _rf(u)),
         "predictor.bias": d_logits.sum(axis=1),
     }
-    du = np.einsum("trn,tnk->trk", d_logits, cache["w"])
+    du = np.einsum("trn,tnk->trk", _rg(d_logits), _rf(cache["w"]))
     g2, _ = backbone_backward(du, cache["caches"], d.critic_blocks, True, False)
     grads.update(g2)
     return grads, None

@@ -27,6 +27,12 @@ SZ = ctypes.c_size_t
 U64 = ctypes.c_uint64
 
 
+class Plane(ctypes.Structure):
+    """``rl2_plane`` (include/rl2.h): fp16 operand plane or tf32 hi/lo pair."""
+
+    _fields_ = [("h16", P), ("hi", P), ("lo", P), ("ld", LL), ("twin_stride", LL), ("scale", P), ("found_inf", P)]
+
+
 class GemmDesc(ctypes.Structure):
     """``rl2_gemm_desc`` (include/rl2.h)."""
 
@@ -39,6 +45,7 @@ class GemmDesc(ctypes.Structure):
         ("residual", P), ("ldr", LL), ("residual_batch_stride", LL),
         ("stat_mean", P), ("stat_m2", P), ("stat_batch_stride", LL),
         ("scale", P), ("k_splits", I), ("d_split_stride", LL), ("tile_n", I), ("health", P),
+        ("out_plane", Plane),
     ]
 
 
@@ -59,6 +66,84 @@ class CriticObjectiveArgs(ctypes.Structure):
     ]
 
 
+class BnApplyArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", P), ("ldx", LL), ("x_twin_stride", LL), ("twins", I), ("rows", I), ("cols", I),
+        ("mean", P), ("invstd", P), ("gamma", P), ("beta", P), ("relu", I),
+        ("residual", P), ("ldr", LL), ("residual_twin_stride", LL),
+        ("y", P), ("ldy", LL), ("y_twin_stride", LL), ("plane", Plane),
+    ]
+
+
+class BnBackwardArgs(ctypes.Structure):
+    _fields_ = [
+        ("dy", P), ("lddy", LL), ("dy_twin_stride", LL), ("x", P), ("ldx", LL), ("x_twin_stride", LL),
+        ("twins", I), ("rows", I), ("cols", I), ("mean", P), ("invstd", P), ("gamma", P), ("beta", P),
+        ("relu", I), ("training", I), ("s1_part", P), ("s2_part", P), ("coef1", P), ("coef2", P),
+        ("dx", P), ("lddx", LL), ("dx_twin_stride", LL), ("sum_twins", I), ("plane", Plane),
+    ]
+
+
+class PolicyArgs(ctypes.Structure):
+    _fields_ = [
+        ("head", P), ("ld_head", LL), ("noise", P), ("ld_noise", LL), ("rows", I), ("act", I),
+        ("actions", P), ("ld_actions", LL), ("log_pi", P), ("grad_rows", I), ("d_action", P), ("ld_d_action", LL),
+        ("d_log_pi", P), ("d_log_pi_value", P), ("bc_alpha", F), ("q_abs", P), ("replay_action", P),
+        ("ld_replay_action", LL), ("d_head", P), ("ld_d_head", LL), ("d_plane", Plane), ("bias_part", P),
+    ]
+
+
+class ActorObjectiveArgs(ctypes.Structure):
+    _fields_ = [
+        ("logits", P), ("logits_row_stride", LL), ("logits_twin_stride", LL), ("support", P),
+        ("bins", I), ("batch", I), ("act", I), ("log_pi", P), ("actions", P), ("actions_row_stride", LL),
+        ("replay_action", P), ("replay_row_stride", LL), ("bc_alpha", F), ("alpha", P), ("d_logits", Plane),
+        ("workspace", P), ("counter", P), ("loss_out", P), ("entropy_out", P), ("mean_action_out", P),
+        ("q_abs_out", P), ("d_log_pi_out", P),
+    ]
+
+
+class TemperatureArgs(ctypes.Structure):
+    _fields_ = [
+        ("log_temp", P), ("entropy", P), ("target_entropy", F), ("adam_state", P), ("beta1", F), ("beta2", F),
+        ("eps", F), ("lr_init", D), ("lr_peak", D), ("lr_end", D), ("warmup_steps", D), ("decay_steps", D),
+        ("update", I), ("value_out", P), ("loss_out", P), ("alpha_out", P),
+    ]
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [("offset", LL), ("offset2", LL), ("plane_offset", LL), ("length", I), ("kind", I)]
+
+
+class AdamPrepareArgs(ctypes.Structure):
+    _fields_ = [
+        ("state", P), ("found_inf", P), ("formula", I), ("beta1", F), ("beta2", F),
+        ("lr_init", D), ("lr_peak", D), ("lr_end", D), ("warmup_steps", D), ("decay_steps", D),
+        ("schedule_on_attempts", I), ("lr_override", P), ("scaler", I), ("growth", F), ("backoff", F),
+        ("growth_interval", I), ("scale_out", P), ("inv_scale_out", P),
+    ]
+
+
+class AdamArgs(ctypes.Structure):
+    _fields_ = [
+        ("params", P), ("grads", P), ("m", P), ("v", P), ("segments", P), ("count", I), ("state", P),
+        ("formula", I), ("beta1", F), ("beta2", F), ("eps", F), ("project", I), ("weight_plane", Plane),
+        ("target_params", P), ("tau", F), ("target_plane", Plane),
+    ]
+
+
+class ReplayGatherArgs(ctypes.Structure):
+    _fields_ = [
+        ("indices", P), ("batch", I), ("obs", P), ("next_obs", P), ("ld_obs", LL), ("action", P),
+        ("ld_action", LL), ("reward", P), ("terminated", P), ("truncated", P), ("discount", P),
+        ("obs_dim", I), ("act_dim", I), ("actor_obs_dim", I), ("critic_x", P), ("ld_critic_x", LL),
+        ("actor_x", P), ("ld_actor_x", LL), ("reward_out", P), ("terminated_out", P), ("truncated_out", P),
+        ("discount_out", P), ("g_var", P), ("g_r_max", P), ("g_max", F), ("norm_eps", F),
+        ("batch_obs", P), ("batch_next_obs", P), ("batch_action", P), ("batch_reward", P),
+        ("critic_x_pi", P), ("ld_critic_x_pi", LL),
+    ]
+
+
 # name -> (argtypes, restype); every symbol here is declared in include/rl2.h
 SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_last_error": ([], ctypes.c_char_p),
@@ -70,6 +155,29 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_split_reduce": ([P, LL, I, P, LL, I, P], I),
     "rl2_categorical_workspace_floats": ([I, I], I),
     "rl2_critic_objective": ([ctypes.POINTER(CriticObjectiveArgs), P], I),
+    "rl2_colstats": ([P, LL, LL, I, I, I, P, P, LL, P], I),
+    "rl2_bn_finalize": ([P, P, LL, I, I, I, P, P, P, P, F, F, I, P], I),
+    "rl2_bn_eval_prepare": ([P, P, LL, F, P, P, P], I),
+    "rl2_bn_apply": ([ctypes.POINTER(BnApplyArgs), P], I),
+    "rl2_bn_backward_reduce": ([ctypes.POINTER(BnBackwardArgs), P], I),
+    "rl2_bn_backward_finalize": ([P, P, I, I, I, P, P, LL, I, P, P, P], I),
+    "rl2_bn_backward_apply": ([ctypes.POINTER(BnBackwardArgs), P], I),
+    "rl2_rms_forward": ([P, LL, LL, I, I, I, P, F, P, P, LL, LL, ctypes.POINTER(Plane), P], I),
+    "rl2_rms_backward": ([P, LL, LL, P, LL, LL, P, P, I, I, I, P, LL, LL, P, P], I),
+    "rl2_colsum_finalize": ([P, I, I, I, P, LL, I, P], I),
+    "rl2_policy_sample": ([ctypes.POINTER(PolicyArgs), I, P], I),
+    "rl2_policy_backward": ([ctypes.POINTER(PolicyArgs), P], I),
+    "rl2_actor_objective_workspace_floats": ([I], I),
+    "rl2_actor_objective": ([ctypes.POINTER(ActorObjectiveArgs), P], I),
+    "rl2_temperature_step": ([ctypes.POINTER(TemperatureArgs), P], I),
+    "rl2_adam_prepare": ([ctypes.POINTER(AdamPrepareArgs), P], I),
+    "rl2_adam_step": ([ctypes.POINTER(AdamArgs), P], I),
+    "rl2_segment_max_length": ([], I),
+    "rl2_replay_sample": ([ctypes.c_ulonglong, P, P, LL, I, P, P, P], I),
+    "rl2_counter_advance": ([P, ctypes.c_ulonglong, P], I),
+    "rl2_replay_gather": ([ctypes.POINTER(ReplayGatherArgs), P], I),
+    "rl2_normal_noise": ([ctypes.c_ulonglong, P, I, I, P, LL, P], I),
+    "rl2_philox4x32": ([ctypes.c_uint] * 6 + [ctypes.POINTER(ctypes.c_uint)], None),
 }
 
 
@@ -117,6 +225,15 @@ def created(handle, what: str):
 def ptr(t) -> int | None:
     """Device address of a torch tensor (None passes a null pointer)."""
     return None if t is None else t.data_ptr()
+
+
+def addr(x) -> int | None:
+    """Device address of a tensor, or an integer address passed through; None stays null."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
 
 
 def stream_ptr(stream=None) -> int:

@@ -27,8 +27,7 @@
 // sum of squared deviations) feed training-mode batch norm without another read
 // of the output.
 
-#include "common.cuh"
-#include "../../include/rl2.h"
+#include "planes.cuh"
 
 #include <algorithm>
 #include <cstring>
@@ -57,6 +56,7 @@ struct Params {
     long long stat_bstride;
     const float* scale;
     int* health;
+    Plane out_plane;
 };
 
 // Wall-clock bounded mbarrier wait (4 s), so a lost arrival cannot hang the GPU.
@@ -285,9 +285,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int valid = min(max(p.M - (m_tile * kBM + q * 32), 0), 32);
         const bool ok = wait_bar(acc_full, 0, p.health);
         ptx::tc_fence_after();
+        PlaneWriter pw(p.out_plane);
         if (ok && n_kb > 0) {
             const float scale = p.scale ? *p.scale : 1.0f;
-            float* d = p.d + static_cast<long long>(z) * p.d_bstride + static_cast<long long>(split) * p.d_split_stride;
+            float* d = p.d ? p.d + static_cast<long long>(z) * p.d_bstride + static_cast<long long>(split) * p.d_split_stride
+                           : nullptr;
             const float* bias = p.bias ? p.bias + static_cast<long long>(z) * p.bias_bstride : nullptr;
             const float* res = p.residual ? p.residual + static_cast<long long>(z) * p.r_bstride : nullptr;
             const int group = (m_tile * kBM) / 32 + q;
@@ -303,11 +305,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (col < p.N) {
                         if (bias) x += bias[col];
                         if (res && row_ok) x += res[static_cast<long long>(row) * p.ldr + col];
-                        if (p.accumulate && row_ok) x += d[static_cast<long long>(row) * p.ldd + col];
+                        if (p.accumulate && row_ok && d) x += d[static_cast<long long>(row) * p.ldd + col];
                     }
                     v[i] = x;
                 }
-                if (row_ok) {
+                if (row_ok && pw.active()) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (col0 + i < p.N) pw.store(z, row, col0 + i, v[i]);
+                }
+                if (row_ok && p.d) {
                     float* drow = d + static_cast<long long>(row) * p.ldd + col0;
                     if (col0 + 16 <= p.N && (p.ldd & 3) == 0 && ptx::aligned16(drow)) {
 #pragma unroll
@@ -342,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        pw.flush();
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -471,8 +479,12 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         set_error("GEMM requires kind 0/1 and positive m, n, k, batch");
         return nullptr;
     }
-    if (!g->a || !g->b || !g->d || (g->kind == 1 && (!g->a_lo || !g->b_lo))) {
+    if (!g->a || !g->b || (!g->d && !plane_used(&g->out_plane)) || (g->kind == 1 && (!g->a_lo || !g->b_lo))) {
         set_error("GEMM operands / output must be non-null (kind 1 also needs a_lo and b_lo)");
+        return nullptr;
+    }
+    if (!plane_valid(&g->out_plane) || (plane_used(&g->out_plane) && (g->k_splits > 1 || g->accumulate))) {
+        set_error("GEMM output plane must be a valid fp16 or hi/lo plane, without split-K or accumulate");
         return nullptr;
     }
     if ((g->a_major != 0 && g->a_major != 1) || (g->b_major != 0 && g->b_major != 1)) {
@@ -559,6 +571,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.stat_bstride = g->stat_batch_stride;
     p.scale = g->scale;
     p.health = g->health;
+    p.out_plane = to_plane(&g->out_plane);
     const int planes = g->kind == 0 ? 1 : 2;
     const int stage_bytes = (kBM * 128 + bn * 128) * planes;
     const int overhead = 1024 + 256;
@@ -575,10 +588,12 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         delete plan;
         return nullptr;
     }
+    // The limit is an attribute of the kernel function shared by every plan that uses
+    // it, so it is always raised to the device maximum (never lowered by a small plan).
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             plan->smem) != cudaSuccess) {
-        set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", plan->smem);
+                             kMaxSmem) != cudaSuccess) {
+        set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", kMaxSmem);
         delete plan;
         return nullptr;
     }

@@ -1,0 +1,407 @@
+// Batch norm (training / evaluation), RMS post-norm and column-sum helpers for
+// the residual MLPs. Reference semantics: src/robolearn/flashsac/layers.py:32-81
+// and :189-240; reference native kernels: src/robolearn/cuda/flash_kernels.cuh:142-379.
+//
+// Column statistics travel as per-32-row-group partials (the same layout the
+// GEMM epilogue writes), merged in a fixed order, so every reduction is
+// deterministic run to run and needs no atomics. The element-wise passes are
+// plain HBM-streaming kernels: one thread per (row, column) with consecutive
+// threads on consecutive columns (coalesced), grid-stride over rows.
+
+#include "planes.cuh"
+
+#include <algorithm>
+
+namespace rl2 {
+namespace norm {
+
+constexpr int kT = 256;
+
+__device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_a, float n_b, float mean_b,
+                                           float m2_b) {
+    if (n_b <= 0.0f) return;
+    const float n = n_a + n_b;
+    const float delta = mean_b - mean_a;
+    mean_a = mean_a + delta * (n_b / n);
+    m2_a = m2_a + m2_b + delta * delta * (n_a * n_b / n);
+    n_a = n;
+}
+
+// grid (ceil(cols/kT), G, twins)
+__global__ void colstats_kernel(const float* __restrict__ x, long long ldx, long long xt, int rows, int cols,
+                                float* __restrict__ mean_p, float* __restrict__ m2_p, long long pt) {
+    const int c = blockIdx.x * kT + threadIdx.x;
+    const int g = blockIdx.y;
+    const int t = blockIdx.z;
+    if (c >= cols) return;
+    const int r0 = g * 32;
+    const int n = min(32, rows - r0);
+    const float* src = x + t * xt + static_cast<long long>(r0) * ldx + c;
+    float s = 0.0f;
+    for (int i = 0; i < n; ++i) s += src[i * ldx];
+    const float mean = s / static_cast<float>(n);
+    float m2 = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const float d = src[i * ldx] - mean;
+        m2 += d * d;
+    }
+    const long long o = t * pt + static_cast<long long>(g) * cols + c;
+    mean_p[o] = mean;
+    m2_p[o] = m2;
+}
+
+// thread per (twin, column)
+__global__ void finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p, long long pt,
+                                int twins, int rows, int cols, float* mean, float* invstd, float* rm, float* rv,
+                                float momentum, float eps, int update) {
+    const int i = blockIdx.x * kT + threadIdx.x;
+    if (i >= twins * cols) return;
+    const int t = i / cols, c = i % cols;
+    const int groups = (rows + 31) / 32;
+    const float* mp = mean_p + t * pt + c;
+    const float* qp = m2_p + t * pt + c;
+    float n = 0.0f, mu = 0.0f, m2 = 0.0f;
+    for (int g = 0; g < groups; ++g) {
+        const float ng = static_cast<float>(min(32, rows - g * 32));
+        chan_merge(n, mu, m2, ng, mp[static_cast<long long>(g) * cols], qp[static_cast<long long>(g) * cols]);
+    }
+    const float var = m2 / static_cast<float>(rows);
+    mean[i] = mu;
+    invstd[i] = 1.0f / sqrtf(var + eps);
+    if (update) {
+        const float unbiased = var * (static_cast<float>(rows) / static_cast<float>(rows - 1));
+        rm[i] = rm[i] + momentum * (mu - rm[i]);
+        rv[i] = rv[i] + momentum * (unbiased - rv[i]);
+    }
+}
+
+__global__ void eval_prepare_kernel(const float* rm, const float* rv, long long count, float eps, float* mean,
+                                    float* invstd) {
+    const long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x;
+    if (i >= count) return;
+    mean[i] = rm[i];
+    invstd[i] = 1.0f / sqrtf(rv[i] + eps);
+}
+
+__global__ void apply_kernel(const rl2_bn_apply_args a, const Plane plane) {
+    PlaneWriter pw(plane);
+    const long long per_twin = static_cast<long long>(a.rows) * a.cols;
+    const long long total = per_twin * a.twins;
+    for (long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * kT) {
+        const int t = static_cast<int>(i / per_twin);
+        const long long rc = i % per_twin;
+        const long long r = rc / a.cols;
+        const int c = static_cast<int>(rc % a.cols);
+        const int tc = t * a.cols + c;
+        const float xv = a.x[t * a.x_twin_stride + r * a.ldx + c];
+        float y = (xv - a.mean[tc]) * a.invstd[tc] * a.gamma[tc] + a.beta[tc];
+        if (a.relu) y = fmaxf(y, 0.0f);
+        if (a.residual) y += a.residual[t * a.residual_twin_stride + r * a.ldr + c];
+        if (a.y) a.y[t * a.y_twin_stride + r * a.ldy + c] = y;
+        if (pw.active()) pw.store(t, r, c, y);
+    }
+    pw.flush();
+}
+
+// d(normalised output) for one element: dy masked by the ReLU of the recomputed output
+__device__ __forceinline__ float masked_dbn(const rl2_bn_backward_args& a, int t, long long r, int c, float& xhat) {
+    const int tc = t * a.cols + c;
+    const float xv = a.x[t * a.x_twin_stride + r * a.ldx + c];
+    xhat = (xv - a.mean[tc]) * a.invstd[tc];
+    float d = a.dy[t * a.dy_twin_stride + r * a.lddy + c];
+    if (a.relu && !(xhat * a.gamma[tc] + a.beta[tc] > 0.0f)) d = 0.0f;
+    return d;
+}
+
+// grid (ceil(cols/kT), G, twins)
+__global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
+    const int c = blockIdx.x * kT + threadIdx.x;
+    const int g = blockIdx.y;
+    const int t = blockIdx.z;
+    if (c >= a.cols) return;
+    const int r0 = g * 32;
+    const int n = min(32, a.rows - r0);
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        float xhat;
+        const float d = masked_dbn(a, t, r0 + i, c, xhat);
+        s1 += d;
+        s2 += d * xhat;
+    }
+    const int groups = (a.rows + 31) / 32;
+    const long long o = (static_cast<long long>(t) * groups + g) * a.cols + c;
+    a.s1_part[o] = s1;
+    a.s2_part[o] = s2;
+}
+
+__global__ void bwd_finalize_kernel(const float* s1p, const float* s2p, int twins, int rows, int cols, float* dgamma,
+                                    float* dbeta, long long gts, int accumulate, float* coef1, float* coef2) {
+    const int i = blockIdx.x * kT + threadIdx.x;
+    if (i >= twins * cols) return;
+    const int t = i / cols, c = i % cols;
+    const int groups = (rows + 31) / 32;
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int g = 0; g < groups; ++g) {
+        const long long o = (static_cast<long long>(t) * groups + g) * cols + c;
+        s1 += s1p[o];
+        s2 += s2p[o];
+    }
+    if (dgamma) dgamma[t * gts + c] = accumulate ? dgamma[t * gts + c] + s2 : s2;
+    if (dbeta) dbeta[t * gts + c] = accumulate ? dbeta[t * gts + c] + s1 : s1;
+    if (coef1) coef1[i] = s1 / static_cast<float>(rows);
+    if (coef2) coef2[i] = s2 / static_cast<float>(rows);
+}
+
+__global__ void bwd_apply_kernel(const rl2_bn_backward_args a, const Plane plane) {
+    PlaneWriter pw(plane);
+    const int twins_out = a.sum_twins ? 1 : a.twins;
+    const long long per_twin = static_cast<long long>(a.rows) * a.cols;
+    const long long total = per_twin * twins_out;
+    for (long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * kT) {
+        const int to = static_cast<int>(i / per_twin);
+        const long long rc = i % per_twin;
+        const long long r = rc / a.cols;
+        const int c = static_cast<int>(rc % a.cols);
+        float acc = 0.0f;
+        const int t_begin = a.sum_twins ? 0 : to;
+        const int t_end = a.sum_twins ? a.twins : to + 1;
+        for (int t = t_begin; t < t_end; ++t) {
+            const int tc = t * a.cols + c;
+            float xhat;
+            const float d = masked_dbn(a, t, r, c, xhat);
+            float dx;
+            if (a.training)
+                dx = a.gamma[tc] * a.invstd[tc] * (d - a.coef1[tc] - xhat * a.coef2[tc]);
+            else
+                dx = a.gamma[tc] * a.invstd[tc] * d;
+            acc += dx;
+        }
+        if (a.dx) a.dx[to * a.dx_twin_stride + r * a.lddx + c] = acc;
+        if (pw.active()) pw.store(to, r, c, acc);
+    }
+    pw.flush();
+}
+
+// one warp per row
+__global__ void rms_forward_kernel(const float* __restrict__ h, long long ldh, long long ht, int twins, int rows,
+                                   int cols, const float* __restrict__ gamma, float eps, float* __restrict__ r_out,
+                                   float* __restrict__ u, long long ldu, long long ut, const Plane plane) {
+    PlaneWriter pw(plane);
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (kT / 32);
+    for (long long w = blockIdx.x * static_cast<long long>(kT / 32) + (threadIdx.x >> 5); w < static_cast<long long>(twins) * rows;
+         w += warps) {
+        const int t = static_cast<int>(w / rows);
+        const long long r = w % rows;
+        const float* src = h + t * ht + r * ldh;
+        float ss = 0.0f;
+        for (int c = lane; c < cols; c += 32) ss += src[c] * src[c];
+        ss = warp_sum(ss);
+        const float rr = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+        if (lane == 0) r_out[w] = rr;
+        for (int c = lane; c < cols; c += 32) {
+            const float v = src[c] * rr * gamma[t * cols + c];
+            if (u) u[t * ut + r * ldu + c] = v;
+            if (pw.active()) pw.store(t, r, c, v);
+        }
+    }
+    pw.flush();
+}
+
+__global__ void rms_backward_kernel(const float* __restrict__ du, long long lddu, long long dut,
+                                    const float* __restrict__ h, long long ldh, long long ht,
+                                    const float* __restrict__ rv, const float* __restrict__ gamma, int twins, int rows,
+                                    int cols, float* __restrict__ dh, long long lddh, long long dht) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (kT / 32);
+    for (long long w = blockIdx.x * static_cast<long long>(kT / 32) + (threadIdx.x >> 5); w < static_cast<long long>(twins) * rows;
+         w += warps) {
+        const int t = static_cast<int>(w / rows);
+        const long long r = w % rows;
+        const float* d = du + t * dut + r * lddu;
+        const float* x = h + t * ht + r * ldh;
+        const float* g = gamma + t * cols;
+        float s = 0.0f;
+        for (int c = lane; c < cols; c += 32) s += g[c] * d[c] * x[c];
+        s = warp_sum(s);
+        const float rr = rv[w];
+        const float k = rr * rr * rr * s / static_cast<float>(cols);
+        float* o = dh + t * dht + r * lddh;
+        for (int c = lane; c < cols; c += 32) o[c] = rr * g[c] * d[c] - x[c] * k;
+    }
+}
+
+// grid (ceil(cols/kT), G, twins): per-group column sums of du * h * r
+__global__ void rms_dgamma_kernel(const float* __restrict__ du, long long lddu, long long dut,
+                                  const float* __restrict__ h, long long ldh, long long ht,
+                                  const float* __restrict__ rv, int rows, int cols, float* __restrict__ part) {
+    const int c = blockIdx.x * kT + threadIdx.x;
+    const int g = blockIdx.y;
+    const int t = blockIdx.z;
+    if (c >= cols) return;
+    const int r0 = g * 32;
+    const int n = min(32, rows - r0);
+    float s = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const long long r = r0 + i;
+        s += du[t * dut + r * lddu + c] * h[t * ht + r * ldh + c] * rv[static_cast<long long>(t) * rows + r];
+    }
+    const int groups = (rows + 31) / 32;
+    part[(static_cast<long long>(t) * groups + g) * cols + c] = s;
+}
+
+__global__ void colsum_finalize_kernel(const float* part, int twins, int groups, int cols, float* out, long long ots,
+                                       int accumulate) {
+    const int i = blockIdx.x * kT + threadIdx.x;
+    if (i >= twins * cols) return;
+    const int t = i / cols, c = i % cols;
+    float s = 0.0f;
+    for (int g = 0; g < groups; ++g) s += part[(static_cast<long long>(t) * groups + g) * cols + c];
+    out[t * ots + c] = accumulate ? out[t * ots + c] + s : s;
+}
+
+inline int stream_blocks(long long work) {
+    return static_cast<int>(std::max<long long>(1, std::min<long long>((work + kT - 1) / kT, 148LL * 16)));
+}
+
+}  // namespace norm
+}  // namespace rl2
+
+using namespace rl2;
+
+extern "C" int rl2_colstats(const float* x, long long ldx, long long xt, int twins, int rows, int cols, float* mean_p,
+                            float* m2_p, long long pt, void* stream) {
+    clear_error();
+    if (!x || !mean_p || !m2_p || twins < 1 || rows < 1 || cols < 1) {
+        set_error("colstats: null buffer or empty shape");
+        return -1;
+    }
+    const dim3 grid((cols + norm::kT - 1) / norm::kT, (rows + 31) / 32, twins);
+    norm::colstats_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(x, ldx, xt, rows, cols, mean_p, m2_p, pt);
+    return launch_status("column statistics");
+}
+
+extern "C" int rl2_bn_finalize(const float* mean_p, const float* m2_p, long long pt, int twins, int rows, int cols,
+                               float* mean, float* invstd, float* rm, float* rv, float momentum, float eps,
+                               int update, void* stream) {
+    clear_error();
+    if (!mean_p || !m2_p || !mean || !invstd || twins < 1 || rows < 1 || cols < 1 || !(eps > 0.0f) ||
+        (update && (!rm || !rv || rows < 2))) {
+        set_error("bn finalize: invalid buffers or shape (running update needs rows >= 2)");
+        return -1;
+    }
+    norm::finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+        mean_p, m2_p, pt, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update);
+    return launch_status("batch-norm statistics");
+}
+
+extern "C" int rl2_bn_eval_prepare(const float* rm, const float* rv, long long count, float eps, float* mean,
+                                   float* invstd, void* stream) {
+    clear_error();
+    if (!rm || !rv || !mean || !invstd || count < 1) {
+        set_error("bn eval prepare: invalid buffers");
+        return -1;
+    }
+    norm::eval_prepare_kernel<<<static_cast<int>((count + norm::kT - 1) / norm::kT), norm::kT, 0,
+                                as_stream(stream)>>>(rm, rv, count, eps, mean, invstd);
+    return launch_status("batch-norm eval statistics");
+}
+
+extern "C" int rl2_bn_apply(const rl2_bn_apply_args* a, void* stream) {
+    clear_error();
+    if (!a || !a->x || !a->mean || !a->invstd || !a->gamma || !a->beta || a->twins < 1 || a->rows < 1 ||
+        a->cols < 1 || !plane_valid(&a->plane) || (!a->y && !plane_used(&a->plane))) {
+        set_error("bn apply: invalid arguments");
+        return -1;
+    }
+    const long long work = static_cast<long long>(a->twins) * a->rows * a->cols;
+    norm::apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
+    return launch_status("batch-norm apply");
+}
+
+extern "C" int rl2_bn_backward_reduce(const rl2_bn_backward_args* a, void* stream) {
+    clear_error();
+    if (!a || !a->dy || !a->x || !a->mean || !a->invstd || !a->gamma || !a->beta || !a->s1_part || !a->s2_part ||
+        a->twins < 1 || a->rows < 1 || a->cols < 1) {
+        set_error("bn backward reduce: invalid arguments");
+        return -1;
+    }
+    const dim3 grid((a->cols + norm::kT - 1) / norm::kT, (a->rows + 31) / 32, a->twins);
+    norm::bwd_reduce_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(*a);
+    return launch_status("batch-norm backward reduce");
+}
+
+extern "C" int rl2_bn_backward_finalize(const float* s1p, const float* s2p, int twins, int rows, int cols,
+                                        float* dgamma, float* dbeta, long long gts, int accumulate, float* coef1,
+                                        float* coef2, void* stream) {
+    clear_error();
+    if (!s1p || !s2p || twins < 1 || rows < 1 || cols < 1) {
+        set_error("bn backward finalize: invalid arguments");
+        return -1;
+    }
+    norm::bwd_finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+        s1p, s2p, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+    return launch_status("batch-norm backward finalize");
+}
+
+extern "C" int rl2_bn_backward_apply(const rl2_bn_backward_args* a, void* stream) {
+    clear_error();
+    if (!a || !a->dy || !a->x || !a->mean || !a->invstd || !a->gamma || !a->beta || a->twins < 1 || a->rows < 1 ||
+        a->cols < 1 || (a->training && (!a->coef1 || !a->coef2)) || !plane_valid(&a->plane) ||
+        (!a->dx && !plane_used(&a->plane))) {
+        set_error("bn backward apply: invalid arguments");
+        return -1;
+    }
+    const long long work = static_cast<long long>(a->sum_twins ? 1 : a->twins) * a->rows * a->cols;
+    norm::bwd_apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
+    return launch_status("batch-norm backward apply");
+}
+
+extern "C" int rl2_rms_forward(const float* h, long long ldh, long long ht, int twins, int rows, int cols,
+                               const float* gamma, float eps, float* r_out, float* u, long long ldu, long long ut,
+                               const rl2_plane* plane, void* stream) {
+    clear_error();
+    if (!h || !gamma || !r_out || twins < 1 || rows < 1 || cols < 1 || !plane_valid(plane) ||
+        (!u && !plane_used(plane))) {
+        set_error("rms forward: invalid arguments");
+        return -1;
+    }
+    const long long warps = static_cast<long long>(twins) * rows;
+    norm::rms_forward_kernel<<<norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream)>>>(
+        h, ldh, ht, twins, rows, cols, gamma, eps, r_out, u, ldu, ut, to_plane(plane));
+    return launch_status("rms forward");
+}
+
+extern "C" int rl2_rms_backward(const float* du, long long lddu, long long dut, const float* h, long long ldh,
+                                long long ht, const float* r, const float* gamma, int twins, int rows, int cols,
+                                float* dh, long long lddh, long long dht, float* dgamma_part, void* stream) {
+    clear_error();
+    if (!du || !h || !r || !gamma || !dh || twins < 1 || rows < 1 || cols < 1) {
+        set_error("rms backward: invalid arguments");
+        return -1;
+    }
+    const long long warps = static_cast<long long>(twins) * rows;
+    norm::rms_backward_kernel<<<norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream)>>>(
+        du, lddu, dut, h, ldh, ht, r, gamma, twins, rows, cols, dh, lddh, dht);
+    if (launch_status("rms backward")) return -1;
+    if (dgamma_part) {
+        const dim3 grid((cols + norm::kT - 1) / norm::kT, (rows + 31) / 32, twins);
+        norm::rms_dgamma_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(du, lddu, dut, h, ldh, ht, r, rows, cols,
+                                                                        dgamma_part);
+    }
+    return launch_status("rms weight gradient");
+}
+
+extern "C" int rl2_colsum_finalize(const float* part, int twins, int groups, int cols, float* out, long long ots,
+                                   int accumulate, void* stream) {
+    clear_error();
+    if (!part || !out || twins < 1 || groups < 1 || cols < 1) {
+        set_error("colsum finalize: invalid arguments");
+        return -1;
+    }
+    norm::colsum_finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+        part, twins, groups, cols, out, ots, accumulate);
+    return launch_status("column-sum finalize");
+}

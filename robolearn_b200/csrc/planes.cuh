@@ -1,0 +1,74 @@
+// Operand planes: the derived copies of activations / gradients / weights that
+// feed the tensor-core products. Kind 0 is one fp16 plane (optionally multiplied
+// by a device loss scale, overflow recorded in *found_inf); kind 1 is a pair of
+// fp32 planes hi + lo with hi exactly representable in tf32 (the 3xTF32 split).
+// Rows have their own stride (16-byte aligned for TMA) and an optional twin stride.
+#pragma once
+
+#include "common.cuh"
+#include "../../include/rl2.h"
+
+namespace rl2 {
+
+struct Plane {
+    __half* h16;
+    float* hi;
+    float* lo;
+    long long ld, tstride;
+    const float* scale;
+    int* found_inf;
+};
+
+inline Plane to_plane(const rl2_plane* p) {
+    Plane q{};
+    if (!p) return q;
+    q.h16 = reinterpret_cast<__half*>(p->h16);
+    q.hi = p->hi;
+    q.lo = p->lo;
+    q.ld = p->ld;
+    q.tstride = p->twin_stride;
+    q.scale = p->scale;
+    q.found_inf = p->found_inf;
+    return q;
+}
+
+inline bool plane_valid(const rl2_plane* p) {
+    if (!p) return true;
+    if (p->h16 && (p->hi || p->lo)) return false;
+    if ((p->hi == nullptr) != (p->lo == nullptr)) return false;
+    return true;
+}
+
+inline bool plane_used(const rl2_plane* p) { return p && (p->h16 || p->hi); }
+
+#if defined(__CUDACC__)
+__device__ __forceinline__ float tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+// Per-thread cache of the plane's scale (read once).
+struct PlaneWriter {
+    Plane p;
+    float scale;
+    bool overflow;
+    __device__ __forceinline__ explicit PlaneWriter(const Plane& q) : p(q), scale(1.0f), overflow(false) {
+        if (p.h16 && p.scale) scale = *p.scale;
+    }
+    __device__ __forceinline__ bool active() const { return p.h16 != nullptr || p.hi != nullptr; }
+    __device__ __forceinline__ void store(int t, long long row, int col, float v) {
+        const long long o = static_cast<long long>(t) * p.tstride + row * p.ld + col;
+        if (p.h16) {
+            const float s = v * scale;
+            overflow |= !(fabsf(s) <= 65504.0f);
+            p.h16[o] = __float2half_rn(s);
+        } else if (p.hi) {
+            const float h = tf32_hi(v);
+            p.hi[o] = h;
+            p.lo[o] = v - h;
+        }
+    }
+    __device__ __forceinline__ void flush() {
+        if (p.found_inf && overflow) atomicOr(p.found_inf, 1);
+    }
+};
+#endif
+
+}  // namespace rl2

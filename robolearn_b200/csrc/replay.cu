@@ -1,0 +1,219 @@
+// Replay index sampling and batch gather for the FlashSAC learner.
+//
+// Reference semantics (paths inside the reference project):
+//   unbiased bounded index   src/robolearn/warp/_flash_replay.py:116-128 (threshold = (-n) % n,
+//                            reject v < threshold, index = v % n)
+//   batch gather             src/robolearn/warp/_flash_replay.py:131-160, flashsac/replay.py:179-194
+//   batch assembly           src/robolearn/warp/flashsac.py:53-69,166-182 (actor rows, critic rows)
+//   reward normalisation     src/robolearn/flashsac/_utils/reward_normalization.py:28-38
+//
+// The random stream is Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel
+// random numbers: as easy as 1, 2, 3", SC'11), counter = (row, draw epoch,
+// rejection round, stream) and key = seed. Warp's own generator is not
+// reproduced; parity is anchored on explicit indices, which this gather takes too.
+// The gather writes straight into the concatenated layouts the networks read:
+// critic rows [obs | action] for i and [next_obs | (next action later)] for B+i,
+// actor rows obs_prefix for i and next_obs_prefix for B+i. Copies are bit-exact.
+
+#include "common.cuh"
+#include "../../include/rl2.h"
+
+#include <algorithm>
+
+namespace rl2 {
+namespace replay {
+
+constexpr int kT = 256;
+
+struct U4 {
+    uint32_t x, y, z, w;
+};
+
+__host__ __device__ __forceinline__ void mulhilo(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
+    const uint64_t p = static_cast<uint64_t>(a) * static_cast<uint64_t>(b);
+    hi = static_cast<uint32_t>(p >> 32);
+    lo = static_cast<uint32_t>(p);
+}
+
+// Philox4x32 with 10 rounds: multipliers 0xD2511F53 / 0xCD9E8D57, Weyl key
+// increments 0x9E3779B9 / 0xBB67AE85 (constants from the published algorithm).
+__host__ __device__ __forceinline__ U4 philox(U4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        uint32_t hi0, lo0, hi1, lo1;
+        mulhilo(0xD2511F53u, c.x, hi0, lo0);
+        mulhilo(0xCD9E8D57u, c.z, hi1, lo1);
+        c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return c;
+}
+
+__global__ void sample_kernel(uint64_t seed, const unsigned long long* epoch, const long long* population,
+                              long long fixed_population, int batch, int* out, int* health) {
+    const int i = blockIdx.x * kT + threadIdx.x;
+    if (i >= batch) return;
+    const uint32_t n = static_cast<uint32_t>(population ? *population : fixed_population);
+    if (n == 0) {
+        out[i] = 0;
+        return;
+    }
+    const uint32_t threshold = (0u - n) % n;
+    const unsigned long long e = epoch ? *epoch : 0ull;
+    const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+    for (uint32_t round = 0; round < 64; ++round) {
+        const U4 r = philox(U4{static_cast<uint32_t>(i), static_cast<uint32_t>(e), static_cast<uint32_t>(e >> 32) ^ round, 0x5A11u},
+                            k0, k1);
+        const uint32_t vals[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (vals[j] >= threshold) {
+                out[i] = static_cast<int>(vals[j] % n);
+                return;
+            }
+        }
+    }
+    out[i] = 0;  // unreachable in practice (probability < 2^-256); reported, never silent
+    if (health) atomicOr(health, kHealthTimeout);
+}
+
+__global__ void advance_kernel(unsigned long long* epoch, unsigned long long by) { *epoch += by; }
+
+// Standard normal samples by the Box-Muller transform of two Philox uniforms per pair.
+__global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, int rows, int cols, float* out,
+                              long long ld) {
+    const long long total = static_cast<long long>(rows) * cols;
+    const unsigned long long e = epoch ? *epoch : 0ull;
+    const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+    for (long long q = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; q * 4 < total;
+         q += static_cast<long long>(gridDim.x) * kT) {
+        const U4 r = philox(U4{static_cast<uint32_t>(q), static_cast<uint32_t>(q >> 32), static_cast<uint32_t>(e),
+                               static_cast<uint32_t>(e >> 32) ^ 0x0A0Fu},
+                            k0, k1);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            // uniforms in (0, 1]: (u + 1) * 2^-32 with u in [0, 2^32)
+            const float u1 = (static_cast<float>(w[2 * p]) + 1.0f) * 2.3283064365386963e-10f;
+            const float u2 = static_cast<float>(w[2 * p + 1]) * 2.3283064365386963e-10f;
+            const float rad = sqrtf(-2.0f * logf(u1));
+            float sn, cs;
+            sincospif(2.0f * u2, &sn, &cs);
+            const float z[2] = {rad * cs, rad * sn};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const long long i = q * 4 + 2 * p + h;
+                if (i < total) out[(i / cols) * ld + (i % cols)] = z[h];
+            }
+        }
+    }
+}
+
+// one warp per sampled row
+__global__ void gather_kernel(const rl2_replay_gather_args a) {
+    const int lane = threadIdx.x & 31;
+    const int B = a.batch;
+    float rscale = 1.0f;
+    if (a.g_var) {
+        // r / max(sqrt(var + eps), G_r_max / G_max)
+        const float den = fmaxf(sqrtf(a.g_var[0] + a.norm_eps), a.g_r_max[0] / a.g_max);
+        rscale = den;
+    }
+    for (long long w = blockIdx.x * static_cast<long long>(kT / 32) + (threadIdx.x >> 5); w < B;
+         w += static_cast<long long>(gridDim.x) * (kT / 32)) {
+        const int i = static_cast<int>(w);
+        const long long src = a.indices[i];
+        const float* o = a.obs + src * a.ld_obs;
+        const float* no = a.next_obs + src * a.ld_obs;
+        const float* ac = a.action + src * a.ld_action;
+        for (int c = lane; c < a.obs_dim; c += 32) {
+            const float ov = o[c], nv = no[c];
+            if (a.critic_x_pi) a.critic_x_pi[static_cast<long long>(i) * a.ld_critic_x_pi + c] = ov;
+            if (a.critic_x) {
+                a.critic_x[static_cast<long long>(i) * a.ld_critic_x + c] = ov;
+                a.critic_x[static_cast<long long>(B + i) * a.ld_critic_x + c] = nv;
+            }
+            if (a.actor_x && c < a.actor_obs_dim) {
+                a.actor_x[static_cast<long long>(i) * a.ld_actor_x + c] = ov;
+                a.actor_x[static_cast<long long>(B + i) * a.ld_actor_x + c] = nv;
+            }
+            if (a.batch_obs) a.batch_obs[static_cast<long long>(i) * a.obs_dim + c] = ov;
+            if (a.batch_next_obs) a.batch_next_obs[static_cast<long long>(i) * a.obs_dim + c] = nv;
+        }
+        for (int c = lane; c < a.act_dim; c += 32) {
+            const float av = ac[c];
+            if (a.critic_x) a.critic_x[static_cast<long long>(i) * a.ld_critic_x + a.obs_dim + c] = av;
+            if (a.batch_action) a.batch_action[static_cast<long long>(i) * a.act_dim + c] = av;
+        }
+        if (lane == 0) {
+            const float r = a.reward[src];
+            if (a.reward_out) a.reward_out[i] = a.g_var ? r / rscale : r;
+            if (a.batch_reward) a.batch_reward[i] = r;
+            if (a.terminated_out) a.terminated_out[i] = a.terminated[src];
+            if (a.truncated_out && a.truncated) a.truncated_out[i] = a.truncated[src];
+            if (a.discount_out) a.discount_out[i] = a.discount[src];
+        }
+    }
+}
+
+}  // namespace replay
+}  // namespace rl2
+
+using namespace rl2;
+
+extern "C" int rl2_replay_sample(unsigned long long seed, const unsigned long long* epoch, const long long* population,
+                                 long long fixed_population, int batch, int* indices, int* health, void* stream) {
+    clear_error();
+    if (!indices || batch < 1 || (!population && (fixed_population < 1 || fixed_population > 0x7FFFFFFFLL))) {
+        set_error("replay sample: invalid arguments");
+        return -1;
+    }
+    replay::sample_kernel<<<(batch + replay::kT - 1) / replay::kT, replay::kT, 0, as_stream(stream)>>>(
+        seed, epoch, population, fixed_population, batch, indices, health);
+    return launch_status("replay sample");
+}
+
+extern "C" int rl2_counter_advance(unsigned long long* epoch, unsigned long long by, void* stream) {
+    clear_error();
+    if (!epoch) {
+        set_error("counter advance: null counter");
+        return -1;
+    }
+    replay::advance_kernel<<<1, 1, 0, as_stream(stream)>>>(epoch, by);
+    return launch_status("counter advance");
+}
+
+extern "C" int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols,
+                                float* out, long long ld, void* stream) {
+    clear_error();
+    if (!out || rows < 1 || cols < 1 || ld < cols) {
+        set_error("normal noise: invalid arguments");
+        return -1;
+    }
+    const long long quads = (static_cast<long long>(rows) * cols + 3) / 4;
+    const int blocks = static_cast<int>(std::min<long long>((quads + replay::kT - 1) / replay::kT, 148 * 8));
+    replay::normal_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(seed, epoch, rows, cols, out, ld);
+    return launch_status("normal noise");
+}
+
+extern "C" int rl2_replay_gather(const rl2_replay_gather_args* a, void* stream) {
+    clear_error();
+    if (!a || !a->indices || !a->obs || !a->next_obs || !a->action || !a->reward || !a->terminated ||
+        !a->discount || a->batch < 1 || a->obs_dim < 1 || a->act_dim < 1 || (a->g_var && !a->g_r_max)) {
+        set_error("replay gather: invalid arguments");
+        return -1;
+    }
+    const int blocks = std::min((a->batch + 7) / 8, 148 * 16);
+    replay::gather_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(*a);
+    return launch_status("replay gather");
+}
+
+extern "C" void rl2_philox4x32(unsigned int c0, unsigned int c1, unsigned int c2, unsigned int c3, unsigned int k0,
+                               unsigned int k1, unsigned int* out4) {
+    const replay::U4 r = replay::philox(replay::U4{c0, c1, c2, c3}, k0, k1);
+    out4[0] = r.x;
+    out4[1] = r.y;
+    out4[2] = r.z;
+    out4[3] = r.w;
+}

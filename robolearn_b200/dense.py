@@ -68,18 +68,20 @@ class DensePlan:
         d_split_stride: int = 0,
         tile_n: int = 0,
         health: torch.Tensor | None = None,
+        out_plane=None,
     ):
-        self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health]
+        self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health, out_plane]
+        A = N.addr
         desc = N.GemmDesc(
             kind=kind, m=m, n=n, k=k, batch=batch,
-            a=N.ptr(a), a_lo=N.ptr(a_lo), a_major=a_major, lda=lda, a_batch_stride=a_batch_stride,
-            b=N.ptr(b), b_lo=N.ptr(b_lo), b_major=b_major, ldb=ldb, b_batch_stride=b_batch_stride,
-            d=N.ptr(d), ldd=ldd, d_batch_stride=d_batch_stride, accumulate=int(accumulate),
-            bias=N.ptr(bias), bias_batch_stride=bias_batch_stride,
-            residual=N.ptr(residual), ldr=ldr, residual_batch_stride=residual_batch_stride,
-            stat_mean=N.ptr(stat_mean), stat_m2=N.ptr(stat_m2), stat_batch_stride=stat_batch_stride,
-            scale=N.ptr(scale), k_splits=k_splits, d_split_stride=d_split_stride, tile_n=tile_n,
-            health=N.ptr(health),
+            a=A(a), a_lo=A(a_lo), a_major=a_major, lda=lda, a_batch_stride=a_batch_stride,
+            b=A(b), b_lo=A(b_lo), b_major=b_major, ldb=ldb, b_batch_stride=b_batch_stride,
+            d=A(d), ldd=ldd, d_batch_stride=d_batch_stride, accumulate=int(accumulate),
+            bias=A(bias), bias_batch_stride=bias_batch_stride,
+            residual=A(residual), ldr=ldr, residual_batch_stride=residual_batch_stride,
+            stat_mean=A(stat_mean), stat_m2=A(stat_m2), stat_batch_stride=stat_batch_stride,
+            scale=A(scale), k_splits=k_splits, d_split_stride=d_split_stride, tile_n=tile_n,
+            health=A(health), out_plane=out_plane if out_plane is not None else N.Plane(),
         )
         self._lib = N.load()
         self.handle = N.created(self._lib.rl2_gemm_create(ctypes.byref(desc)), "create tcgen05 GEMM plan")
@@ -88,6 +90,9 @@ class DensePlan:
 
     def run(self, stream=None) -> None:
         N.check(self._lib.rl2_gemm_run(self.handle, N.stream_ptr(stream)), "tcgen05 GEMM")
+
+    def __call__(self) -> None:
+        self.run()
 
     def close(self) -> None:
         if self.handle:
