@@ -467,6 +467,61 @@ int rl2_replay_gather(const rl2_replay_gather_args* args, void* stream);
 int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols, float* out,
                      long long ld, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * replay ingest (one vector-environment step): stage the step in an n-step
+ * ring, then commit the n-step transition that began n-1 steps ago into the
+ * replay ring at (write position + env) % capacity. Replaces _copy_pending /
+ * _commit_pending / _advance_replay (src/robolearn/warp/_flash_replay.py:26-113);
+ * Torch semantics TorchUniformBuffer.add (src/robolearn/flashsac/replay.py:109-174):
+ * a done (terminated or truncated) step ends the return, keeps its own next
+ * observation and flags, discount = gamma^(steps included).
+ * counters (device int64): [0] steps seen, [1] write position, [2] filled rows.
+ * Done flags are fp32 (0/1) or uint8 (bool), whichever pointer is set.
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_replay_ingest_args {
+    const float* obs;
+    const float* next_obs;
+    long long ld_obs;
+    const float* action;
+    long long ld_action;
+    const float* reward;
+    const float* terminated;
+    const float* truncated;
+    const unsigned char* terminated_u8;
+    const unsigned char* truncated_u8;
+    long long num_envs;
+    int obs_dim, act_dim, n_step;
+    float gamma;
+    float* pend_obs;      /* [n_step][num_envs][obs_dim] */
+    float* pend_next_obs; /* [n_step][num_envs][obs_dim] */
+    float* pend_act;      /* [n_step][num_envs][act_dim] */
+    float* pend_reward;   /* [n_step][num_envs] */
+    float* pend_term;
+    float* pend_trunc;
+    long long* counters;
+    long long capacity;
+    float* r_obs;
+    float* r_next_obs;
+    long long ld_replay_obs;
+    float* r_act;
+    long long ld_replay_act;
+    float* r_reward;
+    float* r_term;
+    float* r_trunc;
+    float* r_discount;
+} rl2_replay_ingest_args;
+
+int rl2_replay_ingest(const rl2_replay_ingest_args* args, void* stream);
+
+/* Reward normaliser statistics for one environment step (replaces _update_returns /
+ * _return_variance / _update_running_moments, src/robolearn/warp/_flash_replay.py:347-389;
+ * Torch semantics src/robolearn/flashsac/_utils/reward_normalization.py:14-125):
+ * g_r = gamma * (1 - done) * g_r + r per environment; state = [mean, var, count, G_r_max]
+ * updated from the batch moments of g_r by Chan's rule with count epsilon. */
+int rl2_reward_stats_update(const float* reward, const float* terminated, const float* truncated,
+                            const unsigned char* terminated_u8, const unsigned char* truncated_u8, float* g_r,
+                            int num_envs, float gamma, float* state, float epsilon, void* stream);
+
 /* Host-side Philox4x32-10 block (for checking device streams against the published algorithm). */
 void rl2_philox4x32(unsigned int c0, unsigned int c1, unsigned int c2, unsigned int c3, unsigned int k0,
                     unsigned int k1, unsigned int* out4);

@@ -179,7 +179,17 @@ def rms_backward(dy, cache):
 
 def linear(x, w):
     """``x[T,R,K] @ w[T,N,K]^T`` (``layers.py:15-22,174-183``)."""
-    return np.einsum("trk,tnk->trn", x, w)
+    return np.matmul(x, np.swapaxes(w, -1, -2))
+
+
+def _tn(d, x):
+    """weight gradient ``d[T,R,N]^T @ x[T,R,K] -> [T,N,K]``"""
+    return np.matmul(np.swapaxes(d, -1, -2), x)
+
+
+def _nn(d, w):
+    """input gradient ``d[T,R,N] @ w[T,N,K] -> [T,R,K]``"""
+    return np.matmul(d, w)
 
 
 # Operand rounding of the dense products. The FP32 recipe leaves operands as they
@@ -303,15 +313,15 @@ def backbone_backward(du, caches, blocks, twin, need_input_grad):
         suffix = ".weight" if twin else ".w.weight"
         d_n2 = dh * (n2 > 0)
         d_t2, grads[f"encoder.{i}.norm2.weight"], grads[f"encoder.{i}.norm2.bias"] = bn_backward(d_n2, c2)
-        grads[f"encoder.{i}.w2{suffix}"] = np.einsum("trn,trk->tnk", _rg(d_t2), _rf(a1))
-        d_a1 = np.einsum("trn,tnk->trk", _rg(d_t2), _rf(w2))
+        grads[f"encoder.{i}.w2{suffix}"] = _tn(_rg(d_t2), _rf(a1))
+        d_a1 = _nn(_rg(d_t2), _rf(w2))
         d_n1 = d_a1 * (n1 > 0)
         d_t1, grads[f"encoder.{i}.norm1.weight"], grads[f"encoder.{i}.norm1.bias"] = bn_backward(d_n1, c1)
-        grads[f"encoder.{i}.w1{suffix}"] = np.einsum("trn,trk->tnk", _rg(d_t1), _rf(h_in))
-        dh = np.einsum("trn,tnk->trk", _rg(d_t1), _rf(w1)) + dh
+        grads[f"encoder.{i}.w1{suffix}"] = _tn(_rg(d_t1), _rf(h_in))
+        dh = _nn(_rg(d_t1), _rf(w1)) + dh
     _, y_e, c_bn, w_e = caches[0]
-    grads["embedder.w.weight" if twin else "embedder.w.w.weight"] = np.einsum("trn,trk->tnk", _rg(dh), _rf(y_e))
-    d_y = np.einsum("trn,tnk->trk", _rg(dh), _rf(w_e))
+    grads["embedder.w.weight" if twin else "embedder.w.w.weight"] = _tn(_rg(dh), _rf(y_e))
+    d_y = _nn(_rg(dh), _rf(w_e))
     dx, grads["embedder.norm.weight"], grads["embedder.norm.bias"] = bn_backward(d_y, c_bn)
     if not twin:
         grads = {k: v[0] for k, v in grads.items()}
@@ -399,10 +409,10 @@ def critic_backward(cache, d: Dims, d_log_probs=None, d_q=None, need_input_grad=
         d_logits += d_q[..., None] * probs * (z - q[..., None])
     u = cache["u"]
     grads = {
-        "predictor.w.weight": np.einsum("trn,trk->tnk", _rg(d_logits), _rf(u)),
+        "predictor.w.weight": _tn(_rg(d_logits), _rf(u)),
         "predictor.bias": d_logits.sum(axis=1),
     }
-    du = np.einsum("trn,tnk->trk", _rg(d_logits), _rf(cache["w"]))
+    du = _nn(_rg(d_logits), _rf(cache["w"]))
     g2, dx = backbone_backward(du, cache["caches"], d.critic_blocks, True, need_input_grad)
     grads.update(g2)
     return grads, (dx.sum(axis=0) if need_input_grad else None)
@@ -679,10 +689,10 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
 def _critic_backward_from_logits(cache, d: Dims, d_logits):
     u = cache["u"]
     grads = {
-        "predictor.w.weight": np.einsum("trn,trk->tnk", _rg(d_logits), _rf(u)),
+        "predictor.w.weight": _tn(_rg(d_logits), _rf(u)),
         "predictor.bias": d_logits.sum(axis=1),
     }
-    du = np.einsum("trn,tnk->trk", _rg(d_logits), _rf(cache["w"]))
+    du = _nn(_rg(d_logits), _rf(cache["w"]))
     g2, _ = backbone_backward(du, cache["caches"], d.critic_blocks, True, False)
     grads.update(g2)
     return grads, None

@@ -241,3 +241,23 @@ def stream_ptr(stream=None) -> int:
 
     s = stream if stream is not None else torch.cuda.current_stream()
     return s.cuda_stream
+
+
+class ReplayIngestArgs(ctypes.Structure):
+    """``rl2_replay_ingest_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("obs", P), ("next_obs", P), ("ld_obs", LL), ("action", P), ("ld_action", LL), ("reward", P),
+        ("terminated", P), ("truncated", P), ("terminated_u8", P), ("truncated_u8", P), ("num_envs", LL),
+        ("obs_dim", I), ("act_dim", I), ("n_step", I), ("gamma", F),
+        ("pend_obs", P), ("pend_next_obs", P), ("pend_act", P), ("pend_reward", P), ("pend_term", P),
+        ("pend_trunc", P), ("counters", P), ("capacity", LL), ("r_obs", P), ("r_next_obs", P),
+        ("ld_replay_obs", LL), ("r_act", P), ("ld_replay_act", LL), ("r_reward", P), ("r_term", P),
+        ("r_trunc", P), ("r_discount", P),
+    ]
+
+
+SIGNATURES.update({
+    "rl2_replay_ingest": ([ctypes.POINTER(ReplayIngestArgs), P], I),
+    "rl2_reward_stats_update": ([P, P, P, P, P, P, I, F, P, F, P], I),
+})

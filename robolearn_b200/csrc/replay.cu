@@ -217,3 +217,177 @@ extern "C" void rl2_philox4x32(unsigned int c0, unsigned int c1, unsigned int c2
     out4[2] = r.z;
     out4[3] = r.w;
 }
+
+// ===========================================================================
+// replay ingest: n-step staging ring + commit, and the reward normaliser
+// ===========================================================================
+//
+// Semantics (paths inside the reference project): n-step return, done handling and
+// timeout bootstrap of src/robolearn/flashsac/replay.py:109-174 and the Warp
+// restatement _copy_pending / _commit_pending / _advance_replay
+// (src/robolearn/warp/_flash_replay.py:26-113); reward statistics of
+// src/robolearn/flashsac/_utils/reward_normalization.py:14-125.
+// counters (int64): [0] steps seen, [1] write position, [2] filled rows.
+namespace rl2 {
+namespace ingest {
+
+constexpr int kT = 256;
+
+// one warp per environment: stage this step, then (from step n-1 on) commit the
+// n-step transition that starts n-1 steps ago into the replay ring
+__global__ void stage_commit_kernel(const rl2_replay_ingest_args a) {
+    const int lane = threadIdx.x & 31;
+    const long long step = a.counters[0];
+    const int n = a.n_step;
+    const int latest = static_cast<int>(step % n);
+    const long long E = a.num_envs;
+    for (long long i = blockIdx.x * static_cast<long long>(kT / 32) + (threadIdx.x >> 5); i < E;
+         i += static_cast<long long>(gridDim.x) * (kT / 32)) {
+        const long long ps = static_cast<long long>(latest) * E + i;  // pending row of this step
+        for (int c = lane; c < a.obs_dim; c += 32) {
+            a.pend_obs[ps * a.obs_dim + c] = a.obs[i * a.ld_obs + c];
+            a.pend_next_obs[ps * a.obs_dim + c] = a.next_obs[i * a.ld_obs + c];
+        }
+        for (int c = lane; c < a.act_dim; c += 32) a.pend_act[ps * a.act_dim + c] = a.action[i * a.ld_action + c];
+        if (lane == 0) {
+            a.pend_reward[ps] = a.reward[i];
+            a.pend_term[ps] = a.terminated_u8 ? static_cast<float>(a.terminated_u8[i] != 0) : a.terminated[i];
+            a.pend_trunc[ps] = a.truncated_u8 ? static_cast<float>(a.truncated_u8[i] != 0) : a.truncated[i];
+        }
+        __syncwarp();
+        if (step < n - 1) continue;
+        const int oldest = (latest + 1) % n;
+        int next_slot = latest;
+        float total = a.pend_reward[ps];
+        float term = a.pend_term[ps];
+        float trunc = a.pend_trunc[ps];
+        float factor = a.gamma;
+        for (int off = 1; off < n; ++off) {
+            const int slot = (latest - off + n) % n;
+            const long long q = static_cast<long long>(slot) * E + i;
+            const bool done = a.pend_term[q] != 0.0f || a.pend_trunc[q] != 0.0f;
+            if (done) {
+                total = a.pend_reward[q];
+                factor = a.gamma;
+                term = a.pend_term[q];
+                trunc = a.pend_trunc[q];
+                next_slot = slot;
+            } else {
+                total = a.pend_reward[q] + a.gamma * total;
+                factor = a.gamma * factor;
+            }
+        }
+        const long long dst = (a.counters[1] + i) % a.capacity;
+        const long long po = static_cast<long long>(oldest) * E + i;
+        const long long pn = static_cast<long long>(next_slot) * E + i;
+        for (int c = lane; c < a.obs_dim; c += 32) {
+            a.r_obs[dst * a.ld_replay_obs + c] = a.pend_obs[po * a.obs_dim + c];
+            a.r_next_obs[dst * a.ld_replay_obs + c] = a.pend_next_obs[pn * a.obs_dim + c];
+        }
+        for (int c = lane; c < a.act_dim; c += 32) a.r_act[dst * a.ld_replay_act + c] = a.pend_act[po * a.act_dim + c];
+        if (lane == 0) {
+            a.r_reward[dst] = total;
+            a.r_term[dst] = term;
+            a.r_trunc[dst] = trunc;
+            a.r_discount[dst] = factor;
+        }
+    }
+}
+
+__global__ void advance_kernel(long long* counters, int n_step, long long num_envs, long long capacity) {
+    if (counters[0] >= n_step - 1) {
+        counters[1] = (counters[1] + num_envs) % capacity;
+        counters[2] = counters[2] + num_envs < capacity ? counters[2] + num_envs : capacity;
+    }
+    counters[0] += 1;
+}
+
+// One block: per-environment discounted return, running max |G|, and the running
+// mean / variance of G by Chan's parallel update (reward_normalization.py:14-38,
+// :64-91). state = [mean, var, count, G_r_max].
+__global__ void reward_stats_kernel(const float* reward, const float* term, const float* trunc,
+                                    const unsigned char* term_u8, const unsigned char* trunc_u8, float* g_r,
+                                    int num_envs, float gamma, float* state, float epsilon) {
+    __shared__ double red[3][kT];
+    double s = 0.0, mx = 0.0;
+    for (int i = threadIdx.x; i < num_envs; i += kT) {
+        const bool done = (term_u8 ? term_u8[i] != 0 : term[i] != 0.0f) || (trunc_u8 ? trunc_u8[i] != 0 : trunc[i] != 0.0f);
+        const float g = gamma * (done ? 0.0f : 1.0f) * g_r[i] + reward[i];
+        g_r[i] = g;
+        s += g;
+        mx = fmax(mx, fabs(static_cast<double>(g)));
+    }
+    red[0][threadIdx.x] = s;
+    red[2][threadIdx.x] = mx;
+    __syncthreads();
+    for (int o = kT / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) {
+            red[0][threadIdx.x] += red[0][threadIdx.x + o];
+            red[2][threadIdx.x] = fmax(red[2][threadIdx.x], red[2][threadIdx.x + o]);
+        }
+        __syncthreads();
+    }
+    const double mean_b = red[0][0] / num_envs;
+    double q = 0.0;
+    for (int i = threadIdx.x; i < num_envs; i += kT) {
+        const double d = g_r[i] - mean_b;
+        q += d * d;
+    }
+    red[1][threadIdx.x] = q;
+    __syncthreads();
+    for (int o = kT / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) red[1][threadIdx.x] += red[1][threadIdx.x + o];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const float batch_mean = static_cast<float>(mean_b);
+        const float batch_var = static_cast<float>(red[1][0] / num_envs);
+        const float batch_count = static_cast<float>(num_envs);
+        const float mean = state[0], var = state[1], count = state[2];
+        const float delta = batch_mean - mean;
+        const float total = count + batch_count;
+        const float ratio = batch_count / total;
+        const float m_a = var * (count + epsilon);
+        const float m_b = batch_var * batch_count;
+        const float m2 = m_a + m_b + delta * delta * count * ratio;
+        state[0] = mean + delta * ratio;
+        state[1] = m2 / total;
+        state[2] = total;
+        state[3] = fmaxf(state[3], static_cast<float>(red[2][0]));
+    }
+}
+
+}  // namespace ingest
+}  // namespace rl2
+
+extern "C" int rl2_replay_ingest(const rl2_replay_ingest_args* a, void* stream) {
+    using namespace rl2;
+    clear_error();
+    if (!a || !a->counters || !a->obs || !a->next_obs || !a->action || !a->reward ||
+        (!a->terminated && !a->terminated_u8) || (!a->truncated && !a->truncated_u8) || a->n_step < 1 ||
+        a->num_envs < 1 || a->capacity < a->num_envs || !a->pend_obs || !a->r_obs) {
+        set_error("replay ingest: invalid arguments");
+        return -1;
+    }
+    const int blocks = static_cast<int>(std::min<long long>((a->num_envs + 7) / 8, 148 * 16));
+    ingest::stage_commit_kernel<<<blocks, ingest::kT, 0, as_stream(stream)>>>(*a);
+    if (launch_status("replay ingest")) return -1;
+    ingest::advance_kernel<<<1, 1, 0, as_stream(stream)>>>(a->counters, a->n_step, a->num_envs, a->capacity);
+    return launch_status("replay advance");
+}
+
+extern "C" int rl2_reward_stats_update(const float* reward, const float* terminated, const float* truncated,
+                                       const unsigned char* terminated_u8, const unsigned char* truncated_u8,
+                                       float* g_r, int num_envs, float gamma, float* state, float epsilon,
+                                       void* stream) {
+    using namespace rl2;
+    clear_error();
+    if (!reward || (!terminated && !terminated_u8) || (!truncated && !truncated_u8) || !g_r || !state ||
+        num_envs < 1) {
+        set_error("reward stats: invalid arguments");
+        return -1;
+    }
+    ingest::reward_stats_kernel<<<1, ingest::kT, 0, as_stream(stream)>>>(
+        reward, terminated, truncated, terminated_u8, truncated_u8, g_r, num_envs, gamma, state, epsilon);
+    return launch_status("reward statistics");
+}
