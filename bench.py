@@ -1,0 +1,353 @@
+"""FlashSAC learner-update benchmark (BASELINE.json metric: FlashSAC updates/s, obs 123 / act 37, batch 4096).
+
+``python bench.py --gpus N --steps K --warmup W`` times K learner updates after W
+warm-up updates and prints ONE JSON line on rank 0. A step is one ``update()``:
+replay index sampling + fused gather + one learner phase (actor + critic every
+``actor_update_period`` = 2 updates, critic otherwise), each phase one CUDA graph.
+
+Workload: obs 123 ~N(0,1), act 37 ~U[-1,1], 4096
+environments, batch 4096 per GPU, twin critics hidden 512 x 2 blocks, 101 atoms on
+[-10, 10], actor hidden 256 x 2 blocks, FP16 dense operands with FP32 activations,
+master weights and Adam. Synthetic data (no simulator, no dataset); random-init
+weights of the reference architecture. The replay holds 16 x 4096 rows; the
+per-update working set (> 1 GB of activations) exceeds the 126 MB L2, so no flush
+is needed between steps.
+
+``--impl reference`` times the CPU restatement of the reference update (the
+reference is Python/Torch and cannot travel to the GPU box) on all host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+OBS, ACT, ENVS, BATCH = 123, 37, 4096, 4096
+METRIC = "FlashSAC updates/s (obs123/act37, batch 4096)"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--warmup", type=int, default=6)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
+                "samples": len(self.rows), "reasons": reasons}
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def build(precision: str, device, seed: int = 0):
+    """Learner + synthetic device replay at the config-3 shapes."""
+    import torch
+
+    from robolearn_b200.flashsac.config import FlashSACConfig
+    from robolearn_b200.flashsac.learner import Learner
+    from robolearn_b200.flashsac.replay import DeviceReplay
+    from robolearn_b200.flashsac.sampling import sampling_program
+
+    cfg = FlashSACConfig(device=str(device), sample_batch_size=BATCH, critic_hidden_dim=512, critic_num_blocks=2,
+                         actor_hidden_dim=256, actor_num_blocks=2, critic_num_bins=101, critic_min_v=-10.0,
+                         critic_max_v=10.0, critic_target_update_tau=0.005, learning_rate_init=3e-4,
+                         learning_rate_peak=3e-4, learning_rate_end=3e-4, n_step=1, buffer_max_length=16 * ENVS,
+                         buffer_min_length=BATCH, dense_precision=precision, seed=seed)
+    L = Learner(OBS, OBS, ACT, cfg, device)
+    R = DeviceReplay(OBS, ACT, ENVS, 16 * ENVS, 1, 0.99, BATCH, device, seed=seed)
+    g = torch.Generator(device=device).manual_seed(2026 + seed)
+    cap = R.capacity
+    R.observation.copy_(torch.randn(cap, OBS, device=device, generator=g))
+    R.next_observation.copy_(torch.randn(cap, OBS, device=device, generator=g))
+    R.action.uniform_(-1, 1, generator=g)
+    R.reward.copy_(torch.randn(cap, device=device, generator=g))
+    R.terminated.copy_((torch.rand(cap, device=device, generator=g) < 0.01).float())
+    R.discount.fill_(0.99)
+    R.counters.copy_(torch.tensor([0, 0, cap], device=device))
+    R._host_count = cap
+    feed = sampling_program(L, R, seed=seed)
+    return L, R, feed
+
+
+def count_launches(prog) -> int:
+    from robolearn_b200.dense import DensePlan
+
+    n = 0
+    for f in prog:
+        n += 1 if isinstance(f, DensePlan) else getattr(f, "launches", 1)
+    return n
+
+
+def gemm_roofline(L, peak_tflops):
+    """Average tcgen05 GEMM throughput over one update's products, timed as one CUDA graph."""
+    import torch
+
+    from robolearn_b200.dense import DensePlan
+
+    plans = []
+    for phase in (True, False):
+        plans += [f for f in L.programs[phase] if isinstance(f, DensePlan)]
+    flops = sum(p.flops for p in plans)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+        for p in plans:
+            p.run()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    achieved = flops / sec / 1e12
+    return {"kernel": "rl2 tcgen05 GEMM (all products of one actor+critic update pair)", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tflops, 4), "traffic": None, "launches": len(plans),
+            "flops_per_pair": flops, "ms_per_pair": round(sec * 1e3, 4)}
+
+
+def cpu_update_rate(batch: int, pairs: int = 1):
+    """CPU restatement of the reference update (oracle, float32, all host cores): updates/s at ``batch``.
+
+    Returns (updates_per_s_at_batch, seconds, cores). Used by the cpu_baseline field
+    and by ``--impl reference``; the oracle is the checker, never the product path.
+    """
+    import numpy as np
+
+    from oracle import flashsac_np as fs
+    from robolearn_b200.flashsac.config import FlashSACConfig
+    from robolearn_b200.flashsac.learner import _init_reference_weights
+
+    d = fs.Dims(obs=OBS, act=ACT, actor_hidden=256, actor_blocks=2, critic_hidden=512, critic_blocks=2, bins=101,
+                min_v=-10.0, max_v=10.0)
+    a0, c0, lt = _init_reference_weights(OBS, OBS, ACT, FlashSACConfig(device="cpu", actor_hidden_dim=256,
+                                                                       critic_hidden_dim=512))
+
+    def with_buffers(p, twin, H, cin):
+        out = {k: v.numpy() for k, v in p.items()}
+        for pre in fs.bn_buffer_prefixes(2):
+            C = cin if pre == "embedder.norm" else (4 * H if pre.endswith("norm1") else H)
+            shape = (2, C) if twin else (C,)
+            out[pre + ".running_mean"] = np.zeros(shape, np.float32)
+            out[pre + ".running_var"] = np.ones(shape, np.float32)
+        return out
+
+    st = dict(actor=with_buffers(a0, False, 256, OBS), critic=with_buffers(c0, True, 512, OBS + ACT),
+              target=with_buffers(c0, True, 512, OBS + ACT), log_temp=lt, opt_actor=fs.OptState(),
+              opt_critic=fs.OptState(), opt_temp=fs.OptState())
+    rng = np.random.default_rng(2026)
+    B = batch
+    bt = dict(observation=rng.standard_normal((B, OBS)).astype(np.float32),
+              next_observation=rng.standard_normal((B, OBS)).astype(np.float32),
+              action=rng.uniform(-1, 1, (B, ACT)).astype(np.float32), reward=rng.standard_normal(B).astype(np.float32),
+              terminated=(rng.random(B) < 0.01).astype(np.float32), discount=np.full(B, 0.99, np.float32))
+    an = rng.standard_normal((2 * B, ACT)).astype(np.float32)
+    nn = rng.standard_normal((B, ACT)).astype(np.float32)
+    h = fs.Hyper(tau=0.005, lr_end=3e-4, target_entropy=float(0.5 * ACT * np.log(2 * np.pi * np.e * 0.15**2)))
+    t0 = time.perf_counter()
+    for i in range(2 * pairs):
+        st, _ = fs.update_networks(st, bt, an, nn, d, h, do_actor=(i % 2 == 0), dtype=np.float32)
+    sec = time.perf_counter() - t0
+    return 2 * pairs / sec, sec, len(os.sched_getaffinity(0))
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    L, R, feed = build(args.precision, device, seed=rank)
+    for phase in (True, False):  # one eager pass loads every kernel module before capture
+        for f in feed:
+            f()
+        L.run(phase)
+    torch.cuda.synchronize()
+    graphs = {phase: L.capture(phase, pre=feed) for phase in (True, False)}
+    period = L.cfg.actor_update_period
+
+    def step(i):
+        graphs[i % period == 0].replay()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local_rank) as clocks:
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record()
+        torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3
+    launches = sum(count_launches(feed) + count_launches(L.programs[(args.warmup + i) % period == 0])
+                   for i in range(args.steps))
+    # ---- end to end through the public replay + learner API with host buffers:
+    # each step copies one vector-environment step of transitions from pinned host
+    # memory, ingests it, runs the update and reads the critic loss back to the host.
+    host = {k: torch.randn(ENVS, d).pin_memory() for k, d in (("obs", OBS), ("next_obs", OBS))}
+    host["act"] = torch.rand(ENVS, ACT).mul_(2).sub_(1).pin_memory()
+    host["rew"] = torch.randn(ENVS).pin_memory()
+    host["term"] = (torch.rand(ENVS) < 0.01).float().pin_memory()
+    host["trunc"] = torch.zeros(ENVS).pin_memory()
+    dev = {k: torch.empty(v.shape, device=device) for k, v in host.items()}
+    loss_host = torch.zeros(1).pin_memory()
+    h2d = sum(v.numel() * 4 for v in host.values())
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        for k in host:
+            dev[k].copy_(host[k], non_blocking=True)
+        R.add(dev["obs"], dev["act"], dev["rew"], dev["term"], dev["trunc"], dev["next_obs"])
+        step(i)
+        loss_host.copy_(L.metrics[3:4], non_blocking=True)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_sec = t0.elapsed_time(t1) / 1e3
+    return L, sec, e2e_sec, h2d, launches, clocks.summary()
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    base = {"metric": METRIC, "unit": "updates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        sample = BATCH // 4
+        times = []
+        for i in range(args.warmup + args.steps):
+            rate, sec, cores = cpu_update_rate(sample, pairs=1)
+            if i >= args.warmup:
+                times.append(sec / 2 * (BATCH / sample))
+        per_update = statistics.median(times)
+        value = 1.0 / per_update
+        out = dict(base, impl="reference", value=value, ms_per_step=per_update * 1e3, dtype="f32",
+                   config={"workload": "cfg3 FlashSAC update, CPU restatement of the reference (oracle port)",
+                           "global_batch": BATCH, "parallelism": "cpu"},
+                   cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
+                                 "sample": f"one actor+critic update pair at batch {sample} per step, "
+                                           f"time scaled x{BATCH // sample} to batch {BATCH}"},
+                   e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(out))
+        return
+    import torch
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    L, sec, e2e_sec, h2d, launches, clocks = run_b200(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([sec, e2e_sec], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec, e2e_sec = t.tolist()
+    pk, src = peaks()
+    roof = gemm_roofline(L, pk["bf16_tflops"])
+    roof["peak_source"] = f"{src} bf16_tflops (burst; fp16 dense rate taken equal)"
+    out = dict(base, impl="b200", value=world * args.steps / sec, ms_per_step=sec / args.steps * 1e3,
+               dtype=args.precision, gpu_launches=launches, clocks=clocks, roofline=roof,
+               config={"workload": "cfg3 FlashSAC update (obs 123, act 37, batch 4096 per GPU, critic 512x2, "
+                                   "actor 256x2, 101 atoms)", "global_batch": BATCH * world, "seq_len": None,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "working set > 126 MB L2 (no flush needed)"},
+               e2e={"value": world * args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4})
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = BATCH // 4
+        rate, csec, cores = cpu_update_rate(sample, pairs=1)
+        out["cpu_baseline"] = {"value": rate * sample / BATCH, "unit": "updates/s", "cores": cores, "kind": "port",
+                               "sample": f"one actor+critic update pair at batch {sample} ({csec:.1f} s), "
+                                         f"rate scaled to batch {BATCH}"}
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
