@@ -166,6 +166,17 @@ typedef struct rl2_critic_objective_args {
 int rl2_categorical_workspace_floats(int batch, int bins);
 int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
 
+/* Allocation-free variant of rl2_critic_objective (no counterpart in the reference).
+ * For callers that cannot allocate device memory where they run this objective, e.g. a
+ * real-time control loop that must not stall in the driver's allocator, or a host whose
+ * device memory is owned by another framework's pool. args->workspace and args->counter
+ * are ignored: the kernel uses a file-scope device array (about 1.2 MB per GPU, held
+ * until process exit). Limits: batch <= 65536, bins <= 128; larger sizes return -1.
+ * The first call on each device looks up that array's address (make it before any
+ * stream capture). All calls share the array: calls that overlap on the GPU race,
+ * so issue them in order on one stream. Nothing is allocated or freed. */
+int rl2_critic_objective_noalloc(const rl2_critic_objective_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------
  * batch norm over the rows of [twins][rows][cols] matrices, training or
  * evaluation mode. Replaces rl_flash_bn_forward / rl_flash_bn_backward and their

@@ -261,3 +261,5 @@ SIGNATURES.update({
     "rl2_replay_ingest": ([ctypes.POINTER(ReplayIngestArgs), P], I),
     "rl2_reward_stats_update": ([P, P, P, P, P, P, I, F, P, F, P], I),
 })
+
+SIGNATURES["rl2_critic_objective_noalloc"] = ([ctypes.POINTER(CriticObjectiveArgs), P], I)

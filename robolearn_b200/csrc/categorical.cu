@@ -372,3 +372,88 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
     cat::critic_objective_kernel<<<grid, cat::kThreads, 0, as_stream(stream)>>>(a);
     return launch_status("critic objective");
 }
+
+// ===========================================================================
+// Allocation-free variant of rl2_critic_objective.
+//
+// Some callers cannot allocate device memory where they need this objective: a
+// robot controller's real-time loop must not stall in the driver's allocator, and
+// a host that embeds this library inside another framework may own all device
+// memory through that framework's pool with no hook to hand out a workspace. This
+// entry point needs no workspace from them: its block partials and completion
+// counter live in the file-scope array below, which every GPU that loads the
+// library holds until the process exits (about 1.2 MB).
+//
+// Limits: batch <= kNoAllocMaxBatch rows and bins <= 128 atoms; larger sizes are
+// rejected with an error. The first call on a device looks up the array's device
+// address (cudaGetSymbolAddress) with that device current; make that first call
+// before any stream capture. All calls share the one array and it keeps the last
+// call's contents: the counter is cleared at the start of every call (the partials
+// are fully rewritten before they are read), and calls that overlap on the GPU
+// (concurrent streams, or concurrent host threads) race on it, so issue them in
+// order on one stream.
+// ===========================================================================
+#include <mutex>
+
+namespace rl2 {
+namespace cat {
+
+constexpr int kNoAllocMaxBatch = 65536;
+constexpr int kNoAllocMaxGrid = 148 * 8;                        // same grid rule as rl2_critic_objective
+constexpr int kNoAllocFloats = kNoAllocMaxGrid * (2 * kMaxBins + 2);  // 305,472 floats of block partials
+constexpr int kNoAllocCounterPad = 64;                          // counter word kept 256-byte aligned
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats + kNoAllocCounterPad];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[256] = {};
+}  // namespace
+
+// Device address of the scratch array for the current device (looked up once per device).
+static float* noalloc_scratch(int device) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            set_error("critic objective (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_noalloc_addr[device] = p;
+    }
+    return static_cast<float*>(g_noalloc_addr[device]);
+}
+
+}  // namespace cat
+}  // namespace rl2
+
+extern "C" int rl2_critic_objective_noalloc(const rl2_critic_objective_args* g, void* stream) {
+    using namespace rl2;
+    clear_error();
+    if (!g) {
+        set_error("critic objective (no-alloc): null arguments");
+        return -1;
+    }
+    if (g->batch < 1 || g->batch > cat::kNoAllocMaxBatch || g->bins < 2 || g->bins > cat::kMaxBins) {
+        set_error("critic objective (no-alloc): batch must be in [1, %d] and bins in [2, %d] (got batch %d, bins %d)",
+                  cat::kNoAllocMaxBatch, cat::kMaxBins, g->batch, g->bins);
+        return -1;
+    }
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 256) {
+        set_error("critic objective (no-alloc): no current CUDA device");
+        return -1;
+    }
+    float* scratch = cat::noalloc_scratch(device);
+    if (!scratch) return -1;
+    unsigned* counter = reinterpret_cast<unsigned*>(scratch + cat::kNoAllocFloats);
+    if (cudaMemsetAsync(counter, 0, sizeof(unsigned), as_stream(stream)) != cudaSuccess) {
+        set_error("critic objective (no-alloc): clearing the completion counter failed");
+        return -1;
+    }
+    rl2_critic_objective_args a = *g;
+    a.workspace = scratch;
+    a.counter = counter;
+    return rl2_critic_objective(&a, stream);
+}
