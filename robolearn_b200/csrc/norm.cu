@@ -50,21 +50,38 @@ __global__ void colstats_kernel(const float* __restrict__ x, long long ldx, long
     m2_p[o] = m2;
 }
 
-// thread per (twin, column)
-__global__ void finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p, long long pt,
-                                int twins, int rows, int cols, float* mean, float* invstd, float* rm, float* rv,
-                                float momentum, float eps, int update) {
-    const int i = blockIdx.x * kT + threadIdx.x;
-    if (i >= twins * cols) return;
-    const int t = i / cols, c = i % cols;
+// grid (ceil(cols/32), twins), 8 warps: lane = column, warp w merges a contiguous
+// range of groups in order, then warp 0 merges the 8 results in order (deterministic).
+__global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p,
+                                                      long long pt, int twins, int rows, int cols, float* mean,
+                                                      float* invstd, float* rm, float* rv, float momentum, float eps,
+                                                      int update) {
+    __shared__ float sh[3][kT / 32][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const int t = blockIdx.y;
     const int groups = (rows + 31) / 32;
-    const float* mp = mean_p + t * pt + c;
-    const float* qp = m2_p + t * pt + c;
+    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int g0 = warp * per, g1 = min(groups, g0 + per);
     float n = 0.0f, mu = 0.0f, m2 = 0.0f;
-    for (int g = 0; g < groups; ++g) {
-        const float ng = static_cast<float>(min(32, rows - g * 32));
-        chan_merge(n, mu, m2, ng, mp[static_cast<long long>(g) * cols], qp[static_cast<long long>(g) * cols]);
+    if (c < cols) {
+        const float* mp = mean_p + t * pt + c;
+        const float* qp = m2_p + t * pt + c;
+        for (int g = g0; g < g1; ++g) {
+            const float ng = static_cast<float>(min(32, rows - g * 32));
+            chan_merge(n, mu, m2, ng, mp[static_cast<long long>(g) * cols], qp[static_cast<long long>(g) * cols]);
+        }
     }
+    sh[0][warp][lane] = n;
+    sh[1][warp][lane] = mu;
+    sh[2][warp][lane] = m2;
+    __syncthreads();
+    if (warp != 0 || c >= cols) return;
+    n = sh[0][0][lane];
+    mu = sh[1][0][lane];
+    m2 = sh[2][0][lane];
+    for (int w = 1; w < kT / 32; ++w) chan_merge(n, mu, m2, sh[0][w][lane], sh[1][w][lane], sh[2][w][lane]);
+    const int i = t * cols + c;
     const float var = m2 / static_cast<float>(rows);
     mean[i] = mu;
     invstd[i] = 1.0f / sqrtf(var + eps);
@@ -104,6 +121,77 @@ __global__ void apply_kernel(const rl2_bn_apply_args a, const Plane plane) {
     pw.flush();
 }
 
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Vectorised apply: four columns per thread, 32-bit index math, grid.y = twin.
+__global__ void __launch_bounds__(kT) apply_vec4_kernel(const rl2_bn_apply_args a, const Plane plane) {
+    PlaneWriter pw(plane);
+    const int t = blockIdx.y;
+    const int c4n = a.cols >> 2;
+    const int total = a.rows * c4n;
+    const float* x = a.x + t * a.x_twin_stride;
+    const float* res = a.residual ? a.residual + t * a.residual_twin_stride : nullptr;
+    float* y = a.y ? a.y + t * a.y_twin_stride : nullptr;
+    const int tc0 = t * a.cols;
+    for (int i = blockIdx.x * kT + threadIdx.x; i < total; i += gridDim.x * kT) {
+        const int r = i / c4n;
+        const int c = (i - r * c4n) << 2;
+        const float4 xv = ld4(x + static_cast<long long>(r) * a.ldx + c);
+        const float4 mu = ld4(a.mean + tc0 + c), is = ld4(a.invstd + tc0 + c);
+        const float4 g = ld4(a.gamma + tc0 + c), b = ld4(a.beta + tc0 + c);
+        float4 o = make_float4((xv.x - mu.x) * is.x * g.x + b.x, (xv.y - mu.y) * is.y * g.y + b.y,
+                               (xv.z - mu.z) * is.z * g.z + b.z, (xv.w - mu.w) * is.w * g.w + b.w);
+        if (a.relu) o = make_float4(fmaxf(o.x, 0.f), fmaxf(o.y, 0.f), fmaxf(o.z, 0.f), fmaxf(o.w, 0.f));
+        if (res) {
+            const float4 rv = ld4(res + static_cast<long long>(r) * a.ldr + c);
+            o = make_float4(o.x + rv.x, o.y + rv.y, o.z + rv.z, o.w + rv.w);
+        }
+        if (y) *reinterpret_cast<float4*>(y + static_cast<long long>(r) * a.ldy + c) = o;
+        if (pw.active()) pw.store4(t, r, c, o);
+    }
+    pw.flush();
+}
+
+// Vectorised backward apply (twins kept separate, or summed into one output when sum_twins).
+__global__ void __launch_bounds__(kT) bwd_apply_vec4_kernel(const rl2_bn_backward_args a, const Plane plane) {
+    PlaneWriter pw(plane);
+    const int to = blockIdx.y;
+    const int c4n = a.cols >> 2;
+    const int total = a.rows * c4n;
+    const int t_begin = a.sum_twins ? 0 : to, t_end = a.sum_twins ? a.twins : to + 1;
+    for (int i = blockIdx.x * kT + threadIdx.x; i < total; i += gridDim.x * kT) {
+        const int r = i / c4n;
+        const int c = (i - r * c4n) << 2;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int t = t_begin; t < t_end; ++t) {
+            const int tc = t * a.cols + c;
+            const float4 xv = ld4(a.x + t * a.x_twin_stride + static_cast<long long>(r) * a.ldx + c);
+            const float4 dv = ld4(a.dy + t * a.dy_twin_stride + static_cast<long long>(r) * a.lddy + c);
+            const float4 mu = ld4(a.mean + tc), is = ld4(a.invstd + tc), g = ld4(a.gamma + tc), b = ld4(a.beta + tc);
+            const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ds[4] = {dv.x, dv.y, dv.z, dv.w};
+            const float ms[4] = {mu.x, mu.y, mu.z, mu.w}, iv[4] = {is.x, is.y, is.z, is.w};
+            const float gs[4] = {g.x, g.y, g.z, g.w}, bs[4] = {b.x, b.y, b.z, b.w};
+            float c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+            if (a.training) {
+                const float4 p1 = ld4(a.coef1 + tc), p2 = ld4(a.coef2 + tc);
+                c1[0] = p1.x; c1[1] = p1.y; c1[2] = p1.z; c1[3] = p1.w;
+                c2[0] = p2.x; c2[1] = p2.y; c2[2] = p2.z; c2[3] = p2.w;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float xhat = (xs[j] - ms[j]) * iv[j];
+                float d = ds[j];
+                if (a.relu && !(xhat * gs[j] + bs[j] > 0.0f)) d = 0.0f;
+                acc[j] += a.training ? gs[j] * iv[j] * (d - c1[j] - xhat * c2[j]) : gs[j] * iv[j] * d;
+            }
+        }
+        const float4 o = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (a.dx) *reinterpret_cast<float4*>(a.dx + to * a.dx_twin_stride + static_cast<long long>(r) * a.lddx + c) = o;
+        if (pw.active()) pw.store4(to, r, c, o);
+    }
+    pw.flush();
+}
+
 // d(normalised output) for one element: dy masked by the ReLU of the recomputed output
 __device__ __forceinline__ float masked_dbn(const rl2_bn_backward_args& a, int t, long long r, int c, float& xhat) {
     const int tc = t * a.cols + c;
@@ -135,18 +223,36 @@ __global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
     a.s2_part[o] = s2;
 }
 
-__global__ void bwd_finalize_kernel(const float* s1p, const float* s2p, int twins, int rows, int cols, float* dgamma,
-                                    float* dbeta, long long gts, int accumulate, float* coef1, float* coef2) {
-    const int i = blockIdx.x * kT + threadIdx.x;
-    if (i >= twins * cols) return;
-    const int t = i / cols, c = i % cols;
+// grid (ceil(cols/32), twins), 8 warps over contiguous group ranges, fixed-order combine.
+__global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, const float* s2p, int twins, int rows,
+                                                          int cols, float* dgamma, float* dbeta, long long gts,
+                                                          int accumulate, float* coef1, float* coef2) {
+    __shared__ float sh[2][kT / 32][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const int t = blockIdx.y;
     const int groups = (rows + 31) / 32;
+    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int g0 = warp * per, g1 = min(groups, g0 + per);
     float s1 = 0.0f, s2 = 0.0f;
-    for (int g = 0; g < groups; ++g) {
-        const long long o = (static_cast<long long>(t) * groups + g) * cols + c;
-        s1 += s1p[o];
-        s2 += s2p[o];
+    if (c < cols) {
+        for (int g = g0; g < g1; ++g) {
+            const long long o = (static_cast<long long>(t) * groups + g) * cols + c;
+            s1 += s1p[o];
+            s2 += s2p[o];
+        }
     }
+    sh[0][warp][lane] = s1;
+    sh[1][warp][lane] = s2;
+    __syncthreads();
+    if (warp != 0 || c >= cols) return;
+    s1 = 0.0f;
+    s2 = 0.0f;
+    for (int w = 0; w < kT / 32; ++w) {
+        s1 += sh[0][w][lane];
+        s2 += sh[1][w][lane];
+    }
+    const int i = t * cols + c;
     if (dgamma) dgamma[t * gts + c] = accumulate ? dgamma[t * gts + c] + s2 : s2;
     if (dbeta) dbeta[t * gts + c] = accumulate ? dbeta[t * gts + c] + s1 : s1;
     if (coef1) coef1[i] = s1 / static_cast<float>(rows);
@@ -262,6 +368,30 @@ __global__ void colsum_finalize_kernel(const float* part, int twins, int groups,
     out[t * ots + c] = accumulate ? out[t * ots + c] + s : s;
 }
 
+inline bool a16(const void* p) { return p == nullptr || aligned(p, 16); }
+inline bool m4(long long v) { return (v & 3) == 0; }
+
+// Whether a plane can take 4-column stores (fp16: 8-byte pairs; tf32: float4 pairs).
+inline bool plane_vec4(const rl2_plane& p) {
+    if (!plane_used(&p)) return true;
+    if (!m4(p.ld) || !m4(p.twin_stride)) return false;
+    return p.h16 ? aligned(p.h16, 8) : (aligned(p.hi, 16) && aligned(p.lo, 16));
+}
+
+inline bool apply_vec4(const rl2_bn_apply_args& a) {
+    return m4(a.cols) && m4(a.ldx) && m4(a.x_twin_stride) && m4(a.ldr) && m4(a.residual_twin_stride) && m4(a.ldy) &&
+           m4(a.y_twin_stride) && a16(a.x) && a16(a.residual) && a16(a.y) && a16(a.mean) && a16(a.invstd) &&
+           a16(a.gamma) && a16(a.beta) && plane_vec4(a.plane) &&
+           static_cast<long long>(a.rows) * a.cols < (1LL << 31);
+}
+
+inline bool backward_vec4(const rl2_bn_backward_args& a) {
+    return m4(a.cols) && m4(a.ldx) && m4(a.x_twin_stride) && m4(a.lddy) && m4(a.dy_twin_stride) && m4(a.lddx) &&
+           m4(a.dx_twin_stride) && a16(a.x) && a16(a.dy) && a16(a.dx) && a16(a.mean) && a16(a.invstd) &&
+           a16(a.gamma) && a16(a.beta) && a16(a.coef1) && a16(a.coef2) && plane_vec4(a.plane) &&
+           static_cast<long long>(a.rows) * a.cols < (1LL << 31);
+}
+
 inline int stream_blocks(long long work) {
     return static_cast<int>(std::max<long long>(1, std::min<long long>((work + kT - 1) / kT, 148LL * 16)));
 }
@@ -292,7 +422,7 @@ extern "C" int rl2_bn_finalize(const float* mean_p, const float* m2_p, long long
         set_error("bn finalize: invalid buffers or shape (running update needs rows >= 2)");
         return -1;
     }
-    norm::finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+    norm::finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
         mean_p, m2_p, pt, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update);
     return launch_status("batch-norm statistics");
 }
@@ -317,6 +447,12 @@ extern "C" int rl2_bn_apply(const rl2_bn_apply_args* a, void* stream) {
         return -1;
     }
     const long long work = static_cast<long long>(a->twins) * a->rows * a->cols;
+    if (norm::apply_vec4(*a)) {
+        const long long per_twin = static_cast<long long>(a->rows) * (a->cols / 4);
+        const int blocks = std::max(1, norm::stream_blocks(per_twin) / a->twins);
+        norm::apply_vec4_kernel<<<dim3(blocks, a->twins), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
+        return launch_status("batch-norm apply");
+    }
     norm::apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
     return launch_status("batch-norm apply");
 }
@@ -341,7 +477,7 @@ extern "C" int rl2_bn_backward_finalize(const float* s1p, const float* s2p, int 
         set_error("bn backward finalize: invalid arguments");
         return -1;
     }
-    norm::bwd_finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+    norm::bwd_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
         s1p, s2p, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
     return launch_status("batch-norm backward finalize");
 }
@@ -355,6 +491,13 @@ extern "C" int rl2_bn_backward_apply(const rl2_bn_backward_args* a, void* stream
         return -1;
     }
     const long long work = static_cast<long long>(a->sum_twins ? 1 : a->twins) * a->rows * a->cols;
+    if (norm::backward_vec4(*a)) {
+        const int outs = a->sum_twins ? 1 : a->twins;
+        const long long per_twin = static_cast<long long>(a->rows) * (a->cols / 4);
+        const int blocks = std::max(1, norm::stream_blocks(per_twin) / outs);
+        norm::bwd_apply_vec4_kernel<<<dim3(blocks, outs), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
+        return launch_status("batch-norm backward apply");
+    }
     norm::bwd_apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
     return launch_status("batch-norm backward apply");
 }

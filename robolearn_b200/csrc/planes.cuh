@@ -65,6 +65,22 @@ struct PlaneWriter {
             p.lo[o] = v - h;
         }
     }
+    // four consecutive columns (col % 4 == 0, row stride % 4 == 0, 16-byte aligned base)
+    __device__ __forceinline__ void store4(int t, long long row, int col, float4 v) {
+        const long long o = static_cast<long long>(t) * p.tstride + row * p.ld + col;
+        if (p.h16) {
+            const float4 s = make_float4(v.x * scale, v.y * scale, v.z * scale, v.w * scale);
+            overflow |= !(fabsf(s.x) <= 65504.0f && fabsf(s.y) <= 65504.0f && fabsf(s.z) <= 65504.0f &&
+                          fabsf(s.w) <= 65504.0f);
+            __half2* dst = reinterpret_cast<__half2*>(p.h16 + o);
+            dst[0] = __floats2half2_rn(s.x, s.y);
+            dst[1] = __floats2half2_rn(s.z, s.w);
+        } else if (p.hi) {
+            const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+            *reinterpret_cast<float4*>(p.hi + o) = h;
+            *reinterpret_cast<float4*>(p.lo + o) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+    }
     __device__ __forceinline__ void flush() {
         if (p.found_inf && overflow) atomicOr(p.found_inf, 1);
     }
