@@ -16,16 +16,20 @@
 //           keeps the products within ~1e-6 relative of fp32 (the reference's
 //           FP32 recipe uses pedantic fp32 GEMMs, kernels.cu:436-444).
 //
-// Layout: 128 x BN output tile per CTA (BN multiple of 16, <= 256), K staged
-// 128 bytes at a time through a multi-stage TMA -> smem ring with 128-byte
-// swizzle, accumulator in TMEM. Warp roles: warp 0 = TMA producer, warp 1 =
-// TMEM allocation + MMA issue (one elected thread), warps 2..5 = epilogue
-// (TMEM -> registers -> fused epilogue -> global). Every mbarrier wait is bounded
-// by wall-clock time and reports through the caller's health word.
+// Layout: persistent kernel, one CTA per SM walking 128 x BN output tiles (BN a
+// multiple of 16, <= 256). K is staged 128 bytes at a time through a multi-stage
+// TMA -> smem ring with 128-byte swizzle; the accumulator lives in TMEM, double
+// buffered (2 x BN columns) so that the epilogue of tile i overlaps the main loop of
+// tile i + 1 and the producer runs ahead across tile boundaries. Warp roles: warp 0 =
+// TMA producer, warp 1 = TMEM allocation + MMA issue (one elected thread), warps 2..5
+// = epilogue. Every mbarrier wait is bounded by wall-clock time, reports through the
+// caller's health word and stops the other roles through a shared abort word.
 //
-// Epilogue extras: per-column partial moments over each 32-row group (mean and
-// sum of squared deviations) feed training-mode batch norm without another read
-// of the output.
+// The epilogue stages each 32 x 32 accumulator slice in shared memory and walks it
+// 4 rows x 32 columns per warp step, so every global access of a warp covers whole
+// row segments (bias, residual, fp32 output, fp16 or tf32 hi/lo operand plane).
+// Extras: per-column partial moments over each 32-row group (mean and sum of squared
+// deviations) feed training-mode batch norm without another read of the output.
 
 #include "planes.cuh"
 
@@ -38,7 +42,7 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kThreads = 192;
-constexpr int kMaxSmem = 232448;
+constexpr int kMaxSmem = 232448;           // dynamic shared memory one CTA may use
 
 struct Params {
     int M, N, K;
@@ -57,25 +61,10 @@ struct Params {
     const float* scale;
     int* health;
     Plane out_plane;
+    int tiles_n, tiles_m, tiles_total;  // persistent work list (n fastest)
+    uint32_t buf_cols;                  // TMEM columns per accumulator buffer (power of two >= 32, >= BN)
+    bool vec_d, vec_res, vec_bias, vec_plane, vec_stat;  // 16-byte (plane: 8-byte) column-group access allowed
 };
-
-// Wall-clock bounded mbarrier wait (4 s), so a lost arrival cannot hang the GPU.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, int* health) {
-    if (ptx::mbar_try_wait(bar, phase)) return true;
-    uint64_t start;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
-    for (uint32_t i = 1;; ++i) {
-        if (ptx::mbar_try_wait(bar, phase)) return true;
-        if ((i & 1023u) == 0) {
-            uint64_t now;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-            if (now - start > 4000000000ull) {
-                if (health) atomicOr(health, kHealthTimeout);
-                return false;
-            }
-        }
-    }
-}
 
 // Shared-memory matrix descriptor. layout 2 = 128-byte swizzle (16-byte granules,
 // 8-row atoms); layout 1 = 128-byte swizzle with 32-byte granules (4-row atoms),
@@ -90,89 +79,365 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return d;
 }
 
-// Reduce-scatter of 16 per-lane values over the 32 lanes of a warp: afterwards
-// lane l holds the warp total of column (l >> 1) & 15.
-__device__ __forceinline__ float reduce_scatter16(float (&v)[16]) {
-    const int lane = threadIdx.x & 31;
-    float a[8];
-    {
-        const bool hi = lane & 16;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float keep = hi ? v[8 + j] : v[j];
-            const float send = hi ? v[j] : v[8 + j];
-            a[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+// Wall-clock bounded mbarrier wait (4 s) that also gives up as soon as another role of
+// the CTA has raised the shared abort word, so a lost arrival cannot hang the GPU.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, int* health, volatile int* abort_flag) {
+    if (ptx::mbar_try_wait(bar, phase)) return true;
+    uint64_t start;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+    for (uint32_t i = 1;; ++i) {
+        if (ptx::mbar_try_wait(bar, phase)) return true;
+        if ((i & 1023u) == 0) {
+            if (*abort_flag) return false;
+            uint64_t now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (now - start > 4000000000ull) {
+                if (health) atomicOr(health, kHealthTimeout);
+                *abort_flag = 1;
+                return false;
+            }
         }
     }
-    float b[4];
-    {
-        const bool hi = lane & 8;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float keep = hi ? a[4 + j] : a[j];
-            const float send = hi ? a[j] : a[4 + j];
-            b[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-        }
-    }
-    float c[2];
-    {
-        const bool hi = lane & 4;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const float keep = hi ? b[2 + j] : b[j];
-            const float send = hi ? b[j] : b[2 + j];
-            c[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-        }
-    }
-    float e;
-    {
-        const bool hi = lane & 2;
-        const float keep = hi ? c[1] : c[0];
-        const float send = hi ? c[0] : c[1];
-        e = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    return e + __shfl_xor_sync(0xffffffffu, e, 1);
 }
 
+// Output tile of a linear work index: n fastest (consecutive CTAs share the A rows),
+// then m, then (batch, split).
+struct Tile {
+    int n_tile, m_tile, z, split, kb_begin, kb_end;
+};
+
+__device__ __forceinline__ Tile decode(const Params& p, int t) {
+    Tile w;
+    w.n_tile = t % p.tiles_n;
+    t /= p.tiles_n;
+    w.m_tile = t % p.tiles_m;
+    t /= p.tiles_m;
+    w.z = t / p.splits;
+    w.split = t % p.splits;
+    w.kb_begin = w.split * p.kblocks_per_split;
+    w.kb_end = min(p.kblocks_total, w.kb_begin + p.kblocks_per_split);
+    return w;
+}
+
+template <int KIND, int A_MN, int B_MN>
+__device__ __forceinline__ void produce(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const CUtensorMap* tma_a_lo,
+                                        const CUtensorMap* tma_b_lo, const Params& p, int stages, uint8_t* smem,
+                                        uint32_t stage_bytes, uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
+    constexpr int kElem = KIND == 0 ? 2 : 4;
+    constexpr int kBK = 128 / kElem;
+    constexpr int kChunk = 128 / kElem;
+    constexpr int kPlanes = KIND == 0 ? 1 : 2;
+    const int BN = p.BN;
+    const uint32_t a_bytes = kBM * 128;
+    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
+    ptx::prefetch_tensormap(tma_a);
+    ptx::prefetch_tensormap(tma_b);
+    int s = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+        const Tile w = decode(p, t);
+        const int za = p.a_batched ? w.z : 0;
+        const int zb = p.b_batched ? w.z : 0;
+        const int m0 = w.m_tile * kBM;
+        const int n0 = w.n_tile * BN;
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+            if (!wait_bar(&empty[s], phase ^ 1, p.health, abort_flag)) {
+                ok = false;
+                break;
+            }
+            ptx::mbar_arrive_expect_tx(&full[s], stage_bytes);
+            ++issued;
+            uint8_t* sa = smem + s * stage_bytes;
+            uint8_t* sb = sa + a_bytes * kPlanes;
+            const int k0 = kb * kBK;
+            for (int plane = 0; plane < kPlanes; ++plane) {
+                const CUtensorMap* ma = plane == 0 ? tma_a : tma_a_lo;
+                const CUtensorMap* mb = plane == 0 ? tma_b : tma_b_lo;
+                uint8_t* da = sa + plane * a_bytes;
+                uint8_t* db = sb + plane * b_bytes;
+                if (A_MN) {
+                    for (int c = 0; c < kBM / kChunk; ++c)
+                        ptx::tma_load_3d(da + c * (kBK * 128), ma, &full[s], m0 + c * kChunk, k0, za);
+                } else {
+                    ptx::tma_load_3d(da, ma, &full[s], k0, m0, za);
+                }
+                if (B_MN) {
+                    for (int c = 0; c < BN / kChunk; ++c)
+                        ptx::tma_load_3d(db + c * (kBK * 128), mb, &full[s], n0 + c * kChunk, k0, zb);
+                } else {
+                    ptx::tma_load_3d(db, mb, &full[s], k0, n0, zb);
+                }
+            }
+            if (++s == stages) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+    }
+    // Before the CTA may exit (and free its shared memory), every armed stage must have
+    // landed, including loads nobody consumed after an abort (bounded waits).
+    for (int st = 0; st < stages; ++st) {
+        const long long arms = issued > st ? (issued - 1 - st) / stages + 1 : 0;
+        if (arms > 0) {
+            volatile int no_abort = 0;
+            wait_bar(&full[st], static_cast<uint32_t>((arms - 1) & 1), p.health, &no_abort);
+        }
+    }
+}
+
+// One elected thread issues every tcgen05.mma of the CTA. Local tile i accumulates into
+// TMEM buffer i & 1 once the epilogue has drained that buffer's previous tile.
+template <int KIND, int A_MN, int B_MN>
+__device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem, uint32_t stage_bytes, uint64_t* full,
+                                      uint64_t* empty, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
+                                      uint32_t buf_cols, volatile int* abort_flag) {
+    constexpr int kElem = KIND == 0 ? 2 : 4;
+    constexpr int kBK = 128 / kElem;
+    constexpr int kUK = 32 / kElem;
+    constexpr int kPlanes = KIND == 0 ? 1 : 2;
+    const int BN = p.BN;
+    const uint32_t a_bytes = kBM * 128;
+    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
+    const uint32_t fmt = KIND == 0 ? 0u : 2u;
+    const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(A_MN) << 15) |
+                           (static_cast<uint32_t>(B_MN) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                           (static_cast<uint32_t>(kBM >> 4) << 24);
+    // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = one swizzle
+    // atom of K rows (8 rows = 1024 B for fp16; 4 rows = 512 B for the tf32 32-byte-granule
+    // swizzle). K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
+    const uint32_t lbo_mn = kBK * 128;
+    const uint32_t sbo_mn = KIND == 0 ? 1024u : 512u;
+    const uint32_t lay_mn = KIND == 0 ? 2u : 1u;
+    int s = 0;
+    uint32_t phase = 0;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+        const Tile w = decode(p, t);
+        const int buf = i & 1;
+        if (!wait_bar(&acc_empty[buf], ((i >> 1) & 1) ^ 1, p.health, abort_flag)) return;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf) * buf_cols;
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+            if (!wait_bar(&full[s], phase, p.health, abort_flag)) return;
+            ptx::tc_fence_after();
+            const uint32_t sa = ptx::smem_u32(smem + s * stage_bytes);
+            const uint32_t sb = sa + a_bytes * kPlanes;
+            const bool first = kb == w.kb_begin;
+#pragma unroll
+            for (int j = 0; j < kBK / kUK; ++j) {
+                const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
+                const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
+                const uint64_t da = A_MN ? smem_desc(sa + a_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sa + a_off, 16, 1024);
+                const uint64_t db = B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
+                const uint32_t acc = (!first || j > 0) ? 1u : 0u;
+                if (KIND == 0) {
+                    ptx::mma_f16(d_tmem, da, db, idesc, acc);
+                } else {
+                    const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
+                                                : smem_desc(sa + a_bytes + a_off, 16, 1024);
+                    const uint64_t db_lo = B_MN ? smem_desc(sb + b_bytes + b_off, lbo_mn, sbo_mn, lay_mn)
+                                                : smem_desc(sb + b_bytes + b_off, 16, 1024);
+                    ptx::mma_tf32(d_tmem, da_lo, db, idesc, acc);
+                    ptx::mma_tf32(d_tmem, da, db_lo, idesc, 1u);
+                    ptx::mma_tf32(d_tmem, da, db, idesc, 1u);
+                }
+            }
+            ptx::mma_commit(&empty[s]);
+            if (++s == stages) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+        ptx::mma_commit(&acc_full[buf]);
+    }
+}
+
+constexpr int kStagePitch = 36;  // floats per staged row: 16-byte aligned, conflict-free float4 access
+
+__device__ __forceinline__ float4 load_cols(const float* src, int n, bool vec) {
+    if (vec && n == 4) return *reinterpret_cast<const float4*>(src);
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n > 0) r.x = src[0];
+    if (n > 1) r.y = src[1];
+    if (n > 2) r.z = src[2];
+    if (n > 3) r.w = src[3];
+    return r;
+}
+
+__device__ __forceinline__ void store_cols(float* dst, float4 v, int n, bool vec) {
+    if (vec && n == 4) {
+        *reinterpret_cast<float4*>(dst) = v;
+        return;
+    }
+    if (n > 0) dst[0] = v.x;
+    if (n > 1) dst[1] = v.y;
+    if (n > 2) dst[2] = v.z;
+    if (n > 3) dst[3] = v.w;
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+
+__device__ __forceinline__ float4 xor_sum4(float4 v, int mask) {
+    v.x += __shfl_xor_sync(0xffffffffu, v.x, mask);
+    v.y += __shfl_xor_sync(0xffffffffu, v.y, mask);
+    v.z += __shfl_xor_sync(0xffffffffu, v.z, mask);
+    v.w += __shfl_xor_sync(0xffffffffu, v.w, mask);
+    return v;
+}
+
+// Epilogue warps 2..5. Warp w may only read TMEM lanes (tile rows) 32*(w % 4) .. +31.
+// Each 32 x 32 accumulator slice is read with lane = row, staged in shared memory and
+// then walked 4 rows x 32 columns per step (lane = 4 consecutive columns of one row),
+// so every global access of the warp covers whole 128-byte row segments. After the
+// last TMEM read of a tile the warp releases the accumulator buffer to the MMA issuer.
+__device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
+                                      float* staging, volatile int* abort_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = warp & 3;
+    float* sq = staging + q * (32 * kStagePitch);
+    const int cg = lane & 7;
+    const int rsub = lane >> 3;
+    const float scale = p.scale ? *p.scale : 1.0f;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    PlaneWriter pw(p.out_plane);
+    const int BN = p.BN;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+        const Tile w = decode(p, t);
+        const int buf = i & 1;
+        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
+        ptx::tc_fence_after();
+        const int r0 = w.m_tile * kBM + q * 32;
+        const int valid = min(max(p.M - r0, 0), 32);
+        float* d = p.d ? p.d + static_cast<long long>(w.z) * p.d_bstride + static_cast<long long>(w.split) * p.d_split_stride
+                       : nullptr;
+        const float* bias = p.bias ? p.bias + static_cast<long long>(w.z) * p.bias_bstride : nullptr;
+        const float* res = p.residual ? p.residual + static_cast<long long>(w.z) * p.r_bstride : nullptr;
+        const long long group = static_cast<long long>(w.m_tile * kBM) / 32 + q;
+        const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            const int col0 = w.n_tile * BN + c0;
+            if (col0 >= p.N) break;  // warp-uniform
+            {
+                float v[32];
+                // columns past BN stay inside the buffer (buf_cols >= BN rounded up to 32)
+                ptx::tmem_ld32(t_base + static_cast<uint32_t>(c0), v);
+                float4* mine = reinterpret_cast<float4*>(sq + lane * kStagePitch);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) mine[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+            __syncwarp();
+            if (valid > 0) {
+                const int col = col0 + 4 * cg;
+                const int nc = max(0, min(4, min(BN - c0 - 4 * cg, p.N - col)));
+                const float4 b4 = (bias && nc > 0) ? load_cols(bias + col, nc, p.vec_bias) : zero;
+                float4 rv[8], ov[8];
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int r = 4 * it + rsub;
+                    const long long row = r0 + r;
+                    const bool live = r < valid && nc > 0;
+                    rv[it] = (res && live) ? load_cols(res + row * p.ldr + col, nc, p.vec_res) : zero;
+                    ov[it] = (d && p.accumulate && live) ? load_cols(d + row * p.ldd + col, nc, p.vec_d) : zero;
+                }
+                float4 xs[8];
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int r = 4 * it + rsub;
+                    const float4 a = *reinterpret_cast<const float4*>(sq + r * kStagePitch + 4 * cg);
+                    float4 x = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+                    if (bias) x = add4(x, b4);
+                    if (res) x = add4(x, rv[it]);
+                    if (d && p.accumulate) x = add4(x, ov[it]);
+                    const bool live = r < valid && nc > 0;
+                    if (live) {
+                        const long long row = r0 + r;
+                        if (d) store_cols(d + row * p.ldd + col, x, nc, p.vec_d);
+                        if (pw.active()) {
+                            if (nc == 4 && p.vec_plane) {
+                                pw.store4(w.z, row, col, x);
+                            } else {
+                                if (nc > 0) pw.store(w.z, row, col, x.x);
+                                if (nc > 1) pw.store(w.z, row, col + 1, x.y);
+                                if (nc > 2) pw.store(w.z, row, col + 2, x.z);
+                                if (nc > 3) pw.store(w.z, row, col + 3, x.w);
+                            }
+                        }
+                    }
+                    xs[it] = r < valid ? x : zero;
+                }
+                if (p.stat_mean) {
+                    float4 sum = zero;
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) sum = add4(sum, xs[it]);
+                    sum = xor_sum4(xor_sum4(sum, 8), 16);
+                    const float fv = static_cast<float>(valid);
+                    const float4 mean = make_float4(sum.x / fv, sum.y / fv, sum.z / fv, sum.w / fv);
+                    float4 m2 = zero;
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        if (4 * it + rsub < valid) {
+                            const float4 dv = make_float4(xs[it].x - mean.x, xs[it].y - mean.y, xs[it].z - mean.z,
+                                                          xs[it].w - mean.w);
+                            m2 = make_float4(m2.x + dv.x * dv.x, m2.y + dv.y * dv.y, m2.z + dv.z * dv.z,
+                                             m2.w + dv.w * dv.w);
+                        }
+                    }
+                    m2 = xor_sum4(xor_sum4(m2, 8), 16);
+                    if (rsub == 0 && nc > 0) {
+                        const long long idx = static_cast<long long>(w.z) * p.stat_bstride + group * p.N + col;
+                        store_cols(p.stat_mean + idx, mean, nc, p.vec_stat);
+                        store_cols(p.stat_m2 + idx, m2, nc, p.vec_stat);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+    }
+    pw.flush();
+}
+
+// Persistent kernel: one CTA per SM walks the output tiles blockIdx.x, +gridDim.x, ...
+// Shared memory: [stage ring][epilogue staging 4 x 32 x 36 floats][barriers].
 template <int KIND, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_a_lo, const __grid_constant__ CUtensorMap tma_b_lo,
                 const Params p, const int stages) {
-    constexpr int kElem = KIND == 0 ? 2 : 4;
-    constexpr int kBK = 128 / kElem;       // K elements per stage (one 128-byte swizzle row)
-    constexpr int kUK = 32 / kElem;        // K per MMA instruction (32 bytes)
-    constexpr int kChunk = 128 / kElem;    // MN elements per 128-byte chunk (MN-major boxes)
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
-    const int BN = p.BN;
-    const uint32_t a_bytes = kBM * 128;                 // 128 rows x 128 B per plane
-    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
-    const uint32_t stage_bytes = (a_bytes + b_bytes) * kPlanes;
+    const uint32_t stage_bytes = (kBM * 128 + static_cast<uint32_t>(p.BN) * 128) * kPlanes;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
+    float* staging = reinterpret_cast<float*>(smem + stages * stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 4 * 32 * kStagePitch);
     uint64_t* empty = full + stages;
     uint64_t* acc_full = empty + stages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int n_tile = blockIdx.x;
-    const int m_tile = blockIdx.y;
-    const int z = blockIdx.z / p.splits;
-    const int split = blockIdx.z % p.splits;
-    const int kb_begin = split * p.kblocks_per_split;
-    const int kb_end = min(p.kblocks_total, kb_begin + p.kblocks_per_split);
-    const int n_kb = kb_end - kb_begin;
-    const uint32_t tmem_cols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    const uint32_t tmem_cols = 2 * p.buf_cols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], 1);
         }
-        ptx::mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        }
+        ptx::mbar_init(mma_done, 1);
+        *abort_flag = 0;
         ptx::fence_barrier_init();
     }
     if (warp == 1) {
@@ -185,171 +450,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (ptx::elect_one()) {
-            ptx::prefetch_tensormap(&tma_a);
-            ptx::prefetch_tensormap(&tma_b);
-            const int za = p.a_batched ? z : 0;
-            const int zb = p.b_batched ? z : 0;
-            const int m0 = m_tile * kBM;
-            const int n0 = n_tile * BN;
-            int s = 0;
-            uint32_t phase = 0;
-            for (int kb = kb_begin; kb < kb_end; ++kb) {
-                if (!wait_bar(&empty[s], phase ^ 1, p.health)) break;
-                ptx::mbar_arrive_expect_tx(&full[s], stage_bytes);
-                uint8_t* sa = smem + s * stage_bytes;
-                uint8_t* sb = sa + a_bytes * kPlanes;
-                const int k0 = kb * kBK;
-                for (int plane = 0; plane < kPlanes; ++plane) {
-                    const CUtensorMap* ma = plane == 0 ? &tma_a : &tma_a_lo;
-                    const CUtensorMap* mb = plane == 0 ? &tma_b : &tma_b_lo;
-                    uint8_t* da = sa + plane * a_bytes;
-                    uint8_t* db = sb + plane * b_bytes;
-                    if (A_MN) {
-                        for (int c = 0; c < kBM / kChunk; ++c)
-                            ptx::tma_load_3d(da + c * (kBK * 128), ma, &full[s], m0 + c * kChunk, k0, za);
-                    } else {
-                        ptx::tma_load_3d(da, ma, &full[s], k0, m0, za);
-                    }
-                    if (B_MN) {
-                        for (int c = 0; c < BN / kChunk; ++c)
-                            ptx::tma_load_3d(db + c * (kBK * 128), mb, &full[s], n0 + c * kChunk, k0, zb);
-                    } else {
-                        ptx::tma_load_3d(db, mb, &full[s], k0, n0, zb);
-                    }
-                }
-                if (++s == stages) {
-                    s = 0;
-                    phase ^= 1;
-                }
-            }
-        }
+        if (ptx::elect_one())
+            produce<KIND, A_MN, B_MN>(&tma_a, &tma_b, &tma_a_lo, &tma_b_lo, p, stages, smem, stage_bytes, full, empty,
+                                      abort_flag);
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
         if (ptx::elect_one()) {
-            const uint32_t fmt = KIND == 0 ? 0u : 2u;
-            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(A_MN) << 15) |
-                                   (static_cast<uint32_t>(B_MN) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                                   (static_cast<uint32_t>(kBM >> 4) << 24);
-            // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = one swizzle
-            // atom of K rows (8 rows = 1024 B for fp16; 4 rows = 512 B for the tf32 32-byte-granule
-            // swizzle). K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
-            const uint32_t lbo_mn = kBK * 128;
-            const uint32_t sbo_mn = KIND == 0 ? 1024u : 512u;
-            const uint32_t lay_mn = KIND == 0 ? 2u : 1u;
-            int s = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int i = 0; i < n_kb; ++i) {
-                if (!wait_bar(&full[s], phase, p.health)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after();
-                const uint32_t sa = ptx::smem_u32(smem + s * stage_bytes);
-                const uint32_t sb = sa + a_bytes * kPlanes;
-#pragma unroll
-                for (int j = 0; j < kBK / kUK; ++j) {
-                    const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
-                    const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
-                    const uint64_t da = A_MN ? smem_desc(sa + a_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sa + a_off, 16, 1024);
-                    const uint64_t db = B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
-                    const uint32_t acc = (i > 0 || j > 0) ? 1u : 0u;
-                    if (KIND == 0) {
-                        ptx::mma_f16(tmem, da, db, idesc, acc);
-                    } else {
-                        const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
-                                                    : smem_desc(sa + a_bytes + a_off, 16, 1024);
-                        const uint64_t db_lo = B_MN ? smem_desc(sb + b_bytes + b_off, lbo_mn, sbo_mn, lay_mn)
-                                                    : smem_desc(sb + b_bytes + b_off, 16, 1024);
-                        ptx::mma_tf32(tmem, da_lo, db, idesc, acc);
-                        ptx::mma_tf32(tmem, da, db_lo, idesc, 1u);
-                        ptx::mma_tf32(tmem, da, db, idesc, 1u);
-                    }
-                }
-                ptx::mma_commit(&empty[s]);
-                if (++s == stages) {
-                    s = 0;
-                    phase ^= 1;
-                }
-            }
-            if (ok) ptx::mma_commit(acc_full);
+            issue<KIND, A_MN, B_MN>(p, stages, smem, stage_bytes, full, empty, acc_full, acc_empty, tmem, p.buf_cols,
+                                    abort_flag);
+            // every issued MMA has completed before TMEM is released (also after an abort)
+            ptx::mma_commit(mma_done);
+            volatile int no_abort = 0;
+            wait_bar(mma_done, 0, p.health, &no_abort);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const int row_local = q * 32 + lane;
-        const int row = m_tile * kBM + row_local;
-        const bool row_ok = row < p.M;
-        const int valid = min(max(p.M - (m_tile * kBM + q * 32), 0), 32);
-        const bool ok = wait_bar(acc_full, 0, p.health);
-        ptx::tc_fence_after();
-        PlaneWriter pw(p.out_plane);
-        if (ok && n_kb > 0) {
-            const float scale = p.scale ? *p.scale : 1.0f;
-            float* d = p.d ? p.d + static_cast<long long>(z) * p.d_bstride + static_cast<long long>(split) * p.d_split_stride
-                           : nullptr;
-            const float* bias = p.bias ? p.bias + static_cast<long long>(z) * p.bias_bstride : nullptr;
-            const float* res = p.residual ? p.residual + static_cast<long long>(z) * p.r_bstride : nullptr;
-            const int group = (m_tile * kBM) / 32 + q;
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float v[16];
-                ptx::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0), v);
-                const int col0 = n_tile * BN + c0;
-                if (col0 >= p.N) break;  // warp-uniform
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float x = v[i] * scale;
-                    const int col = col0 + i;
-                    if (col < p.N) {
-                        if (bias) x += bias[col];
-                        if (res && row_ok) x += res[static_cast<long long>(row) * p.ldr + col];
-                        if (p.accumulate && row_ok && d) x += d[static_cast<long long>(row) * p.ldd + col];
-                    }
-                    v[i] = x;
-                }
-                if (row_ok && pw.active()) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        if (col0 + i < p.N) pw.store(z, row, col0 + i, v[i]);
-                }
-                if (row_ok && p.d) {
-                    float* drow = d + static_cast<long long>(row) * p.ldd + col0;
-                    if (col0 + 16 <= p.N && (p.ldd & 3) == 0 && ptx::aligned16(drow)) {
-#pragma unroll
-                        for (int i = 0; i < 16; i += 4)
-                            *reinterpret_cast<float4*>(drow + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (col0 + i < p.N) drow[i] = v[i];
-                    }
-                }
-                if (p.stat_mean && valid > 0) {
-                    float t[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) t[i] = row_ok ? v[i] : 0.0f;
-                    const float total = reduce_scatter16(t);
-                    const float mean_mine = total / static_cast<float>(valid);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float m_i = __shfl_sync(0xffffffffu, mean_mine, 2 * i);
-                        const float dv = row_ok ? v[i] - m_i : 0.0f;
-                        t[i] = dv * dv;
-                    }
-                    const float m2 = reduce_scatter16(t);
-                    const int col = col0 + ((lane >> 1) & 15);
-                    if ((lane & 1) == 0 && col < p.N) {
-                        const long long idx = static_cast<long long>(z) * p.stat_bstride +
-                                              static_cast<long long>(group) * p.N + col;
-                        p.stat_mean[idx] = mean_mine;
-                        p.stat_m2[idx] = m2;
-                    }
-                }
-            }
-        }
-        pw.flush();
+        drain(p, acc_full, acc_empty, tmem, staging, abort_flag);
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -574,7 +688,9 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.out_plane = to_plane(&g->out_plane);
     const int planes = g->kind == 0 ? 1 : 2;
     const int stage_bytes = (kBM * 128 + bn * 128) * planes;
-    const int overhead = 1024 + 256;
+    // ring + epilogue staging + barriers (2 x stages + 5 words, TMEM slot, abort word) + alignment slack
+    const int staging = 4 * 32 * kStagePitch * 4;
+    const int overhead = 1024 + staging + 256;
     plan->stages = std::min(8, (kMaxSmem - overhead) / stage_bytes);
     if (plan->stages < 2) {
         set_error("GEMM tile does not fit shared memory");
@@ -582,12 +698,34 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         return nullptr;
     }
     plan->smem = plan->stages * stage_bytes + overhead;
-    plan->grid = dim3((g->n + bn - 1) / bn, (g->m + kBM - 1) / kBM, g->batch * p.splits);
-    if (plan->grid.y > 65535 || plan->grid.z > 65535) {
-        set_error("GEMM grid exceeds launch limits");
+    const long long tiles_n = (g->n + bn - 1) / bn;
+    const long long tiles_m = (g->m + kBM - 1) / kBM;
+    const long long tiles = tiles_n * tiles_m * g->batch * p.splits;
+    if (tiles > 0x7FFFFFFFLL) {
+        set_error("GEMM has too many output tiles");
         delete plan;
         return nullptr;
     }
+    p.tiles_n = static_cast<int>(tiles_n);
+    p.tiles_m = static_cast<int>(tiles_m);
+    p.tiles_total = static_cast<int>(tiles);
+    p.buf_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+    auto a16 = [](const void* q) { return aligned(q, 16); };
+    p.vec_d = g->d && a16(g->d) && g->ldd % 4 == 0 && g->d_batch_stride % 4 == 0 && g->d_split_stride % 4 == 0;
+    p.vec_res = g->residual && a16(g->residual) && g->ldr % 4 == 0 && g->residual_batch_stride % 4 == 0;
+    p.vec_bias = g->bias && a16(g->bias) && g->bias_batch_stride % 4 == 0;
+    p.vec_stat = g->stat_mean && a16(g->stat_mean) && a16(g->stat_m2) && g->n % 4 == 0 && g->stat_batch_stride % 4 == 0;
+    p.vec_plane = plane_used(&g->out_plane) && g->out_plane.ld % 4 == 0 && g->out_plane.twin_stride % 4 == 0 &&
+                  (g->out_plane.h16 ? aligned(g->out_plane.h16, 8)
+                                    : a16(g->out_plane.hi) && a16(g->out_plane.lo));
+    int device = 0, sms = 0;
+    if (cudaGetDevice(&device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms < 1) {
+        set_error("cannot query the SM count of the current device");
+        delete plan;
+        return nullptr;
+    }
+    plan->grid = dim3(static_cast<unsigned>(std::min<long long>(tiles, sms)), 1, 1);
     // The limit is an attribute of the kernel function shared by every plan that uses
     // it, so it is always raised to the device maximum (never lowered by a small plan).
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);

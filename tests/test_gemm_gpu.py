@@ -130,3 +130,53 @@ def test_gemm_rejects_misaligned_stride():
     d = torch.zeros(16, 16, device="cuda")
     with pytest.raises(RuntimeError, match="16 bytes"):
         dense.DensePlan(kind=0, m=16, n=16, k=10, a=a, b=b, d=d, lda=10, ldb=16, ldd=16)
+
+
+@pytest.mark.parametrize("kind,tile_n", [(0, 0), (0, 48), (1, 0)])
+def test_gemm_multi_wave_epilogue_moments_and_plane(kind, tile_n):
+    """More CTAs than SMs (two co-resident CTAs per SM for fp16 tiles), ragged M and N,
+    bias + residual, 32-row column moments and an operand-plane copy of the output."""
+    from robolearn_b200 import _native as N
+
+    m, n, k, batch = 8200, 600, 256, 2
+    groups = (m + 31) // 32
+    bias = torch.randn(batch, n, device="cuda")
+    res = torch.randn(batch, m, n, device="cuda")
+    mean = torch.zeros(batch, groups, n, device="cuda")
+    m2 = torch.zeros(batch, groups, n, device="cuda")
+    pld = dense.operand_ld(n, kind)
+    if kind == 0:
+        h16 = torch.zeros(batch, m, pld, device="cuda", dtype=torch.float16)
+        plane = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=m * pld)
+        keep = [h16]
+    else:
+        hi = torch.zeros(batch, m, pld, device="cuda")
+        lo = torch.zeros(batch, m, pld, device="cuda")
+        plane = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld)
+        keep = [hi, lo]
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, bias=bias, bias_batch_stride=n, residual=res, ldr=n,
+                        residual_batch_stride=m * n, stat_mean=mean, stat_m2=m2, stat_batch_stride=groups * n,
+                        out_plane=plane, tile_n=tile_n)
+    plan.run()
+    torch.cuda.synchronize()
+    expect = ref + bias.double()[:, None, :] + res.double()
+    out = D[:, :, :n].double()
+    tol = 2e-3 if kind == 0 else 2e-5
+    assert (out - expect).abs().max().item() < tol * expect.abs().max().item()
+    if kind == 0:
+        assert torch.equal(keep[0][:, :, :n], D[:, :, :n].half())
+    else:
+        hi_ref = (D[:, :, :n].view(torch.int32) & -8192).view(torch.float32)
+        assert torch.equal(keep[0][:, :, :n], hi_ref)
+        assert torch.equal(keep[1][:, :, :n], D[:, :, :n] - hi_ref)
+    full = torch.zeros(batch, groups * 32, n, device="cuda", dtype=torch.float64)
+    full[:, :m] = out
+    rows = full.view(batch, groups, 32, n)
+    counts = torch.full((groups,), 32.0, device="cuda", dtype=torch.float64)
+    counts[-1] = m - 32 * (groups - 1)
+    mu = rows.sum(2) / counts[None, :, None]
+    valid = (torch.arange(groups * 32, device="cuda") < m).view(groups, 32)[None, :, :, None]
+    dev = torch.where(valid, rows - mu[:, :, None, :], torch.zeros_like(rows))
+    assert torch.allclose(mean.double(), mu, atol=1e-4, rtol=1e-4)
+    assert torch.allclose(m2.double(), (dev**2).sum(2), atol=1e-3, rtol=1e-4)
+    del keep
