@@ -21,12 +21,12 @@
 // TMA -> smem ring with 128-byte swizzle; the accumulator lives in TMEM, double
 // buffered (2 x BN columns) so that the epilogue of tile i overlaps the main loop of
 // tile i + 1 and the producer runs ahead across tile boundaries. Warp roles: warp 0 =
-// TMA producer, warp 1 = TMEM allocation + MMA issue (one elected thread), warps 2..5
-// = epilogue. Every mbarrier wait is bounded by wall-clock time, reports through the
+// TMA producer, warp 1 = TMEM allocation + MMA issue (one elected thread), warps 2..9
+// = epilogue (two per TMEM lane quarter). Every mbarrier wait is bounded by wall-clock time, reports through the
 // caller's health word and stops the other roles through a shared abort word.
 //
-// The epilogue stages each 32 x 32 accumulator slice in shared memory and walks it
-// 4 rows x 32 columns per warp step, so every global access of a warp covers whole
+// The epilogue stages each 32 x 16 accumulator slice in shared memory and walks it
+// 8 rows x 16 columns per warp step, so every global access of a warp covers whole
 // row segments (bias, residual, fp32 output, fp16 or tf32 hi/lo operand plane).
 // Extras: per-column partial moments over each 32-row group (mean and sum of squared
 // deviations) feed training-mode batch norm without another read of the output.
@@ -41,7 +41,8 @@ namespace rl2 {
 namespace gemm {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxSmem = 232448;           // dynamic shared memory one CTA may use
 
 struct Params {
@@ -254,7 +255,10 @@ __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem
     }
 }
 
-constexpr int kStagePitch = 36;  // floats per staged row: 16-byte aligned, conflict-free float4 access
+// Staged 32 x 16 slice: rows of 16 floats, 16-byte chunk j of row r stored at chunk
+// j ^ ((r >> 1) & 3), which keeps both the row-per-lane writes and the 8-row x 16-column
+// reads free of bank conflicts.
+constexpr int kStagePitch = 16;
 
 __device__ __forceinline__ float4 load_cols(const float* src, int n, bool vec) {
     if (vec && n == 4) return *reinterpret_cast<const float4*>(src);
@@ -287,22 +291,30 @@ __device__ __forceinline__ float4 xor_sum4(float4 v, int mask) {
     return v;
 }
 
-// Epilogue warps 2..5. Warp w may only read TMEM lanes (tile rows) 32*(w % 4) .. +31.
-// Each 32 x 32 accumulator slice is read with lane = row, staged in shared memory and
-// then walked 4 rows x 32 columns per step (lane = 4 consecutive columns of one row),
-// so every global access of the warp covers whole 128-byte row segments. After the
-// last TMEM read of a tile the warp releases the accumulator buffer to the MMA issuer.
+// Epilogue warps 2 .. 2 + kEpiWarps - 1, two per TMEM lane quarter: warp w may only read
+// TMEM lanes (tile rows) 32*(w % 4) .. +31, and the two warps of a quarter take
+// alternate 16-column chunks. A 32 x 16 accumulator slice is read with lane = row,
+// staged in shared memory and walked 8 rows x 16 columns per step (lane = 4
+// consecutive columns of one row), so every global access covers whole row segments.
+// Interior chunks (32 valid rows, 16 valid columns, vector-aligned operands) take a
+// branch-free path whose loads are all issued before the stores; edge chunks take a
+// guarded path. After its last TMEM read of a tile each warp releases the accumulator
+// buffer to the MMA issuer.
 __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
                                       float* staging, volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
-    float* sq = staging + q * (32 * kStagePitch);
-    const int cg = lane & 7;
-    const int rsub = lane >> 3;
+    const int half = (warp - 2) >> 2;
+    float* sq = staging + (warp - 2) * (32 * kStagePitch);
+    const int cg = lane & 3;
+    const int rsub = lane >> 2;
     const float scale = p.scale ? *p.scale : 1.0f;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     PlaneWriter pw(p.out_plane);
+    const bool plane_on = pw.active();
+    const bool fast_ok = (!p.d || p.vec_d) && (!p.residual || p.vec_res) && (!p.bias || p.vec_bias) &&
+                         (!plane_on || p.vec_plane) && (!p.stat_mean || p.vec_stat);
     const int BN = p.BN;
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
@@ -318,80 +330,109 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
         const float* res = p.residual ? p.residual + static_cast<long long>(w.z) * p.r_bstride : nullptr;
         const long long group = static_cast<long long>(w.m_tile * kBM) / 32 + q;
         const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 16 * half; c0 < BN; c0 += 32) {
             const int col0 = w.n_tile * BN + c0;
             if (col0 >= p.N) break;  // warp-uniform
             {
-                float v[32];
-                // columns past BN stay inside the buffer (buf_cols >= BN rounded up to 32)
-                ptx::tmem_ld32(t_base + static_cast<uint32_t>(c0), v);
+                float v[16];
+                ptx::tmem_ld16(t_base + static_cast<uint32_t>(c0), v);
                 float4* mine = reinterpret_cast<float4*>(sq + lane * kStagePitch);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) mine[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                for (int j = 0; j < 4; ++j)
+                    mine[j ^ ((lane >> 1) & 3)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
             __syncwarp();
-            if (valid > 0) {
-                const int col = col0 + 4 * cg;
-                const int nc = max(0, min(4, min(BN - c0 - 4 * cg, p.N - col)));
-                const float4 b4 = (bias && nc > 0) ? load_cols(bias + col, nc, p.vec_bias) : zero;
-                float4 rv[8], ov[8];
+            const int col = col0 + 4 * cg;
+            float4 x[4];
 #pragma unroll
-                for (int it = 0; it < 8; ++it) {
-                    const int r = 4 * it + rsub;
-                    const long long row = r0 + r;
-                    const bool live = r < valid && nc > 0;
-                    rv[it] = (res && live) ? load_cols(res + row * p.ldr + col, nc, p.vec_res) : zero;
-                    ov[it] = (d && p.accumulate && live) ? load_cols(d + row * p.ldd + col, nc, p.vec_d) : zero;
+            for (int it = 0; it < 4; ++it) {
+                const float4 a = *reinterpret_cast<const float4*>(sq + (8 * it + rsub) * kStagePitch + 4 * (cg ^ ((rsub >> 1) & 3)));
+                x[it] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+            }
+            if (fast_ok && valid == 32 && col0 + 16 <= p.N) {
+                // ---- interior chunk: no per-row or per-lane guards ----
+                if (bias) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(bias + col);
+#pragma unroll
+                    for (int it = 0; it < 4; ++it) x[it] = add4(x[it], b4);
                 }
-                float4 xs[8];
+                if (res) {
+                    float4 rv[4];
 #pragma unroll
-                for (int it = 0; it < 8; ++it) {
-                    const int r = 4 * it + rsub;
-                    const float4 a = *reinterpret_cast<const float4*>(sq + r * kStagePitch + 4 * cg);
-                    float4 x = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
-                    if (bias) x = add4(x, b4);
-                    if (res) x = add4(x, rv[it]);
-                    if (d && p.accumulate) x = add4(x, ov[it]);
-                    const bool live = r < valid && nc > 0;
-                    if (live) {
-                        const long long row = r0 + r;
-                        if (d) store_cols(d + row * p.ldd + col, x, nc, p.vec_d);
-                        if (pw.active()) {
+                    for (int it = 0; it < 4; ++it)
+                        rv[it] = *reinterpret_cast<const float4*>(res + static_cast<long long>(r0 + 8 * it + rsub) * p.ldr + col);
+#pragma unroll
+                    for (int it = 0; it < 4; ++it) x[it] = add4(x[it], rv[it]);
+                }
+                if (d) {
+                    float* dcol = d + col;
+                    if (p.accumulate) {
+                        float4 ov[4];
+#pragma unroll
+                        for (int it = 0; it < 4; ++it)
+                            ov[it] = *reinterpret_cast<const float4*>(dcol + static_cast<long long>(r0 + 8 * it + rsub) * p.ldd);
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) x[it] = add4(x[it], ov[it]);
+                    }
+#pragma unroll
+                    for (int it = 0; it < 4; ++it)
+                        *reinterpret_cast<float4*>(dcol + static_cast<long long>(r0 + 8 * it + rsub) * p.ldd) = x[it];
+                }
+                if (plane_on) {
+#pragma unroll
+                    for (int it = 0; it < 4; ++it) pw.store4(w.z, r0 + 8 * it + rsub, col, x[it]);
+                }
+            } else {
+                // ---- edge chunk: guarded per row and per column ----
+                const int nc = max(0, min(4, p.N - col));
+                const float4 b4 = (bias && nc > 0) ? load_cols(bias + col, nc, p.vec_bias) : zero;
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                    const int r = 8 * it + rsub;
+                    const long long row = r0 + r;
+                    if (bias) x[it] = add4(x[it], b4);
+                    if (r < valid && nc > 0) {
+                        if (res) x[it] = add4(x[it], load_cols(res + row * p.ldr + col, nc, p.vec_res));
+                        if (d) {
+                            float* dp = d + row * p.ldd + col;
+                            if (p.accumulate) x[it] = add4(x[it], load_cols(dp, nc, p.vec_d));
+                            store_cols(dp, x[it], nc, p.vec_d);
+                        }
+                        if (plane_on) {
                             if (nc == 4 && p.vec_plane) {
-                                pw.store4(w.z, row, col, x);
+                                pw.store4(w.z, row, col, x[it]);
                             } else {
-                                if (nc > 0) pw.store(w.z, row, col, x.x);
-                                if (nc > 1) pw.store(w.z, row, col + 1, x.y);
-                                if (nc > 2) pw.store(w.z, row, col + 2, x.z);
-                                if (nc > 3) pw.store(w.z, row, col + 3, x.w);
+                                if (nc > 0) pw.store(w.z, row, col, x[it].x);
+                                if (nc > 1) pw.store(w.z, row, col + 1, x[it].y);
+                                if (nc > 2) pw.store(w.z, row, col + 2, x[it].z);
+                                if (nc > 3) pw.store(w.z, row, col + 3, x[it].w);
                             }
                         }
                     }
-                    xs[it] = r < valid ? x : zero;
+                    if (r >= valid) x[it] = zero;
                 }
-                if (p.stat_mean) {
-                    float4 sum = zero;
+            }
+            if (p.stat_mean && valid > 0) {
+                // rows >= valid hold zeros here (interior chunks have none)
+                float4 sum = add4(add4(x[0], x[1]), add4(x[2], x[3]));
+                sum = xor_sum4(xor_sum4(xor_sum4(sum, 4), 8), 16);
+                const float fv = static_cast<float>(valid);
+                const float4 mean = make_float4(sum.x / fv, sum.y / fv, sum.z / fv, sum.w / fv);
+                float4 m2 = zero;
 #pragma unroll
-                    for (int it = 0; it < 8; ++it) sum = add4(sum, xs[it]);
-                    sum = xor_sum4(xor_sum4(sum, 8), 16);
-                    const float fv = static_cast<float>(valid);
-                    const float4 mean = make_float4(sum.x / fv, sum.y / fv, sum.z / fv, sum.w / fv);
-                    float4 m2 = zero;
-#pragma unroll
-                    for (int it = 0; it < 8; ++it) {
-                        if (4 * it + rsub < valid) {
-                            const float4 dv = make_float4(xs[it].x - mean.x, xs[it].y - mean.y, xs[it].z - mean.z,
-                                                          xs[it].w - mean.w);
-                            m2 = make_float4(m2.x + dv.x * dv.x, m2.y + dv.y * dv.y, m2.z + dv.z * dv.z,
-                                             m2.w + dv.w * dv.w);
-                        }
+                for (int it = 0; it < 4; ++it) {
+                    if (8 * it + rsub < valid) {
+                        const float4 dv = make_float4(x[it].x - mean.x, x[it].y - mean.y, x[it].z - mean.z,
+                                                      x[it].w - mean.w);
+                        m2 = make_float4(m2.x + dv.x * dv.x, m2.y + dv.y * dv.y, m2.z + dv.z * dv.z, m2.w + dv.w * dv.w);
                     }
-                    m2 = xor_sum4(xor_sum4(m2, 8), 16);
-                    if (rsub == 0 && nc > 0) {
-                        const long long idx = static_cast<long long>(w.z) * p.stat_bstride + group * p.N + col;
-                        store_cols(p.stat_mean + idx, mean, nc, p.vec_stat);
-                        store_cols(p.stat_m2 + idx, m2, nc, p.vec_stat);
-                    }
+                }
+                m2 = xor_sum4(xor_sum4(xor_sum4(m2, 4), 8), 16);
+                const int nc = max(0, min(4, p.N - col));
+                if (rsub == 0 && nc > 0) {
+                    const long long idx = static_cast<long long>(w.z) * p.stat_bstride + group * p.N + col;
+                    store_cols(p.stat_mean + idx, mean, nc, p.vec_stat);
+                    store_cols(p.stat_m2 + idx, m2, nc, p.vec_stat);
                 }
             }
             __syncwarp();
@@ -404,7 +445,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
 }
 
 // Persistent kernel: one CTA per SM walks the output tiles blockIdx.x, +gridDim.x, ...
-// Shared memory: [stage ring][epilogue staging 4 x 32 x 36 floats][barriers].
+// Shared memory: [stage ring][epilogue staging kEpiWarps x 32 x 16 floats][barriers].
 template <int KIND, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -416,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* staging = reinterpret_cast<float*>(smem + stages * stage_bytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + 4 * 32 * kStagePitch);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * 32 * kStagePitch);
     uint64_t* empty = full + stages;
     uint64_t* acc_full = empty + stages;
     uint64_t* acc_empty = acc_full + 2;
@@ -434,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(&acc_full[b], 1);
-            ptx::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+            ptx::mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
         }
         ptx::mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -689,7 +730,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     const int planes = g->kind == 0 ? 1 : 2;
     const int stage_bytes = (kBM * 128 + bn * 128) * planes;
     // ring + epilogue staging + barriers (2 x stages + 5 words, TMEM slot, abort word) + alignment slack
-    const int staging = 4 * 32 * kStagePitch * 4;
+    const int staging = kEpiWarps * 32 * kStagePitch * 4;
     const int overhead = 1024 + staging + 256;
     plan->stages = std::min(8, (kMaxSmem - overhead) / stage_bytes);
     if (plan->stages < 2) {
