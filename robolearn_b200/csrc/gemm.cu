@@ -291,21 +291,33 @@ __device__ __forceinline__ float4 xor_sum4(float4 v, int mask) {
     return v;
 }
 
-// Epilogue warps 2 .. 2 + kEpiWarps - 1, two per TMEM lane quarter: warp w may only read
-// TMEM lanes (tile rows) 32*(w % 4) .. +31, and the two warps of a quarter take
-// alternate 16-column chunks. A 32 x 16 accumulator slice is read with lane = row,
-// staged in shared memory and walked 8 rows x 16 columns per step (lane = 4
+// Epilogue warps 2 .. 2 + kEpiWarps - 1, kEpiWarps / 4 per TMEM lane quarter: warp w may
+// only read TMEM lanes (tile rows) 32*(w % 4) .. +31, and the warps of a quarter take
+// every (kEpiWarps / 4)-th 16-column chunk. A 32 x 16 accumulator slice is read with
+// lane = row, staged in shared memory and walked 8 rows x 16 columns per step (lane = 4
 // consecutive columns of one row), so every global access covers whole row segments.
 // Interior chunks (32 valid rows, 16 valid columns, vector-aligned operands) take a
-// branch-free path whose loads are all issued before the stores; edge chunks take a
-// guarded path. After its last TMEM read of a tile each warp releases the accumulator
-// buffer to the MMA issuer.
+// branch-free path; edge chunks take a guarded path. The bias of all of a warp's chunks
+// is fetched once per tile before the accumulator wait, and a chunk's residual / old
+// output rows are fetched before its TMEM read. After its last TMEM read of a tile each
+// warp releases the accumulator buffer to the MMA issuer.
+constexpr int kEpiSlots = kEpiWarps / 4;        // warps per TMEM lane quarter
+constexpr int kMaxChunks = 256 / (16 * kEpiSlots);  // chunks per warp and tile (BN <= 256)
+
+__device__ __forceinline__ float4 pick4(const float4 (&v)[kMaxChunks], int k) {
+    float4 r = v[0];
+#pragma unroll
+    for (int j = 1; j < kMaxChunks; ++j)
+        if (k == j) r = v[j];
+    return r;
+}
+
 __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
                                       float* staging, volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int slot = (warp - 2) >> 2;
     float* sq = staging + (warp - 2) * (32 * kStagePitch);
     const int cg = lane & 3;
     const int rsub = lane >> 2;
@@ -320,19 +332,40 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
         const Tile w = decode(p, t);
         const int buf = i & 1;
-        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
-        ptx::tc_fence_after();
         const int r0 = w.m_tile * kBM + q * 32;
         const int valid = min(max(p.M - r0, 0), 32);
+        const float inv_valid = 1.0f / static_cast<float>(max(valid, 1));  // exact for full 32-row groups
         float* d = p.d ? p.d + static_cast<long long>(w.z) * p.d_bstride + static_cast<long long>(w.split) * p.d_split_stride
                        : nullptr;
         const float* bias = p.bias ? p.bias + static_cast<long long>(w.z) * p.bias_bstride : nullptr;
         const float* res = p.residual ? p.residual + static_cast<long long>(w.z) * p.r_bstride : nullptr;
         const long long group = static_cast<long long>(w.m_tile * kBM) / 32 + q;
+        float4 bias_k[kMaxChunks];
+#pragma unroll
+        for (int k = 0; k < kMaxChunks; ++k) {
+            const int c0 = 16 * slot + 16 * kEpiSlots * k;
+            const int col = w.n_tile * BN + c0 + 4 * cg;
+            const int nc = c0 < BN ? max(0, min(4, p.N - col)) : 0;
+            bias_k[k] = (bias && nc > 0) ? load_cols(bias + col, nc, p.vec_bias) : zero;
+        }
+        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
+        ptx::tc_fence_after();
         const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
-        for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+        for (int k = 0; k < kMaxChunks; ++k) {
+            const int c0 = 16 * slot + 16 * kEpiSlots * k;
             const int col0 = w.n_tile * BN + c0;
-            if (col0 >= p.N) break;  // warp-uniform
+            if (c0 >= BN || col0 >= p.N) break;  // warp-uniform
+            const int col = col0 + 4 * cg;
+            // interior chunks add at most one of residual / old output (both: guarded path)
+            const float* add_src = res ? res : ((d && p.accumulate) ? d : nullptr);
+            const long long add_ld = res ? p.ldr : p.ldd;
+            const bool fast = fast_ok && valid == 32 && col0 + 16 <= p.N && !(res && d && p.accumulate);
+            float4 rv[4];
+            if (fast && add_src) {
+#pragma unroll
+                for (int it = 0; it < 4; ++it)
+                    rv[it] = *reinterpret_cast<const float4*>(add_src + static_cast<long long>(r0 + 8 * it + rsub) * add_ld + col);
+            }
             {
                 float v[16];
                 ptx::tmem_ld16(t_base + static_cast<uint32_t>(c0), v);
@@ -342,41 +375,24 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                     mine[j ^ ((lane >> 1) & 3)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
             __syncwarp();
-            const int col = col0 + 4 * cg;
             float4 x[4];
 #pragma unroll
             for (int it = 0; it < 4; ++it) {
                 const float4 a = *reinterpret_cast<const float4*>(sq + (8 * it + rsub) * kStagePitch + 4 * (cg ^ ((rsub >> 1) & 3)));
                 x[it] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
             }
-            if (fast_ok && valid == 32 && col0 + 16 <= p.N) {
+            const float4 b4 = pick4(bias_k, k);
+            if (fast) {
                 // ---- interior chunk: no per-row or per-lane guards ----
-                if (bias) {
-                    const float4 b4 = *reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
-                    for (int it = 0; it < 4; ++it) x[it] = add4(x[it], b4);
-                }
-                if (res) {
-                    float4 rv[4];
-#pragma unroll
-                    for (int it = 0; it < 4; ++it)
-                        rv[it] = *reinterpret_cast<const float4*>(res + static_cast<long long>(r0 + 8 * it + rsub) * p.ldr + col);
-#pragma unroll
-                    for (int it = 0; it < 4; ++it) x[it] = add4(x[it], rv[it]);
+                for (int it = 0; it < 4; ++it) {
+                    if (bias) x[it] = add4(x[it], b4);
+                    if (add_src) x[it] = add4(x[it], rv[it]);
                 }
                 if (d) {
-                    float* dcol = d + col;
-                    if (p.accumulate) {
-                        float4 ov[4];
-#pragma unroll
-                        for (int it = 0; it < 4; ++it)
-                            ov[it] = *reinterpret_cast<const float4*>(dcol + static_cast<long long>(r0 + 8 * it + rsub) * p.ldd);
-#pragma unroll
-                        for (int it = 0; it < 4; ++it) x[it] = add4(x[it], ov[it]);
-                    }
 #pragma unroll
                     for (int it = 0; it < 4; ++it)
-                        *reinterpret_cast<float4*>(dcol + static_cast<long long>(r0 + 8 * it + rsub) * p.ldd) = x[it];
+                        *reinterpret_cast<float4*>(d + static_cast<long long>(r0 + 8 * it + rsub) * p.ldd + col) = x[it];
                 }
                 if (plane_on) {
 #pragma unroll
@@ -385,7 +401,6 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
             } else {
                 // ---- edge chunk: guarded per row and per column ----
                 const int nc = max(0, min(4, p.N - col));
-                const float4 b4 = (bias && nc > 0) ? load_cols(bias + col, nc, p.vec_bias) : zero;
 #pragma unroll
                 for (int it = 0; it < 4; ++it) {
                     const int r = 8 * it + rsub;
@@ -416,8 +431,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                 // rows >= valid hold zeros here (interior chunks have none)
                 float4 sum = add4(add4(x[0], x[1]), add4(x[2], x[3]));
                 sum = xor_sum4(xor_sum4(xor_sum4(sum, 4), 8), 16);
-                const float fv = static_cast<float>(valid);
-                const float4 mean = make_float4(sum.x / fv, sum.y / fv, sum.z / fv, sum.w / fv);
+                const float4 mean = make_float4(sum.x * inv_valid, sum.y * inv_valid, sum.z * inv_valid, sum.w * inv_valid);
                 float4 m2 = zero;
 #pragma unroll
                 for (int it = 0; it < 4; ++it) {

@@ -65,16 +65,20 @@ struct PlaneWriter {
             p.lo[o] = v - h;
         }
     }
-    // four consecutive columns (col % 4 == 0, row stride % 4 == 0, 16-byte aligned base)
+    // four consecutive columns (col % 4 == 0, row and twin strides % 4 == 0; base 8-byte
+    // aligned for fp16, 16-byte aligned for hi/lo)
     __device__ __forceinline__ void store4(int t, long long row, int col, float4 v) {
         const long long o = static_cast<long long>(t) * p.tstride + row * p.ld + col;
         if (p.h16) {
             const float4 s = make_float4(v.x * scale, v.y * scale, v.z * scale, v.w * scale);
             overflow |= !(fabsf(s.x) <= 65504.0f && fabsf(s.y) <= 65504.0f && fabsf(s.z) <= 65504.0f &&
                           fabsf(s.w) <= 65504.0f);
-            __half2* dst = reinterpret_cast<__half2*>(p.h16 + o);
-            dst[0] = __floats2half2_rn(s.x, s.y);
-            dst[1] = __floats2half2_rn(s.z, s.w);
+            const __half2 lo2 = __floats2half2_rn(s.x, s.y);
+            const __half2 hi2 = __floats2half2_rn(s.z, s.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<const uint32_t*>(&lo2);
+            packed.y = *reinterpret_cast<const uint32_t*>(&hi2);
+            *reinterpret_cast<uint2*>(p.h16 + o) = packed;
         } else if (p.hi) {
             const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
             *reinterpret_cast<float4*>(p.hi + o) = h;
