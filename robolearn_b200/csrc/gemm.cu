@@ -22,8 +22,9 @@
 // buffered (2 x BN columns) so that the epilogue of tile i overlaps the main loop of
 // tile i + 1 and the producer runs ahead across tile boundaries. Warp roles: warp 0 =
 // TMA producer, warp 1 = TMEM allocation + MMA issue (one elected thread), warps 2..9
-// = epilogue (two per TMEM lane quarter). Every mbarrier wait is bounded by wall-clock time, reports through the
-// caller's health word and stops the other roles through a shared abort word.
+// = epilogue (two per TMEM lane quarter). Every mbarrier wait is bounded by
+// wall-clock time, reports through the caller's health word and stops the other
+// roles through a shared abort word.
 //
 // The epilogue stages each 32 x 16 accumulator slice in shared memory and walks it
 // 8 rows x 16 columns per warp step, so every global access of a warp covers whole
