@@ -68,6 +68,12 @@ typedef struct rl2_plane {
  *         (no bias / residual / accumulate / stats), reduced by rl2_split_reduce.
  * out_plane (optional): operand plane copy of the final output (twin_stride per batch).
  * d may be null when out_plane is set (plane-only output).
+ * activation (1 = ELU, 2 = tanh; 0 = none), applied last (after bias / residual /
+ *         accumulate), before stats and outputs:
+ *         act_aux == null: out = f(x)                        (layer forward)
+ *         act_aux != null: out = x * f'(y), y = act_aux[z][m][n], the stored
+ *                          f outputs (ELU: y > 0 ? 1 : y + 1; tanh: 1 - y^2)
+ *         (activation layers of the PPO MLP, warp/ppo.py:313-350).
  * ------------------------------------------------------------------------- */
 typedef struct rl2_gemm_desc {
     int kind;
@@ -96,6 +102,9 @@ typedef struct rl2_gemm_desc {
     int tile_n;
     int* health;
     rl2_plane out_plane;
+    int activation;
+    const float* act_aux;
+    long long ld_aux, aux_batch_stride;
 } rl2_gemm_desc;
 
 void* rl2_gemm_create(const rl2_gemm_desc* desc);

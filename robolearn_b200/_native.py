@@ -46,6 +46,7 @@ class GemmDesc(ctypes.Structure):
         ("stat_mean", P), ("stat_m2", P), ("stat_batch_stride", LL),
         ("scale", P), ("k_splits", I), ("d_split_stride", LL), ("tile_n", I), ("health", P),
         ("out_plane", Plane),
+        ("activation", I), ("act_aux", P), ("ld_aux", LL), ("aux_batch_stride", LL),
     ]
 
 

@@ -66,7 +66,19 @@ struct Params {
     int tiles_n, tiles_m, tiles_total;  // persistent work list (n fastest)
     uint32_t buf_cols;                  // TMEM columns per accumulator buffer (power of two >= 32, >= BN)
     bool vec_d, vec_res, vec_bias, vec_plane, vec_stat;  // 16-byte (plane: 8-byte) column-group access allowed
+    int activation;  // 0 none, 1 ELU, 2 tanh
+    const float* aux;  // stored activation outputs: multiply by the derivative instead of applying f
+    long long ld_aux, aux_bstride;
+    bool vec_aux;
 };
+
+// Epilogue activations. ELU (alpha 1) and tanh; derivatives from the stored outputs y.
+__device__ __forceinline__ float act_fwd(int a, float x) { return a == 1 ? (x > 0.f ? x : expf(x) - 1.0f) : tanhf(x); }
+__device__ __forceinline__ float act_grad(int a, float y) { return a == 1 ? (y > 0.f ? 1.0f : y + 1.0f) : 1.0f - y * y; }
+__device__ __forceinline__ float4 act4(int a, const float* aux_row, float4 x, float4 y) {
+    if (aux_row) return make_float4(x.x * act_grad(a, y.x), x.y * act_grad(a, y.y), x.z * act_grad(a, y.z), x.w * act_grad(a, y.w));
+    return make_float4(act_fwd(a, x.x), act_fwd(a, x.y), act_fwd(a, x.z), act_fwd(a, x.w));
+}
 
 // Shared-memory matrix descriptor. layout 2 = 128-byte swizzle (16-byte granules,
 // 8-row atoms); layout 1 = 128-byte swizzle with 32-byte granules (4-row atoms),
@@ -327,7 +339,8 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     PlaneWriter pw(p.out_plane);
     const bool plane_on = pw.active();
     const bool fast_ok = (!p.d || p.vec_d) && (!p.residual || p.vec_res) && (!p.bias || p.vec_bias) &&
-                         (!plane_on || p.vec_plane) && (!p.stat_mean || p.vec_stat);
+                         (!plane_on || p.vec_plane) && (!p.stat_mean || p.vec_stat) && (!p.aux || p.vec_aux);
+    const int actv = p.activation;
     const int BN = p.BN;
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
@@ -340,6 +353,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                        : nullptr;
         const float* bias = p.bias ? p.bias + static_cast<long long>(w.z) * p.bias_bstride : nullptr;
         const float* res = p.residual ? p.residual + static_cast<long long>(w.z) * p.r_bstride : nullptr;
+        const float* aux = p.aux ? p.aux + static_cast<long long>(w.z) * p.aux_bstride : nullptr;
         const long long group = static_cast<long long>(w.m_tile * kBM) / 32 + q;
         float4 bias_k[kMaxChunks];
 #pragma unroll
@@ -361,11 +375,16 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
             const float* add_src = res ? res : ((d && p.accumulate) ? d : nullptr);
             const long long add_ld = res ? p.ldr : p.ldd;
             const bool fast = fast_ok && valid == 32 && col0 + 16 <= p.N && !(res && d && p.accumulate);
-            float4 rv[4];
+            float4 rv[4], av[4];
             if (fast && add_src) {
 #pragma unroll
                 for (int it = 0; it < 4; ++it)
                     rv[it] = *reinterpret_cast<const float4*>(add_src + static_cast<long long>(r0 + 8 * it + rsub) * add_ld + col);
+            }
+            if (fast && aux) {
+#pragma unroll
+                for (int it = 0; it < 4; ++it)
+                    av[it] = *reinterpret_cast<const float4*>(aux + static_cast<long long>(r0 + 8 * it + rsub) * p.ld_aux + col);
             }
             {
                 float v[16];
@@ -389,6 +408,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                 for (int it = 0; it < 4; ++it) {
                     if (bias) x[it] = add4(x[it], b4);
                     if (add_src) x[it] = add4(x[it], rv[it]);
+                    if (actv) x[it] = act4(actv, aux, x[it], aux ? av[it] : x[it]);
                 }
                 if (d) {
 #pragma unroll
@@ -409,11 +429,13 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                     if (bias) x[it] = add4(x[it], b4);
                     if (r < valid && nc > 0) {
                         if (res) x[it] = add4(x[it], load_cols(res + row * p.ldr + col, nc, p.vec_res));
-                        if (d) {
-                            float* dp = d + row * p.ldd + col;
-                            if (p.accumulate) x[it] = add4(x[it], load_cols(dp, nc, p.vec_d));
-                            store_cols(dp, x[it], nc, p.vec_d);
+                        float* dp = d ? d + row * p.ldd + col : nullptr;
+                        if (dp && p.accumulate) x[it] = add4(x[it], load_cols(dp, nc, p.vec_d));
+                        if (actv) {
+                            const float* arow = aux ? aux + row * p.ld_aux + col : nullptr;
+                            x[it] = act4(actv, arow, x[it], arow ? load_cols(arow, nc, p.vec_aux) : x[it]);
                         }
+                        if (dp) store_cols(dp, x[it], nc, p.vec_d);
                         if (plane_on) {
                             if (nc == 4 && p.vec_plane) {
                                 pw.store4(w.z, row, col, x[it]);
@@ -662,8 +684,9 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         return nullptr;
     }
     const int splits = g->k_splits < 1 ? 1 : g->k_splits;
-    if (splits > 1 && (g->bias || g->residual || g->accumulate || g->stat_mean || g->d_split_stride <= 0)) {
-        set_error("split-K GEMMs write plain partials: no bias/residual/accumulate/stats, positive split stride");
+    if (splits > 1 && (g->bias || g->residual || g->accumulate || g->stat_mean || g->activation ||
+                       g->d_split_stride <= 0)) {
+        set_error("split-K GEMMs write plain partials: no bias/residual/accumulate/stats/activation, positive split stride");
         return nullptr;
     }
     if ((g->stat_mean == nullptr) != (g->stat_m2 == nullptr)) {
@@ -771,6 +794,16 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.vec_res = g->residual && a16(g->residual) && g->ldr % 4 == 0 && g->residual_batch_stride % 4 == 0;
     p.vec_bias = g->bias && a16(g->bias) && g->bias_batch_stride % 4 == 0;
     p.vec_stat = g->stat_mean && a16(g->stat_mean) && a16(g->stat_m2) && g->n % 4 == 0 && g->stat_batch_stride % 4 == 0;
+    if (g->activation < 0 || g->activation > 2 || (g->act_aux && !g->activation)) {
+        set_error("GEMM activation must be 0 (none), 1 (ELU) or 2 (tanh); act_aux needs an activation");
+        delete plan;
+        return nullptr;
+    }
+    p.activation = g->activation;
+    p.aux = g->act_aux;
+    p.ld_aux = g->ld_aux;
+    p.aux_bstride = g->aux_batch_stride;
+    p.vec_aux = g->act_aux && a16(g->act_aux) && g->ld_aux % 4 == 0 && g->aux_batch_stride % 4 == 0;
     p.vec_plane = plane_used(&g->out_plane) && g->out_plane.ld % 4 == 0 && g->out_plane.twin_stride % 4 == 0 &&
                   (g->out_plane.h16 ? aligned(g->out_plane.h16, 8)
                                     : a16(g->out_plane.hi) && a16(g->out_plane.lo));

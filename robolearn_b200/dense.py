@@ -16,6 +16,9 @@ from . import _native as N
 
 FP16 = 0
 TF32X3 = 1
+# epilogue activations (rl2_gemm_desc.activation)
+ELU = 1
+TANH = 2
 
 
 def operand_ld(cols: int, kind: int) -> int:
@@ -69,8 +72,12 @@ class DensePlan:
         tile_n: int = 0,
         health: torch.Tensor | None = None,
         out_plane=None,
+        activation: int = 0,
+        act_aux=None,
+        ld_aux: int = 0,
+        aux_batch_stride: int = 0,
     ):
-        self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health, out_plane]
+        self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health, out_plane, act_aux]
         A = N.addr
         desc = N.GemmDesc(
             kind=kind, m=m, n=n, k=k, batch=batch,
@@ -82,6 +89,7 @@ class DensePlan:
             stat_mean=A(stat_mean), stat_m2=A(stat_m2), stat_batch_stride=stat_batch_stride,
             scale=A(scale), k_splits=k_splits, d_split_stride=d_split_stride, tile_n=tile_n,
             health=A(health), out_plane=out_plane if out_plane is not None else N.Plane(),
+            activation=activation, act_aux=A(act_aux), ld_aux=ld_aux, aux_batch_stride=aux_batch_stride,
         )
         self._lib = N.load()
         self.handle = N.created(self._lib.rl2_gemm_create(ctypes.byref(desc)), "create tcgen05 GEMM plan")

@@ -180,3 +180,30 @@ def test_gemm_multi_wave_epilogue_moments_and_plane(kind, tile_n):
     assert torch.allclose(mean.double(), mu, atol=1e-4, rtol=1e-4)
     assert torch.allclose(m2.double(), (dev**2).sum(2), atol=1e-3, rtol=1e-4)
     del keep
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("activation", [dense.ELU, dense.TANH])
+@pytest.mark.parametrize("m,n", [(300, 200), (4096, 512)])
+def test_gemm_activation_forward_and_derivative(kind, activation, m, n):
+    """out = f(A B^T + bias) and, with act_aux = y, out = (A B^T + bias) * f'(y)."""
+    k, batch = 96, 2
+    bias = torch.randn(batch, n, device="cuda")
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, bias=bias, bias_batch_stride=n, activation=activation)
+    plan.run()
+    torch.cuda.synchronize()
+    pre = ref + bias.double()[:, None, :]
+    f = (lambda x: torch.where(x > 0, x, torch.expm1(x))) if activation == dense.ELU else torch.tanh
+    expect = f(pre)
+    tol = 2e-3 if kind == 0 else 2e-5
+    assert (D[:, :, :n].double() - expect).abs().max().item() < tol * max(expect.abs().max().item(), 1.0)
+    # derivative mode: y = stored outputs (any values in f's range), out = x * f'(y)
+    y = f(torch.randn(batch, m, n, device="cuda"))
+    plan2, D2, ref2 = _run(kind, m, n, k, 0, 0, batch=batch, bias=bias, bias_batch_stride=n, activation=activation,
+                           act_aux=y, ld_aux=n, aux_batch_stride=m * n)
+    plan2.run()
+    torch.cuda.synchronize()
+    yd = y.double()
+    grad = torch.where(yd > 0, torch.ones_like(yd), yd + 1) if activation == dense.ELU else 1 - yd * yd
+    expect2 = (ref2 + bias.double()[:, None, :]) * grad
+    assert (D2[:, :, :n].double() - expect2).abs().max().item() < tol * max(expect2.abs().max().item(), 1.0)
