@@ -63,7 +63,8 @@ typedef struct rl2_plane {
  *         (a_lo, b_lo), three tensor-core products per step.
  * Batch strides are in elements; 0 shares the operand across the batch.
  * stat_mean / stat_m2 (optional): per-column moments of each 32-row group of
- *         the output, laid out [batch][ceil(m/32)][n] with stat_batch_stride.
+ *         the output, laid out [batch][ceil(m/32)][n] with stat_batch_stride;
+ *         stat_m2 == null: stat_mean receives per-group column SUMS instead.
  * k_splits > 1 writes independent partial products to d + s * d_split_stride
  *         (no bias / residual / accumulate / stats), reduced by rl2_split_reduce.
  * out_plane (optional): operand plane copy of the final output (twin_stride per batch).
@@ -545,6 +546,175 @@ int rl2_reward_stats_update(const float* reward, const float* terminated, const 
 /* Host-side Philox4x32-10 block (for checking device streams against the published algorithm). */
 void rl2_philox4x32(unsigned int c0, unsigned int c1, unsigned int c2, unsigned int c3, unsigned int k0,
                     unsigned int k1, unsigned int* out4);
+
+/* ---------------------------------------------------------------------------
+ * PPO learner update (replaces the Warp kernels of src/robolearn/warp/ppo.py).
+ * Rollout index k = t * num_envs + i; flags are int32 (0 / nonzero).
+ * ------------------------------------------------------------------------- */
+
+/* GAE (_gae, ppo.py:101-133) as a warp-shuffle reverse scan: each environment's
+ * horizon is split into up to 32 segments held by neighbouring lanes; every lane
+ * composes its segment's affine map A -> delta + g A, the maps are combined by a
+ * reverse shuffle scan, and each lane re-runs its segment from the exact carry-in. */
+typedef struct rl2_ppo_gae_args {
+    const float* rewards;
+    const float* values;
+    const float* next_values;
+    const int* terminated;
+    const int* truncated;
+    int horizon, num_envs;
+    float gamma, gae_lambda;
+    int current_timeout_bootstrap; /* timeout_bootstrap == "current": V' = V(s_t) on truncation */
+    float* advantages;
+    float* returns;
+} rl2_ppo_gae_args;
+
+int rl2_ppo_gae(const rl2_ppo_gae_args* args, void* stream);
+
+/* Advantage normalisation (_advantage_sum / _advantage_variance / _normalize,
+ * ppo.py:136-159): two-pass mean and centred variance accumulated in double in a
+ * fixed order; population (eps inside the sqrt) or sample (n - 1, eps outside).
+ * stats: 2 doubles of workspace [sum, centred sum of squares]; counter: one int that
+ * must start at zero (left at zero). */
+int rl2_ppo_normalize_advantages(float* advantages, int n, int sample_std, double* stats, double* partials,
+                                 int* counter, void* stream);
+/* doubles of partials needed for n elements */
+int rl2_ppo_partials(int n);
+
+/* Minibatch permutation (replaces _shuffle_keys + radix_sort_pairs, ppo.py:162-169,
+ * 603): indices[i] = pi(i) for a keyed Feistel bijection of [0, n) (cycle walking on
+ * the enclosing power-of-four domain), keys from Philox4x32-10(seed, *epoch). */
+int rl2_ppo_permutation(unsigned long long seed, const unsigned long long* epoch, int n, int* indices,
+                        int* health, void* stream);
+
+/* Minibatch gather (_gather_batch, ppo.py:172-204): row r of the batch is rollout row
+ * indices[offset + r]; observations go straight into the first layer's operand plane.
+ * Each batch_* output is optional (null: not copied). */
+typedef struct rl2_ppo_gather_args {
+    const int* indices; /* null: identity */
+    int offset, rows, obs_dim, act_dim;
+    const float* observations;
+    const float* actions;
+    const float* means;
+    const float* stds;
+    const float* log_probs;
+    const float* values;
+    const float* advantages;
+    const float* returns;
+    rl2_plane obs_plane;
+    float* batch_actions;
+    float* batch_means;
+    float* batch_stds;
+    float* batch_log_probs;
+    float* batch_values;
+    float* batch_advantages;
+    float* batch_returns;
+} rl2_ppo_gather_args;
+
+int rl2_ppo_gather(const rl2_ppo_gather_args* args, void* stream);
+
+/* Fused clipped-surrogate / value / entropy loss and its gradient (_make_ppo_loss,
+ * ppo.py:255-310, with Warp's adjoint rules for min / max / clamp). head[0] holds the
+ * actor means (columns 0..act-1), head[1] the critic value in column 0 (twin stride
+ * head_twin_stride). Writes loss (1 float), metrics [policy, value, entropy] (means),
+ * d_head (fp32 and/or operand plane; other columns of the critic twin zero), the
+ * head bias gradients d_bias_actor [act] and d_bias_critic [1], and d_std_param [act].
+ * std_type 0 = log std, 1 = scalar std clamped to [std_min, std_max]. Deterministic:
+ * per-block partials reduced in a fixed order by the last block. */
+typedef struct rl2_ppo_loss_args {
+    const float* head;
+    long long ld_head, head_twin_stride;
+    const float* std_param;
+    int rows, act;
+    const float* actions;
+    const float* old_log_probs;
+    const float* old_values;
+    const float* advantages;
+    const float* returns;
+    float clip_ratio, value_coefficient, entropy_coefficient, value_loss_scale;
+    int clip_value, std_type;
+    float std_min, std_max;
+    float* loss;
+    float* metrics;
+    float* d_head;
+    long long ld_d_head, d_head_twin_stride;
+    rl2_plane d_plane;
+    float* d_bias_actor;
+    float* d_bias_critic;
+    float* d_std_param;
+    double* partials; /* rl2_ppo_loss_partials(rows, act) doubles */
+    int* counter;    /* one int, zero on entry, left at zero */
+} rl2_ppo_loss_args;
+
+int rl2_ppo_loss(const rl2_ppo_loss_args* args, void* stream);
+int rl2_ppo_loss_partials(int rows, int act);
+
+/* KL(old || new) mean and adaptive learning rate (_make_kl_kernel / _adapt_learning_rate,
+ * ppo.py:207-238): lr /= 1.5 (>= 1e-5) when kl > 2 desired_kl, lr *= 1.5 (<= 1e-2) when
+ * 0 < kl < desired_kl / 2. partials: rl2_ppo_partials(rows) doubles. */
+int rl2_ppo_kl(const float* mean, long long ld_mean, const float* std_param, const float* old_means,
+               const float* old_stds, int rows, int act, int std_type, float std_min, float std_max,
+               float desired_kl, float* kl, float* learning_rate, double* partials, int* counter, void* stream);
+
+/* Gradient-norm clipping over the flat gradient arena laid out [actor | critic | std]
+ * (ppo.py:241-252 and the optimizer's max_norm): separate = 0 clips all gradients by
+ * one total norm, 1 clips (actor + std) and critic separately; coefficient =
+ * min(1, max_norm / (sqrt(sum g^2) + 1e-6)). norms_out (5 floats) receives the sums of
+ * squares [actor + std, critic, total] and the applied coefficients [actor + std, critic].
+ * partials: 3 * rl2_ppo_partials(n) doubles. */
+int rl2_ppo_clip_gradients(float* grads, long long actor_count, long long critic_count, long long std_count,
+                           int separate, float max_norm, float* norms_out, double* partials, int* counter,
+                           void* stream);
+
+/* Rollout-side kernels (_sample / _store, ppo.py:26-98). head[0] = actor means,
+ * head[1] column 0 = critic values (twin stride head_twin_stride). noise: standard
+ * normal [rows][act] or null (deterministic). sampled_std receives the action std. */
+typedef struct rl2_ppo_sample_args {
+    const float* head;
+    long long ld_head, head_twin_stride;
+    const float* std_param;
+    int std_type;
+    float std_min, std_max;
+    const float* noise;
+    int rows, act;
+    float* actions;
+    float* log_probs;
+    float* values;
+    float* sampled_std;
+} rl2_ppo_sample_args;
+
+int rl2_ppo_sample(const rl2_ppo_sample_args* args, void* stream);
+
+/* Store rollout step `step` (rows k = step * num_envs + i): observations, the last sampled
+ * actions / log probs / values / means / std, rewards, flags and the next-state values
+ * (critic column of next_head). */
+typedef struct rl2_ppo_store_args {
+    int step, num_envs, obs_dim, act;
+    const float* observations;
+    const float* actions;
+    const float* log_probs;
+    const float* values;
+    const float* rewards;
+    const int* terminated;
+    const int* truncated;
+    const float* mean;
+    long long ld_mean;
+    const float* next_values;
+    long long next_values_stride;
+    const float* sampled_std;
+    float* r_observations;
+    float* r_actions;
+    float* r_log_probs;
+    float* r_values;
+    float* r_rewards;
+    int* r_terminated;
+    int* r_truncated;
+    float* r_next_values;
+    float* r_means;
+    float* r_stds;
+} rl2_ppo_store_args;
+
+int rl2_ppo_store(const rl2_ppo_store_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -17,7 +17,8 @@ Follows ``src/robolearn/warp/ppo.py`` of the reference:
                                Warp's adjoint rules: min -> first argument only if
                                strictly smaller, max -> first argument only if strictly
                                larger, clamp -> passes at and inside the bounds;
-  * ``kl_mean`` / ``adapt_learning_rate`` -> ppo.py:207-238;
+  * ``kl_mean`` / ``adapt_learning_rate`` -> ppo.py:207-238 (the KL in float32, as its
+                               comparisons with zero and the thresholds depend on it);
   * ``clip_coefficient``    -> ``_clip_gradients`` (ppo.py:248-252): min(1, max_norm /
                                (sqrt(sum g^2) + 1e-6)). The combined-norm clip of
                                Warp-NN's Adam (``max_norm``) is not vendored; the same
@@ -234,13 +235,21 @@ def ppo_loss(mean, value, std_param, actions, old_log_probs, old_values, advanta
 
 
 def kl_mean(mean, std_param, old_mean, old_std, h: PPOHyper) -> float:
-    mean = np.asarray(mean, np.float64)
-    p = np.asarray(std_param, np.float64)
-    std = np.clip(p, *h.std_range) if h.std_type == "scalar" else np.exp(p)
-    vr = np.asarray(old_std, np.float64) / std
-    md = (np.asarray(old_mean, np.float64) - mean) / std
-    per_row = (0.5 * (vr * vr + md * md - 1.0) - np.log(vr)).sum(1)
-    return float(per_row.mean())
+    """KL(old || new) per row in float32 with the kernel's operation order (ppo.py:207-230),
+    mean over rows. The adaptive schedule compares this value with zero and with
+    thresholds, so the float32 rounding of the reference decides: for a policy that has
+    not moved, 1 + md^2 rounds to 1 and every row contributes exactly zero."""
+    f = np.float32
+    mean = np.asarray(mean, f)
+    p = np.asarray(std_param, f)
+    sd = np.clip(p, f(h.std_range[0]), f(h.std_range[1])) if h.std_type == "scalar" else np.exp(p)
+    vr = np.asarray(old_std, f) / sd
+    md = (np.asarray(old_mean, f) - mean) / sd
+    acc = np.zeros(mean.shape[0], f)
+    for j in range(mean.shape[1]):
+        acc = acc + f(0.5) * (vr[:, j] * vr[:, j] + md[:, j] * md[:, j] - f(1.0))
+        acc = acc - np.log(vr[:, j])
+    return float(acc.astype(np.float64).sum() / mean.shape[0])
 
 
 def adapt_learning_rate(kl: float, desired_kl: float, lr: float) -> float:

@@ -264,3 +264,80 @@ SIGNATURES.update({
 })
 
 SIGNATURES["rl2_critic_objective_noalloc"] = ([ctypes.POINTER(CriticObjectiveArgs), P], I)
+
+
+class PPOGaeArgs(ctypes.Structure):
+    """``rl2_ppo_gae_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("rewards", P), ("values", P), ("next_values", P), ("terminated", P), ("truncated", P),
+        ("horizon", I), ("num_envs", I), ("gamma", F), ("gae_lambda", F), ("current_timeout_bootstrap", I),
+        ("advantages", P), ("returns", P),
+    ]
+
+
+class PPOGatherArgs(ctypes.Structure):
+    """``rl2_ppo_gather_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("indices", P), ("offset", I), ("rows", I), ("obs_dim", I), ("act_dim", I),
+        ("observations", P), ("actions", P), ("means", P), ("stds", P), ("log_probs", P), ("values", P),
+        ("advantages", P), ("returns", P), ("obs_plane", Plane), ("batch_actions", P), ("batch_means", P),
+        ("batch_stds", P), ("batch_log_probs", P), ("batch_values", P), ("batch_advantages", P),
+        ("batch_returns", P),
+    ]
+
+
+class PPOLossArgs(ctypes.Structure):
+    """``rl2_ppo_loss_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("head", P), ("ld_head", LL), ("head_twin_stride", LL), ("std_param", P), ("rows", I), ("act", I),
+        ("actions", P), ("old_log_probs", P), ("old_values", P), ("advantages", P), ("returns", P),
+        ("clip_ratio", F), ("value_coefficient", F), ("entropy_coefficient", F), ("value_loss_scale", F),
+        ("clip_value", I), ("std_type", I), ("std_min", F), ("std_max", F),
+        ("loss", P), ("metrics", P), ("d_head", P), ("ld_d_head", LL), ("d_head_twin_stride", LL),
+        ("d_plane", Plane), ("d_bias_actor", P), ("d_bias_critic", P), ("d_std_param", P),
+        ("partials", P), ("counter", P),
+    ]
+
+
+SIGNATURES.update({
+    "rl2_ppo_gae": ([ctypes.POINTER(PPOGaeArgs), P], I),
+    "rl2_ppo_normalize_advantages": ([P, I, I, P, P, P, P], I),
+    "rl2_ppo_partials": ([I], I),
+    "rl2_ppo_permutation": ([ctypes.c_ulonglong, P, I, P, P, P], I),
+    "rl2_ppo_gather": ([ctypes.POINTER(PPOGatherArgs), P], I),
+    "rl2_ppo_loss": ([ctypes.POINTER(PPOLossArgs), P], I),
+    "rl2_ppo_loss_partials": ([I, I], I),
+    "rl2_ppo_kl": ([P, LL, P, P, P, I, I, I, F, F, F, P, P, P, P, P], I),
+    "rl2_ppo_clip_gradients": ([P, LL, LL, LL, I, F, P, P, P, P], I),
+})
+
+
+class PPOSampleArgs(ctypes.Structure):
+    """``rl2_ppo_sample_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("head", P), ("ld_head", LL), ("head_twin_stride", LL), ("std_param", P), ("std_type", I),
+        ("std_min", F), ("std_max", F), ("noise", P), ("rows", I), ("act", I), ("actions", P), ("log_probs", P),
+        ("values", P), ("sampled_std", P),
+    ]
+
+
+class PPOStoreArgs(ctypes.Structure):
+    """``rl2_ppo_store_args`` (include/rl2.h)."""
+
+    _fields_ = [
+        ("step", I), ("num_envs", I), ("obs_dim", I), ("act", I), ("observations", P), ("actions", P),
+        ("log_probs", P), ("values", P), ("rewards", P), ("terminated", P), ("truncated", P), ("mean", P),
+        ("ld_mean", LL), ("next_values", P), ("next_values_stride", LL), ("sampled_std", P),
+        ("r_observations", P), ("r_actions", P), ("r_log_probs", P), ("r_values", P), ("r_rewards", P),
+        ("r_terminated", P), ("r_truncated", P), ("r_next_values", P), ("r_means", P), ("r_stds", P),
+    ]
+
+
+SIGNATURES.update({
+    "rl2_ppo_sample": ([ctypes.POINTER(PPOSampleArgs), P], I),
+    "rl2_ppo_store": ([ctypes.POINTER(PPOStoreArgs), P], I),
+})

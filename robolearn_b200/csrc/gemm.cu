@@ -454,6 +454,14 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
                 // rows >= valid hold zeros here (interior chunks have none)
                 float4 sum = add4(add4(x[0], x[1]), add4(x[2], x[3]));
                 sum = xor_sum4(xor_sum4(xor_sum4(sum, 4), 8), 16);
+                if (!p.stat_m2) {  // sums mode: per-group column sums only
+                    const int nc = max(0, min(4, p.N - col));
+                    if (rsub == 0 && nc > 0)
+                        store_cols(p.stat_mean + static_cast<long long>(w.z) * p.stat_bstride + group * p.N + col, sum,
+                                   nc, p.vec_stat);
+                    __syncwarp();
+                    continue;
+                }
                 const float4 mean = make_float4(sum.x * inv_valid, sum.y * inv_valid, sum.z * inv_valid, sum.w * inv_valid);
                 float4 m2 = zero;
 #pragma unroll
@@ -689,8 +697,8 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         set_error("split-K GEMMs write plain partials: no bias/residual/accumulate/stats/activation, positive split stride");
         return nullptr;
     }
-    if ((g->stat_mean == nullptr) != (g->stat_m2 == nullptr)) {
-        set_error("GEMM column statistics need both stat_mean and stat_m2");
+    if (!g->stat_mean && g->stat_m2) {
+        set_error("GEMM column statistics: stat_m2 needs stat_mean");
         return nullptr;
     }
     const int elem = g->kind == 0 ? 2 : 4;
@@ -793,7 +801,8 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.vec_d = g->d && a16(g->d) && g->ldd % 4 == 0 && g->d_batch_stride % 4 == 0 && g->d_split_stride % 4 == 0;
     p.vec_res = g->residual && a16(g->residual) && g->ldr % 4 == 0 && g->residual_batch_stride % 4 == 0;
     p.vec_bias = g->bias && a16(g->bias) && g->bias_batch_stride % 4 == 0;
-    p.vec_stat = g->stat_mean && a16(g->stat_mean) && a16(g->stat_m2) && g->n % 4 == 0 && g->stat_batch_stride % 4 == 0;
+    p.vec_stat = g->stat_mean && a16(g->stat_mean) && (!g->stat_m2 || a16(g->stat_m2)) && g->n % 4 == 0 &&
+                 g->stat_batch_stride % 4 == 0;
     if (g->activation < 0 || g->activation > 2 || (g->act_aux && !g->activation)) {
         set_error("GEMM activation must be 0 (none), 1 (ELU) or 2 (tanh); act_aux needs an activation");
         delete plan;

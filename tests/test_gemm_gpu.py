@@ -207,3 +207,18 @@ def test_gemm_activation_forward_and_derivative(kind, activation, m, n):
     grad = torch.where(yd > 0, torch.ones_like(yd), yd + 1) if activation == dense.ELU else 1 - yd * yd
     expect2 = (ref2 + bias.double()[:, None, :]) * grad
     assert (D2[:, :, :n].double() - expect2).abs().max().item() < tol * max(expect2.abs().max().item(), 1.0)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_gemm_column_sums_mode(kind):
+    """stat_m2 == null: per-32-row-group column sums (bias gradients of the PPO layers)."""
+    m, n, k, batch = 4100, 200, 64, 2
+    groups = (m + 31) // 32
+    sums = torch.zeros(batch, groups, n, device="cuda")
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, stat_mean=sums, stat_batch_stride=groups * n)
+    plan.run()
+    torch.cuda.synchronize()
+    full = torch.zeros(batch, groups * 32, n, device="cuda", dtype=torch.float64)
+    full[:, :m] = D[:, :, :n].double()
+    expect = full.view(batch, groups, 32, n).sum(2)
+    assert torch.allclose(sums.double(), expect, atol=1e-3, rtol=1e-4)
