@@ -44,6 +44,8 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=("flashsac", "ppo"), default="flashsac",
+                   help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms)")
     return p.parse_args()
 
 
@@ -280,6 +282,134 @@ def run_b200(args, rank, world, local_rank):
     return L, sec, e2e_sec, h2d, launches, clocks.summary()
 
 
+# ---------------------------------------------------------------------------
+# PPO: WarpPPO(48, 12, 4096, 24), 512-256-128 ELU,
+# 5 epochs x 4 minibatches of 24576 rows, clip 0.2, value coef 1.0, entropy 0.01, lr 1e-3
+# ---------------------------------------------------------------------------
+PPO_METRIC = "PPO update ms (4096 envs x 24 steps, obs 48, act 12, 512-256-128 ELU, 5x4 minibatches)"
+PPO_OBS, PPO_ACT, PPO_ENVS, PPO_T, PPO_HIDDEN = 48, 12, 4096, 24, (512, 256, 128)
+
+
+def ppo_config():
+    from robolearn_b200.ppo import PPOConfig
+
+    return PPOConfig(hidden_dims=PPO_HIDDEN, activation="elu", epochs=5, num_mini_batches=4, clip_ratio=0.2,
+                     value_coefficient=1.0, entropy_coefficient=0.01, learning_rate=1e-3, gamma=0.99,
+                     gae_lambda=0.95)
+
+
+def ppo_flops() -> float:
+    """Executed GEMM FLOPs of one update: per minibatch row, forward 2*sum(K*N) per net, backward
+    dW 2*sum(K*N) and dX 2*sum(K*N) without the first layer's input gradient; 20 minibatches."""
+    widths = (PPO_OBS, *PPO_HIDDEN)
+    total = 0
+    for out in (PPO_ACT, 1):
+        kn = [k * n for k, n in zip(widths, (*PPO_HIDDEN, out))]
+        total += 2 * sum(kn) + 2 * sum(kn) + 2 * sum(kn[1:])
+    return float(total) * PPO_ENVS * PPO_T * 5
+
+
+def ppo_rollout(agent, seed: int = 0) -> dict:
+    """Synthetic rollout with the cfg2 distributions: obs ~N(0,1), actions = initial means + N(0,1),
+    rewards ~N(0,1), terminated ~Bernoulli(0.005), truncated 0, next values from N(0,1)."""
+    import torch
+
+    g = torch.Generator(device=agent.device).manual_seed(2026 + seed)
+    B = agent.batch_size
+    data = {"observations": torch.randn(B, PPO_OBS, device=agent.device, generator=g)}
+    data["means"] = torch.randn(B, PPO_ACT, device=agent.device, generator=g) * 0.1
+    data["actions"] = data["means"] + torch.randn(B, PPO_ACT, device=agent.device, generator=g)
+    data["stds"] = torch.ones(B, PPO_ACT, device=agent.device)
+    data["log_probs"] = (-0.5 * ((data["actions"] - data["means"]) ** 2 + 1.8378770664093453)).sum(1)
+    data["values"] = torch.randn(B, device=agent.device, generator=g)
+    data["rewards"] = torch.randn(B, device=agent.device, generator=g)
+    data["next_values"] = torch.randn(B, device=agent.device, generator=g)
+    data["terminated"] = (torch.rand(B, device=agent.device, generator=g) < 0.005).int()
+    data["truncated"] = torch.zeros(B, dtype=torch.int32, device=agent.device)
+    for k, v in data.items():
+        getattr(agent, k).copy_(v)
+    return data
+
+
+def ppo_cpu_minibatch_seconds() -> tuple[float, int]:
+    """One oracle minibatch step (24576 rows, forward + loss + backward + clip + Adam) on the host."""
+    import numpy as np
+
+    from oracle import ppo_np as P
+
+    h = P.PPOHyper(hidden_dims=PPO_HIDDEN, activation="elu", epochs=5, num_mini_batches=4, clip_ratio=0.2,
+                   value_coefficient=1.0, entropy_coefficient=0.01, learning_rate=1e-3)
+    params = P.init_params(PPO_OBS, PPO_ACT, h, seed=42)
+    M = PPO_ENVS * PPO_T // 4
+    rng = np.random.default_rng(0)
+    batch = dict(observations=rng.normal(size=(M, PPO_OBS)), actions=rng.normal(size=(M, PPO_ACT)),
+                 means=np.zeros((M, PPO_ACT)), stds=np.ones((M, PPO_ACT)), log_probs=rng.normal(-15, 1, size=M),
+                 values=rng.normal(size=M), advantages=rng.normal(size=M), returns=rng.normal(size=M))
+    state = P.PPOState.fresh(params, 1e-3)
+    t0 = time.perf_counter()
+    P.minibatch_step(state, batch, h)
+    return time.perf_counter() - t0, len(os.sched_getaffinity(0))
+
+
+def run_ppo(args) -> dict:
+    import torch
+
+    from robolearn_b200.ppo import WarpPPO
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    agent = WarpPPO(PPO_OBS, PPO_ACT, PPO_ENVS, PPO_T, ppo_config(), device=str(device))
+    data = ppo_rollout(agent)
+    agent.update()  # warm-up pass + capture
+    for _ in range(max(args.warmup - 1, 0)):
+        agent.update()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device.index) as clocks:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            agent.update()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end through the public API: rollout copied from pinned host memory, update, loss read back
+    host = {k: v.cpu().pin_memory() for k, v in data.items()}
+    loss_host = torch.zeros(4).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        for k, v in host.items():
+            getattr(agent, k).copy_(v, non_blocking=True)
+        agent.update()
+        loss_host[:1].copy_(agent.loss, non_blocking=True)
+        loss_host[1:].copy_(agent.metrics, non_blocking=True)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1) / args.steps
+    pk, src = peaks()
+    peak = pk["bf16_tflops"] / 6.0
+    achieved = ppo_flops() / (ms * 1e-3) / 1e12
+    out = {"metric": PPO_METRIC, "value": ms, "unit": "ms/update", "higher_is_better": False, "ms_per_step": ms,
+           "gpu_launches": agent.launch_count(), "clocks": clocks.summary(), "dtype": "f32 (tf32x3 GEMMs)",
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                        "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                        "flops_per_update": ppo_flops(),
+                        "peak_source": f"{src} bf16_tflops / 6 (tf32 dense = bf16 / 2; three tf32 products per "
+                                       "fp32 product)"},
+           "e2e": {"value": e2e_ms, "unit": "ms/update", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 16},
+           "config": {"workload": "cfg2 WarpPPO update (4096 envs x 24, obs 48, act 12, 512-256-128 ELU, "
+                                  "5 epochs x 4 minibatches)", "global_batch": agent.batch_size,
+                      "parallelism": "single", "l2": "rollout + activations > 126 MB L2 (no flush needed)"}}
+    if not args.no_cpu_baseline:
+        sec, cores = ppo_cpu_minibatch_seconds()
+        out["cpu_baseline"] = {"value": sec * 20 * 1e3, "unit": "ms/update", "cores": cores, "kind": "port",
+                               "sample": f"one minibatch step of 24576 rows ({sec:.1f} s, numpy), x20 minibatches"}
+    return out
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -287,6 +417,25 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     base = {"metric": METRIC, "unit": "updates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "ppo":
+        if rank != 0:
+            return
+        if args.impl == "reference":
+            sec, cores = ppo_cpu_minibatch_seconds()
+            value = sec * 20 * 1e3
+            print(json.dumps({"metric": PPO_METRIC, "impl": "reference", "value": value, "unit": "ms/update",
+                              "higher_is_better": False, "n_gpus": args.gpus, "steps": 1, "warmup": 0,
+                              "ms_per_step": value, "dtype": "f64", "data": "synthetic",
+                              "config": {"workload": "cfg2 WarpPPO update, CPU restatement (oracle port)"},
+                              "cpu_baseline": {"value": value, "unit": "ms/update", "cores": cores, "kind": "port",
+                                               "sample": "one minibatch step of 24576 rows, x20 minibatches"},
+                              "e2e": {"value": value, "unit": "ms/update", "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}))
+            return
+        out = dict(n_gpus=args.gpus, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None,
+                   data="synthetic", impl="b200", **run_ppo(args))
+        print(json.dumps(out))
+        return
     if args.impl == "reference":
         if rank != 0:
             return
@@ -340,6 +489,13 @@ def main():
         out["cpu_baseline"] = {"value": rate * sample / BATCH, "unit": "updates/s", "cores": cores, "kind": "port",
                                "sample": f"one actor+critic update pair at batch {sample} ({csec:.1f} s), "
                                          f"rate scaled to batch {BATCH}"}
+    if rank == 0 and world == 1:
+        # the cfg2 PPO update beside the headline (full line: --workload ppo)
+        import types
+
+        pp = run_ppo(types.SimpleNamespace(steps=10, warmup=3, no_cpu_baseline=True))
+        out["ppo"] = {"metric": pp["metric"], "value": pp["value"], "unit": pp["unit"],
+                      "roofline_frac": pp["roofline"]["frac"], "e2e": pp["e2e"]["value"]}
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

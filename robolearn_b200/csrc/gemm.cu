@@ -874,6 +874,8 @@ __global__ void split_reduce_kernel(const float* __restrict__ part, long long st
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         if (vec) {
             float4 acc = accumulate ? reinterpret_cast<const float4*>(out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            // unrolled so that eight partial rows are in flight; the sum keeps split order
+#pragma unroll 8
             for (int s = 0; s < splits; ++s) {
                 const float4 v = reinterpret_cast<const float4*>(part + s * stride)[i];
                 acc.x += v.x;
@@ -884,6 +886,7 @@ __global__ void split_reduce_kernel(const float* __restrict__ part, long long st
             reinterpret_cast<float4*>(out)[i] = acc;
         } else {
             float acc = accumulate ? out[i] : 0.0f;
+#pragma unroll 8
             for (int s = 0; s < splits; ++s) acc += part[s * stride + i];
             out[i] = acc;
         }
@@ -891,6 +894,7 @@ __global__ void split_reduce_kernel(const float* __restrict__ part, long long st
     if (vec && blockIdx.x == 0) {
         for (long long i = n4 * 4 + threadIdx.x; i < count; i += blockDim.x) {
             float acc = accumulate ? out[i] : 0.0f;
+#pragma unroll 8
             for (int s = 0; s < splits; ++s) acc += part[s * stride + i];
             out[i] = acc;
         }

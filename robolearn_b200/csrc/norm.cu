@@ -358,14 +358,37 @@ __global__ void rms_dgamma_kernel(const float* __restrict__ du, long long lddu, 
     part[(static_cast<long long>(t) * groups + g) * cols + c] = s;
 }
 
+// out[t][c] (+)= sum_g part[t][g][c]. Block (32 columns, twin t); warp w sums the contiguous
+// group range w of 8 (lane = column, coalesced rows), then warp 0 adds the eight partial
+// sums in warp order: a fixed order for given (groups, cols).
 __global__ void colsum_finalize_kernel(const float* part, int twins, int groups, int cols, float* out, long long ots,
                                        int accumulate) {
-    const int i = blockIdx.x * kT + threadIdx.x;
-    if (i >= twins * cols) return;
-    const int t = i / cols, c = i % cols;
+    __shared__ float sh[kT / 32][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * 32 + lane;
+    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int g0 = min(warp * per, groups), g1 = min(g0 + per, groups);
     float s = 0.0f;
-    for (int g = 0; g < groups; ++g) s += part[(static_cast<long long>(t) * groups + g) * cols + c];
-    out[t * ots + c] = accumulate ? out[t * ots + c] + s : s;
+    if (c < cols) {
+        const float* src = part + static_cast<long long>(t) * groups * cols + c;
+        int g = g0;
+        for (; g + 4 <= g1; g += 4) {
+            const float a = src[static_cast<long long>(g) * cols], b = src[static_cast<long long>(g + 1) * cols];
+            const float d = src[static_cast<long long>(g + 2) * cols], e = src[static_cast<long long>(g + 3) * cols];
+            s = (((s + a) + b) + d) + e;
+        }
+        for (; g < g1; ++g) s += src[static_cast<long long>(g) * cols];
+    }
+    sh[warp][lane] = s;
+    __syncthreads();
+    if (warp == 0 && c < cols) {
+        float r = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kT / 32; ++w) r += sh[w][lane];
+        float* o = out + t * ots + c;
+        *o = accumulate ? *o + r : r;
+    }
 }
 
 inline bool a16(const void* p) { return p == nullptr || aligned(p, 16); }
@@ -544,7 +567,7 @@ extern "C" int rl2_colsum_finalize(const float* part, int twins, int groups, int
         set_error("colsum finalize: invalid arguments");
         return -1;
     }
-    norm::colsum_finalize_kernel<<<(twins * cols + norm::kT - 1) / norm::kT, norm::kT, 0, as_stream(stream)>>>(
+    norm::colsum_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
         part, twins, groups, cols, out, ots, accumulate);
     return launch_status("column-sum finalize");
 }
