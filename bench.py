@@ -13,6 +13,12 @@ weights of the reference architecture. The replay holds 16 x 4096 rows; the
 per-update working set (> 1 GB of activations) exceeds the 126 MB L2, so no flush
 is needed between steps.
 
+With ``--gpus N`` (one process per GPU under torch.distributed.run) the ranks train ONE
+learner data-parallel: every rank processes 4096 rows of the N x 4096 global batch
+(same replay, indices and noise streams), batch-norm statistics are merged over all
+ranks and gradients averaged with NCCL before Adam; ``value`` counts N x 4096-row
+updates per second (weak scaling).
+
 ``--impl reference`` times the CPU restatement of the reference update (the
 reference is Python/Torch and cannot travel to the GPU box) on all host cores.
 """
@@ -101,8 +107,9 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def build(precision: str, device, seed: int = 0):
-    """Learner + synthetic device replay at the config-3 shapes."""
+def build(precision: str, device, seed: int = 0, dp=None):
+    """Learner + synthetic device replay at the config-3 shapes (batch 4096 per rank; with
+    ``dp`` the ranks train one learner on the global batch, replay replicated)."""
     import torch
 
     from robolearn_b200.flashsac.config import FlashSACConfig
@@ -115,7 +122,7 @@ def build(precision: str, device, seed: int = 0):
                          critic_max_v=10.0, critic_target_update_tau=0.005, learning_rate_init=3e-4,
                          learning_rate_peak=3e-4, learning_rate_end=3e-4, n_step=1, buffer_max_length=16 * ENVS,
                          buffer_min_length=BATCH, dense_precision=precision, seed=seed)
-    L = Learner(OBS, OBS, ACT, cfg, device)
+    L = Learner(OBS, OBS, ACT, cfg, device, dp=dp)
     R = DeviceReplay(OBS, ACT, ENVS, 16 * ENVS, 1, 0.99, BATCH, device, seed=seed)
     g = torch.Generator(device=device).manual_seed(2026 + seed)
     cap = R.capacity
@@ -225,7 +232,12 @@ def run_b200(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    L, R, feed = build(args.precision, device, seed=rank)
+    dp = None
+    if world > 1:
+        from robolearn_b200.flashsac.dp import DataParallel
+
+        dp = DataParallel()
+    L, R, feed = build(args.precision, device, seed=0, dp=dp)
     for phase in (True, False):  # one eager pass loads every kernel module before capture
         for f in feed:
             f()
@@ -258,6 +270,7 @@ def run_b200(args, rank, world, local_rank):
     # ---- end to end through the public replay + learner API with host buffers:
     # each step copies one vector-environment step of transitions from pinned host
     # memory, ingests it, runs the update and reads the critic loss back to the host.
+    torch.manual_seed(1234)  # the same transitions on every rank (replicated replay)
     host = {k: torch.randn(ENVS, d).pin_memory() for k, d in (("obs", OBS), ("next_obs", OBS))}
     host["act"] = torch.rand(ENVS, ACT).mul_(2).sub_(1).pin_memory()
     host["rew"] = torch.randn(ENVS).pin_memory()
@@ -479,7 +492,7 @@ def main():
                dtype=args.precision, gpu_launches=launches, clocks=clocks, roofline=roof,
                config={"workload": "cfg3 FlashSAC update (obs 123, act 37, batch 4096 per GPU, critic 512x2, "
                                    "actor 256x2, 101 atoms)", "global_batch": BATCH * world, "seq_len": None,
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "parallelism": f"dp{world}" if world > 1 else "single",
                        "l2": "working set > 126 MB L2 (no flush needed)"},
                e2e={"value": world * args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4})

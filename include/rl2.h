@@ -203,6 +203,13 @@ int rl2_colstats(const float* x, long long ldx, long long x_twin_stride, int twi
 int rl2_bn_finalize(const float* mean_part, const float* m2_part, long long part_twin_stride, int twins, int rows,
                     int cols, float* mean, float* invstd, float* running_mean, float* running_var, float momentum,
                     float eps, int update_running, void* stream);
+/* Partials gathered from several data-parallel ranks: group g of twin t lives at
+ * t * part_twin_stride + (g / groups_per_rank) * rank_stride + (g % groups_per_rank) * cols
+ * (rank-major blocks as an all-gather leaves them); rows = all ranks' rows. */
+int rl2_bn_finalize_ranked(const float* mean_part, const float* m2_part, long long part_twin_stride,
+                           int groups_per_rank, long long rank_stride, int twins, int rows, int cols, float* mean,
+                           float* invstd, float* running_mean, float* running_var, float momentum, float eps,
+                           int update_running, void* stream);
 
 /* eval mode: mean = running_mean, invstd = 1 / sqrt(running_var + eps), count elements */
 int rl2_bn_eval_prepare(const float* running_mean, const float* running_var, long long count, float eps,
@@ -251,6 +258,11 @@ int rl2_bn_backward_reduce(const rl2_bn_backward_args* args, void* stream);
 int rl2_bn_backward_finalize(const float* s1_part, const float* s2_part, int twins, int rows, int cols,
                              float* dgamma, float* dbeta, long long grad_twin_stride, int accumulate, float* coef1,
                              float* coef2, void* stream);
+/* Same with gathered partials (layout as rl2_bn_finalize_ranked; part_twin_stride explicit). */
+int rl2_bn_backward_finalize_ranked(const float* s1_part, const float* s2_part, long long part_twin_stride,
+                                    int groups_per_rank, long long rank_stride, int twins, int rows, int cols,
+                                    float* dgamma, float* dbeta, long long dgamma_twin_stride, int accumulate,
+                                    float* coef1, float* coef2, void* stream);
 int rl2_bn_backward_apply(const rl2_bn_backward_args* args, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -487,6 +499,10 @@ int rl2_replay_gather(const rl2_replay_gather_args* args, void* stream);
  * _normal_noise kernel, src/robolearn/warp/flashsac.py:44-50): out[r][c], r < rows, c < cols. */
 int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols, float* out,
                      long long ld, void* stream);
+/* Rows row0 .. row0 + rows - 1 of the same stream (data-parallel ranks draw their slice of
+ * the global noise array; bit-identical to the matching rows of one full launch). */
+int rl2_normal_noise_rows(unsigned long long seed, const unsigned long long* epoch, long long row0, int rows,
+                          int cols, float* out, long long ld, void* stream);
 
 /* ---------------------------------------------------------------------------
  * replay ingest (one vector-environment step): stage the step in an n-step

@@ -341,3 +341,10 @@ SIGNATURES.update({
     "rl2_ppo_sample": ([ctypes.POINTER(PPOSampleArgs), P], I),
     "rl2_ppo_store": ([ctypes.POINTER(PPOStoreArgs), P], I),
 })
+
+SIGNATURES["rl2_normal_noise_rows"] = ([ctypes.c_ulonglong, P, LL, I, I, P, LL, P], I)
+
+SIGNATURES.update({
+    "rl2_bn_finalize_ranked": ([P, P, LL, I, LL, I, I, I, P, P, P, P, F, F, I, P], I),
+    "rl2_bn_backward_finalize_ranked": ([P, P, LL, I, LL, I, I, I, P, P, LL, I, P, P, P], I),
+})

@@ -52,10 +52,12 @@ __global__ void colstats_kernel(const float* __restrict__ x, long long ldx, long
 
 // grid (ceil(cols/32), twins), 8 warps: lane = column, warp w merges a contiguous
 // range of groups in order, then warp 0 merges the 8 results in order (deterministic).
+// Group g of the partials lives at (g / gpr) * rs + (g % gpr) * cols: gpr groups per rank,
+// rank blocks rs floats apart (one rank: gpr = groups, rs = 0).
 __global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p,
-                                                      long long pt, int twins, int rows, int cols, float* mean,
-                                                      float* invstd, float* rm, float* rv, float momentum, float eps,
-                                                      int update) {
+                                                      long long pt, int gpr, long long rs, int twins, int rows,
+                                                      int cols, float* mean, float* invstd, float* rm, float* rv,
+                                                      float momentum, float eps, int update) {
     __shared__ float sh[3][kT / 32][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -69,7 +71,8 @@ __global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ 
         const float* qp = m2_p + t * pt + c;
         for (int g = g0; g < g1; ++g) {
             const float ng = static_cast<float>(min(32, rows - g * 32));
-            chan_merge(n, mu, m2, ng, mp[static_cast<long long>(g) * cols], qp[static_cast<long long>(g) * cols]);
+            const long long o = static_cast<long long>(g / gpr) * rs + static_cast<long long>(g % gpr) * cols;
+            chan_merge(n, mu, m2, ng, mp[o], qp[o]);
         }
     }
     sh[0][warp][lane] = n;
@@ -224,9 +227,10 @@ __global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
 }
 
 // grid (ceil(cols/32), twins), 8 warps over contiguous group ranges, fixed-order combine.
-__global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, const float* s2p, int twins, int rows,
-                                                          int cols, float* dgamma, float* dbeta, long long gts,
-                                                          int accumulate, float* coef1, float* coef2) {
+__global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, const float* s2p, long long pt, int gpr,
+                                                          long long rs, int twins, int rows, int cols, float* dgamma,
+                                                          float* dbeta, long long gts, int accumulate, float* coef1,
+                                                          float* coef2) {
     __shared__ float sh[2][kT / 32][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -237,7 +241,8 @@ __global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, cons
     float s1 = 0.0f, s2 = 0.0f;
     if (c < cols) {
         for (int g = g0; g < g1; ++g) {
-            const long long o = (static_cast<long long>(t) * groups + g) * cols + c;
+            const long long o = static_cast<long long>(t) * pt + static_cast<long long>(g / gpr) * rs +
+                                static_cast<long long>(g % gpr) * cols + c;
             s1 += s1p[o];
             s2 += s2p[o];
         }
@@ -436,18 +441,27 @@ extern "C" int rl2_colstats(const float* x, long long ldx, long long xt, int twi
     return launch_status("column statistics");
 }
 
-extern "C" int rl2_bn_finalize(const float* mean_p, const float* m2_p, long long pt, int twins, int rows, int cols,
-                               float* mean, float* invstd, float* rm, float* rv, float momentum, float eps,
-                               int update, void* stream) {
+extern "C" int rl2_bn_finalize_ranked(const float* mean_p, const float* m2_p, long long pt, int groups_per_rank,
+                                      long long rank_stride, int twins, int rows, int cols, float* mean,
+                                      float* invstd, float* rm, float* rv, float momentum, float eps, int update,
+                                      void* stream) {
     clear_error();
     if (!mean_p || !m2_p || !mean || !invstd || twins < 1 || rows < 1 || cols < 1 || !(eps > 0.0f) ||
-        (update && (!rm || !rv || rows < 2))) {
+        groups_per_rank < 1 || rank_stride < 0 || (update && (!rm || !rv || rows < 2))) {
         set_error("bn finalize: invalid buffers or shape (running update needs rows >= 2)");
         return -1;
     }
     norm::finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
-        mean_p, m2_p, pt, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update);
+        mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
+        update);
     return launch_status("batch-norm statistics");
+}
+
+extern "C" int rl2_bn_finalize(const float* mean_p, const float* m2_p, long long pt, int twins, int rows, int cols,
+                               float* mean, float* invstd, float* rm, float* rv, float momentum, float eps,
+                               int update, void* stream) {
+    return rl2_bn_finalize_ranked(mean_p, m2_p, pt, (rows + 31) / 32, 0, twins, rows, cols, mean, invstd, rm, rv,
+                                  momentum, eps, update, stream);
 }
 
 extern "C" int rl2_bn_eval_prepare(const float* rm, const float* rv, long long count, float eps, float* mean,
@@ -492,17 +506,26 @@ extern "C" int rl2_bn_backward_reduce(const rl2_bn_backward_args* a, void* strea
     return launch_status("batch-norm backward reduce");
 }
 
-extern "C" int rl2_bn_backward_finalize(const float* s1p, const float* s2p, int twins, int rows, int cols,
-                                        float* dgamma, float* dbeta, long long gts, int accumulate, float* coef1,
-                                        float* coef2, void* stream) {
+extern "C" int rl2_bn_backward_finalize_ranked(const float* s1p, const float* s2p, long long pt, int groups_per_rank,
+                                               long long rank_stride, int twins, int rows, int cols, float* dgamma,
+                                               float* dbeta, long long gts, int accumulate, float* coef1, float* coef2,
+                                               void* stream) {
     clear_error();
-    if (!s1p || !s2p || twins < 1 || rows < 1 || cols < 1) {
+    if (!s1p || !s2p || twins < 1 || rows < 1 || cols < 1 || groups_per_rank < 1 || rank_stride < 0) {
         set_error("bn backward finalize: invalid arguments");
         return -1;
     }
     norm::bwd_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
-        s1p, s2p, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+        s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
     return launch_status("batch-norm backward finalize");
+}
+
+extern "C" int rl2_bn_backward_finalize(const float* s1p, const float* s2p, int twins, int rows, int cols,
+                                        float* dgamma, float* dbeta, long long gts, int accumulate, float* coef1,
+                                        float* coef2, void* stream) {
+    const int groups = (rows + 31) / 32;
+    return rl2_bn_backward_finalize_ranked(s1p, s2p, static_cast<long long>(groups) * cols, groups, 0, twins, rows,
+                                           cols, dgamma, dbeta, gts, accumulate, coef1, coef2, stream);
 }
 
 extern "C" int rl2_bn_backward_apply(const rl2_bn_backward_args* a, void* stream) {

@@ -62,12 +62,16 @@ __global__ void sample_kernel(uint64_t seed, const unsigned long long* epoch, co
 __global__ void advance_kernel(unsigned long long* epoch, unsigned long long by) { *epoch += by; }
 
 // Standard normal samples by the Box-Muller transform of two Philox uniforms per pair.
-__global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, int rows, int cols, float* out,
-                              long long ld) {
+// Elements e0 .. e0 + rows * cols - 1 of the row-major [*, cols] stream (element i comes
+// from Philox counter quad i / 4), written as rows 0.. of out: any row range of the
+// global array reproduces exactly the values a single launch over all rows would give.
+__global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, long long e0, int rows, int cols,
+                              float* out, long long ld) {
     const long long total = static_cast<long long>(rows) * cols;
     const unsigned long long e = epoch ? *epoch : 0ull;
     const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
-    for (long long q = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; q * 4 < total;
+    const long long q_first = e0 / 4, q_end = (e0 + total + 3) / 4;
+    for (long long q = q_first + blockIdx.x * static_cast<long long>(kT) + threadIdx.x; q < q_end;
          q += static_cast<long long>(gridDim.x) * kT) {
         const U4 r = philox(U4{static_cast<uint32_t>(q), static_cast<uint32_t>(q >> 32), static_cast<uint32_t>(e),
                                static_cast<uint32_t>(e >> 32) ^ 0x0A0Fu},
@@ -84,8 +88,8 @@ __global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, in
             const float z[2] = {rad * cs, rad * sn};
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const long long i = q * 4 + 2 * p + h;
-                if (i < total) out[(i / cols) * ld + (i % cols)] = z[h];
+                const long long i = q * 4 + 2 * p + h - e0;
+                if (i >= 0 && i < total) out[(i / cols) * ld + (i % cols)] = z[h];
             }
         }
     }
@@ -165,17 +169,23 @@ extern "C" int rl2_counter_advance(unsigned long long* epoch, unsigned long long
     return launch_status("counter advance");
 }
 
-extern "C" int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols,
-                                float* out, long long ld, void* stream) {
+extern "C" int rl2_normal_noise_rows(unsigned long long seed, const unsigned long long* epoch, long long row0,
+                                     int rows, int cols, float* out, long long ld, void* stream) {
     clear_error();
-    if (!out || rows < 1 || cols < 1 || ld < cols) {
+    if (!out || rows < 1 || cols < 1 || ld < cols || row0 < 0) {
         set_error("normal noise: invalid arguments");
         return -1;
     }
-    const long long quads = (static_cast<long long>(rows) * cols + 3) / 4;
+    const long long e0 = row0 * cols;
+    const long long quads = (e0 + static_cast<long long>(rows) * cols + 3) / 4 - e0 / 4;
     const int blocks = static_cast<int>(std::min<long long>((quads + replay::kT - 1) / replay::kT, 148 * 8));
-    replay::normal_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(seed, epoch, rows, cols, out, ld);
+    replay::normal_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(seed, epoch, e0, rows, cols, out, ld);
     return launch_status("normal noise");
+}
+
+extern "C" int rl2_normal_noise(unsigned long long seed, const unsigned long long* epoch, int rows, int cols,
+                                float* out, long long ld, void* stream) {
+    return rl2_normal_noise_rows(seed, epoch, 0, rows, cols, out, ld, stream);
 }
 
 extern "C" int rl2_replay_gather(const rl2_replay_gather_args* a, void* stream) {

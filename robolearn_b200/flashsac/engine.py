@@ -360,8 +360,11 @@ class Run:
 
     def __init__(self, net: Net, rows: int, training: bool, x_addr: int, ldx: int, *, update_running: bool,
                  need_param_grads: bool, need_input_grad: bool, scaler: Scaler | None = None,
-                 pool: dict | None = None, head_ld: int | None = None, out_plane_rows: int | None = None):
+                 pool: dict | None = None, head_ld: int | None = None, out_plane_rows: int | None = None,
+                 dp=None):
         self.net, self.rows, self.training = net, rows, training
+        # data parallel: batch-norm statistics over the global batch of all ranks
+        self.dp = dp if (dp is not None and dp.world > 1 and training) else None
         self.x_addr, self.ldx = x_addr, ldx
         self.update_running = update_running and training
         self.need_param_grads = need_param_grads
@@ -396,8 +399,13 @@ class Run:
         self.out = buf("out", lambda: f32(T, R, self.head_ld))
         # batch statistics of this run (per BN layer): partials + mean / invstd
         Cmax = max(spec.in_dim, E)
-        self.pm = buf("pm", lambda: f32(T, self.G, Cmax))
-        self.pq = buf("pq", lambda: f32(T, self.G, Cmax))
+        # per-group column moments of the current BN layer, packed [mean: T][G][C] | [M2: T][G][C]
+        self.pmq = buf("pmq", lambda: f32(2 * T * self.G * Cmax))
+        if self.dp is not None:
+            if rows % 32:
+                raise ValueError("data-parallel batch norm needs a per-rank batch that is a multiple of 32")
+            W = self.dp.world
+            self.gpmq = buf("gpmq", lambda: f32(W * 2 * T * self.G * Cmax))
         self.stats = {}
         for pre, C in net.bn_layers:
             self.stats[pre] = (buf(f"mean.{pre}", lambda C=C: f32(T, C)), buf(f"inv.{pre}", lambda C=C: f32(T, C)))
@@ -411,11 +419,15 @@ class Run:
             self.dt2 = buf("dt2", lambda: PlaneBuf(kind, T, R, H, dev))
             self.dt1 = buf("dt1", lambda: PlaneBuf(kind, T, R, E, dev))
             self.de = buf("de", lambda: f32(T, R, spec.in_dim))
-            self.s1 = buf("s1", lambda: f32(T, self.G, Cmax))
-            self.s2 = buf("s2", lambda: f32(T, self.G, Cmax))
+            # backward per-group sums of the current BN layer, packed [s1: T][G][C] | [s2: T][G][C]
+            self.s12 = buf("s12", lambda: f32(2 * T * self.G * Cmax))
             self.coef1 = buf("c1", lambda: f32(T, Cmax))
             self.coef2 = buf("c2", lambda: f32(T, Cmax))
             self.rms_part = buf("rmsp", lambda: f32(T, self.G, H))
+            if self.dp is not None:
+                W = self.dp.world
+                self.gs12 = buf("gs12", lambda: f32(W * 2 * T * self.G * Cmax))
+                self.coef_local = buf("cl", lambda: f32(2, T, Cmax))
             if need_input_grad:
                 self.dx = buf("dx", lambda: f32(R, _a4(spec.in_dim)))
         self.split_ws = None
@@ -430,7 +442,8 @@ class Run:
         kp = operand_ld(lin.inp, net.kind)
         kw = {}
         if stats:
-            kw = dict(stat_mean=self.pm, stat_m2=self.pq, stat_batch_stride=self.G * lin.out)
+            base = self.pmq.data_ptr()
+            kw = dict(stat_mean=base, stat_m2=base + 4 * self.T * self.G * lin.out, stat_batch_stride=self.G * lin.out)
         return DensePlan(kind=net.kind, m=self.rows, n=lin.out, k=lin.inp, batch=self.T,
                          a=a.main, a_lo=a.lo, a_major=0, lda=a.ld, a_batch_stride=a.tstride,
                          b=bm, b_lo=bl, b_major=0, ldb=kp, b_batch_stride=lin.out * kp,
@@ -490,10 +503,26 @@ class Run:
         rv = self.net.buffer(pre + ".running_var")
         pt = 0 if src_part_shared else self.G * C
         T, R, upd = self.T, self.rows, int(self.update_running)
-        pm, pq = self.pm, self.pq
+        tw = 1 if src_part_shared else T  # twins holding partials (the shared input has one set)
+        n = tw * self.G * C
+        pmq = self.pmq
+        dp = self.dp
+        if dp is not None:  # one all-gather of every rank's packed partials, then a global merge
+            gpmq, W, G = self.gpmq, dp.world, self.G
+
+            def launch():
+                dp.all_gather(pmq[:2 * n], gpmq[:W * 2 * n])
+                base = gpmq.data_ptr()
+                N.check(lib.rl2_bn_finalize_ranked(base, base + 4 * n, pt, G, 2 * n, T, W * R, C, mean.data_ptr(),
+                                                   inv.data_ptr(), rm.data_ptr(), rv.data_ptr(), BN_MOMENTUM, BN_EPS,
+                                                   upd, N.stream_ptr()), "bn finalize (global)")
+
+            launch.launches = 1
+            return launch
 
         def launch():
-            N.check(lib.rl2_bn_finalize(pm.data_ptr(), pq.data_ptr(), pt, T, R, C, mean.data_ptr(), inv.data_ptr(),
+            base = pmq.data_ptr()
+            N.check(lib.rl2_bn_finalize(base, base + 4 * n, pt, T, R, C, mean.data_ptr(), inv.data_ptr(),
                                         rm.data_ptr(), rv.data_ptr(), BN_MOMENTUM, BN_EPS, upd, N.stream_ptr()),
                     "bn finalize")
 
@@ -526,10 +555,11 @@ class Run:
         # embedder BN on the shared fp32 input
         Cin = spec.in_dim
         if self.training:
-            x_addr, ldx, pm, pq, G = self.x_addr, self.ldx, self.pm, self.pq, self.G
+            x_addr, ldx, pmq, G = self.x_addr, self.ldx, self.pmq, self.G
 
             def colstats():
-                N.check(lib.rl2_colstats(x_addr, ldx, 0, 1, R, Cin, pm.data_ptr(), pq.data_ptr(), G * Cin,
+                base = pmq.data_ptr()  # one shared set: [mean: G][Cin] | [M2: G][Cin]
+                N.check(lib.rl2_colstats(x_addr, ldx, 0, 1, R, Cin, base, base + 4 * G * Cin, G * Cin,
                                          N.stream_ptr()), "input column statistics")
 
             prog += [colstats, self._bn_stats("embedder.norm", Cin, src_part_shared=True)]
@@ -566,10 +596,13 @@ class Run:
         lib, net = _lib(), self.net
         mean, inv = self._stats_ptrs(pre)
         sc = self.scaler
+        n12 = self.T * self.G * C  # packed [s1 | s2] of this layer
+        s1p = self.s12.data_ptr() if self.training else None
+        s2p = s1p + 4 * n12 if self.training else None
         a = N.BnBackwardArgs(dy=dy.data_ptr(), lddy=C, dy_twin_stride=self.rows * C, x=x_addr, ldx=ldx,
                              x_twin_stride=xts, twins=self.T, rows=self.rows, cols=C, mean=mean, invstd=inv,
                              gamma=net.addr(pre + ".weight"), beta=net.addr(pre + ".bias"), relu=int(relu),
-                             training=int(self.training), s1_part=N.addr(self.s1), s2_part=N.addr(self.s2),
+                             training=int(self.training), s1_part=N.addr(s1p), s2_part=N.addr(s2p),
                              coef1=N.addr(self.coef1), coef2=N.addr(self.coef2), dx=N.addr(dx), lddx=lddx,
                              dx_twin_stride=dxts, sum_twins=int(sum_twins),
                              plane=plane.c(sc.scale, sc.found_inf) if plane is not None else N.Plane())
@@ -577,15 +610,33 @@ class Run:
         if self.training:
             prog.append(_call(lib.rl2_bn_backward_reduce, a, "bn backward reduce"))
             T, R = self.T, self.rows
-            s1, s2, c1, c2 = self.s1, self.s2, self.coef1, self.coef2
+            s12, c1, c2 = self.s12, self.coef1, self.coef2
             gw = net.addr(pre + ".weight", "grads") if self.need_param_grads else None
             gb = net.addr(pre + ".bias", "grads") if self.need_param_grads else None
             gts = C if self.T == 2 else 0
 
-            def fin():
-                N.check(lib.rl2_bn_backward_finalize(s1.data_ptr(), s2.data_ptr(), T, R, C, gw, gb, gts, 0,
-                                                     c1.data_ptr(), c2.data_ptr(), N.stream_ptr()),
-                        "bn backward finalize")
+            dp = self.dp
+            if dp is None:
+                def fin():
+                    N.check(lib.rl2_bn_backward_finalize(s1p, s2p, T, R, C, gw, gb, gts, 0, c1.data_ptr(),
+                                                         c2.data_ptr(), N.stream_ptr()), "bn backward finalize")
+            else:
+                # gamma / beta gradients from this rank's rows (averaged with the other
+                # gradients later); dx coefficients from the global sums of all ranks
+                gs12, cl, W, G = self.gs12, self.coef_local, dp.world, self.G
+
+                def fin():
+                    s = N.stream_ptr()
+                    if gw is not None:
+                        N.check(lib.rl2_bn_backward_finalize(s1p, s2p, T, R, C, gw, gb, gts, 0, cl[0].data_ptr(),
+                                                             cl[1].data_ptr(), s), "bn backward finalize (local)")
+                    dp.all_gather(s12[:2 * n12], gs12[:W * 2 * n12])
+                    base = gs12.data_ptr()
+                    N.check(lib.rl2_bn_backward_finalize_ranked(base, base + 4 * n12, G * C, G, 2 * n12, T, W * R, C,
+                                                                None, None, 0, 0, c1.data_ptr(), c2.data_ptr(),
+                                                                N.stream_ptr()), "bn backward finalize (global)")
+
+                fin.launches = 2 if gw is not None else 1
 
             prog.append(fin)
         if plane is not None or dx is not None:

@@ -123,8 +123,12 @@ class Learner:
     """Device state and launch programs of one FlashSAC learner."""
 
     def __init__(self, obs_a: int, obs_c: int, act: int, cfg: FlashSACConfig, device, *, adam_formula: int = 0,
-                 init_weights: bool = True, init_loss_scale: float = 65536.0):
+                 init_weights: bool = True, init_loss_scale: float = 65536.0, dp=None):
+        """``cfg.sample_batch_size`` is this rank's batch; with ``dp`` (a ``DataParallel``) the
+        update runs on the global batch of all ranks (batch-norm statistics, gradients and
+        the temperature's entropy exchanged; see ``dp.py``)."""
         self.cfg = cfg
+        self.dp = dp if (dp is not None and dp.world > 1) else None
         self.device = device = torch.device(device)
         self.obs_a, self.obs_c, self.act = obs_a, obs_c, act
         self.kind = FP16 if cfg.precision == "fp16" else TF32X3
@@ -193,16 +197,16 @@ class Learner:
         pa, pa_eval, pc, pc_eval = {}, {}, {}, {}
         sa, scc = self.scalers["actor"], self.scalers["critic"]
         self.actor_train = Run(self.actor, 2 * B, True, self.actor_x.data_ptr(), self.ldax, update_running=True,
-                               need_param_grads=True, need_input_grad=False, scaler=sa, pool=pa)
+                               need_param_grads=True, need_input_grad=False, scaler=sa, pool=pa, dp=self.dp)
         self.actor_next = Run(self.actor, B, False, self.actor_x.data_ptr() + 4 * B * self.ldax, self.ldax,
                               update_running=False, need_param_grads=False, need_input_grad=False, pool=pa_eval)
         self.critic_pi = Run(self.critic, B, False, self.critic_x_pi.data_ptr(), self.ldx, update_running=False,
                              need_param_grads=False, need_input_grad=True, scaler=sa, pool=pc_eval)
         self.target_run = Run(self.target, 2 * B, True, self.critic_x.data_ptr(), self.ldx, update_running=True,
-                              need_param_grads=False, need_input_grad=False, pool=pc)
+                              need_param_grads=False, need_input_grad=False, pool=pc, dp=self.dp)
         pc_online = {k: v for k, v in pc.items() if k != "out"}
         self.critic_run = Run(self.critic, 2 * B, True, self.critic_x.data_ptr(), self.ldx, update_running=True,
-                              need_param_grads=True, need_input_grad=False, scaler=scc, pool=pc_online)
+                              need_param_grads=True, need_input_grad=False, scaler=scc, pool=pc_online, dp=self.dp)
         self.graphs = {}
         self.programs = {True: self._program(True), False: self._program(False)}
 
@@ -231,12 +235,18 @@ class Learner:
             tau=cfg.critic_target_update_tau if target is not None else 0.0,
             target_plane=target.plane_c() if target is not None else N.Plane())
         pref, sref = ctypes.byref(prep), ctypes.byref(step)
+        dp = self.dp
 
         def launch():
+            if dp is not None:  # average the gradients of all ranks; skip the step on any rank's overflow
+                dp.all_reduce_mean(net.grads)
+                if sc.found_inf is not None and self.kind == FP16:
+                    dp.all_reduce_max(sc.found_inf)
             N.check(lib.rl2_adam_prepare(pref, N.stream_ptr()), f"{name} adam prepare")
             N.check(lib.rl2_adam_step(sref, N.stream_ptr()), f"{name} adam step")
 
         launch.keep = (prep, step)
+        launch.launches = 2
         return launch
 
     def _program(self, actor_phase: bool):
@@ -298,6 +308,10 @@ class Learner:
                 warmup_steps=float(cfg.learning_rate_warmup_step), decay_steps=float(cfg.learning_rate_decay_step),
                 update=1, value_out=mi["temperature/value"], loss_out=mi["temperature/loss"],
                 alpha_out=self.alpha.data_ptr())
+            if self.dp is not None:
+                ent = self.metrics[METRIC_KEYS.index("actor/entropy"):METRIC_KEYS.index("actor/entropy") + 1]
+                prog.append(lambda ent=ent: self.dp.all_reduce_mean(ent))
+                prog[-1].launches = 0
             prog.append(_wrap(lib.rl2_temperature_step, temp, None, "temperature step"))
         else:
             temp = N.TemperatureArgs(log_temp=self.log_temp.data_ptr(), update=0, alpha_out=self.alpha.data_ptr())
@@ -335,6 +349,15 @@ class Learner:
         prog.append(_wrap(lib.rl2_critic_objective, co, None, "critic objective"))
         prog += self.critic_run.backward_program
         prog.append(self._optimizer("critic", self.critic, target=self.target))
+        if self.dp is not None:  # reported metrics over the global batch
+            mx = METRIC_KEYS.index("critic/max_entropy_bonus")
+
+            def metrics_exchange():
+                self.dp.all_reduce_max(self.metrics[mx:mx + 1])
+                self.dp.all_reduce_mean(self.metrics)
+
+            metrics_exchange.launches = 0
+            prog.append(metrics_exchange)
         return prog
 
     # ------------------------------------------------------------------

@@ -19,9 +19,12 @@ def sampling_program(learner, replay, reward_state=None, g_max: float = 5.0, see
     lib = N.load()
     L = learner
     B = L.B
-    idx = replay_indices(L)
+    dp = getattr(L, "dp", None)
+    world, rank = (dp.world, dp.rank) if dp is not None else (1, 0)
+    BG, row0 = B * world, B * rank  # global batch and this rank's first row
+    idx = replay_indices(L, BG)
     g = N.ReplayGatherArgs(
-        indices=idx.data_ptr(), batch=B, obs=replay.observation.data_ptr(),
+        indices=idx.data_ptr() + 4 * row0, batch=B, obs=replay.observation.data_ptr(),
         next_obs=replay.next_observation.data_ptr(), ld_obs=replay.obs_dim, action=replay.action.data_ptr(),
         ld_action=replay.act_dim, reward=replay.reward.data_ptr(), terminated=replay.terminated.data_ptr(),
         truncated=replay.truncated.data_ptr(), discount=replay.discount.data_ptr(), obs_dim=L.obs_c,
@@ -43,27 +46,34 @@ def sampling_program(learner, replay, reward_state=None, g_max: float = 5.0, see
 
     def sample():
         s = N.stream_ptr()
-        N.check(lib.rl2_replay_sample(seed_idx, epoch.data_ptr(), pop, 0, B, idx.data_ptr(), health, s), "sample")
+        N.check(lib.rl2_replay_sample(seed_idx, epoch.data_ptr(), pop, 0, BG, idx.data_ptr(), health, s), "sample")
         N.check(lib.rl2_replay_gather(gref, s), "gather")
+
+    # global noise arrays: actor phase [observations (BG) | next observations (BG)], next actions [BG];
+    # this rank draws its rows of each
+    an, A = L.actor_noise.data_ptr(), L.act
 
     def make_noise():
         s = N.stream_ptr()
-        N.check(lib.rl2_normal_noise(seed_a, epoch.data_ptr(), 2 * B, L.act, L.actor_noise.data_ptr(), L.act, s),
-                "actor noise")
-        N.check(lib.rl2_normal_noise(seed_n, epoch.data_ptr(), B, L.act, L.next_noise.data_ptr(), L.act, s),
+        N.check(lib.rl2_normal_noise_rows(seed_a, epoch.data_ptr(), row0, B, A, an, A, s), "actor noise")
+        N.check(lib.rl2_normal_noise_rows(seed_a, epoch.data_ptr(), BG + row0, B, A, an + 4 * B * A, A, s),
+                "actor noise (next observations)")
+        N.check(lib.rl2_normal_noise_rows(seed_n, epoch.data_ptr(), row0, B, A, L.next_noise.data_ptr(), A, s),
                 "next noise")
 
     def advance():
         N.check(lib.rl2_counter_advance(epoch.data_ptr(), 1, N.stream_ptr()), "advance epoch")
 
     sample.keep = g
-    sample.launches, make_noise.launches, advance.launches = 2, 2, 1
+    sample.launches, make_noise.launches, advance.launches = 2, 3, 1
     return [sample, make_noise, advance] if noise else [sample, advance]
 
 
-def replay_indices(learner):
+def replay_indices(learner, rows: int | None = None):
+    """The learner's replay-index buffer (the global batch's indices under data parallelism)."""
     import torch
 
-    if not hasattr(learner, "_indices"):
-        learner._indices = torch.zeros(learner.B, dtype=torch.int32, device=learner.device)
+    rows = rows or learner.B
+    if not hasattr(learner, "_indices") or learner._indices.numel() < rows:
+        learner._indices = torch.zeros(rows, dtype=torch.int32, device=learner.device)
     return learner._indices

@@ -1,0 +1,61 @@
+"""Host-side logic of data-parallel FlashSAC on CPU ranks (gloo, world size 2): the
+batch-norm partial all-gather layout, mean / max reductions and row slicing."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from robolearn_b200.flashsac.dp import DataParallel
+
+        dp = DataParallel()
+        T, G, C = 2, 3, 5
+        local = torch.arange(T * G * C, dtype=torch.float32).view(T, G, C) + 1000 * rank
+        big = torch.zeros(T, world * G, C + 2)  # wider buffer: only the [T][W*G][C] prefix is used
+        dp.gather_groups(local, big, T, G, C)
+        flat = big.view(-1)[: T * world * G * C].view(T, world * G, C)
+        ok = True
+        for t in range(T):
+            for r in range(world):
+                ok &= torch.equal(flat[t, r * G:(r + 1) * G], torch.arange(T * G * C).view(T, G, C)[t] + 1000 * r)
+        x = torch.tensor([float(rank + 1), 10.0 * rank])
+        dp.all_reduce_mean(x)
+        ok &= torch.allclose(x, torch.tensor([1.5, 5.0]))
+        y = torch.tensor([float(rank)])
+        dp.all_reduce_max(y)
+        ok &= y.item() == world - 1
+        ok &= dp.row_slice(8) == (4 * rank, 4)
+        out[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_data_parallel_collectives_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, out)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            assert p.exitcode == 0
+        assert dict(out) == {0: True, 1: True}
