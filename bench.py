@@ -50,6 +50,7 @@ def parse():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-ppo", action="store_true", help="leave the PPO summary out of the FlashSAC line")
     p.add_argument("--workload", choices=("flashsac", "ppo"), default="flashsac",
                    help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms)")
     return p.parse_args()
@@ -502,7 +503,7 @@ def main():
         out["cpu_baseline"] = {"value": rate * sample / BATCH, "unit": "updates/s", "cores": cores, "kind": "port",
                                "sample": f"one actor+critic update pair at batch {sample} ({csec:.1f} s), "
                                          f"rate scaled to batch {BATCH}"}
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_ppo:
         # the cfg2 PPO update beside the headline (full line: --workload ppo)
         import types
 

@@ -867,9 +867,9 @@ extern "C" int rl2_gemm_tile_n(void* opaque) {
 namespace rl2 {
 namespace gemm {
 __global__ void split_reduce_kernel(const float* __restrict__ part, long long stride, int splits,
-                                    float* __restrict__ out, long long count, int accumulate) {
+                                    float* __restrict__ out, long long count, int accumulate, int allow_vec) {
     const long long n4 = count / 4;
-    const bool vec = (stride % 4 == 0) && ptx::aligned16(part) && ptx::aligned16(out);
+    const bool vec = allow_vec && (stride % 4 == 0) && ptx::aligned16(part) && ptx::aligned16(out);
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < (vec ? n4 : count);
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         if (vec) {
@@ -911,9 +911,12 @@ extern "C" int rl2_split_reduce(const float* partial, long long split_stride, in
         set_error("split reduce needs non-null buffers, splits >= 1 and split_stride >= count");
         return -1;
     }
-    const long long work = count / 4 + 1;
-    const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 148LL * 8));
+    // small outputs: one thread per element (more loads in flight than float4 threads);
+    // large outputs: float4 per thread
+    const int vec = count > (1LL << 22) ? 1 : 0;
+    const long long work = vec ? count / 4 + 1 : count;
+    const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 148LL * 16));
     gemm::split_reduce_kernel<<<blocks, 256, 0, as_stream(stream)>>>(partial, split_stride, splits, out, count,
-                                                                      accumulate);
+                                                                      accumulate, vec);
     return launch_status("split-K reduce");
 }

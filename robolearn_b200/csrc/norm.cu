@@ -69,10 +69,19 @@ __global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ 
     if (c < cols) {
         const float* mp = mean_p + t * pt + c;
         const float* qp = m2_p + t * pt + c;
-        for (int g = g0; g < g1; ++g) {
-            const float ng = static_cast<float>(min(32, rows - g * 32));
-            const long long o = static_cast<long long>(g / gpr) * rs + static_cast<long long>(g % gpr) * cols;
-            chan_merge(n, mu, m2, ng, mp[o], qp[o]);
+        // eight groups' partials are loaded before they are merged (same merge order)
+        for (int g = g0; g < g1; g += 8) {
+            float pm[8], pq[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int gg = g + j;
+                const long long o = static_cast<long long>(gg / gpr) * rs + static_cast<long long>(gg % gpr) * cols;
+                pm[j] = gg < g1 ? mp[o] : 0.0f;
+                pq[j] = gg < g1 ? qp[o] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (g + j < g1) chan_merge(n, mu, m2, static_cast<float>(min(32, rows - (g + j) * 32)), pm[j], pq[j]);
         }
     }
     sh[0][warp][lane] = n;
@@ -240,11 +249,23 @@ __global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, cons
     const int g0 = warp * per, g1 = min(groups, g0 + per);
     float s1 = 0.0f, s2 = 0.0f;
     if (c < cols) {
-        for (int g = g0; g < g1; ++g) {
-            const long long o = static_cast<long long>(t) * pt + static_cast<long long>(g / gpr) * rs +
-                                static_cast<long long>(g % gpr) * cols + c;
-            s1 += s1p[o];
-            s2 += s2p[o];
+        for (int g = g0; g < g1; g += 8) {
+            float a[8], b[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int gg = g + j;
+                const long long o = static_cast<long long>(t) * pt + static_cast<long long>(gg / gpr) * rs +
+                                    static_cast<long long>(gg % gpr) * cols + c;
+                a[j] = gg < g1 ? s1p[o] : 0.0f;
+                b[j] = gg < g1 ? s2p[o] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (g + j < g1) {
+                    s1 += a[j];
+                    s2 += b[j];
+                }
+            }
         }
     }
     sh[0][warp][lane] = s1;
@@ -364,15 +385,19 @@ __global__ void rms_dgamma_kernel(const float* __restrict__ du, long long lddu, 
 }
 
 // out[t][c] (+)= sum_g part[t][g][c]. Block (32 columns, twin t); warp w sums the contiguous
-// group range w of 8 (lane = column, coalesced rows), then warp 0 adds the eight partial
-// sums in warp order: a fixed order for given (groups, cols).
-__global__ void colsum_finalize_kernel(const float* part, int twins, int groups, int cols, float* out, long long ots,
-                                       int accumulate) {
-    __shared__ float sh[kT / 32][32];
+// group range w of 32 (lane = column, coalesced rows), then warp 0 adds the partial sums
+// in warp order: a fixed order for given (groups, cols).
+constexpr int kColsumThreads = 1024;
+
+__global__ void __launch_bounds__(kColsumThreads) colsum_finalize_kernel(const float* part, int twins, int groups,
+                                                                        int cols, float* out, long long ots,
+                                                                        int accumulate) {
+    constexpr int kW = kColsumThreads / 32;
+    __shared__ float sh[kW][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.y;
     const int c = blockIdx.x * 32 + lane;
-    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int per = (groups + kW - 1) / kW;
     const int g0 = min(warp * per, groups), g1 = min(g0 + per, groups);
     float s = 0.0f;
     if (c < cols) {
@@ -390,7 +415,7 @@ __global__ void colsum_finalize_kernel(const float* part, int twins, int groups,
     if (warp == 0 && c < cols) {
         float r = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kT / 32; ++w) r += sh[w][lane];
+        for (int w = 0; w < kW; ++w) r += sh[w][lane];
         float* o = out + t * ots + c;
         *o = accumulate ? *o + r : r;
     }
@@ -590,7 +615,7 @@ extern "C" int rl2_colsum_finalize(const float* part, int twins, int groups, int
         set_error("colsum finalize: invalid arguments");
         return -1;
     }
-    norm::colsum_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
+    norm::colsum_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kColsumThreads, 0, as_stream(stream)>>>(
         part, twins, groups, cols, out, ots, accumulate);
     return launch_status("column-sum finalize");
 }
