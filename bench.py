@@ -51,7 +51,7 @@ def parse():
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ppo", action="store_true", help="leave the PPO summary out of the FlashSAC line")
-    p.add_argument("--workload", choices=("flashsac", "ppo"), default="flashsac",
+    p.add_argument("--workload", choices=("flashsac", "ppo", "categorical"), default="flashsac",
                    help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms)")
     return p.parse_args()
 
@@ -424,6 +424,99 @@ def run_ppo(args) -> dict:
     return out
 
 
+# ---------------------------------------------------------------------------
+# categorical critic objective microbench
+# ---------------------------------------------------------------------------
+CAT_METRIC = "categorical critic objective us/launch (B 65536, 101 atoms, twin logits, fp32 dlogits)"
+CAT_B, CAT_BINS = 65536, 101
+
+
+def categorical_inputs(device, seed: int = 0) -> dict:
+    """Target and online logits [2][B][101] ~N(0,1), rewards ~N(0,1), discount 0.99,
+    done ~Bernoulli(0.01), next log-probs ~N(0,1), alpha 0.01."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(4000 + seed)
+    B, K = CAT_B, CAT_BINS
+    return {"target": torch.randn(2, B, K, device=device, generator=g),
+            "online": torch.randn(2, B, K, device=device, generator=g),
+            "reward": torch.randn(B, device=device, generator=g),
+            "terminated": (torch.rand(B, device=device, generator=g) < 0.01).float(),
+            "discount": torch.full((B,), 0.99, device=device),
+            "next_log_pi": torch.randn(B, device=device, generator=g),
+            "alpha": torch.full((1,), 0.01, device=device)}
+
+
+def categorical_bytes() -> int:
+    # read target + online logits, write dlogits (fp32), read 4 per-row vectors
+    return 3 * 2 * CAT_B * CAT_BINS * 4 + 4 * CAT_B * 4
+
+
+def run_categorical(args) -> dict:
+    import torch
+
+    from robolearn_b200.categorical import CriticObjective
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    x = categorical_inputs(device)
+    obj = CriticObjective(CAT_B, CAT_BINS, -10.0, 10.0, device=device)
+    dlogits = torch.zeros(2, CAT_B, CAT_BINS, device=device)
+    loss = torch.zeros(1, device=device)
+    mx = torch.zeros(1, device=device)
+
+    def launch():
+        obj.run(target_logits=x["target"], target_row_stride=CAT_BINS, target_twin_stride=CAT_B * CAT_BINS,
+                target_row_offset=0, online_logits=x["online"], online_row_stride=CAT_BINS,
+                online_twin_stride=CAT_B * CAT_BINS, reward=x["reward"], terminated=x["terminated"],
+                discount=x["discount"], next_log_pi=x["next_log_pi"], alpha=x["alpha"], loss_weight=1.0 / (2 * CAT_B),
+                loss_out=loss, max_entropy_out=mx, dlogits=dlogits, dlogits_row_stride=CAT_BINS,
+                dlogits_twin_stride=CAT_B * CAT_BINS)
+
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MB > L2
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        launch()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    us = statistics.median(times)
+    pk, src = peaks()
+    gbs = categorical_bytes() / (us * 1e-6) / 1e9
+    out = {"metric": CAT_METRIC, "value": us, "unit": "us/launch", "higher_is_better": False, "ms_per_step": us / 1e3,
+           "gpu_launches": 1, "dtype": "f32", "rows_per_s": CAT_B / (us * 1e-6),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
+                        "algorithmic_bytes": categorical_bytes(), "peak_source": f"{src} hbm_gbs"},
+           "config": {"workload": "cfg4 categorical projection + CE + gradient, B 65536, 101 atoms on [-10, 10], "
+                                  "both twins", "l2": "L2 flushed (256 MB write) before every timed launch",
+                      "timing": "median of per-launch CUDA-event times"}}
+    if not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import flashsac_np as fs
+
+        xs = {k: v.cpu().numpy() for k, v in x.items()}
+        t0 = time.perf_counter()
+        tl = xs["target"] - np.log(np.exp(xs["target"]).sum(-1, keepdims=True))
+        q = (np.exp(tl) * fs.support(CAT_BINS, -10.0, 10.0)).sum(-1)
+        lp = fs.select_min_q(q, tl)
+        ent = 0.01 * xs["next_log_pi"]
+        tgt, _ = fs.categorical_target(lp, xs["reward"], xs["terminated"], ent, 0.99, CAT_BINS, -10.0, 10.0)
+        ol = xs["online"] - np.log(np.exp(xs["online"]).sum(-1, keepdims=True))
+        fs.categorical_loss_grad(ol, tgt, CAT_B)
+        sec = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sec * 1e6, "unit": "us/launch", "cores": len(os.sched_getaffinity(0)),
+                               "kind": "port", "sample": "one full launch (B 65536) of the numpy restatement"}
+    return out
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -431,6 +524,13 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     base = {"metric": METRIC, "unit": "updates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "categorical":
+        if rank != 0:
+            return
+        out = dict(n_gpus=1, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None, data="synthetic",
+                   impl="b200", **run_categorical(args))
+        print(json.dumps(out))
+        return
     if args.workload == "ppo":
         if rank != 0:
             return

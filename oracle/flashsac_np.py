@@ -567,16 +567,18 @@ class Hyper:
     decay: int = 10_000
     target_entropy: float = 0.0
     bc_alpha: float = 0.0
+    adam: str = "torch"  # "torch" (FlashSAC) or "warp" (Warp-NN formula, WarpFlashSAC)
 
 
-def _adam_net(params: dict, grads: dict, opt: OptState, names: list[str], lr: float, dtype):
+def _adam_net(params: dict, grads: dict, opt: OptState, names: list[str], lr: float, dtype, formula: str = "torch"):
     opt.step += 1
     out = dict(params)
+    rule = adam_warp if formula == "warp" else adam_torch
     for k in names:
         p = params[k].astype(dtype)
         m = opt.m.get(k, np.zeros_like(p))
         v = opt.v.get(k, np.zeros_like(p))
-        out[k], opt.m[k], opt.v[k] = adam_torch(p, grads[k].astype(dtype), m, v, opt.step, lr)
+        out[k], opt.m[k], opt.v[k] = rule(p, grads[k].astype(dtype), m, v, opt.step, lr)
     return out
 
 
@@ -644,14 +646,15 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
         metrics["actor/mean_action"] = acts.mean()
         lr = warmup_cosine(opt_a.step, h.lr_init, h.lr_peak, h.lr_end, h.warmup, h.decay)
         actor = _apply_stats(actor, a_stats)
-        actor = _adam_net(actor, grads, opt_a, a_names, lr, dtype)
+        actor = _adam_net(actor, grads, opt_a, a_names, lr, dtype, h.adam)
         actor = project(actor, a_names, False, d.actor_blocks)
         # ---- update_temperature (updates.py:297-326)
         tval = math.exp(log_temp)
         t_loss = tval * (entropy - h.target_entropy)
         g_t = np.array([tval * (entropy - h.target_entropy)])
         lr_t = warmup_cosine(opt_t.step, h.lr_init, h.lr_peak, h.lr_end, h.warmup, h.decay)
-        tp = _adam_net({"log_temp": np.array([log_temp])}, {"log_temp": g_t}, opt_t, ["log_temp"], lr_t, dtype)
+        tp = _adam_net({"log_temp": np.array([log_temp])}, {"log_temp": g_t}, opt_t, ["log_temp"], lr_t, dtype,
+                       h.adam)
         log_temp = float(tp["log_temp"][0])
         metrics["temperature/value"] = tval
         metrics["temperature/loss"] = t_loss
@@ -675,7 +678,7 @@ def update_networks(state: dict, batch: dict, actor_noise, next_noise, d: Dims, 
     grads_out["critic"] = grads
     lr = warmup_cosine(opt_c.step, h.lr_init, h.lr_peak, h.lr_end, h.warmup, h.decay)
     critic = _apply_stats(critic, c_stats)
-    critic = _adam_net(critic, grads, opt_c, c_names, lr, dtype)
+    critic = _adam_net(critic, grads, opt_c, c_names, lr, dtype, h.adam)
     critic = project(critic, c_names, True, d.critic_blocks)
     # ---- update_target_network (updates.py:287-294)
     target = ema(target, critic, c_names, h.tau)

@@ -70,7 +70,7 @@ class FlashSAC:
     """Tensor agent for a vectorized environment (actions in normalised [-1, 1])."""
 
     def __init__(self, observation_dim: int, action_dim: int, num_envs: int = 1, cfg: FlashSACConfig | None = None,
-                 critic_observation_dim: int | None = None):
+                 critic_observation_dim: int | None = None, *, _adam_formula: int = 0):
         cfg = cfg or FlashSACConfig()
         if min(observation_dim, action_dim, num_envs) <= 0:
             raise ValueError("Observation, action, and environment dimensions must be positive.")
@@ -94,7 +94,7 @@ class FlashSAC:
             device = torch.device("cuda", torch.cuda.current_device())
         self._device = device
         torch.manual_seed(cfg.seed)
-        self._learner = L = Learner(observation_dim, total_dim, action_dim, cfg, device)
+        self._learner = L = Learner(observation_dim, total_dim, action_dim, cfg, device, adam_formula=_adam_formula)
         self._replay = DeviceReplay(total_dim, action_dim, num_envs, cfg.buffer_max_length, cfg.n_step, cfg.gamma,
                                     cfg.buffer_min_length, device, seed=cfg.seed)
         f32 = dict(dtype=torch.float32, device=device)

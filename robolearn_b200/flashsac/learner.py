@@ -208,6 +208,7 @@ class Learner:
         self.critic_run = Run(self.critic, 2 * B, True, self.critic_x.data_ptr(), self.ldx, update_running=True,
                               need_param_grads=True, need_input_grad=False, scaler=scc, pool=pc_online, dp=self.dp)
         self.graphs = {}
+        self._extra_programs = {}
         self.programs = {True: self._program(True), False: self._program(False)}
 
     # ------------------------------------------------------------------
@@ -249,7 +250,9 @@ class Learner:
         launch.launches = 2
         return launch
 
-    def _program(self, actor_phase: bool):
+    def _program(self, actor_phase: bool, apply_optimizer: bool = True):
+        """Launch list of one phase; ``apply_optimizer=False`` stops after the gradients
+        (no Adam / projection / EMA / temperature step), for diagnostics."""
         cfg, lib, B, A = self.cfg, self.lib, self.B, self.act
         prog = []
         m = self.metrics.data_ptr()
@@ -300,7 +303,8 @@ class Learner:
 
             prog.append(bias_fin)
             prog += self.actor_train.backward_program
-            prog.append(self._optimizer("actor", self.actor))
+            if apply_optimizer:
+                prog.append(self._optimizer("actor", self.actor))
             temp = N.TemperatureArgs(
                 log_temp=self.log_temp.data_ptr(), entropy=mi["actor/entropy"], target_entropy=self.target_entropy,
                 adam_state=self.temp_state.data_ptr(), beta1=0.9, beta2=0.999, eps=1e-8,
@@ -312,7 +316,8 @@ class Learner:
                 ent = self.metrics[METRIC_KEYS.index("actor/entropy"):METRIC_KEYS.index("actor/entropy") + 1]
                 prog.append(lambda ent=ent: self.dp.all_reduce_mean(ent))
                 prog[-1].launches = 0
-            prog.append(_wrap(lib.rl2_temperature_step, temp, None, "temperature step"))
+            if apply_optimizer:
+                prog.append(_wrap(lib.rl2_temperature_step, temp, None, "temperature step"))
         else:
             temp = N.TemperatureArgs(log_temp=self.log_temp.data_ptr(), update=0, alpha_out=self.alpha.data_ptr())
             prog.append(_wrap(lib.rl2_temperature_step, temp, None, "alpha"))
@@ -348,7 +353,8 @@ class Learner:
             co.dplane_twin_stride = cr.dhead.tstride
         prog.append(_wrap(lib.rl2_critic_objective, co, None, "critic objective"))
         prog += self.critic_run.backward_program
-        prog.append(self._optimizer("critic", self.critic, target=self.target))
+        if apply_optimizer:
+            prog.append(self._optimizer("critic", self.critic, target=self.target))
         if self.dp is not None:  # reported metrics over the global batch
             mx = METRIC_KEYS.index("critic/max_entropy_bonus")
 
@@ -382,8 +388,16 @@ class Learner:
         if next_noise is not None:
             self.next_noise.copy_(torch.as_tensor(next_noise, dtype=torch.float32, device=self.device))
 
-    def run(self, actor_phase: bool) -> None:
-        for f in self.programs[actor_phase]:
+    def program(self, actor_phase: bool, apply_optimizer: bool = True) -> list:
+        if apply_optimizer:
+            return self.programs[actor_phase]
+        key = (actor_phase, False)
+        if key not in self._extra_programs:
+            self._extra_programs[key] = self._program(actor_phase, apply_optimizer=False)
+        return self._extra_programs[key]
+
+    def run(self, actor_phase: bool, apply_optimizer: bool = True) -> None:
+        for f in self.program(actor_phase, apply_optimizer):
             f()
 
     def capture(self, actor_phase: bool, pre=()) -> torch.cuda.CUDAGraph:
