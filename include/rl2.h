@@ -732,6 +732,50 @@ typedef struct rl2_ppo_store_args {
 
 int rl2_ppo_store(const rl2_ppo_store_args* args, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Data-parallel batch-norm statistics over NVLink peer memory (one kernel per BN
+ * layer, no collective library call). Replaces, for the data-parallel learner, the
+ * all-gather + merge of per-group partials; the reference has no multi-GPU path
+ * (its SyncBN design is the build's own, following the global-batch semantics of
+ * src/robolearn/flashsac/layers.py:32-64 / updates.py:226-230).
+ *
+ * Every rank first merges its own per-32-row-group partials ([part_twins][G][cols],
+ * twin stride part_twin_stride; part_twins = 1 shares one set across the twins) into one
+ * entry per column, pushes the entry into every rank's exchange slot (plain stores
+ * through peer pointers), raises a per-(column slab, rank) flag with the slot's epoch on
+ * every rank, waits (bounded: timeout_s, then kHealthTimeout in *health) for all ranks'
+ * flags of its slab and merges the ranks' entries in rank order: bit-identical results
+ * on every rank. Epochs advance on the device (graph-capturable).
+ *
+ * Exchange slot layout (every rank): data [world][twins][2][cols] floats at
+ * peer_data[r]; flags [twins * ceil(cols / 32)][world] u64 at peer_flags[r]; epoch[2]
+ * (use counter, block ticket) local, zero-initialised. rows = this rank's rows.
+ * ------------------------------------------------------------------------- */
+typedef struct rl2_syncbn_exchange {
+    float* const* peer_data;               /* device array [world] */
+    unsigned long long* const* peer_flags; /* device array [world] */
+    unsigned int* epoch;                   /* 2 words, this rank */
+    int world, rank;
+    int* health;
+    float timeout_s;
+} rl2_syncbn_exchange;
+
+/* Forward: global mean / invstd (and running statistics, unbiased by world * rows). */
+int rl2_syncbn_forward(const float* mean_part, const float* m2_part, long long part_twin_stride, int part_twins,
+                       int twins, int rows, int cols, float* mean, float* invstd, float* running_mean,
+                       float* running_var, float momentum, float eps, int update_running,
+                       const rl2_syncbn_exchange* ex, void* stream);
+
+/* Backward: dgamma / dbeta from this rank's rows (optional), coef1 / coef2 from the
+ * global sums (sum over all ranks' rows / (world * rows)). */
+int rl2_syncbn_backward(const float* s1_part, const float* s2_part, long long part_twin_stride, int twins, int rows,
+                        int cols, float* dgamma, float* dbeta, long long dgamma_twin_stride, float* coef1,
+                        float* coef2, const rl2_syncbn_exchange* ex, void* stream);
+
+/* Bytes of one exchange slot's data and flag regions for (world, twins, cols). */
+long long rl2_syncbn_slot_data_bytes(int world, int twins, int cols);
+long long rl2_syncbn_slot_flag_bytes(int world, int twins, int cols);
+
 #ifdef __cplusplus
 }
 #endif

@@ -348,3 +348,18 @@ SIGNATURES.update({
     "rl2_bn_finalize_ranked": ([P, P, LL, I, LL, I, I, I, P, P, P, P, F, F, I, P], I),
     "rl2_bn_backward_finalize_ranked": ([P, P, LL, I, LL, I, I, I, P, P, LL, I, P, P, P], I),
 })
+
+
+class SyncBNExchange(ctypes.Structure):
+    """``rl2_syncbn_exchange`` (include/rl2.h)."""
+
+    _fields_ = [("peer_data", P), ("peer_flags", P), ("epoch", P), ("world", I), ("rank", I), ("health", P),
+                ("timeout_s", F)]
+
+
+SIGNATURES.update({
+    "rl2_syncbn_forward": ([P, P, LL, I, I, I, I, P, P, P, P, F, F, I, ctypes.POINTER(SyncBNExchange), P], I),
+    "rl2_syncbn_backward": ([P, P, LL, I, I, I, P, P, LL, P, P, ctypes.POINTER(SyncBNExchange), P], I),
+    "rl2_syncbn_slot_data_bytes": ([I, I, I], LL),
+    "rl2_syncbn_slot_flag_bytes": ([I, I, I], LL),
+})

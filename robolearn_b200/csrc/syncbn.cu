@@ -1,0 +1,281 @@
+// Data-parallel batch-norm statistics exchanged through NVLink peer memory.
+//
+// One kernel per BN layer and direction. Block (slab of 32 columns, twin t), 8 warps:
+// the warps merge this rank's per-32-row-group partials (contiguous group ranges,
+// fixed order); warp 0 pushes the per-column entry into every rank's exchange slot
+// with plain peer stores, fences at system scope and raises one epoch flag per rank for
+// its slab, then polls its own slot's flags (acquire loads, bounded by wall-clock time)
+// and merges the ranks' entries in rank order. Blocks never wait on one another, and a
+// wait that runs out records kHealthTimeout and returns.
+
+#include "common.cuh"
+#include "../../include/rl2.h"
+
+namespace rl2 {
+namespace syncbn {
+
+constexpr int kT = 256;
+constexpr int kW = kT / 32;
+
+__device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_a, float n_b, float mean_b,
+                                           float m2_b) {
+    if (n_b <= 0.0f) return;
+    const float n = n_a + n_b;
+    const float delta = mean_b - mean_a;
+    mean_a = mean_a + delta * (n_b / n);
+    m2_a = m2_a + m2_b + delta * delta * (n_a * n_b / n);
+    n_a = n;
+}
+
+__device__ __forceinline__ unsigned long long load_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void store_release(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Warp 0: push two per-column values of this rank to every rank, flag the slab, wait for
+// every rank's flag of the slab. Returns false on a timeout (recorded in *health).
+__device__ bool exchange(const rl2_syncbn_exchange& ex, int twins, int t, int cols, int c, float a, float b,
+                         unsigned long long epoch) {
+    const int lane = threadIdx.x & 31;
+    const int W = ex.world;
+    const int slabs = (cols + 31) / 32;
+    const long long flag_index = (static_cast<long long>(t) * slabs + blockIdx.x) * W;
+    if (c < cols) {
+        for (int p = 0; p < W; ++p) {
+            float* dst = ex.peer_data[p] + (static_cast<long long>(ex.rank) * twins + t) * 2 * cols;
+            dst[c] = a;
+            dst[cols + c] = b;
+        }
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane < W) store_release(ex.peer_flags[lane] + flag_index + ex.rank, epoch);
+    bool ok = true;
+    if (lane < W) {
+        const unsigned long long* f = ex.peer_flags[ex.rank] + flag_index + lane;
+        if (load_acquire(f) < epoch) {
+            const uint64_t start = now_ns();
+            const uint64_t limit = static_cast<uint64_t>(ex.timeout_s * 1e9f);
+            for (uint32_t i = 1;; ++i) {
+                if (load_acquire(f) >= epoch) break;
+                if ((i & 255u) == 0 && now_ns() - start > limit) {
+                    ok = false;
+                    if (ex.health) atomicOr(ex.health, kHealthTimeout);
+                    break;
+                }
+            }
+        }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    __threadfence_system();
+    return ok;
+}
+
+// Epoch of this launch (read by every block before it takes its ticket) and advance by
+// the last block to finish.
+__device__ __forceinline__ unsigned long long launch_epoch(const rl2_syncbn_exchange& ex) {
+    return static_cast<unsigned long long>(*reinterpret_cast<volatile unsigned int*>(ex.epoch)) + 1ull;
+}
+
+__device__ __forceinline__ void finish_launch(const rl2_syncbn_exchange& ex, unsigned long long epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int blocks = gridDim.x * gridDim.y;
+        const unsigned int ticket = atomicAdd(ex.epoch + 1, 1u);
+        if (ticket == blocks - 1) {
+            ex.epoch[1] = 0u;
+            ex.epoch[0] = static_cast<unsigned int>(epoch);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kT) forward_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p,
+                                                     long long pt, int twins, int rows, int cols, float* mean,
+                                                     float* invstd, float* rm, float* rv, float momentum, float eps,
+                                                     int update, const rl2_syncbn_exchange ex) {
+    __shared__ float sh[3][kW][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * 32 + lane;
+    const unsigned long long epoch = launch_epoch(ex);
+    // this rank's groups, eight loaded ahead of the fixed-order merge
+    const int groups = (rows + 31) / 32;
+    const int per = (groups + kW - 1) / kW;
+    const int g0 = min(warp * per, groups), g1 = min(g0 + per, groups);
+    float n = 0.0f, mu = 0.0f, m2 = 0.0f;
+    if (c < cols) {
+        const float* mp = mean_p + t * pt + c;
+        const float* qp = m2_p + t * pt + c;
+        for (int g = g0; g < g1; g += 8) {
+            float a[8], b[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                a[j] = g + j < g1 ? mp[static_cast<long long>(g + j) * cols] : 0.0f;
+                b[j] = g + j < g1 ? qp[static_cast<long long>(g + j) * cols] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (g + j < g1) chan_merge(n, mu, m2, static_cast<float>(min(32, rows - (g + j) * 32)), a[j], b[j]);
+        }
+    }
+    sh[0][warp][lane] = n;
+    sh[1][warp][lane] = mu;
+    sh[2][warp][lane] = m2;
+    __syncthreads();
+    if (warp == 0) {
+        n = sh[0][0][lane];
+        mu = sh[1][0][lane];
+        m2 = sh[2][0][lane];
+        for (int w = 1; w < kW; ++w) chan_merge(n, mu, m2, sh[0][w][lane], sh[1][w][lane], sh[2][w][lane]);
+        exchange(ex, twins, t, cols, c, mu, m2, epoch);
+        if (c < cols) {
+            // all ranks' entries, rank order (each rank holds `rows` rows)
+            float gn = 0.0f, gmu = 0.0f, gm2 = 0.0f;
+            const float* base = ex.peer_data[ex.rank];
+            for (int r = 0; r < ex.world; ++r) {
+                const float* src = base + (static_cast<long long>(r) * twins + t) * 2 * cols;
+                chan_merge(gn, gmu, gm2, static_cast<float>(rows), __ldcv(src + c), __ldcv(src + cols + c));
+            }
+            const int i = t * cols + c;
+            const float total = static_cast<float>(rows) * ex.world;
+            const float var = gm2 / total;
+            mean[i] = gmu;
+            invstd[i] = 1.0f / sqrtf(var + eps);
+            if (update) {
+                const float unbiased = var * (total / (total - 1.0f));
+                rm[i] = rm[i] + momentum * (gmu - rm[i]);
+                rv[i] = rv[i] + momentum * (unbiased - rv[i]);
+            }
+        }
+    }
+    finish_launch(ex, epoch);
+}
+
+__global__ void __launch_bounds__(kT) backward_kernel(const float* __restrict__ s1p, const float* __restrict__ s2p,
+                                                      long long pt, int twins, int rows, int cols, float* dgamma,
+                                                      float* dbeta, long long gts, float* coef1, float* coef2,
+                                                      const rl2_syncbn_exchange ex) {
+    __shared__ float sh[2][kW][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * 32 + lane;
+    const unsigned long long epoch = launch_epoch(ex);
+    const int groups = (rows + 31) / 32;
+    const int per = (groups + kW - 1) / kW;
+    const int g0 = min(warp * per, groups), g1 = min(g0 + per, groups);
+    float s1 = 0.0f, s2 = 0.0f;
+    if (c < cols) {
+        const float* a = s1p + t * pt + c;
+        const float* b = s2p + t * pt + c;
+        for (int g = g0; g < g1; g += 8) {
+            float x[8], y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                x[j] = g + j < g1 ? a[static_cast<long long>(g + j) * cols] : 0.0f;
+                y[j] = g + j < g1 ? b[static_cast<long long>(g + j) * cols] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (g + j < g1) {
+                    s1 += x[j];
+                    s2 += y[j];
+                }
+            }
+        }
+    }
+    sh[0][warp][lane] = s1;
+    sh[1][warp][lane] = s2;
+    __syncthreads();
+    if (warp == 0) {
+        s1 = 0.0f;
+        s2 = 0.0f;
+        for (int w = 0; w < kW; ++w) {
+            s1 += sh[0][w][lane];
+            s2 += sh[1][w][lane];
+        }
+        // gamma / beta gradients of this rank's rows (averaged with the other gradients later)
+        if (c < cols) {
+            if (dgamma) dgamma[t * gts + c] = s2;
+            if (dbeta) dbeta[t * gts + c] = s1;
+        }
+        exchange(ex, twins, t, cols, c, s1, s2, epoch);
+        if (c < cols) {
+            float g1s = 0.0f, g2s = 0.0f;
+            const float* base = ex.peer_data[ex.rank];
+            for (int r = 0; r < ex.world; ++r) {
+                const float* src = base + (static_cast<long long>(r) * twins + t) * 2 * cols;
+                g1s += __ldcv(src + c);
+                g2s += __ldcv(src + cols + c);
+            }
+            const float total = static_cast<float>(rows) * ex.world;
+            coef1[t * cols + c] = g1s / total;
+            coef2[t * cols + c] = g2s / total;
+        }
+    }
+    finish_launch(ex, epoch);
+}
+
+}  // namespace syncbn
+}  // namespace rl2
+
+using namespace rl2;
+
+namespace {
+bool exchange_valid(const rl2_syncbn_exchange* ex) {
+    return ex && ex->peer_data && ex->peer_flags && ex->epoch && ex->world >= 1 && ex->world <= 32 && ex->rank >= 0 &&
+           ex->rank < ex->world && ex->timeout_s > 0.0f;
+}
+
+// Every block of a launch must be resident while peers wait on its flags: keep the grid
+// within a few blocks per SM.
+bool grid_resident(int twins, int cols) { return static_cast<long long>(twins) * ((cols + 31) / 32) <= 148LL * 4; }
+}  // namespace
+
+extern "C" long long rl2_syncbn_slot_data_bytes(int world, int twins, int cols) {
+    return static_cast<long long>(world) * twins * 2 * cols * 4;
+}
+
+extern "C" long long rl2_syncbn_slot_flag_bytes(int world, int twins, int cols) {
+    return static_cast<long long>(twins) * ((cols + 31) / 32) * world * 8;
+}
+
+extern "C" int rl2_syncbn_forward(const float* mean_p, const float* m2_p, long long pt, int part_twins, int twins,
+                                  int rows, int cols, float* mean, float* invstd, float* rm, float* rv, float momentum,
+                                  float eps, int update, const rl2_syncbn_exchange* ex, void* stream) {
+    clear_error();
+    if (!mean_p || !m2_p || !mean || !invstd || twins < 1 || rows < 1 || cols < 1 || !(eps > 0.0f) ||
+        (part_twins != 1 && part_twins != twins) || (update && (!rm || !rv)) || !exchange_valid(ex) ||
+        !grid_resident(twins, cols)) {
+        set_error("syncbn forward: invalid arguments");
+        return -1;
+    }
+    syncbn::forward_kernel<<<dim3((cols + 31) / 32, twins), syncbn::kT, 0, as_stream(stream)>>>(
+        mean_p, m2_p, part_twins == 1 ? 0 : pt, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update, *ex);
+    return launch_status("data-parallel batch-norm statistics");
+}
+
+extern "C" int rl2_syncbn_backward(const float* s1p, const float* s2p, long long pt, int twins, int rows, int cols,
+                                   float* dgamma, float* dbeta, long long gts, float* coef1, float* coef2,
+                                   const rl2_syncbn_exchange* ex, void* stream) {
+    clear_error();
+    if (!s1p || !s2p || !coef1 || !coef2 || twins < 1 || rows < 1 || cols < 1 || !exchange_valid(ex) ||
+        !grid_resident(twins, cols)) {
+        set_error("syncbn backward: invalid arguments");
+        return -1;
+    }
+    syncbn::backward_kernel<<<dim3((cols + 31) / 32, twins), syncbn::kT, 0, as_stream(stream)>>>(
+        s1p, s2p, pt, twins, rows, cols, dgamma, dbeta, gts, coef1, coef2, *ex);
+    return launch_status("data-parallel batch-norm backward sums");
+}

@@ -23,7 +23,10 @@ gradients of batch norm are reduced from LOCAL partials so that the final averag
 the global gradient.
 
 Collectives go through ``torch.distributed`` (NCCL on GPUs: AVG / MAX reductions and
-all-gather are recorded into the learner's CUDA graphs; gloo on CPU for tests).
+all-gather are recorded into the learner's CUDA graphs; gloo on CPU for tests). On
+NVLink-connected GPUs the batch-norm exchanges instead run inside one kernel per sync
+point over peer memory (``PeerExchange``): the all-gather's launch and protocol latency
+was most of the exchange time for these kilobyte-sized partials.
 """
 
 from __future__ import annotations
@@ -44,6 +47,18 @@ class DataParallel:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.nccl = dist.get_backend(group) == "nccl"
+        self.peer: PeerExchange | None = None
+
+    def enable_peer(self, device, slots: int, max_cols: int, health_ptr: int, timeout_s: float = 10.0) -> bool:
+        """Exchange batch-norm statistics through NVLink peer memory instead of NCCL all-gathers
+        (one kernel per sync point). Collective; needs NCCL ranks on GPUs of one node with
+        symmetric memory. ``RL2_DP_PEER=0`` keeps the all-gather path. Returns whether it is on."""
+        import os
+
+        if self.world == 1 or not self.nccl or os.environ.get("RL2_DP_PEER", "1") == "0":
+            return False
+        self.peer = PeerExchange(self, slots, max_cols, device, health_ptr=health_ptr, timeout_s=timeout_s)
+        return True
 
     # ---- reductions -------------------------------------------------------
     def all_reduce_mean(self, t: torch.Tensor) -> None:
@@ -81,3 +96,60 @@ class DataParallel:
             raise ValueError("the global batch must split evenly over the ranks")
         per = global_rows // self.world
         return self.rank * per, per
+
+
+class PeerExchange:
+    """NVLink peer-memory slots for the data-parallel batch-norm kernels.
+
+    One symmetric buffer per rank (``torch.distributed._symmetric_memory``: every rank
+    maps every other rank's buffer), split into ``slots`` equal slots, one per batch-norm
+    sync point of the learner's programs (assigned in program-construction order, the
+    same on every rank). A slot holds the ranks' per-column entries and per-(column
+    slab, rank) epoch flags; epochs live in a local device counter per slot.
+    """
+
+    def __init__(self, dp: DataParallel, slots: int, max_cols: int, device, twins: int = 2, health_ptr: int = 0,
+                 timeout_s: float = 10.0):
+        import torch.distributed._symmetric_memory as symm
+
+        from .. import _native as N
+
+        lib = N.load()
+        W = dp.world
+        align = lambda b: (int(b) + 255) // 256 * 256  # noqa: E731
+        self.data_bytes = align(lib.rl2_syncbn_slot_data_bytes(W, twins, max_cols))
+        self.flag_bytes = align(lib.rl2_syncbn_slot_flag_bytes(W, twins, max_cols))
+        self.slot_bytes = self.data_bytes + self.flag_bytes
+        self.slots, self.max_cols, self.twins, self.timeout_s = slots, max_cols, twins, timeout_s
+        self.buf = symm.empty(slots * self.slot_bytes // 4, dtype=torch.float32, device=device)
+        self.buf.zero_()
+        group = dp.group if dp.group is not None else dp.dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, group)
+        torch.cuda.synchronize(device)
+        dp.dist.barrier(group=dp.group)
+        self.ptrs = list(self.handle.buffer_ptrs)
+        self.world, self.rank = W, dp.rank
+        self.device = device
+        self.epochs = torch.zeros(2 * slots, dtype=torch.int32, device=device)
+        self.health_ptr = health_ptr or None
+        self.next = 0
+        self._keep: list = []
+
+    def slot(self, cols: int, twins: int):
+        """Exchange arguments of the next free slot (host struct; keep it alive while in use)."""
+        from .. import _native as N
+
+        if self.next >= self.slots:
+            raise RuntimeError("peer exchange: all batch-norm slots are in use")
+        if cols > self.max_cols or twins > self.twins:
+            raise ValueError("peer exchange: a batch-norm layer is wider than the slots")
+        s = self.next
+        self.next += 1
+        base = s * self.slot_bytes
+        data = torch.tensor([p + base for p in self.ptrs], dtype=torch.int64, device=self.device)
+        flags = torch.tensor([p + base + self.data_bytes for p in self.ptrs], dtype=torch.int64, device=self.device)
+        ex = N.SyncBNExchange(peer_data=data.data_ptr(), peer_flags=flags.data_ptr(),
+                              epoch=self.epochs.data_ptr() + 8 * s, world=self.world, rank=self.rank,
+                              health=self.health_ptr, timeout_s=self.timeout_s)
+        self._keep += [data, flags, ex]
+        return ex

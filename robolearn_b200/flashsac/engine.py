@@ -507,6 +507,16 @@ class Run:
         n = tw * self.G * C
         pmq = self.pmq
         dp = self.dp
+        if dp is not None and dp.peer is not None:  # one kernel: local merge, peer exchange, global merge
+            ex = dp.peer.slot(C, T)
+
+            def launch():
+                base = pmq.data_ptr()
+                N.check(lib.rl2_syncbn_forward(base, base + 4 * n, pt, tw, T, R, C, mean.data_ptr(), inv.data_ptr(),
+                                               rm.data_ptr(), rv.data_ptr(), BN_MOMENTUM, BN_EPS, upd,
+                                               ctypes.byref(ex), N.stream_ptr()), "bn statistics (peer exchange)")
+
+            return launch
         if dp is not None:  # one all-gather of every rank's packed partials, then a global merge
             gpmq, W, G = self.gpmq, dp.world, self.G
 
@@ -616,7 +626,16 @@ class Run:
             gts = C if self.T == 2 else 0
 
             dp = self.dp
-            if dp is None:
+            if dp is not None and dp.peer is not None:
+                # gamma / beta gradients from this rank's rows, dx coefficients from the
+                # global sums, exchanged over peer memory inside the kernel
+                ex = dp.peer.slot(C, T)
+
+                def fin():
+                    N.check(lib.rl2_syncbn_backward(s1p, s2p, self.G * C, T, R, C, gw, gb, gts, c1.data_ptr(),
+                                                    c2.data_ptr(), ctypes.byref(ex), N.stream_ptr()),
+                            "bn backward sums (peer exchange)")
+            elif dp is None:
                 def fin():
                     N.check(lib.rl2_bn_backward_finalize(s1p, s2p, T, R, C, gw, gb, gts, 0, c1.data_ptr(),
                                                          c2.data_ptr(), N.stream_ptr()), "bn backward finalize")

@@ -194,6 +194,12 @@ class Learner:
         self.counter = torch.zeros(2, dtype=torch.int32, device=device)
         self.objective = CriticObjective(B, bins, cfg.critic_min_v, cfg.critic_max_v, device=device)
         # ---- backbone runs
+        if self.dp is not None and self.dp.peer is None:
+            # one peer-exchange slot per batch-norm sync point: forward + backward of the
+            # actor and online critic, forward of the target critic
+            la, lc = self.actor.bn_layers, self.critic.bn_layers
+            self.dp.enable_peer(device, 2 * len(la) + 3 * len(lc), max(C for _, C in la + lc),
+                                self.health.data_ptr())
         pa, pa_eval, pc, pc_eval = {}, {}, {}, {}
         sa, scc = self.scalers["actor"], self.scalers["critic"]
         self.actor_train = Run(self.actor, 2 * B, True, self.actor_x.data_ptr(), self.ldax, update_running=True,

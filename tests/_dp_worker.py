@@ -3,7 +3,8 @@
 Every rank runs data-parallel FlashSAC updates with a per-rank batch of B; rank 0 also
 runs a single-GPU learner with the global batch world * B on the same replay, indices
 and noise, and writes the largest relative differences (per tensor) to a JSON file.
-The third update replays a CUDA graph that contains the NCCL collectives.
+The third update replays a CUDA graph that contains the NCCL collectives (and, with the
+peer exchange on, the batch-norm kernels that exchange statistics over NVLink).
 """
 
 import datetime
@@ -76,7 +77,9 @@ def main():
     dp = DataParallel()
     L, R, feed = make(B, dp, device, precision)
     single = make(B * dp.world, None, device, precision) if dp.rank == 0 else None
-    report = {"world": dp.world, "precision": precision, "updates": []}
+    torch.cuda.synchronize()
+    dist.barrier()  # rank 0 built a second learner: start the updates together
+    report = {"world": dp.world, "precision": precision, "peer": dp.peer is not None, "updates": []}
     phases = (True, False)
     for phase in phases:
         for f in feed:
@@ -108,6 +111,9 @@ def main():
     ok = torch.tensor([1 if same else 0], device=device)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     report["ranks_identical"] = bool(ok.item())
+    health = L.health.clone()
+    dist.all_reduce(health, op=dist.ReduceOp.MAX)
+    report["health"] = int(health.item())
     del graph, g_single
     torch.cuda.synchronize()
     dist.barrier()

@@ -7,7 +7,10 @@ temperature of the 2-rank learner must match the single-GPU learner at the globa
 batch: FP32 recipe within 1e-4 relative to each tensor's largest magnitude (batch-norm
 buffers with a 1e-3 floor); FP16-operand recipe within 1e-2 in relative L2 norm (the
 two runs sum weight gradients in different orders and Adam's first steps amplify that
-for near-zero gradients). Both ranks must hold bit-identical parameters. Skipped with fewer than two GPUs.
+for near-zero gradients). Both ranks must hold bit-identical parameters and report no
+health flag. Batch-norm statistics go through the NVLink peer-memory kernels
+(``RL2_DP_PEER=1``, the default) and, in one FP32 case, through NCCL all-gathers.
+Skipped with fewer than two GPUs.
 """
 
 import json
@@ -32,17 +35,20 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("precision,measure,tol", [("fp32", 0, 1e-4), ("fp16", 1, 1e-2)])
-def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol):
+@pytest.mark.parametrize("precision,measure,tol,peer", [("fp32", 0, 1e-4, "1"), ("fp16", 1, 1e-2, "1"),
+                                                        ("fp32", 0, 1e-4, "0")])
+def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol, peer):
     out = tmp_path / "dp.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "tests" / "_dp_worker.py"),
            str(out), precision]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", RL2_DP_PEER=peer)
     done = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert done.returncode == 0, done.stdout[-4000:] + done.stderr[-4000:]
     report = json.loads(out.read_text())
     assert report["ranks_identical"]
+    assert report["peer"] == (peer == "1")
+    assert report["health"] == 0
     for upd in report["updates"]:
         worst = max(upd["errors"].items(), key=lambda kv: kv[1][measure])
         assert worst[1][measure] < tol, (upd["phase"], worst)
