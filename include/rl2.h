@@ -113,6 +113,10 @@ int rl2_gemm_run(void* plan, void* stream);
 int rl2_gemm_destroy(void* plan);
 /* Tile width chosen by the plan (for tests and tuning reports). */
 int rl2_gemm_tile_n(void* plan);
+/* 1 when the plan writes its outputs through TMA stores (no residual / accumulate /
+ * activation / split-K; 16-byte aligned fp32 output and fp16 plane), 2 when it also
+ * keeps the accumulator transposed (products with column statistics, n >= 128), else 0. */
+int rl2_gemm_uses_tma_store(void* plan);
 
 /* out[i] (+)= sum_s partial[s * split_stride + i], fixed order, i < count. */
 int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out, long long count,

@@ -35,6 +35,7 @@
 #include "planes.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -70,6 +71,14 @@ struct Params {
     const float* aux;  // stored activation outputs: multiply by the derivative instead of applying f
     long long ld_aux, aux_bstride;
     bool vec_aux;
+    // store-engine epilogue: output boxes written by TMA stores (tma_d: fp32 output map,
+    // tma_plane: fp16 plane map)
+    bool tma_epi, tma_d, tma_plane;
+    bool tma_reduce;   // store-engine epilogue adds into D in L2 (D += result: in-place residual / accumulate)
+    bool swap;         // accumulator holds D^T: kernel M = output columns, kernel N = output rows
+    int out_m, out_n;  // output rows / columns (the kernel's N / M when swapped)
+    int epi_bufs;      // staging boxes per warp and output (store-engine epilogue: 1 or 2)
+    int stage_floats;  // per-warp staging floats (multiple of 256: 1 KB-aligned regions)
 };
 
 // Epilogue activations. ELU (alpha 1) and tanh; derivatives from the stored outputs y.
@@ -272,6 +281,10 @@ __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem
 // j ^ ((r >> 1) & 3), which keeps both the row-per-lane writes and the 8-row x 16-column
 // reads free of bank conflicts.
 constexpr int kStagePitch = 16;
+// Per-warp staging region (Params::stage_floats floats, a multiple of 256 so every region
+// starts on a 1 KB boundary): the register-store epilogue uses one 32 x 16 fp32 slice;
+// the store-engine epilogue uses epi_bufs fp32 boxes (2 KB each) then epi_bufs fp16 plane
+// boxes (1 KB each), every box on a 1 KB boundary (beyond the swizzle repeats).
 
 __device__ __forceinline__ float4 load_cols(const float* src, int n, bool vec) {
     if (vec && n == 4) return *reinterpret_cast<const float4*>(src);
@@ -331,7 +344,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
     const int slot = (warp - 2) >> 2;
-    float* sq = staging + (warp - 2) * (32 * kStagePitch);
+    float* sq = staging + (warp - 2) * p.stage_floats;
     const int cg = lane & 3;
     const int rsub = lane >> 2;
     const float scale = p.scale ? *p.scale : 1.0f;
@@ -489,20 +502,335 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     pw.flush();
 }
 
+// Store-engine epilogue, for products without activation or split-K whose residual, if
+// any, is the output itself (D += result then goes out as TMA reduce-add stores).
+// A warp reads its 32 x 16 accumulator slices with lane = row (the next slice's TMEM read
+// is in flight while the current one is processed), applies scale and bias in registers
+// and writes each slice once into a staging box in the TMA layout (fp32 box: 64-byte
+// rows, 16-byte chunk j of row r at slot j ^ ((r >> 1) & 3), the 64-byte swizzle; fp16
+// plane box: 32-byte rows, chunk j at slot j ^ ((r >> 2) & 1), the 32-byte swizzle). One
+// lane hands the boxes to the TMA store engine, which writes whole lines and leaves out
+// rows and columns beyond the output; with two boxes per warp the engine reads one while
+// the warp fills the other. Column moments are then read back from the fp32 box with
+// lane = (column c, row half h): lane (c, h) visits rows 16h + (e ^ h), so the 32 lanes of
+// every load hit 32 different banks.
+struct TmaEpi {
+    const CUtensorMap* tma_d;
+    const CUtensorMap* tma_p;
+    float* region;  // this warp's staging: [fp32 box][fp32 box][fp16 box][fp16 box]
+    int nbuf;
+    int lane, sc, sh, cq, dsw, psw;
+    bool scaled, plane16;
+    float scale;
+    PlaneWriter pw;
+    uint32_t count;  // slices handed to the store engine so far
+
+    __device__ __forceinline__ TmaEpi(const CUtensorMap* d, const CUtensorMap* pm, const Params& p, float* r, int nb)
+        : tma_d(d), tma_p(pm), region(r), nbuf(nb), pw(p.out_plane), count(0) {
+        lane = threadIdx.x & 31;
+        sc = lane & 15;
+        sh = lane >> 4;
+        cq = sc >> 2;
+        dsw = (lane >> 1) & 3;
+        psw = (lane >> 2) & 1;
+        scaled = p.scale != nullptr;
+        scale = scaled ? *p.scale : 1.0f;
+        plane16 = p.tma_plane;
+    }
+
+    // One 32 x 16 slice: rows r0 .. r0 + 31 (valid of them inside the output), columns
+    // col0 .. col0 + 15 (ncols inside), accumulator values v (lane = row).
+    __device__ __forceinline__ void slice(const Params& p, const float* bias, float (&v)[16], int col0, int ncols,
+                                          int r0, int valid, float inv_valid, int z, long long stat_row) {
+        if (bias) {
+            if (ncols == 16 && p.vec_bias) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias + col0) + j);
+                    v[4 * j] = (scaled ? v[4 * j] * scale : v[4 * j]) + b4.x;
+                    v[4 * j + 1] = (scaled ? v[4 * j + 1] * scale : v[4 * j + 1]) + b4.y;
+                    v[4 * j + 2] = (scaled ? v[4 * j + 2] * scale : v[4 * j + 2]) + b4.z;
+                    v[4 * j + 3] = (scaled ? v[4 * j + 3] * scale : v[4 * j + 3]) + b4.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    v[j] = (scaled ? v[j] * scale : v[j]) + (j < ncols ? __ldg(bias + col0 + j) : 0.0f);
+            }
+        } else if (scaled) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = v[j] * scale;
+        }
+        const int b = nbuf == 2 ? static_cast<int>(count & 1u) : 0;
+        float* sd = region + b * 512;
+        __half* sp = reinterpret_cast<__half*>(region + nbuf * 512 + b * 256);
+        // the box this slice uses has been read by the store engine
+        if (lane == 0) {
+            if (nbuf == 2)
+                ptx::bulk_wait_read1();
+            else
+                ptx::bulk_wait_read0();
+        }
+        __syncwarp();
+        float4* drow = reinterpret_cast<float4*>(sd + lane * 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) drow[j ^ dsw] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (plane16) {
+            uint32_t h[8];
+            bool over = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float s0 = v[2 * j] * pw.scale, s1 = v[2 * j + 1] * pw.scale;
+                over |= (2 * j < ncols && !(fabsf(s0) <= 65504.0f)) || (2 * j + 1 < ncols && !(fabsf(s1) <= 65504.0f));
+                const __half2 hh = __floats2half2_rn(s0, s1);
+                h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            pw.overflow |= over && lane < valid;
+            uint4* prow = reinterpret_cast<uint4*>(sp + lane * 16);
+            prow[psw] = make_uint4(h[0], h[1], h[2], h[3]);
+            prow[1 ^ psw] = make_uint4(h[4], h[5], h[6], h[7]);
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            if (p.tma_reduce)
+                ptx::tma_reduce_add_3d(tma_d, sd, col0, r0, z);
+            else if (p.tma_d)
+                ptx::tma_store_3d(tma_d, sd, col0, r0, z);
+            if (plane16) ptx::tma_store_3d(tma_p, sp, col0, r0, z);
+            ptx::bulk_commit();
+        }
+        ++count;
+        if (!p.stat_mean) return;
+        // rows 16h + (e ^ h): e = 2m -> 16h + h + 2m, e = 2m + 1 -> 16h + 1 - h + 2m; swizzle term m & 3
+        const float* col_even = sd + (16 * sh + sh) * 16 + (sc & 3);
+        const float* col_odd = sd + (16 * sh + 1 - sh) * 16 + (sc & 3);
+        float y[16];
+        float sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int m = e >> 1;
+            y[e] = ((e & 1) ? col_odd : col_even)[32 * m + 4 * (cq ^ (m & 3))];
+            if (valid < 32 && 16 * sh + (e ^ sh) >= valid) y[e] = 0.0f;
+            sum += y[e];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        const long long idx = static_cast<long long>(z) * p.stat_bstride + stat_row * p.N + col0 + sc;
+        if (!p.stat_m2) {  // sums mode: per-group column sums only
+            if (sh == 0 && sc < ncols) p.stat_mean[idx] = sum;
+            return;
+        }
+        const float mean = sum * inv_valid;
+        float m2 = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const float dv = y[e] - mean;
+            if (valid == 32 || 16 * sh + (e ^ sh) < valid) m2 = fmaf(dv, dv, m2);
+        }
+        m2 += __shfl_xor_sync(0xffffffffu, m2, 16);
+        if (sh == 0 && sc < ncols) {
+            p.stat_mean[idx] = mean;
+            p.stat_m2[idx] = m2;
+        }
+    }
+};
+
+__device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtensorMap* tma_p, const Params& p,
+                                          uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem, float* staging,
+                                          volatile int* abort_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = warp & 3;
+    const int slot = (warp - 2) >> 2;
+    TmaEpi epi(tma_d, tma_p, p, staging + (warp - 2) * p.stage_floats, p.epi_bufs);
+    const int BN = p.BN;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+        const Tile w = decode(p, t);
+        const int buf = i & 1;
+        const int r0 = w.m_tile * kBM + q * 32;
+        const int valid = min(max(p.M - r0, 0), 32);
+        const float inv_valid = 1.0f / static_cast<float>(max(valid, 1));
+        const float* bias = p.bias ? p.bias + static_cast<long long>(w.z) * p.bias_bstride : nullptr;
+        const long long stat_row = static_cast<long long>(w.m_tile * kBM) / 32 + q;
+        // this warp's slices of the tile: c0 = 16 * slot + 16 * kEpiSlots * k
+        const int col_base = w.n_tile * BN + 16 * slot;
+        int nk = 0;
+        while (nk < kMaxChunks && 16 * slot + 16 * kEpiSlots * nk < BN && col_base + 16 * kEpiSlots * nk < p.N) ++nk;
+        if (valid == 0) nk = 0;
+        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
+        ptx::tc_fence_after();
+        const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16) +
+                                static_cast<uint32_t>(16 * slot);
+        // the next slice's TMEM read is in flight while this one is processed
+        uint32_t cur[16];
+        if (nk > 0) {
+            ptx::tmem_ld16_issue(t_base, cur);
+            ptx::tmem_ld_wait(cur);
+        }
+#pragma unroll 1
+        for (int k = 0; k < nk; ++k) {
+            uint32_t nxt[16];
+            const bool more = k + 1 < nk;
+            if (more) ptx::tmem_ld16_issue(t_base + static_cast<uint32_t>(16 * kEpiSlots * (k + 1)), nxt);
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(cur[j]);
+            const int col0 = col_base + 16 * kEpiSlots * k;
+            epi.slice(p, bias, v, col0, min(16, p.N - col0), r0, valid, inv_valid, w.z, stat_row);
+            if (more) {
+                ptx::tmem_ld_wait(nxt);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) cur[j] = nxt[j];
+            }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+    }
+    if (lane == 0) ptx::bulk_wait0();
+    __syncwarp();
+    epi.pw.flush();
+}
+
+// Transposed-accumulator epilogue (swapped plans: products with column statistics). TMEM
+// lane = output column, TMEM column = output row, so one 32x32b.x32 read gives every lane
+// 32 consecutive rows of its own column: scale and bias (one value per lane), and the
+// 32-row column moments are plain register arithmetic (pairwise sums, no shared memory,
+// no shuffles). The rows are then written as 16-row x 32-column staging boxes (lane =
+// column; fp32 box: 128-byte rows, 16-byte chunk j of row r at slot j ^ (r & 7), the
+// 128-byte swizzle; fp16 box: 64-byte rows, chunk j at slot j ^ ((r >> 1) & 3), the
+// 64-byte swizzle) and handed to the TMA store engine. The two warps of a TMEM lane
+// quarter take alternate 32-row groups of the tile.
+__device__ __forceinline__ float sum32(const float (&x)[32]) {
+    float s[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) s[j] = x[j] + x[j + 16];
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) s[j] = s[j] + s[j + w];
+    return s[0];
+}
+
+__device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUtensorMap* tma_p, const Params& p,
+                                           uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem, float* staging,
+                                           volatile int* abort_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = warp & 3;
+    const int slot = (warp - 2) >> 2;
+    float* region = staging + (warp - 2) * p.stage_floats;
+    const int nbuf = p.epi_bufs;
+    const bool scaled = p.scale != nullptr;
+    const float scale = scaled ? *p.scale : 1.0f;
+    PlaneWriter pw(p.out_plane);
+    const bool plane16 = p.tma_plane;
+    const int BN = p.BN;  // output rows per tile (a multiple of 32)
+    uint32_t count = 0;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+        const Tile w = decode(p, t);
+        const int buf = i & 1;
+        const int col0 = w.m_tile * kBM + q * 32;  // this warp's 32 output columns
+        const int n = col0 + lane;
+        const bool col_ok = n < p.out_n;
+        const float bv = (p.bias && col_ok) ? __ldg(p.bias + static_cast<long long>(w.z) * p.bias_bstride + n) : 0.0f;
+        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
+        ptx::tc_fence_after();
+        const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
+        for (int gl = slot; gl < BN / 32 && col0 < p.out_n; gl += kEpiSlots) {
+            const int m0 = w.n_tile * BN + 32 * gl;  // first output row of the group
+            const int vr = min(32, p.out_m - m0);
+            if (vr <= 0) break;  // warp-uniform
+            float v[32];
+            ptx::tmem_ld32(t_base + static_cast<uint32_t>(32 * gl), v);
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+                if (scaled) v[r] = v[r] * scale;
+                if (p.bias) v[r] = v[r] + bv;
+            }
+            if (p.stat_mean) {
+                float x[32];
+#pragma unroll
+                for (int r = 0; r < 32; ++r) x[r] = (vr == 32 || r < vr) ? v[r] : 0.0f;
+                const float sum = sum32(x);
+                const long long idx = static_cast<long long>(w.z) * p.stat_bstride + static_cast<long long>(m0 / 32) * p.out_n + n;
+                if (!p.stat_m2) {
+                    if (col_ok) p.stat_mean[idx] = sum;
+                } else {
+                    const float mean = sum * (vr == 32 ? 0.03125f : 1.0f / static_cast<float>(vr));
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) {
+                        const float dv = v[r] - mean;
+                        x[r] = (vr == 32 || r < vr) ? dv * dv : 0.0f;
+                    }
+                    const float m2 = sum32(x);
+                    if (col_ok) {
+                        p.stat_mean[idx] = mean;
+                        p.stat_m2[idx] = m2;
+                    }
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (16 * h >= vr) break;  // warp-uniform
+                const int b = nbuf == 2 ? static_cast<int>(count & 1u) : 0;
+                float* sd = region + b * 512;
+                __half* sp = reinterpret_cast<__half*>(region + nbuf * 512 + b * 256);
+                if (lane == 0) {
+                    if (nbuf == 2)
+                        ptx::bulk_wait_read1();
+                    else
+                        ptx::bulk_wait_read0();
+                }
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < 16; ++r) sd[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = v[16 * h + r];
+                if (plane16) {
+                    bool over = false;
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) {
+                        const float s = v[16 * h + r] * pw.scale;
+                        over |= 16 * h + r < vr && !(fabsf(s) <= 65504.0f);
+                        sp[r * 32 + (((lane >> 3) ^ ((r >> 1) & 3)) << 3) + (lane & 7)] = __float2half_rn(s);
+                    }
+                    pw.overflow |= over && col_ok;
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (p.tma_d) ptx::tma_store_3d(tma_d, sd, col0, m0 + 16 * h, w.z);
+                    if (plane16) ptx::tma_store_3d(tma_p, sp, col0, m0 + 16 * h, w.z);
+                    ptx::bulk_commit();
+                }
+                ++count;
+            }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+    }
+    if (lane == 0) ptx::bulk_wait0();
+    __syncwarp();
+    pw.flush();
+}
+
 // Persistent kernel: one CTA per SM walks the output tiles blockIdx.x, +gridDim.x, ...
 // Shared memory: [stage ring][epilogue staging kEpiWarps x 32 x 16 floats][barriers].
 template <int KIND, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_a_lo, const __grid_constant__ CUtensorMap tma_b_lo,
-                const Params p, const int stages) {
+                const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_p, const Params p,
+                const int stages) {
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
     const uint32_t stage_bytes = (kBM * 128 + static_cast<uint32_t>(p.BN) * 128) * kPlanes;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* staging = reinterpret_cast<float*>(smem + stages * stage_bytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * 32 * kStagePitch);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * p.stage_floats);
     uint64_t* empty = full + stages;
     uint64_t* acc_full = empty + stages;
     uint64_t* acc_empty = acc_full + 2;
@@ -548,6 +876,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             volatile int no_abort = 0;
             wait_bar(mma_done, 0, p.health, &no_abort);
         }
+    } else if (p.swap) {
+        drain_swap(&tma_d, &tma_p, p, acc_full, acc_empty, tmem, staging, abort_flag);
+    } else if (p.tma_epi) {
+        drain_tma(&tma_d, &tma_p, p, acc_full, acc_empty, tmem, staging, abort_flag);
     } else {
         drain(p, acc_full, acc_empty, tmem, staging, abort_flag);
     }
@@ -630,15 +962,36 @@ bool make_map(CUtensorMap* map, const void* base, int elem, long long inner, lon
     return true;
 }
 
+// RL2_GEMM_TMA_STORE=0 keeps the register-store epilogue for every product.
+bool tma_store_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("RL2_GEMM_TMA_STORE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// The fp32 output and the fp16 plane (if any) satisfy the TMA store rules: 16-byte aligned
+// bases, row and batch strides in multiples of 16 bytes, rows at least n wide.
+bool outputs_tma_ok(const rl2_gemm_desc* g) {
+    const bool batched = g->batch > 1;
+    const bool d_ok = !g->d || (aligned(g->d, 16) && (g->ldd * 4) % 16 == 0 && g->ldd >= g->n &&
+                                 (!batched || (g->d_batch_stride > 0 && (g->d_batch_stride * 4) % 16 == 0)));
+    if (!plane_used(&g->out_plane)) return d_ok;
+    const rl2_plane& q = g->out_plane;
+    return d_ok && q.h16 && aligned(q.h16, 16) && (q.ld * 2) % 16 == 0 && q.ld >= g->n &&
+           (!batched || (q.twin_stride > 0 && (q.twin_stride * 2) % 16 == 0));
+}
+
 struct Plan {
-    CUtensorMap ta, tb, ta_lo, tb_lo;
+    CUtensorMap ta, tb, ta_lo, tb_lo, td, tp;
     Params p;
     int kind, a_mn, b_mn, stages, smem;
     dim3 grid;
 };
 
-typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params,
-                         const int);
+typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                         const CUtensorMap, const Params, const int);
 
 KernelFn pick(int kind, int a_mn, int b_mn) {
     const int key = kind * 4 + a_mn * 2 + b_mn;
@@ -704,8 +1057,31 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     const int elem = g->kind == 0 ? 2 : 4;
     const int bk = 128 / elem;
     const int chunk = 128 / elem;
-    int bn = g->tile_n > 0 ? g->tile_n : auto_tile_n(g->n, g->kind, g->b_major);
-    if (bn % 16 != 0 || bn < 16 || bn > 256 || (g->b_major == 1 && bn % chunk != 0)) {
+    // Products with column statistics (no residual / accumulate / activation / split-K)
+    // run with the operands swapped: the accumulator tile is D^T (TMEM lane = output
+    // column), so a thread holds 32 rows of its column and the 32-row moments stay in
+    // registers. Kernel view of a swapped plan: M' = n, N' = m, A' = B, B' = A.
+    const bool swap = tma_store_enabled() && splits == 1 && g->stat_mean && !g->residual && !g->accumulate &&
+                      !g->activation && !g->act_aux && g->tile_n <= 0 && g->n >= 128 && outputs_tma_ok(g);
+    rl2_gemm_desc sw = *g;
+    if (swap) {
+        sw.m = g->n;
+        sw.n = g->m;
+        sw.a = g->b;
+        sw.a_lo = g->b_lo;
+        sw.a_major = g->b_major;
+        sw.lda = g->ldb;
+        sw.a_batch_stride = g->b_batch_stride;
+        sw.b = g->a;
+        sw.b_lo = g->a_lo;
+        sw.b_major = g->a_major;
+        sw.ldb = g->lda;
+        sw.b_batch_stride = g->a_batch_stride;
+    }
+    const rl2_gemm_desc& o = sw;  // operands and tiles (the caller's view unless swapped)
+    int bn = o.tile_n > 0 ? o.tile_n : auto_tile_n(o.n, o.kind, o.b_major);
+    if (swap) bn = std::min(256, (bn + 31) / 32 * 32);  // whole 32-row groups per tile
+    if (bn % 16 != 0 || bn < 16 || bn > 256 || (o.b_major == 1 && bn % chunk != 0)) {
         set_error("GEMM tile_n must be a multiple of 16 in [16, 256] (and of %d for an N-contiguous B)", chunk);
         return nullptr;
     }
@@ -716,26 +1092,26 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     }
     std::memset(plan, 0, sizeof(Plan));
     plan->kind = g->kind;
-    plan->a_mn = g->a_major;
-    plan->b_mn = g->b_major;
-    const long long a_batch = g->a_batch_stride ? g->batch : 1;
-    const long long b_batch = g->b_batch_stride ? g->batch : 1;
+    plan->a_mn = o.a_major;
+    plan->b_mn = o.b_major;
+    const long long a_batch = o.a_batch_stride ? o.batch : 1;
+    const long long b_batch = o.b_batch_stride ? o.batch : 1;
     bool ok = true;
     for (int plane = 0; plane < (g->kind == 0 ? 1 : 2) && ok; ++plane) {
-        const void* a = plane == 0 ? g->a : g->a_lo;
-        const void* b = plane == 0 ? g->b : g->b_lo;
+        const void* a = plane == 0 ? o.a : o.a_lo;
+        const void* b = plane == 0 ? o.b : o.b_lo;
         CUtensorMap* ma = plane == 0 ? &plan->ta : &plan->ta_lo;
         CUtensorMap* mb = plane == 0 ? &plan->tb : &plan->tb_lo;
         // MN-major tf32 tiles use the 32-byte-granule 128-byte swizzle (see smem_desc).
         const CUtensorMapSwizzle mn_swz = g->kind == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-        if (g->a_major == 0)
-            ok = ok && make_map(ma, a, elem, g->k, g->m, a_batch, g->lda, g->a_batch_stride, bk, kBM);
+        if (o.a_major == 0)
+            ok = ok && make_map(ma, a, elem, o.k, o.m, a_batch, o.lda, o.a_batch_stride, bk, kBM);
         else
-            ok = ok && make_map(ma, a, elem, g->m, g->k, a_batch, g->lda, g->a_batch_stride, chunk, bk, mn_swz);
-        if (g->b_major == 0)
-            ok = ok && make_map(mb, b, elem, g->k, g->n, b_batch, g->ldb, g->b_batch_stride, bk, bn);
+            ok = ok && make_map(ma, a, elem, o.m, o.k, a_batch, o.lda, o.a_batch_stride, chunk, bk, mn_swz);
+        if (o.b_major == 0)
+            ok = ok && make_map(mb, b, elem, o.k, o.n, b_batch, o.ldb, o.b_batch_stride, bk, bn);
         else
-            ok = ok && make_map(mb, b, elem, g->n, g->k, b_batch, g->ldb, g->b_batch_stride, chunk, bk, mn_swz);
+            ok = ok && make_map(mb, b, elem, o.n, o.k, b_batch, o.ldb, o.b_batch_stride, chunk, bk, mn_swz);
     }
     if (!ok) {
         delete plan;
@@ -746,17 +1122,20 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         plan->tb_lo = plan->tb;
     }
     Params& p = plan->p;
-    p.M = g->m;
-    p.N = g->n;
-    p.K = g->k;
+    p.M = o.m;
+    p.N = o.n;
+    p.K = o.k;
+    p.swap = swap;
+    p.out_m = g->m;
+    p.out_n = g->n;
     p.batch = g->batch;
     p.kblocks_total = (g->k + bk - 1) / bk;
     p.splits = std::min(splits, p.kblocks_total);
     p.kblocks_per_split = (p.kblocks_total + p.splits - 1) / p.splits;
     p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;  // every split non-empty
     p.BN = bn;
-    p.a_batched = g->a_batch_stride != 0;
-    p.b_batched = g->b_batch_stride != 0;
+    p.a_batched = o.a_batch_stride != 0;
+    p.b_batched = o.b_batch_stride != 0;
     p.d = g->d;
     p.ldd = g->ldd;
     p.d_bstride = g->d_batch_stride;
@@ -773,20 +1152,8 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.scale = g->scale;
     p.health = g->health;
     p.out_plane = to_plane(&g->out_plane);
-    const int planes = g->kind == 0 ? 1 : 2;
-    const int stage_bytes = (kBM * 128 + bn * 128) * planes;
-    // ring + epilogue staging + barriers (2 x stages + 5 words, TMEM slot, abort word) + alignment slack
-    const int staging = kEpiWarps * 32 * kStagePitch * 4;
-    const int overhead = 1024 + staging + 256;
-    plan->stages = std::min(8, (kMaxSmem - overhead) / stage_bytes);
-    if (plan->stages < 2) {
-        set_error("GEMM tile does not fit shared memory");
-        delete plan;
-        return nullptr;
-    }
-    plan->smem = plan->stages * stage_bytes + overhead;
-    const long long tiles_n = (g->n + bn - 1) / bn;
-    const long long tiles_m = (g->m + kBM - 1) / kBM;
+    const long long tiles_n = (o.n + bn - 1) / bn;
+    const long long tiles_m = (o.m + kBM - 1) / kBM;
     const long long tiles = tiles_n * tiles_m * g->batch * p.splits;
     if (tiles > 0x7FFFFFFFLL) {
         set_error("GEMM has too many output tiles");
@@ -816,6 +1183,69 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.vec_plane = plane_used(&g->out_plane) && g->out_plane.ld % 4 == 0 && g->out_plane.twin_stride % 4 == 0 &&
                   (g->out_plane.h16 ? aligned(g->out_plane.h16, 8)
                                     : a16(g->out_plane.hi) && a16(g->out_plane.lo));
+    // store-engine epilogue: outputs written by TMA stores when the product has no
+    // residual / accumulate / activation / split-K and the outputs satisfy the TMA rules.
+    // Boxes: 32 rows x 16 columns (fp32: 64-byte swizzle; fp16: 32-byte swizzle), or, for
+    // swapped plans, 16 rows x 32 columns (fp32: 128-byte swizzle; fp16: 64-byte swizzle).
+    // D += result (accumulate, or a residual that is D itself) goes through TMA reduce-add
+    // stores when nothing else needs the final values (no plane, no statistics).
+    const bool in_place = g->d && (g->accumulate || (g->residual == g->d && g->ldr == g->ldd &&
+                                                      g->residual_batch_stride == g->d_batch_stride)) &&
+                          !(g->accumulate && g->residual);
+    const bool reduce_ok = in_place && !plane_used(&g->out_plane) && !g->stat_mean;
+    if (swap || (tma_store_enabled() && p.splits == 1 && (!(g->residual || g->accumulate) || reduce_ok) &&
+                 !g->activation && !g->act_aux && outputs_tma_ok(g))) {
+        const bool plane_on = plane_used(&g->out_plane);
+        const int bx = swap ? 32 : 16, by = swap ? 16 : 32;
+        bool mok = true;
+        if (g->d)
+            mok = make_map(&plan->td, g->d, 4, g->n, g->m, g->batch, g->ldd, g->d_batch_stride, bx, by,
+                           swap ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+        if (mok && plane_on)
+            mok = make_map(&plan->tp, g->out_plane.h16, 2, g->n, g->m, g->batch, g->out_plane.ld,
+                           g->out_plane.twin_stride, bx, by,
+                           swap ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+        if (mok) {
+            p.tma_epi = true;
+            p.tma_d = g->d != nullptr;
+            p.tma_plane = plane_on;
+            p.tma_reduce = !swap && reduce_ok;
+        } else if (swap) {
+            delete plan;  // the operands are already swapped: no register-store fallback
+            return nullptr;
+        } else {
+            clear_error();  // fall back to the register-store epilogue
+        }
+    }
+    // shared memory: ring + epilogue staging + barriers (2 x stages + 5 words, TMEM slot,
+    // abort word) + alignment slack. The store-engine epilogue double-buffers its boxes
+    // unless that costs the operand ring its fourth stage (RL2_GEMM_EPI_BUFS=1 or 2 forces).
+    {
+        const int planes = g->kind == 0 ? 1 : 2;
+        const int stage_bytes = (kBM * 128 + bn * 128) * planes;
+        auto stages_for = [&](int stage_floats) {
+            return std::min(8, (kMaxSmem - (1024 + kEpiWarps * stage_floats * 4 + 256)) / stage_bytes);
+        };
+        auto tma_floats = [&](int nbuf) { return nbuf * (512 + (p.tma_plane ? 256 : 0)); };
+        p.epi_bufs = 1;
+        p.stage_floats = 512;
+        if (p.tma_epi) {
+            static const int forced = [] {
+                const char* e = std::getenv("RL2_GEMM_EPI_BUFS");
+                return e ? std::atoi(e) : 0;
+            }();
+            const int s1 = stages_for(tma_floats(1)), s2 = stages_for(tma_floats(2));
+            p.epi_bufs = forced == 1 || forced == 2 ? forced : (s2 >= std::min(s1, 4) ? 2 : 1);
+            p.stage_floats = tma_floats(p.epi_bufs);
+        }
+        plan->stages = stages_for(p.stage_floats);
+        if (plan->stages < 2) {
+            set_error("GEMM tile does not fit shared memory");
+            delete plan;
+            return nullptr;
+        }
+        plan->smem = plan->stages * stage_bytes + 1024 + kEpiWarps * p.stage_floats * 4 + 256;
+    }
     int device = 0, sms = 0;
     if (cudaGetDevice(&device) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms < 1) {
@@ -847,7 +1277,7 @@ extern "C" int rl2_gemm_run(void* opaque, void* stream) {
     Plan* plan = static_cast<Plan*>(opaque);
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
     fn<<<plan->grid, kThreads, plan->smem, as_stream(stream)>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo,
-                                                               plan->p, plan->stages);
+                                                               plan->td, plan->tp, plan->p, plan->stages);
     return launch_status("tcgen05 GEMM");
 }
 
@@ -859,6 +1289,11 @@ extern "C" int rl2_gemm_destroy(void* opaque) {
 
 extern "C" int rl2_gemm_tile_n(void* opaque) {
     return opaque ? static_cast<Plan*>(opaque)->p.BN : -1;
+}
+
+extern "C" int rl2_gemm_uses_tma_store(void* opaque) {
+    if (!opaque || !static_cast<Plan*>(opaque)->p.tma_epi) return 0;
+    return static_cast<Plan*>(opaque)->p.swap ? 2 : 1;
 }
 
 // ---------------------------------------------------------------------------

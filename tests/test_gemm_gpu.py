@@ -24,7 +24,7 @@ def _store(logical: torch.Tensor, major: int, kind: int) -> tuple[torch.Tensor, 
     return buf, ld
 
 
-def _run(kind, m, n, k, a_major, b_major, batch=2, shared_a=False, **epi):
+def _run(kind, m, n, k, a_major, b_major, batch=2, shared_a=False, ldd=None, d_rows=None, **epi):
     g = torch.Generator(device="cuda").manual_seed(m * 131 + n * 7 + k)
     A = torch.randn(1 if shared_a else batch, m, k, device="cuda", generator=g)
     B = torch.randn(batch, n, k, device="cuda", generator=g) / k**0.5
@@ -32,8 +32,10 @@ def _run(kind, m, n, k, a_major, b_major, batch=2, shared_a=False, **epi):
         A, B = A.half().float(), B.half().float()
     a_st, lda = _store(A, a_major, kind)
     b_st, ldb = _store(B, b_major, kind)
-    ldd = n + 3
-    D = torch.zeros(batch, m, ldd, device="cuda")
+    ldd = ldd or n + 3
+    D = torch.zeros(batch, d_rows or m, ldd, device="cuda")
+    if isinstance(epi.get("residual"), str):  # "D": the residual is the output itself
+        epi["residual"] = D
     kw = {}
     if kind == 1:
         a_hi, a_lo = dense.tf32_split(a_st)
@@ -222,3 +224,115 @@ def test_gemm_column_sums_mode(kind):
     full[:, :m] = D[:, :, :n].double()
     expect = full.view(batch, groups, 32, n).sum(2)
     assert torch.allclose(sums.double(), expect, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("m,n,k,tile_n", [(300, 200, 96, 0), (8200, 600, 256, 0), (4096, 2048, 512, 0),
+                                          (1000, 72, 64, 48)])
+@pytest.mark.parametrize("mode", ["moments", "sums", "plane"])
+def test_gemm_tma_store_epilogue(kind, m, n, k, tile_n, mode):
+    """Store-engine epilogue (outputs written by TMA stores; with column statistics and
+    n >= 128 the accumulator is kept transposed): output, bias, scale, 32-row column
+    moments or sums and the fp16 plane against fp64 references; rows past M and columns
+    past N (up to the row stride) stay untouched."""
+    from robolearn_b200 import _native as N
+
+    batch = 2
+    groups = (m + 31) // 32
+    ldd = (n + 3) // 4 * 4 + 4
+    extra = 40  # rows after each twin's M rows that must stay untouched
+    bias = torch.randn(batch, n, device="cuda")
+    scale = torch.tensor([0.5], device="cuda")
+    epi = dict(bias=bias, bias_batch_stride=n, scale=scale)
+    mean = torch.zeros(batch, groups, n, device="cuda")
+    m2 = torch.zeros(batch, groups, n, device="cuda")
+    keep = []
+    if mode == "moments":
+        epi.update(stat_mean=mean, stat_m2=m2, stat_batch_stride=groups * n)
+    elif mode == "sums":
+        epi.update(stat_mean=mean, stat_batch_stride=groups * n)
+    elif kind == 0:
+        pld = dense.operand_ld(n, 0)
+        h16 = torch.full((batch, m + extra, pld), 7.0, device="cuda", dtype=torch.float16)
+        pscale = torch.tensor([4.0], device="cuda")
+        found = torch.zeros(1, dtype=torch.int32, device="cuda")
+        epi["out_plane"] = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=(m + extra) * pld,
+                                   scale=pscale.data_ptr(), found_inf=found.data_ptr())
+        epi.update(stat_mean=mean, stat_m2=m2, stat_batch_stride=groups * n)
+        keep = [h16, pscale, found]
+    else:
+        pytest.skip("tf32 output planes take the register-store epilogue")
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + extra, tile_n=tile_n, **epi)
+    assert plan.tma_store
+    assert plan.transposed == (n >= 128 and tile_n == 0)  # every mode here asks for column statistics
+    D.fill_(float("nan"))
+    plan.run()
+    torch.cuda.synchronize()
+    expect = ref * 0.5 + bias.double()[:, None, :]
+    out = D[:, :m, :n].double()
+    tol = 2e-3 if kind == 0 else 2e-5
+    assert (out - expect).abs().max().item() < tol * expect.abs().max().item()
+    assert torch.isnan(D[:, :m, n:]).all() and torch.isnan(D[:, m:]).all()
+    full = torch.zeros(batch, groups * 32, n, device="cuda", dtype=torch.float64)
+    full[:, :m] = out
+    rows = full.view(batch, groups, 32, n)
+    counts = torch.full((groups,), 32.0, device="cuda", dtype=torch.float64)
+    counts[-1] = m - 32 * (groups - 1)
+    if mode == "sums":
+        assert torch.allclose(mean.double(), rows.sum(2), atol=1e-3, rtol=1e-4)
+    else:
+        mu = rows.sum(2) / counts[None, :, None]
+        valid = (torch.arange(groups * 32, device="cuda") < m).view(groups, 32)[None, :, :, None]
+        dev = torch.where(valid, rows - mu[:, :, None, :], torch.zeros_like(rows))
+        assert torch.allclose(mean.double(), mu, atol=1e-4, rtol=1e-4)
+        assert torch.allclose(m2.double(), (dev**2).sum(2), atol=1e-3, rtol=1e-4)
+    if mode == "plane":
+        h16, _, found = keep
+        assert torch.equal(h16[:, :m, :n], (D[:, :m, :n] * 4.0).half())
+        assert (h16[:, m:] == 7.0).all() and (h16[:, :m, n:] == 7.0).all()
+        assert int(found.item()) == 0
+
+
+def test_gemm_tma_store_plane_overflow_flag():
+    """fp16 plane through the store engine: a loss scale that overflows fp16 sets found_inf."""
+    from robolearn_b200 import _native as N
+
+    m, n, k, batch = 256, 128, 64, 2
+    pld = dense.operand_ld(n, 0)
+    h16 = torch.zeros(batch, m, pld, device="cuda", dtype=torch.float16)
+    pscale = torch.tensor([1e6], device="cuda")
+    found = torch.zeros(1, dtype=torch.int32, device="cuda")
+    plane = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=m * pld, scale=pscale.data_ptr(),
+                    found_inf=found.data_ptr())
+    plan, D, _ = _run(0, m, n, k, 0, 0, batch=batch, ldd=n, out_plane=plane)
+    assert plan.tma_store
+    plan.run()
+    torch.cuda.synchronize()
+    assert int(found.item()) == 1
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("how", ["residual_in_place", "accumulate"])
+def test_gemm_tma_reduce_add_epilogue(kind, how):
+    """D += scale * A B^T + bias through TMA reduce-add stores (the residual is D itself, or
+    accumulate); ragged M / N tails; rows past M and columns past N stay untouched."""
+    m, n, k, batch = 1000, 600, 192, 2
+    ldd = (n + 3) // 4 * 4 + 4
+    bias = torch.randn(batch, n, device="cuda")
+    scale = torch.tensor([0.25], device="cuda")
+    old = torch.randn(batch, m + 8, ldd, device="cuda")
+    epi = dict(bias=bias, bias_batch_stride=n, scale=scale)
+    plan, D, ref = None, None, None
+    if how == "accumulate":
+        plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + 8, accumulate=1, **epi)
+    else:
+        plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + 8, residual="D", ldr=ldd,
+                            residual_batch_stride=(m + 8) * ldd, **epi)
+    assert plan.tma_store and not plan.transposed
+    D.copy_(old)
+    plan.run()
+    torch.cuda.synchronize()
+    expect = ref * 0.25 + bias.double()[:, None, :] + old[:, :m, :n].double()
+    tol = 2e-3 if kind == 0 else 2e-5
+    assert (D[:, :m, :n].double() - expect).abs().max().item() < tol * expect.abs().max().item()
+    assert torch.equal(D[:, :m, n:], old[:, :m, n:]) and torch.equal(D[:, m:], old[:, m:])
