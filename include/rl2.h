@@ -113,9 +113,10 @@ int rl2_gemm_run(void* plan, void* stream);
 int rl2_gemm_destroy(void* plan);
 /* Tile width chosen by the plan (for tests and tuning reports). */
 int rl2_gemm_tile_n(void* plan);
-/* 1 when the plan writes its outputs through TMA stores (no residual / accumulate /
- * activation / split-K; 16-byte aligned fp32 output and fp16 plane), 2 when it also
- * keeps the accumulator transposed (products with column statistics, n >= 128), else 0. */
+/* Epilogue form of a plan: 2 = transposed accumulator (n >= 128 and a plan-chosen tile
+ * width: TMEM lane = output column, direct coalesced row-segment loads and stores);
+ * 1 = outputs written by TMA stores (no activation / split-K, a residual only if it is D
+ * itself, 16-byte aligned fp32 output and fp16 plane); 0 = register stores. */
 int rl2_gemm_uses_tma_store(void* plan);
 
 /* out[i] (+)= sum_s partial[s * split_stride + i], fixed order, i < count. */

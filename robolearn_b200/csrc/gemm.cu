@@ -693,15 +693,15 @@ __device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtens
     epi.pw.flush();
 }
 
-// Transposed-accumulator epilogue (swapped plans: products with column statistics). TMEM
-// lane = output column, TMEM column = output row, so one 32x32b.x32 read gives every lane
-// 32 consecutive rows of its own column: scale and bias (one value per lane), and the
-// 32-row column moments are plain register arithmetic (pairwise sums, no shared memory,
-// no shuffles). The rows are then written as 16-row x 32-column staging boxes (lane =
-// column; fp32 box: 128-byte rows, 16-byte chunk j of row r at slot j ^ (r & 7), the
-// 128-byte swizzle; fp16 box: 64-byte rows, chunk j at slot j ^ ((r >> 1) & 3), the
-// 64-byte swizzle) and handed to the TMA store engine. The two warps of a TMEM lane
-// quarter take alternate 32-row groups of the tile.
+// Transposed-accumulator epilogue (swapped plans: every product whose output has at least
+// 128 columns and whose tile width is chosen by the plan). TMEM lane = output column, TMEM
+// column = output row, so one 32x32b.x32 read gives every lane 32 consecutive rows of its
+// own column. Everything after that is per-lane register work plus global accesses in
+// which, for each row, the 32 lanes touch 32 consecutive columns (whole 128-byte lines):
+// residual / old-output / stored-activation rows are loaded that way, the output and the
+// operand plane are stored that way, and the 32-row column moments are pairwise sums in
+// registers (no shared memory and no shuffles). The two warps of a TMEM lane quarter take
+// alternate 32-row groups of the tile.
 __device__ __forceinline__ float sum32(const float (&x)[32]) {
     float s[16];
 #pragma unroll
@@ -713,21 +713,22 @@ __device__ __forceinline__ float sum32(const float (&x)[32]) {
     return s[0];
 }
 
-__device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUtensorMap* tma_p, const Params& p,
-                                           uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem, float* staging,
+// kLoads: the product adds rows of another array (residual / old output) or scales by stored
+// activation outputs; the instance without them keeps the add / aux registers out of the
+// common path.
+template <bool kLoads>
+__device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
                                            volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
     const int slot = (warp - 2) >> 2;
-    float* region = staging + (warp - 2) * p.stage_floats;
-    const int nbuf = p.epi_bufs;
     const bool scaled = p.scale != nullptr;
     const float scale = scaled ? *p.scale : 1.0f;
     PlaneWriter pw(p.out_plane);
-    const bool plane16 = p.tma_plane;
+    const bool plane_on = pw.active();
+    const int actv = p.activation;
     const int BN = p.BN;  // output rows per tile (a multiple of 32)
-    uint32_t count = 0;
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
         const Tile w = decode(p, t);
@@ -736,6 +737,11 @@ __device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUten
         const int n = col0 + lane;
         const bool col_ok = n < p.out_n;
         const float bv = (p.bias && col_ok) ? __ldg(p.bias + static_cast<long long>(w.z) * p.bias_bstride + n) : 0.0f;
+        float* dcol = p.d ? p.d + static_cast<long long>(w.z) * p.d_bstride +
+                                static_cast<long long>(w.split) * p.d_split_stride + n
+                          : nullptr;
+        const float* rcol = kLoads && p.residual ? p.residual + static_cast<long long>(w.z) * p.r_bstride + n : nullptr;
+        const float* acol = kLoads && p.aux ? p.aux + static_cast<long long>(w.z) * p.aux_bstride + n : nullptr;
         if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
         ptx::tc_fence_after();
         const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
@@ -743,6 +749,23 @@ __device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUten
             const int m0 = w.n_tile * BN + 32 * gl;  // first output row of the group
             const int vr = min(32, p.out_m - m0);
             if (vr <= 0) break;  // warp-uniform
+            const bool full = vr == 32;
+            // rows added to the product (residual, else the old output) and stored activation
+            // outputs: loaded before the TMEM read so their latency overlaps it
+            const float* add_src = !kLoads ? nullptr
+                                   : rcol ? rcol + static_cast<long long>(m0) * p.ldr
+                                          : (dcol && p.accumulate ? dcol + static_cast<long long>(m0) * p.ldd : nullptr);
+            const long long add_ld = rcol ? p.ldr : p.ldd;
+            float add[32], aux[32];
+            if (add_src && col_ok) {
+#pragma unroll
+                for (int r = 0; r < 32; ++r) add[r] = (full || r < vr) ? add_src[static_cast<long long>(r) * add_ld] : 0.0f;
+            }
+            if (actv && acol && col_ok) {
+                const float* src = acol + static_cast<long long>(m0) * p.ld_aux;
+#pragma unroll
+                for (int r = 0; r < 32; ++r) aux[r] = (full || r < vr) ? src[static_cast<long long>(r) * p.ld_aux] : 0.0f;
+            }
             float v[32];
             ptx::tmem_ld32(t_base + static_cast<uint32_t>(32 * gl), v);
 #pragma unroll
@@ -750,20 +773,42 @@ __device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUten
                 if (scaled) v[r] = v[r] * scale;
                 if (p.bias) v[r] = v[r] + bv;
             }
+            if (col_ok) {
+                if (add_src) {
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) v[r] = v[r] + add[r];
+                }
+                if (kLoads && rcol && dcol && p.accumulate) {  // both: the old output after the residual
+                    const float* src = dcol + static_cast<long long>(m0) * p.ldd;
+#pragma unroll
+                    for (int r = 0; r < 32; ++r)
+                        if (full || r < vr) v[r] = v[r] + src[static_cast<long long>(r) * p.ldd];
+                }
+                if (actv) {
+                    if (acol) {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) v[r] = v[r] * act_grad(actv, aux[r]);
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) v[r] = act_fwd(actv, v[r]);
+                    }
+                }
+            }
             if (p.stat_mean) {
                 float x[32];
 #pragma unroll
-                for (int r = 0; r < 32; ++r) x[r] = (vr == 32 || r < vr) ? v[r] : 0.0f;
+                for (int r = 0; r < 32; ++r) x[r] = (full || r < vr) ? v[r] : 0.0f;
                 const float sum = sum32(x);
-                const long long idx = static_cast<long long>(w.z) * p.stat_bstride + static_cast<long long>(m0 / 32) * p.out_n + n;
+                const long long idx =
+                    static_cast<long long>(w.z) * p.stat_bstride + static_cast<long long>(m0 / 32) * p.out_n + n;
                 if (!p.stat_m2) {
                     if (col_ok) p.stat_mean[idx] = sum;
                 } else {
-                    const float mean = sum * (vr == 32 ? 0.03125f : 1.0f / static_cast<float>(vr));
+                    const float mean = sum * (full ? 0.03125f : 1.0f / static_cast<float>(vr));
 #pragma unroll
                     for (int r = 0; r < 32; ++r) {
                         const float dv = v[r] - mean;
-                        x[r] = (vr == 32 || r < vr) ? dv * dv : 0.0f;
+                        x[r] = (full || r < vr) ? dv * dv : 0.0f;
                     }
                     const float m2 = sum32(x);
                     if (col_ok) {
@@ -772,47 +817,43 @@ __device__ __forceinline__ void drain_swap(const CUtensorMap* tma_d, const CUten
                     }
                 }
             }
+            if (col_ok) {
+                if (dcol) {
+                    float* dst = dcol + static_cast<long long>(m0) * p.ldd;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (16 * h >= vr) break;  // warp-uniform
-                const int b = nbuf == 2 ? static_cast<int>(count & 1u) : 0;
-                float* sd = region + b * 512;
-                __half* sp = reinterpret_cast<__half*>(region + nbuf * 512 + b * 256);
-                if (lane == 0) {
-                    if (nbuf == 2)
-                        ptx::bulk_wait_read1();
-                    else
-                        ptx::bulk_wait_read0();
+                    for (int r = 0; r < 32; ++r)
+                        if (full || r < vr) dst[static_cast<long long>(r) * p.ldd] = v[r];
                 }
-                __syncwarp();
+                if (plane_on) {
+                    const long long o = static_cast<long long>(w.z) * pw.p.tstride + static_cast<long long>(m0) * pw.p.ld + n;
+                    if (pw.p.h16) {
+                        bool over = false;
 #pragma unroll
-                for (int r = 0; r < 16; ++r) sd[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = v[16 * h + r];
-                if (plane16) {
-                    bool over = false;
+                        for (int r = 0; r < 32; ++r) {
+                            if (full || r < vr) {
+                                const float s = v[r] * pw.scale;
+                                over |= !(fabsf(s) <= 65504.0f);
+                                pw.p.h16[o + static_cast<long long>(r) * pw.p.ld] = __float2half_rn(s);
+                            }
+                        }
+                        pw.overflow |= over;
+                    } else {
 #pragma unroll
-                    for (int r = 0; r < 16; ++r) {
-                        const float s = v[16 * h + r] * pw.scale;
-                        over |= 16 * h + r < vr && !(fabsf(s) <= 65504.0f);
-                        sp[r * 32 + (((lane >> 3) ^ ((r >> 1) & 3)) << 3) + (lane & 7)] = __float2half_rn(s);
+                        for (int r = 0; r < 32; ++r) {
+                            if (full || r < vr) {
+                                const float h = tf32_hi(v[r]);
+                                pw.p.hi[o + static_cast<long long>(r) * pw.p.ld] = h;
+                                pw.p.lo[o + static_cast<long long>(r) * pw.p.ld] = v[r] - h;
+                            }
+                        }
                     }
-                    pw.overflow |= over && col_ok;
                 }
-                ptx::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (p.tma_d) ptx::tma_store_3d(tma_d, sd, col0, m0 + 16 * h, w.z);
-                    if (plane16) ptx::tma_store_3d(tma_p, sp, col0, m0 + 16 * h, w.z);
-                    ptx::bulk_commit();
-                }
-                ++count;
             }
         }
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
     }
-    if (lane == 0) ptx::bulk_wait0();
-    __syncwarp();
     pw.flush();
 }
 
@@ -877,7 +918,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             wait_bar(mma_done, 0, p.health, &no_abort);
         }
     } else if (p.swap) {
-        drain_swap(&tma_d, &tma_p, p, acc_full, acc_empty, tmem, staging, abort_flag);
+        if (p.residual || p.accumulate || p.aux)
+            drain_swap<true>(p, acc_full, acc_empty, tmem, abort_flag);
+        else
+            drain_swap<false>(p, acc_full, acc_empty, tmem, abort_flag);
     } else if (p.tma_epi) {
         drain_tma(&tma_d, &tma_p, p, acc_full, acc_empty, tmem, staging, abort_flag);
     } else {
@@ -960,6 +1004,15 @@ bool make_map(CUtensorMap* map, const void* base, int elem, long long inner, lon
         return false;
     }
     return true;
+}
+
+// RL2_GEMM_SWAP=0 keeps the caller's orientation (no transposed accumulator) for every product.
+bool swap_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("RL2_GEMM_SWAP");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 // RL2_GEMM_TMA_STORE=0 keeps the register-store epilogue for every product.
@@ -1057,12 +1110,21 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     const int elem = g->kind == 0 ? 2 : 4;
     const int bk = 128 / elem;
     const int chunk = 128 / elem;
-    // Products with column statistics (no residual / accumulate / activation / split-K)
-    // run with the operands swapped: the accumulator tile is D^T (TMEM lane = output
-    // column), so a thread holds 32 rows of its column and the 32-row moments stay in
-    // registers. Kernel view of a swapped plan: M' = n, N' = m, A' = B, B' = A.
-    const bool swap = tma_store_enabled() && splits == 1 && g->stat_mean && !g->residual && !g->accumulate &&
-                      !g->activation && !g->act_aux && g->tile_n <= 0 && g->n >= 128 && outputs_tma_ok(g);
+    // Products with at least 128 output columns (and a plan-chosen tile width) run with the
+    // operands swapped: the accumulator tile is D^T (TMEM lane = output column), so a
+    // thread holds 32 rows of its column, the 32-row moments stay in registers and every
+    // global access of the epilogue covers whole 128-byte row segments (drain_swap).
+    // Kernel view of a swapped plan: M' = n, N' = m, A' = B, B' = A. RL2_GEMM_SWAP=0 keeps
+    // the caller's orientation for every product.
+    // D += result with nothing else reading the final values (no plane, no statistics, no
+    // activation) is faster as TMA reduce-add stores in the caller's orientation.
+    const bool in_place = g->d && (g->accumulate || (g->residual == g->d && g->ldr == g->ldd &&
+                                                      g->residual_batch_stride == g->d_batch_stride)) &&
+                          !(g->accumulate && g->residual);
+    const bool reduce_ok = in_place && !plane_used(&g->out_plane) && !g->stat_mean;
+    const bool reduce_path = tma_store_enabled() && splits == 1 && reduce_ok && !g->activation && !g->act_aux &&
+                             outputs_tma_ok(g);
+    const bool swap = swap_enabled() && g->tile_n <= 0 && g->n >= 128 && !reduce_path;
     rl2_gemm_desc sw = *g;
     if (swap) {
         sw.m = g->n;
@@ -1080,7 +1142,10 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     }
     const rl2_gemm_desc& o = sw;  // operands and tiles (the caller's view unless swapped)
     int bn = o.tile_n > 0 ? o.tile_n : auto_tile_n(o.n, o.kind, o.b_major);
-    if (swap) bn = std::min(256, (bn + 31) / 32 * 32);  // whole 32-row groups per tile
+    if (swap) {  // whole 32-row groups per tile (and whole 128-byte chunks of an M-contiguous A)
+        const int q = o.b_major ? chunk : 32;
+        bn = std::min(256, (bn + q - 1) / q * q);
+    }
     if (bn % 16 != 0 || bn < 16 || bn > 256 || (o.b_major == 1 && bn % chunk != 0)) {
         set_error("GEMM tile_n must be a multiple of 16 in [16, 256] (and of %d for an N-contiguous B)", chunk);
         return nullptr;
@@ -1183,36 +1248,26 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.vec_plane = plane_used(&g->out_plane) && g->out_plane.ld % 4 == 0 && g->out_plane.twin_stride % 4 == 0 &&
                   (g->out_plane.h16 ? aligned(g->out_plane.h16, 8)
                                     : a16(g->out_plane.hi) && a16(g->out_plane.lo));
-    // store-engine epilogue: outputs written by TMA stores when the product has no
-    // residual / accumulate / activation / split-K and the outputs satisfy the TMA rules.
-    // Boxes: 32 rows x 16 columns (fp32: 64-byte swizzle; fp16: 32-byte swizzle), or, for
-    // swapped plans, 16 rows x 32 columns (fp32: 128-byte swizzle; fp16: 64-byte swizzle).
+    // store-engine epilogue (plans that keep the caller's orientation): outputs written by
+    // TMA stores of 32-row x 16-column boxes (fp32: 64-byte swizzle; fp16: 32-byte swizzle)
+    // when the product has no activation / split-K and the outputs satisfy the TMA rules.
     // D += result (accumulate, or a residual that is D itself) goes through TMA reduce-add
-    // stores when nothing else needs the final values (no plane, no statistics).
-    const bool in_place = g->d && (g->accumulate || (g->residual == g->d && g->ldr == g->ldd &&
-                                                      g->residual_batch_stride == g->d_batch_stride)) &&
-                          !(g->accumulate && g->residual);
-    const bool reduce_ok = in_place && !plane_used(&g->out_plane) && !g->stat_mean;
-    if (swap || (tma_store_enabled() && p.splits == 1 && (!(g->residual || g->accumulate) || reduce_ok) &&
-                 !g->activation && !g->act_aux && outputs_tma_ok(g))) {
+    // stores when nothing else needs the final values (reduce_ok).
+    if (!swap && tma_store_enabled() && p.splits == 1 && (!(g->residual || g->accumulate) || reduce_ok) &&
+        !g->activation && !g->act_aux && outputs_tma_ok(g)) {
         const bool plane_on = plane_used(&g->out_plane);
-        const int bx = swap ? 32 : 16, by = swap ? 16 : 32;
         bool mok = true;
         if (g->d)
-            mok = make_map(&plan->td, g->d, 4, g->n, g->m, g->batch, g->ldd, g->d_batch_stride, bx, by,
-                           swap ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+            mok = make_map(&plan->td, g->d, 4, g->n, g->m, g->batch, g->ldd, g->d_batch_stride, 16, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
         if (mok && plane_on)
             mok = make_map(&plan->tp, g->out_plane.h16, 2, g->n, g->m, g->batch, g->out_plane.ld,
-                           g->out_plane.twin_stride, bx, by,
-                           swap ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+                           g->out_plane.twin_stride, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B);
         if (mok) {
             p.tma_epi = true;
             p.tma_d = g->d != nullptr;
             p.tma_plane = plane_on;
-            p.tma_reduce = !swap && reduce_ok;
-        } else if (swap) {
-            delete plan;  // the operands are already swapped: no register-store fallback
-            return nullptr;
+            p.tma_reduce = reduce_ok;
         } else {
             clear_error();  // fall back to the register-store epilogue
         }
@@ -1228,7 +1283,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         };
         auto tma_floats = [&](int nbuf) { return nbuf * (512 + (p.tma_plane ? 256 : 0)); };
         p.epi_bufs = 1;
-        p.stage_floats = 512;
+        p.stage_floats = swap ? 0 : 512;  // the transposed epilogue stages nothing
         if (p.tma_epi) {
             static const int forced = [] {
                 const char* e = std::getenv("RL2_GEMM_EPI_BUFS");
@@ -1292,8 +1347,9 @@ extern "C" int rl2_gemm_tile_n(void* opaque) {
 }
 
 extern "C" int rl2_gemm_uses_tma_store(void* opaque) {
-    if (!opaque || !static_cast<Plan*>(opaque)->p.tma_epi) return 0;
-    return static_cast<Plan*>(opaque)->p.swap ? 2 : 1;
+    if (!opaque) return 0;
+    const rl2::gemm::Params& p = static_cast<Plan*>(opaque)->p;
+    return p.swap ? 2 : p.tma_epi ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------

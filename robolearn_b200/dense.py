@@ -95,7 +95,7 @@ class DensePlan:
         self.handle = N.created(self._lib.rl2_gemm_create(ctypes.byref(desc)), "create tcgen05 GEMM plan")
         self.tile_n = self._lib.rl2_gemm_tile_n(self.handle)
         mode = self._lib.rl2_gemm_uses_tma_store(self.handle)
-        self.tma_store = mode > 0
+        self.tma_store = mode == 1
         self.transposed = mode == 2
         self.flops = 2 * m * n * k * batch * (3 if kind == TF32X3 else 1)
 

@@ -35,6 +35,7 @@ def main() -> None:
     p.add_argument("--stats", action="store_true")
     p.add_argument("--plane", action="store_true")
     p.add_argument("--residual", action="store_true")
+    p.add_argument("--in-place", action="store_true", help="residual = the output itself")
     p.add_argument("--no-d", action="store_true", help="write only the operand plane")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
@@ -71,7 +72,9 @@ def main() -> None:
             kw.update(k_splits=splits, d_split_stride=z * m * ldd)
     if splits == 1:
         kw.update(bias=torch.randn(z, n, device=dev, generator=g), bias_batch_stride=n)
-    if a.residual and splits == 1:
+    if a.in_place and splits == 1 and D is not None:
+        kw.update(residual=D[0], ldr=ldd, residual_batch_stride=m * ldd)
+    elif a.residual and splits == 1:
         kw.update(residual=torch.randn(z, m, n, device=dev, generator=g), ldr=n, residual_batch_stride=m * n)
     groups = (m + 31) // 32
     if a.stats and splits == 1:

@@ -263,8 +263,7 @@ def test_gemm_tma_store_epilogue(kind, m, n, k, tile_n, mode):
     else:
         pytest.skip("tf32 output planes take the register-store epilogue")
     plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + extra, tile_n=tile_n, **epi)
-    assert plan.tma_store
-    assert plan.transposed == (n >= 128 and tile_n == 0)  # every mode here asks for column statistics
+    assert plan.transposed if n >= 128 and tile_n == 0 else plan.tma_store
     D.fill_(float("nan"))
     plan.run()
     torch.cuda.synchronize()
@@ -293,8 +292,10 @@ def test_gemm_tma_store_epilogue(kind, m, n, k, tile_n, mode):
         assert int(found.item()) == 0
 
 
-def test_gemm_tma_store_plane_overflow_flag():
-    """fp16 plane through the store engine: a loss scale that overflows fp16 sets found_inf."""
+@pytest.mark.parametrize("tile_n", [0, 64])
+def test_gemm_plane_overflow_flag(tile_n):
+    """fp16 plane through the transposed epilogue (plan-chosen tile) and the store engine
+    (explicit tile width): a loss scale that overflows fp16 sets found_inf."""
     from robolearn_b200 import _native as N
 
     m, n, k, batch = 256, 128, 64, 2
@@ -304,35 +305,65 @@ def test_gemm_tma_store_plane_overflow_flag():
     found = torch.zeros(1, dtype=torch.int32, device="cuda")
     plane = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=m * pld, scale=pscale.data_ptr(),
                     found_inf=found.data_ptr())
-    plan, D, _ = _run(0, m, n, k, 0, 0, batch=batch, ldd=n, out_plane=plane)
-    assert plan.tma_store
+    plan, D, _ = _run(0, m, n, k, 0, 0, batch=batch, ldd=n, out_plane=plane, tile_n=tile_n)
+    assert plan.transposed if tile_n == 0 else plan.tma_store
     plan.run()
     torch.cuda.synchronize()
     assert int(found.item()) == 1
 
 
 @pytest.mark.parametrize("kind", [0, 1])
-@pytest.mark.parametrize("how", ["residual_in_place", "accumulate"])
-def test_gemm_tma_reduce_add_epilogue(kind, how):
-    """D += scale * A B^T + bias through TMA reduce-add stores (the residual is D itself, or
-    accumulate); ragged M / N tails; rows past M and columns past N stay untouched."""
+@pytest.mark.parametrize("how,plane,tile_n,path", [
+    ("residual_in_place", False, 0, "tma"),  # D += result as TMA reduce-add stores
+    ("accumulate", False, 0, "tma"),
+    ("residual_in_place", True, 0, "transposed"),  # the plane needs the final values
+    ("residual_in_place", True, 64, "registers"),
+    ("residual", True, 0, "transposed"),  # a separate residual array, rows loaded per lane
+])
+def test_gemm_residual_and_accumulate_paths(kind, how, plane, tile_n, path):
+    """D = scale * A B^T + bias + residual (the residual being D itself or another array), or
+    D += ... (accumulate), through each epilogue form; ragged M / N tails; rows past M and
+    columns past N untouched; the operand plane equals the output."""
+    from robolearn_b200 import _native as N
+
     m, n, k, batch = 1000, 600, 192, 2
     ldd = (n + 3) // 4 * 4 + 4
     bias = torch.randn(batch, n, device="cuda")
     scale = torch.tensor([0.25], device="cuda")
     old = torch.randn(batch, m + 8, ldd, device="cuda")
-    epi = dict(bias=bias, bias_batch_stride=n, scale=scale)
-    plan, D, ref = None, None, None
+    res = torch.randn(batch, m, n, device="cuda")
+    epi = dict(bias=bias, bias_batch_stride=n, scale=scale, tile_n=tile_n)
+    keep = []
+    if plane:
+        pld = dense.operand_ld(n, kind)
+        if kind == 0:
+            h16 = torch.zeros(batch, m, pld, device="cuda", dtype=torch.float16)
+            epi["out_plane"] = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=m * pld)
+            keep = [h16]
+        else:
+            hi = torch.zeros(batch, m, pld, device="cuda")
+            lo = torch.zeros(batch, m, pld, device="cuda")
+            epi["out_plane"] = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld)
+            keep = [hi, lo]
     if how == "accumulate":
-        plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + 8, accumulate=1, **epi)
+        epi["accumulate"] = 1
+    elif how == "residual_in_place":
+        epi.update(residual="D", ldr=ldd, residual_batch_stride=(m + 8) * ldd)
     else:
-        plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + 8, residual="D", ldr=ldd,
-                            residual_batch_stride=(m + 8) * ldd, **epi)
-    assert plan.tma_store and not plan.transposed
+        epi.update(residual=res, ldr=n, residual_batch_stride=m * n)
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=ldd, d_rows=m + 8, **epi)
+    assert (plan.transposed, plan.tma_store) == (path == "transposed", path == "tma")
     D.copy_(old)
     plan.run()
     torch.cuda.synchronize()
-    expect = ref * 0.25 + bias.double()[:, None, :] + old[:, :m, :n].double()
+    add = res.double() if how == "residual" else old[:, :m, :n].double()
+    expect = ref * 0.25 + bias.double()[:, None, :] + add
     tol = 2e-3 if kind == 0 else 2e-5
-    assert (D[:, :m, :n].double() - expect).abs().max().item() < tol * expect.abs().max().item()
+    out = D[:, :m, :n]
+    assert (out.double() - expect).abs().max().item() < tol * expect.abs().max().item()
     assert torch.equal(D[:, :m, n:], old[:, :m, n:]) and torch.equal(D[:, m:], old[:, m:])
+    if plane and kind == 0:
+        assert torch.equal(keep[0][:, :, :n], out.half())
+    elif plane:
+        hi_ref = (out.contiguous().view(torch.int32) & -8192).view(torch.float32)
+        assert torch.equal(keep[0][:, :, :n], hi_ref) and torch.equal(keep[1][:, :, :n], out - hi_ref)
