@@ -142,7 +142,8 @@ int rl2_split_reduce(const float* partial, long long split_stride, int splits, f
  * d_hi/d_lo tf32 operand planes, target_out [B][bins]. loss_out, max_entropy_out
  * (max of alpha * next_log_pi), bias_grad_out [2][bins] are reduced in a fixed
  * order. workspace holds rl2_categorical_workspace_floats(batch, bins) floats;
- * counter is one zero-initialised unsigned int that the kernel leaves at zero.
+ * counter holds rl2_categorical_counter_words(batch, bins) zero-initialised unsigned
+ * ints that the kernel leaves at zero.
  * ------------------------------------------------------------------------- */
 typedef struct rl2_critic_objective_args {
     const float* target_logits;
@@ -179,13 +180,14 @@ typedef struct rl2_critic_objective_args {
 } rl2_critic_objective_args;
 
 int rl2_categorical_workspace_floats(int batch, int bins);
+int rl2_categorical_counter_words(int batch, int bins);
 int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
 
 /* Allocation-free variant of rl2_critic_objective (no counterpart in the reference).
  * For callers that cannot allocate device memory where they run this objective, e.g. a
  * real-time control loop that must not stall in the driver's allocator, or a host whose
  * device memory is owned by another framework's pool. args->workspace and args->counter
- * are ignored: the kernel uses a file-scope device array (about 1.2 MB per GPU, held
+ * are ignored: the kernel uses a file-scope device array (about 0.65 MB per GPU, held
  * until process exit). Limits: batch <= 65536, bins <= 128; larger sizes return -1.
  * The first call on each device looks up that array's address (make it before any
  * stream capture). All calls share the array: calls that overlap on the GPU race,

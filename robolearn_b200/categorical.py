@@ -31,7 +31,7 @@ class CriticObjective:
         lib = N.load()
         self._lib = lib
         self.workspace = torch.zeros(lib.rl2_categorical_workspace_floats(batch, bins), device=device)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.counter = torch.zeros(lib.rl2_categorical_counter_words(batch, bins), dtype=torch.int32, device=device)
         self.support = torch.from_numpy(support(bins, min_v, max_v)).to(device)
 
     def run(self, *, target_logits, target_row_stride, target_twin_stride, target_row_offset, online_logits,

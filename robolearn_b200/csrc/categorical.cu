@@ -7,16 +7,22 @@
 //   CE + gradient     src/robolearn/flashsac/updates.py:248-257 (mean over [2, B]; autograd)
 //   native version    src/robolearn/cuda/categorical_kernels.cuh:87-114 (shared-memory atomics)
 //
-// Design: one warp per transition row. The target twin's log-softmax and
-// expected value, the min-Q selection, the projection and the online twins'
-// cross-entropy all stay in registers / per-warp shared memory; the only global
-// traffic is the two logits reads and the gradient write. The projection is
-// deterministic without atomics: the shifted atom values are monotone in the
-// source atom index j, so every target atom receives a contiguous run of j and a
-// warp segmented scan produces each run's sum in a fixed order.
-// The float arithmetic of the bin location uses round-to-nearest intrinsics (no
-// FMA contraction) in the reference's operation order, so lower/upper/fraction
-// agree with Torch's float32 evaluation.
+// Design: eight lanes per transition row, four rows per warp. A lane holds E = ceil(bins /
+// 8) atoms of its row, strided (atom k = sub + 8 s) for the elementwise work, so every
+// load and store instruction covers whole 32-byte row segments and every row reduction is
+// three shuffles inside the lane's group of eight; each atom's exp(x - max) serves both the
+// softmax sum and the probabilities (one exponential per atom and twin, the __expf
+// intrinsic). The projection runs on the blocked
+// layout (atom j = E sub + s, exchanged through shared memory): the shifted atom values are
+// monotone in the source atom j, so every target atom receives a contiguous run of j, and a
+// segmented scan (sequential inside a lane, three shuffle steps across the group) produces
+// each run's sum in a fixed order: deterministic without atomics. The float arithmetic of
+// the bin location uses round-to-nearest intrinsics (no FMA contraction) in the reference's
+// operation order, so lower/upper/fraction agree with Torch's float32 evaluation.
+//
+// Cross-block reduction of the head-bias gradient, loss and entropy maximum: each block
+// writes one partial row; the last block of each group of 16 (by ticket) sums its group's
+// rows in block order, and the last group to finish sums the group rows in group order.
 
 #include "common.cuh"
 #include "../../include/rl2.h"
@@ -29,7 +35,11 @@ namespace cat {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxBins = 128;  // 4 atoms per lane
+constexpr int kRowsPerWarp = 4;  // eight lanes per row
+constexpr int kRowsPerBlock = kWarps * kRowsPerWarp;
+constexpr int kMaxBins = 128;
+constexpr int kGroup = 16;  // blocks per first-level reduction group
+constexpr int kMaxGrid = 148 * 4;
 
 struct Args {
     const float* target_logits;
@@ -56,8 +66,8 @@ struct Args {
     long long dp_row, dp_twin;
     float* target_out;
     long long target_row;
-    float* partial;  // [grid][2*bins + 2]
-    unsigned* counter;
+    float* partial;  // [grid][2*bins + 2] block rows, then [groups][2*bins + 2] group rows
+    unsigned* counter;  // [0]: group tickets; [1 + g]: block tickets of group g
     float* loss_out;
     float* max_entropy_out;
     float* bias_grad_out;
@@ -65,122 +75,167 @@ struct Args {
     int* health;
 };
 
-// Warp segmented inclusive scan over 4 blocked elements per lane (element j = 4*lane + s)
-// with monotone non-decreasing keys; writes each run's total to out[key] at the run's end.
-__device__ __forceinline__ void scatter_runs(const int (&key)[4], const float (&val)[4], float* out, int bins) {
-    const int lane = threadIdx.x & 31;
-    float acc[4];
+inline int grid_for(int batch) { return std::max(1, std::min((batch + kRowsPerBlock - 1) / kRowsPerBlock, kMaxGrid)); }
+inline int groups_for(int grid) { return (grid + kGroup - 1) / kGroup; }
+
+// Row pitch of the per-row shared arrays: >= 8E and = 8 (mod 32), so that the strided
+// (k = sub + 8 s) and blocked (j = E sub + s) accesses of the four rows of a warp spread
+// over the banks.
+template <int E>
+__host__ __device__ constexpr int pitch() {
+    return 8 * E + ((8 - (8 * E) % 32) + 32) % 32;
+}
+
+__device__ __forceinline__ float gsum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    return v;
+}
+
+__device__ __forceinline__ float gmax(float v) {
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    return v;
+}
+
+// Segmented inclusive scan over the blocked elements of a row (lane sub holds j = E sub + s)
+// with monotone non-decreasing keys: each run's total goes to out[key] at the run's last
+// element (out[key] += total when add). Keys outside [0, bins) are never written.
+template <int E>
+__device__ __forceinline__ void scatter_runs(const int (&key)[E], const float (&val)[E], float* out, int bins,
+                                             bool add) {
+    const int sub = threadIdx.x & 7;
+    float acc[E];
     acc[0] = val[0];
 #pragma unroll
-    for (int s = 1; s < 4; ++s) acc[s] = (key[s] == key[s - 1]) ? acc[s - 1] + val[s] : val[s];
-    const int tail = key[3];
-    float run = acc[3];
-    bool open = key[0] == key[3];
+    for (int s = 1; s < E; ++s) acc[s] = (key[s] == key[s - 1]) ? acc[s - 1] + val[s] : val[s];
+    const int tail = key[E - 1];
+    float run = acc[E - 1];
+    bool open = key[0] == key[E - 1];
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        const int ok = __shfl_up_sync(0xffffffffu, tail, d);
-        const float os = __shfl_up_sync(0xffffffffu, run, d);
-        const int oo = __shfl_up_sync(0xffffffffu, static_cast<int>(open), d);
-        if (lane >= d && open && ok == tail) {
+    for (int d = 1; d < 8; d <<= 1) {
+        const int ok = __shfl_up_sync(0xffffffffu, tail, d, 8);
+        const float os = __shfl_up_sync(0xffffffffu, run, d, 8);
+        const int oo = __shfl_up_sync(0xffffffffu, static_cast<int>(open), d, 8);
+        if (sub >= d && open && ok == tail) {
             run = os + run;
             open = oo != 0;
         }
     }
-    const int prev_tail = __shfl_up_sync(0xffffffffu, tail, 1);
-    const float prev_run = __shfl_up_sync(0xffffffffu, run, 1);
-    const float carry = (lane > 0 && prev_tail == key[0]) ? prev_run : 0.0f;
+    const int prev_tail = __shfl_up_sync(0xffffffffu, tail, 1, 8);
+    const float prev_run = __shfl_up_sync(0xffffffffu, run, 1, 8);
+    const float carry = (sub > 0 && prev_tail == key[0]) ? prev_run : 0.0f;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
+    for (int s = 0; s < E; ++s)
         if (key[s] == key[0]) acc[s] = carry + acc[s];
-    const int next_head = __shfl_down_sync(0xffffffffu, key[0], 1);
+    const int next_head = __shfl_down_sync(0xffffffffu, key[0], 1, 8);
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const int nk = s < 3 ? key[s + 1] : (lane < 31 ? next_head : INT_MAX - 1);
-        if (key[s] != nk && key[s] >= 0 && key[s] < bins) out[key[s]] = acc[s];
+    for (int s = 0; s < E; ++s) {
+        const int nk = s < E - 1 ? key[s + 1] : (sub < 7 ? next_head : INT_MAX - 1);
+        if (key[s] != nk && key[s] >= 0 && key[s] < bins) out[key[s]] = add ? out[key[s]] + acc[s] : acc[s];
     }
 }
 
+template <int E>
 __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a) {
-    __shared__ float z_s[kMaxBins];
-    __shared__ float p_s[kWarps][kMaxBins];
-    __shared__ float lo_s[kWarps][kMaxBins];
-    __shared__ float up_s[kWarps][kMaxBins];
-    __shared__ float red_s[kWarps][2 * kMaxBins + 2];
-    __shared__ bool last_block;
+    constexpr int P = pitch<E>();
+    __shared__ float z_s[8 * E];
+    __shared__ float p_s[kWarps][kRowsPerWarp][P];  // selected target distribution (strided write, blocked read)
+    __shared__ float t_s[kWarps][kRowsPerWarp][P];  // projected target
+    __shared__ float red_s[kWarps][2 * 8 * E + 2];
+    __shared__ bool last_s;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int sub = lane & 7;
+    const int rg = lane >> 3;
     const int bins = a.bins;
-    for (int k = threadIdx.x; k < kMaxBins; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
+    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
     __syncthreads();
+    float* pw = p_s[warp][rg];
+    float* tw = t_s[warp][rg];
 
     const float alpha = a.alpha[0];
     const float scale16 = a.d16 ? a.d16_scale[0] : 1.0f;
     const float width = a.width;
-    float bias_acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    float bias_acc[2][E];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int s = 0; s < E; ++s) bias_acc[t][s] = 0.0f;
     float loss_acc = 0.0f;
     float ent_max = -INFINITY;
     bool overflow = false;
 
-    for (int row = blockIdx.x * kWarps + warp; row < a.batch; row += gridDim.x * kWarps) {
-        // ---- target twins at the next-observation row: log-softmax and expected value
-        float tl[2][4];
-        float q[2];
+    for (int base = (blockIdx.x * kWarps + warp) * kRowsPerWarp; base < a.batch;
+         base += gridDim.x * kRowsPerBlock) {
+        const int row = base + rg;
+        const bool rv = row < a.batch;
+        // ---- target twins at the next-observation row: softmax and expected value; twin 0's
+        // probabilities go to shared memory and twin 1's replace them when its value is lower
+        float q0 = 0.0f;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
             const float* src = a.target_logits + t * a.t_twin + static_cast<long long>(a.t_row0 + row) * a.t_row;
+            float e[E];
             float mx = -INFINITY;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int k = lane + 32 * s;
-                tl[t][s] = k < bins ? src[k] : -INFINITY;
-                mx = fmaxf(mx, tl[t][s]);
+            for (int s = 0; s < E; ++s) {
+                const int k = sub + 8 * s;
+                e[s] = (rv && k < bins) ? src[k] : -INFINITY;
+                mx = fmaxf(mx, e[s]);
             }
-            mx = warp_max(mx);
+            mx = gmax(mx);
             float se = 0.0f;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) se += (lane + 32 * s < bins) ? expf(tl[t][s] - mx) : 0.0f;
-            const float lse = mx + logf(warp_sum(se));
+            for (int s = 0; s < E; ++s) {
+                e[s] = (sub + 8 * s < bins) ? __expf(e[s] - mx) : 0.0f;
+                se += e[s];
+            }
+            const float inv = 1.0f / gsum(se);
             float qq = 0.0f;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int k = lane + 32 * s;
-                const float lp = tl[t][s] - lse;
-                tl[t][s] = k < bins ? expf(lp) : 0.0f;  // now probabilities
-                qq += tl[t][s] * z_s[k];
+            for (int s = 0; s < E; ++s) {
+                e[s] = e[s] * inv;  // probabilities
+                qq += e[s] * z_s[sub + 8 * s];
             }
-            q[t] = warp_sum(qq);
-        }
-        const int sel = q[1] < q[0] ? 1 : 0;
+            qq = gsum(qq);
+            if (t == 0) {
+                q0 = qq;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) p_s[warp][lane + 32 * s] = sel ? tl[1][s] : tl[0][s];
+                for (int s = 0; s < E; ++s) {
+                    pw[sub + 8 * s] = e[s];
+                    tw[sub + 8 * s] = 0.0f;
+                }
+            } else if (qq < q0) {  // min-Q twin, ties keep twin 0
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            lo_s[warp][lane + 32 * s] = 0.0f;
-            up_s[warp][lane + 32 * s] = 0.0f;
+                for (int s = 0; s < E; ++s) pw[sub + 8 * s] = e[s];
+            }
         }
         __syncwarp();
 
-        // ---- projection of the selected distribution (blocked layout j = 4*lane + s)
-        const float r = a.reward[row];
-        const float done = a.terminated[row];
-        const float g = a.discount[row];
-        const float ent = __fmul_rn(alpha, a.next_log_pi[row]);
+        // ---- projection of the selected distribution (blocked layout j = E sub + s)
+        const float r = rv ? a.reward[row] : 0.0f;
+        const float done = rv ? a.terminated[row] : 0.0f;
+        const float g = rv ? a.discount[row] : 0.0f;
+        const float ent = rv ? __fmul_rn(alpha, a.next_log_pi[row]) : -INFINITY;
         ent_max = fmaxf(ent_max, ent);
         const float cont = __fsub_rn(1.0f, done);
-        int kl[4], ku[4];
-        float ml[4], mu[4];
+        int kl[E], ku[E];
+        float ml[E], mu[E];
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int j = 4 * lane + s;
-            if (j < bins) {
+        for (int s = 0; s < E; ++s) {
+            const int j = E * sub + s;
+            if (rv && j < bins) {
                 float v = __fadd_rn(r, __fmul_rn(__fmul_rn(g, __fsub_rn(z_s[j], ent)), cont));
                 v = fminf(fmaxf(v, a.min_v), a.max_v);
                 const float b = __fdiv_rn(__fsub_rn(v, a.min_v), width);
                 const int lower = static_cast<int>(floorf(b));
                 const int upper = min(max(lower + 1, 0), bins - 1);
                 const float frac = __fsub_rn(b, static_cast<float>(lower));
-                const float p = p_s[warp][j];
+                const float p = pw[j];
                 kl[s] = lower;
                 ku[s] = upper;
                 ml[s] = __fmul_rn(p, __fsub_rn(1.0f, frac));
@@ -192,46 +247,53 @@ __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a
                 mu[s] = 0.0f;
             }
         }
-        scatter_runs(kl, ml, lo_s[warp], bins);
-        scatter_runs(ku, mu, up_s[warp], bins);
+        scatter_runs<E>(kl, ml, tw, bins, false);
         __syncwarp();
-        float tgt[4];
+        scatter_runs<E>(ku, mu, tw, bins, true);
+        __syncwarp();
+        float tgt[E];
         float tsum = 0.0f;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int k = lane + 32 * s;
-            tgt[s] = k < bins ? lo_s[warp][k] + up_s[warp][k] : 0.0f;
+        for (int s = 0; s < E; ++s) {
+            const int k = sub + 8 * s;
+            tgt[s] = k < bins ? tw[k] : 0.0f;
             tsum += tgt[s];
-            if (a.target_out && k < bins) a.target_out[static_cast<long long>(row) * a.target_row + k] = tgt[s];
+            if (a.target_out && rv && k < bins) a.target_out[static_cast<long long>(row) * a.target_row + k] = tgt[s];
         }
-        tsum = warp_sum(tsum);
-        __syncwarp();
+        tsum = gsum(tsum);
 
         // ---- online twins at the current-observation row: CE and logits gradient
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
             const float* src = a.online_logits + t * a.o_twin + static_cast<long long>(row) * a.o_row;
-            float x[4];
+            float x[E];
             float mx = -INFINITY;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int k = lane + 32 * s;
-                x[s] = k < bins ? src[k] : -INFINITY;
+            for (int s = 0; s < E; ++s) {
+                const int k = sub + 8 * s;
+                x[s] = (rv && k < bins) ? src[k] : -INFINITY;
                 mx = fmaxf(mx, x[s]);
             }
-            mx = warp_max(mx);
+            mx = gmax(mx);
+            float ex[E];
             float se = 0.0f;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) se += (lane + 32 * s < bins) ? expf(x[s] - mx) : 0.0f;
-            const float lse = mx + logf(warp_sum(se));
+            for (int s = 0; s < E; ++s) {
+                ex[s] = (sub + 8 * s < bins) ? __expf(x[s] - mx) : 0.0f;
+                se += ex[s];
+            }
+            se = gsum(se);
+            const float lse = mx + logf(se);
+            const float inv = 1.0f / se;
+            if (!rv) continue;
             float ce = 0.0f;
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int k = lane + 32 * s;
+            for (int s = 0; s < E; ++s) {
+                const int k = sub + 8 * s;
                 if (k >= bins) continue;
                 const float lp = x[s] - lse;
                 ce -= tgt[s] * lp;
-                const float grad = (expf(lp) * tsum - tgt[s]) * a.loss_weight;
+                const float grad = (ex[s] * inv * tsum - tgt[s]) * a.loss_weight;
                 bias_acc[t][s] += grad;
                 if (a.dlogits) a.dlogits[t * a.d_twin + static_cast<long long>(row) * a.d_row + k] = grad;
                 if (a.d16) {
@@ -246,52 +308,92 @@ __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a
                     a.d_lo[o] = grad - hi;
                 }
             }
-            loss_acc += warp_sum(ce) * a.loss_weight;
+            loss_acc += ce;
         }
+        __syncwarp();  // the next rows overwrite this warp's shared rows
     }
     if (overflow && a.health) atomicOr(a.health, kHealthOverflow);
 
-    // ---- block partials: bias gradient [2][bins], loss, max entropy
+    // ---- block partial row: bias gradient [2][bins], loss, max entropy
+    // (the four row groups of a warp hold the same atoms: xor 8, 16 combine them)
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int s = 0; s < 4; ++s) red_s[warp][t * kMaxBins + lane + 32 * s] = bias_acc[t][s];
-    if (lane == 0) {
-        red_s[warp][2 * kMaxBins] = loss_acc;
-        red_s[warp][2 * kMaxBins + 1] = warp_max(ent_max);
-    } else {
-        (void)warp_max(ent_max);
-    }
-    __syncthreads();
-    const int width_p = 2 * bins + 2;
-    float* part = a.partial + static_cast<long long>(blockIdx.x) * width_p;
-    for (int i = threadIdx.x; i < 2 * bins; i += kThreads) {
-        const int t = i / bins, k = i % bins;
-        float s = 0.0f;
-        for (int w = 0; w < kWarps; ++w) s += red_s[w][t * kMaxBins + k];
-        part[i] = s;
-    }
-    if (threadIdx.x == 0) {
-        float l = 0.0f, e = -INFINITY;
-        for (int w = 0; w < kWarps; ++w) {
-            l += red_s[w][2 * kMaxBins];
-            e = fmaxf(e, red_s[w][2 * kMaxBins + 1]);
+        for (int s = 0; s < E; ++s) {
+            float v = bias_acc[t][s];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (rg == 0) red_s[warp][t * 8 * E + sub + 8 * s] = v;
         }
-        part[2 * bins] = l;
-        part[2 * bins + 1] = e;
+    {
+        const float l = warp_sum(loss_acc) * a.loss_weight;
+        const float e = warp_max(ent_max);
+        if (lane == 0) {
+            red_s[warp][2 * 8 * E] = l;
+            red_s[warp][2 * 8 * E + 1] = e;
+        }
     }
-    // ---- last block reduces all block partials in a fixed order
+    __syncthreads();
+    const int W = 2 * bins + 2;
+    float* rows = a.partial;
+    const int grid = static_cast<int>(gridDim.x);
+    const int groups = (grid + kGroup - 1) / kGroup;
+    float* group_rows = a.partial + static_cast<long long>(grid) * W;
+    for (int i = threadIdx.x; i < W; i += kThreads) {
+        float s;
+        if (i < 2 * bins) {
+            const int t = i / bins, k = i % bins;
+            s = 0.0f;
+            for (int w = 0; w < kWarps; ++w) s += red_s[w][t * 8 * E + k];
+        } else if (i == 2 * bins) {
+            s = 0.0f;
+            for (int w = 0; w < kWarps; ++w) s += red_s[w][2 * 8 * E];
+        } else {
+            s = -INFINITY;
+            for (int w = 0; w < kWarps; ++w) s = fmaxf(s, red_s[w][2 * 8 * E + 1]);
+        }
+        rows[static_cast<long long>(blockIdx.x) * W + i] = s;
+    }
+    // ---- first level: the last block of the group sums the group's rows in block order
+    const int grp = blockIdx.x / kGroup;
+    const int first = grp * kGroup;
+    const int members = min(kGroup, grid - first);
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) last_block = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) last_s = atomicAdd(a.counter + 1 + grp, 1u) == static_cast<unsigned>(members - 1);
     __syncthreads();
-    if (!last_block) return;
+    if (!last_s) return;
     __threadfence();
-    for (int i = threadIdx.x; i < width_p; i += kThreads) {
-        float s = i == 2 * bins + 1 ? -INFINITY : 0.0f;
-        for (unsigned b = 0; b < gridDim.x; ++b) {
-            const float v = a.partial[static_cast<long long>(b) * width_p + i];
-            s = (i == 2 * bins + 1) ? fmaxf(s, v) : s + v;
+    for (int i = threadIdx.x; i < W; i += kThreads) {
+        const bool is_max = i == 2 * bins + 1;
+        float v[kGroup];
+#pragma unroll
+        for (int b = 0; b < kGroup; ++b) v[b] = b < members ? __ldcg(rows + static_cast<long long>(first + b) * W + i) : 0.0f;
+        float s = is_max ? -INFINITY : 0.0f;
+#pragma unroll
+        for (int b = 0; b < kGroup; ++b)
+            if (b < members) s = is_max ? fmaxf(s, v[b]) : s + v[b];
+        group_rows[static_cast<long long>(grp) * W + i] = s;
+    }
+    if (threadIdx.x == 0) a.counter[1 + grp] = 0u;
+    // ---- second level: the last group sums the group rows in group order
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_s = atomicAdd(a.counter, 1u) == static_cast<unsigned>(groups - 1);
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < W; i += kThreads) {
+        const bool is_max = i == 2 * bins + 1;
+        float s = is_max ? -INFINITY : 0.0f;
+        for (int g0 = 0; g0 < groups; g0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                v[u] = g0 + u < groups ? __ldcg(group_rows + static_cast<long long>(g0 + u) * W + i) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (g0 + u < groups) s = is_max ? fmaxf(s, v[u]) : s + v[u];
         }
         if (i < 2 * bins) {
             if (a.bias_grad_out) a.bias_grad_out[i] = a.bias_accumulate ? a.bias_grad_out[i] + s : s;
@@ -301,15 +403,20 @@ __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a
             if (a.max_entropy_out) a.max_entropy_out[0] = s;
         }
     }
-    if (threadIdx.x == 0) *a.counter = 0u;
+    if (threadIdx.x == 0) a.counter[0] = 0u;
 }
 
 }  // namespace cat
 }  // namespace rl2
 
 extern "C" int rl2_categorical_workspace_floats(int batch, int bins) {
-    const int grid = std::min((batch + rl2::cat::kWarps - 1) / rl2::cat::kWarps, 148 * 8);
-    return grid * (2 * bins + 2);
+    const int grid = rl2::cat::grid_for(batch);
+    return (grid + rl2::cat::groups_for(grid)) * (2 * bins + 2);
+}
+
+extern "C" int rl2_categorical_counter_words(int batch, int bins) {
+    (void)bins;
+    return 1 + rl2::cat::groups_for(rl2::cat::grid_for(batch));
 }
 
 extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* stream) {
@@ -368,8 +475,17 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
     a.bias_grad_out = g->bias_grad_out;
     a.bias_accumulate = g->bias_grad_accumulate;
     a.health = g->health;
-    const int grid = std::min((g->batch + cat::kWarps - 1) / cat::kWarps, 148 * 8);
-    cat::critic_objective_kernel<<<grid, cat::kThreads, 0, as_stream(stream)>>>(a);
+    const int grid = cat::grid_for(g->batch);
+    cudaStream_t s = as_stream(stream);
+    const int e = (g->bins + 7) / 8;
+    if (e <= 4)
+        cat::critic_objective_kernel<4><<<grid, cat::kThreads, 0, s>>>(a);
+    else if (e <= 8)
+        cat::critic_objective_kernel<8><<<grid, cat::kThreads, 0, s>>>(a);
+    else if (e <= 13)
+        cat::critic_objective_kernel<13><<<grid, cat::kThreads, 0, s>>>(a);
+    else
+        cat::critic_objective_kernel<16><<<grid, cat::kThreads, 0, s>>>(a);
     return launch_status("critic objective");
 }
 
@@ -382,13 +498,13 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
 // memory through that framework's pool with no hook to hand out a workspace. This
 // entry point needs no workspace from them: its block partials and completion
 // counter live in the file-scope array below, which every GPU that loads the
-// library holds until the process exits (about 1.2 MB).
+// library holds until the process exits (about 0.65 MB).
 //
 // Limits: batch <= kNoAllocMaxBatch rows and bins <= 128 atoms; larger sizes are
 // rejected with an error. The first call on a device looks up the array's device
 // address (cudaGetSymbolAddress) with that device current; make that first call
 // before any stream capture. All calls share the one array and it keeps the last
-// call's contents: the counter is cleared at the start of every call (the partials
+// call's contents: the counters are cleared at the start of every call (the partials
 // are fully rewritten before they are read), and calls that overlap on the GPU
 // (concurrent streams, or concurrent host threads) race on it, so issue them in
 // order on one stream.
@@ -399,9 +515,9 @@ namespace rl2 {
 namespace cat {
 
 constexpr int kNoAllocMaxBatch = 65536;
-constexpr int kNoAllocMaxGrid = 148 * 8;                        // same grid rule as rl2_critic_objective
-constexpr int kNoAllocFloats = kNoAllocMaxGrid * (2 * kMaxBins + 2);  // 305,472 floats of block partials
-constexpr int kNoAllocCounterPad = 64;                          // counter word kept 256-byte aligned
+constexpr int kNoAllocGroups = (kMaxGrid + kGroup - 1) / kGroup;  // same grid rule as rl2_critic_objective
+constexpr int kNoAllocFloats = (kMaxGrid + kNoAllocGroups) * (2 * kMaxBins + 2);  // 162,282 floats of partial rows
+constexpr int kNoAllocCounterPad = 64;  // counter words (1 + groups <= 64), 256-byte aligned
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats + kNoAllocCounterPad];
 
@@ -448,8 +564,8 @@ extern "C" int rl2_critic_objective_noalloc(const rl2_critic_objective_args* g, 
     float* scratch = cat::noalloc_scratch(device);
     if (!scratch) return -1;
     unsigned* counter = reinterpret_cast<unsigned*>(scratch + cat::kNoAllocFloats);
-    if (cudaMemsetAsync(counter, 0, sizeof(unsigned), as_stream(stream)) != cudaSuccess) {
-        set_error("critic objective (no-alloc): clearing the completion counter failed");
+    if (cudaMemsetAsync(counter, 0, sizeof(unsigned) * (1 + cat::kNoAllocGroups), as_stream(stream)) != cudaSuccess) {
+        set_error("critic objective (no-alloc): clearing the completion counters failed");
         return -1;
     }
     rl2_critic_objective_args a = *g;

@@ -61,7 +61,7 @@ def test_no_alloc_matches_workspace_entry_point_twice(B, bins):
     # reference: the existing entry point with a caller-provided workspace and counter
     a, t = _args(B, bins, seed=B)
     ws = torch.zeros(lib.rl2_categorical_workspace_floats(B, bins), device="cuda")
-    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    counter = torch.zeros(lib.rl2_categorical_counter_words(B, bins), dtype=torch.int32, device="cuda")
     a.workspace, a.counter = ws.data_ptr(), counter.data_ptr()
     assert lib.rl2_critic_objective(ctypes.byref(a), stream) == 0
     torch.cuda.synchronize()
