@@ -19,6 +19,11 @@ learner data-parallel: every rank processes 4096 rows of the N x 4096 global bat
 ranks and gradients averaged with NCCL before Adam; ``value`` counts N x 4096-row
 updates per second (weak scaling).
 
+``--workload cfg5`` times config 5 instead (critic 1024 x 3 blocks, actor 128 x 2,
+FP32 recipe, a global batch of 32768 split over the ranks: strong scaling);
+``--workload ppo`` the config-2 WarpPPO update; ``--workload categorical`` the
+config-4 objective microbench. Only the JSON line goes to stdout.
+
 ``--impl reference`` times the CPU restatement of the reference update (the
 reference is Python/Torch and cannot travel to the GPU box) on all host cores.
 """
@@ -40,6 +45,10 @@ sys.path.insert(0, str(ROOT))
 
 OBS, ACT, ENVS, BATCH = 123, 37, 4096, 4096
 METRIC = "FlashSAC updates/s (obs123/act37, batch 4096)"
+# data-parallel FlashSAC, global batch 32768 split over the ranks
+# (strong scaling), critics 1024 x 3 blocks, actor 128 x 2 (defaults), FP32 recipe
+CFG5_METRIC = "FlashSAC cfg5 updates/s (obs123/act37, global batch 32768, critic 1024x3, FP32)"
+CFG5_BATCH = 32768
 
 
 def parse():
@@ -51,8 +60,10 @@ def parse():
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ppo", action="store_true", help="leave the PPO summary out of the FlashSAC line")
-    p.add_argument("--workload", choices=("flashsac", "ppo", "categorical"), default="flashsac",
-                   help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms)")
+    p.add_argument("--workload", choices=("flashsac", "ppo", "categorical", "cfg5"), default="flashsac",
+                   help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms); "
+                        "categorical: the cfg4 objective microbench; cfg5: the data-parallel FP32 config "
+                        "(global batch 32768 split over --gpus ranks)")
     return p.parse_args()
 
 
@@ -108,9 +119,9 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def build(precision: str, device, seed: int = 0, dp=None):
-    """Learner + synthetic device replay at the config-3 shapes (batch 4096 per rank; with
-    ``dp`` the ranks train one learner on the global batch, replay replicated)."""
+def build(precision: str, device, seed: int = 0, dp=None, batch: int = BATCH, critic=(512, 2), actor=(256, 2)):
+    """Learner + synthetic device replay (config-3 shapes by default: batch 4096 per rank;
+    with ``dp`` the ranks train one learner on the global batch, replay replicated)."""
     import torch
 
     from robolearn_b200.flashsac.config import FlashSACConfig
@@ -118,13 +129,15 @@ def build(precision: str, device, seed: int = 0, dp=None):
     from robolearn_b200.flashsac.replay import DeviceReplay
     from robolearn_b200.flashsac.sampling import sampling_program
 
-    cfg = FlashSACConfig(device=str(device), sample_batch_size=BATCH, critic_hidden_dim=512, critic_num_blocks=2,
-                         actor_hidden_dim=256, actor_num_blocks=2, critic_num_bins=101, critic_min_v=-10.0,
-                         critic_max_v=10.0, critic_target_update_tau=0.005, learning_rate_init=3e-4,
-                         learning_rate_peak=3e-4, learning_rate_end=3e-4, n_step=1, buffer_max_length=16 * ENVS,
-                         buffer_min_length=BATCH, dense_precision=precision, seed=seed)
+    world = dp.world if dp is not None else 1
+    cap = max(16 * ENVS, 2 * batch * world)
+    cfg = FlashSACConfig(device=str(device), sample_batch_size=batch, critic_hidden_dim=critic[0],
+                         critic_num_blocks=critic[1], actor_hidden_dim=actor[0], actor_num_blocks=actor[1],
+                         critic_num_bins=101, critic_min_v=-10.0, critic_max_v=10.0, critic_target_update_tau=0.005,
+                         learning_rate_init=3e-4, learning_rate_peak=3e-4, learning_rate_end=3e-4, n_step=1,
+                         buffer_max_length=cap, buffer_min_length=batch * world, dense_precision=precision, seed=seed)
     L = Learner(OBS, OBS, ACT, cfg, device, dp=dp)
-    R = DeviceReplay(OBS, ACT, ENVS, 16 * ENVS, 1, 0.99, BATCH, device, seed=seed)
+    R = DeviceReplay(OBS, ACT, ENVS, cap, 1, 0.99, batch * world, device, seed=seed)
     g = torch.Generator(device=device).manual_seed(2026 + seed)
     cap = R.capacity
     R.observation.copy_(torch.randn(cap, OBS, device=device, generator=g))
@@ -183,7 +196,7 @@ def gemm_roofline(L, peak_tflops):
             "flops_per_pair": flops, "ms_per_pair": round(sec * 1e3, 4)}
 
 
-def cpu_update_rate(batch: int, pairs: int = 1):
+def cpu_update_rate(batch: int, pairs: int = 1, critic=(512, 2), actor=(256, 2)):
     """CPU restatement of the reference update (oracle, float32, all host cores): updates/s at ``batch``.
 
     Returns (updates_per_s_at_batch, seconds, cores). Used by the cpu_baseline field
@@ -195,22 +208,24 @@ def cpu_update_rate(batch: int, pairs: int = 1):
     from robolearn_b200.flashsac.config import FlashSACConfig
     from robolearn_b200.flashsac.learner import _init_reference_weights
 
-    d = fs.Dims(obs=OBS, act=ACT, actor_hidden=256, actor_blocks=2, critic_hidden=512, critic_blocks=2, bins=101,
-                min_v=-10.0, max_v=10.0)
-    a0, c0, lt = _init_reference_weights(OBS, OBS, ACT, FlashSACConfig(device="cpu", actor_hidden_dim=256,
-                                                                       critic_hidden_dim=512))
+    d = fs.Dims(obs=OBS, act=ACT, actor_hidden=actor[0], actor_blocks=actor[1], critic_hidden=critic[0],
+                critic_blocks=critic[1], bins=101, min_v=-10.0, max_v=10.0)
+    a0, c0, lt = _init_reference_weights(OBS, OBS, ACT, FlashSACConfig(
+        device="cpu", actor_hidden_dim=actor[0], actor_num_blocks=actor[1], critic_hidden_dim=critic[0],
+        critic_num_blocks=critic[1]))
 
-    def with_buffers(p, twin, H, cin):
+    def with_buffers(p, twin, H, cin, blocks):
         out = {k: v.numpy() for k, v in p.items()}
-        for pre in fs.bn_buffer_prefixes(2):
+        for pre in fs.bn_buffer_prefixes(blocks):
             C = cin if pre == "embedder.norm" else (4 * H if pre.endswith("norm1") else H)
             shape = (2, C) if twin else (C,)
             out[pre + ".running_mean"] = np.zeros(shape, np.float32)
             out[pre + ".running_var"] = np.ones(shape, np.float32)
         return out
 
-    st = dict(actor=with_buffers(a0, False, 256, OBS), critic=with_buffers(c0, True, 512, OBS + ACT),
-              target=with_buffers(c0, True, 512, OBS + ACT), log_temp=lt, opt_actor=fs.OptState(),
+    st = dict(actor=with_buffers(a0, False, actor[0], OBS, actor[1]),
+              critic=with_buffers(c0, True, critic[0], OBS + ACT, critic[1]),
+              target=with_buffers(c0, True, critic[0], OBS + ACT, critic[1]), log_temp=lt, opt_actor=fs.OptState(),
               opt_critic=fs.OptState(), opt_temp=fs.OptState())
     rng = np.random.default_rng(2026)
     B = batch
@@ -228,6 +243,17 @@ def cpu_update_rate(batch: int, pairs: int = 1):
     return 2 * pairs / sec, sec, len(os.sched_getaffinity(0))
 
 
+def cpu_update_seconds(full_batch: int, b1: int, b2: int, critic=(512, 2), actor=(256, 2)):
+    """Seconds per update of the CPU restatement at ``full_batch`` rows from one update pair at
+    ``b1`` rows and one at ``b2``: t(B) = t(b2) + (B - b2) (t(b2) - t(b1)) / (b2 - b1). The
+    parameter-sized work (Adam, projection, EMA) is the intercept and the row work the
+    slope, so the intercept is not multiplied up. Returns (seconds, measured seconds, cores)."""
+    _, s1, cores = cpu_update_rate(b1, 1, critic, actor)
+    _, s2, _ = cpu_update_rate(b2, 1, critic, actor)
+    t1, t2 = s1 / 2, s2 / 2
+    return t2 + max(t2 - t1, 0.0) / (b2 - b1) * (full_batch - b2), s1 + s2, cores
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
 
@@ -238,7 +264,12 @@ def run_b200(args, rank, world, local_rank):
         from robolearn_b200.flashsac.dp import DataParallel
 
         dp = DataParallel()
-    L, R, feed = build(args.precision, device, seed=0, dp=dp)
+    if args.workload == "cfg5":
+        if CFG5_BATCH % world:
+            raise SystemExit("cfg5 needs a rank count that divides 32768")
+        L, R, feed = build("fp32", device, seed=0, dp=dp, batch=CFG5_BATCH // world, critic=(1024, 3), actor=(128, 2))
+    else:
+        L, R, feed = build(args.precision, device, seed=0, dp=dp)
     for phase in (True, False):  # one eager pass loads every kernel module before capture
         for f in feed:
             f()
@@ -517,7 +548,23 @@ def run_categorical(args) -> dict:
     return out
 
 
+_JSON_OUT = None
+
+
+def emit(line: str) -> None:
+    """Write the result line to the process's original standard output (everything else,
+    including libraries that print to stdout, goes to standard error)."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(line + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
+    # keep stdout for the JSON line alone: NCCL prints its version on the first collective
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -529,7 +576,7 @@ def main():
             return
         out = dict(n_gpus=1, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None, data="synthetic",
                    impl="b200", **run_categorical(args))
-        print(json.dumps(out))
+        emit(json.dumps(out))
         return
     if args.workload == "ppo":
         if rank != 0:
@@ -537,7 +584,7 @@ def main():
         if args.impl == "reference":
             sec, cores = ppo_cpu_minibatch_seconds()
             value = sec * 20 * 1e3
-            print(json.dumps({"metric": PPO_METRIC, "impl": "reference", "value": value, "unit": "ms/update",
+            emit(json.dumps({"metric": PPO_METRIC, "impl": "reference", "value": value, "unit": "ms/update",
                               "higher_is_better": False, "n_gpus": args.gpus, "steps": 1, "warmup": 0,
                               "ms_per_step": value, "dtype": "f64", "data": "synthetic",
                               "config": {"workload": "cfg2 WarpPPO update, CPU restatement (oracle port)"},
@@ -548,27 +595,48 @@ def main():
             return
         out = dict(n_gpus=args.gpus, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None,
                    data="synthetic", impl="b200", **run_ppo(args))
-        print(json.dumps(out))
+        emit(json.dumps(out))
+        return
+    if args.impl == "reference" and args.workload == "cfg5":
+        if rank != 0:
+            return
+        b1, b2 = 64, 256
+        times = []
+        for i in range(min(args.warmup, 1) + min(args.steps, 3)):  # about 15 s of CPU work each
+            sec, _, cores = cpu_update_seconds(CFG5_BATCH, b1, b2, critic=(1024, 3), actor=(128, 2))
+            if i >= min(args.warmup, 1):
+                times.append(sec)
+        per_update = statistics.median(times)
+        value = 1.0 / per_update
+        out = dict(base, metric=CFG5_METRIC, scaling="strong", impl="reference", value=value,
+                   ms_per_step=per_update * 1e3, dtype="f32",
+                   config={"workload": "cfg5 FlashSAC update, CPU restatement of the reference (oracle port)",
+                           "global_batch": CFG5_BATCH, "parallelism": "cpu"},
+                   cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
+                                 "sample": f"one actor+critic update pair at batch {b1} and one at {b2} per step, "
+                                           f"time extrapolated linearly in the batch to {CFG5_BATCH}"},
+                   e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        emit(json.dumps(out))
         return
     if args.impl == "reference":
         if rank != 0:
             return
-        sample = BATCH // 4
+        b1, b2 = BATCH // 8, BATCH // 4
         times = []
         for i in range(args.warmup + args.steps):
-            rate, sec, cores = cpu_update_rate(sample, pairs=1)
+            sec, _, cores = cpu_update_seconds(BATCH, b1, b2)
             if i >= args.warmup:
-                times.append(sec / 2 * (BATCH / sample))
+                times.append(sec)
         per_update = statistics.median(times)
         value = 1.0 / per_update
         out = dict(base, impl="reference", value=value, ms_per_step=per_update * 1e3, dtype="f32",
                    config={"workload": "cfg3 FlashSAC update, CPU restatement of the reference (oracle port)",
                            "global_batch": BATCH, "parallelism": "cpu"},
                    cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
-                                 "sample": f"one actor+critic update pair at batch {sample} per step, "
-                                           f"time scaled x{BATCH // sample} to batch {BATCH}"},
+                                 "sample": f"one actor+critic update pair at batch {b1} and one at {b2} per step, "
+                                           f"time extrapolated linearly in the batch to {BATCH}"},
                    e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
-        print(json.dumps(out))
+        emit(json.dumps(out))
         return
     import torch
 
@@ -587,6 +655,29 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         sec, e2e_sec = t.tolist()
     pk, src = peaks()
+    if args.workload == "cfg5":
+        # three tf32 tensor passes per product (counted in the executed FLOPs) at the dense
+        # tf32 rate, half the bf16 rate
+        roof = gemm_roofline(L, pk["bf16_tflops"] / 2)
+        roof["peak_source"] = f"{src} bf16_tflops / 2 (dense tf32 rate; FLOPs counted per tf32 pass, 3 per product)"
+        out = dict(base, metric=CFG5_METRIC, scaling="strong", impl="b200", value=args.steps / sec,
+                   ms_per_step=sec / args.steps * 1e3, dtype="f32 (3xTF32 products)", gpu_launches=launches,
+                   clocks=clocks, roofline=roof,
+                   config={"workload": "cfg5 data-parallel FlashSAC update (obs 123, act 37, global batch 32768 "
+                                       "split over the ranks, critic 1024x3, actor 128x2, 101 atoms, FP32 recipe)",
+                           "global_batch": CFG5_BATCH, "seq_len": None,
+                           "parallelism": f"dp{world}" if world > 1 else "single",
+                           "l2": "working set > 126 MB L2 (no flush needed)"},
+                   e2e={"value": args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": 4})
+        if rank == 0:
+            emit(json.dumps(out))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     roof = gemm_roofline(L, pk["bf16_tflops"])
     roof["peak_source"] = f"{src} bf16_tflops (burst; fp16 dense rate taken equal)"
     out = dict(base, impl="b200", value=world * args.steps / sec, ms_per_step=sec / args.steps * 1e3,
@@ -598,11 +689,11 @@ def main():
                e2e={"value": world * args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4})
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = BATCH // 4
-        rate, csec, cores = cpu_update_rate(sample, pairs=1)
-        out["cpu_baseline"] = {"value": rate * sample / BATCH, "unit": "updates/s", "cores": cores, "kind": "port",
-                               "sample": f"one actor+critic update pair at batch {sample} ({csec:.1f} s), "
-                                         f"rate scaled to batch {BATCH}"}
+        b1, b2 = BATCH // 8, BATCH // 4
+        per_update, csec, cores = cpu_update_seconds(BATCH, b1, b2)
+        out["cpu_baseline"] = {"value": 1.0 / per_update, "unit": "updates/s", "cores": cores, "kind": "port",
+                               "sample": f"one actor+critic update pair at batch {b1} and one at {b2} "
+                                         f"({csec:.1f} s), time extrapolated linearly in the batch to {BATCH}"}
     if rank == 0 and world == 1 and not args.no_ppo:
         # the cfg2 PPO update beside the headline (full line: --workload ppo)
         import types
@@ -611,7 +702,7 @@ def main():
         out["ppo"] = {"metric": pp["metric"], "value": pp["value"], "unit": pp["unit"],
                       "roofline_frac": pp["roofline"]["frac"], "e2e": pp["e2e"]["value"]}
     if rank == 0:
-        print(json.dumps(out))
+        emit(json.dumps(out))
     if world > 1:
         import torch.distributed as dist
 

@@ -328,7 +328,7 @@ __device__ __forceinline__ float4 xor_sum4(float4 v, int mask) {
 // output rows are fetched before its TMEM read. After its last TMEM read of a tile each
 // warp releases the accumulator buffer to the MMA issuer.
 constexpr int kEpiSlots = kEpiWarps / 4;        // warps per TMEM lane quarter
-constexpr int kMaxChunks = 256 / (16 * kEpiSlots);  // chunks per warp and tile (BN <= 256)
+constexpr int kMaxChunks = (256 / 16 + kEpiSlots - 1) / kEpiSlots;  // chunks per warp and tile (BN <= 256)
 
 __device__ __forceinline__ float4 pick4(const float4 (&v)[kMaxChunks], int k) {
     float4 r = v[0];
