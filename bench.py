@@ -460,17 +460,23 @@ def run_ppo(args) -> dict:
 # ---------------------------------------------------------------------------
 CAT_METRIC = "categorical critic objective us/launch (B 65536, 101 atoms, twin logits, fp32 dlogits)"
 CAT_B, CAT_BINS = 65536, 101
+CAT_LD = 104  # logits / gradient rows padded to 16 bytes, as the critic head GEMM writes them
 
 
 def categorical_inputs(device, seed: int = 0) -> dict:
-    """Target and online logits [2][B][101] ~N(0,1), rewards ~N(0,1), discount 0.99,
-    done ~Bernoulli(0.01), next log-probs ~N(0,1), alpha 0.01."""
+    """Target and online logits [2][B][101] ~N(0,1) (rows padded to 104 floats, the layout the
+    critic head product writes), rewards ~N(0,1), discount 0.99, done ~Bernoulli(0.01), next
+    log-probs ~N(0,1), alpha 0.01."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(4000 + seed)
     B, K = CAT_B, CAT_BINS
-    return {"target": torch.randn(2, B, K, device=device, generator=g),
-            "online": torch.randn(2, B, K, device=device, generator=g),
+    def logits():
+        buf = torch.zeros(2, B, CAT_LD, device=device)
+        buf[:, :, :K] = torch.randn(2, B, K, device=device, generator=g)
+        return buf
+
+    return {"target": logits(), "online": logits(),
             "reward": torch.randn(B, device=device, generator=g),
             "terminated": (torch.rand(B, device=device, generator=g) < 0.01).float(),
             "discount": torch.full((B,), 0.99, device=device),
@@ -492,17 +498,17 @@ def run_categorical(args) -> dict:
     torch.cuda.set_device(device)
     x = categorical_inputs(device)
     obj = CriticObjective(CAT_B, CAT_BINS, -10.0, 10.0, device=device)
-    dlogits = torch.zeros(2, CAT_B, CAT_BINS, device=device)
+    dlogits = torch.zeros(2, CAT_B, CAT_LD, device=device)
     loss = torch.zeros(1, device=device)
     mx = torch.zeros(1, device=device)
 
     def launch():
-        obj.run(target_logits=x["target"], target_row_stride=CAT_BINS, target_twin_stride=CAT_B * CAT_BINS,
-                target_row_offset=0, online_logits=x["online"], online_row_stride=CAT_BINS,
-                online_twin_stride=CAT_B * CAT_BINS, reward=x["reward"], terminated=x["terminated"],
+        obj.run(target_logits=x["target"], target_row_stride=CAT_LD, target_twin_stride=CAT_B * CAT_LD,
+                target_row_offset=0, online_logits=x["online"], online_row_stride=CAT_LD,
+                online_twin_stride=CAT_B * CAT_LD, reward=x["reward"], terminated=x["terminated"],
                 discount=x["discount"], next_log_pi=x["next_log_pi"], alpha=x["alpha"], loss_weight=1.0 / (2 * CAT_B),
-                loss_out=loss, max_entropy_out=mx, dlogits=dlogits, dlogits_row_stride=CAT_BINS,
-                dlogits_twin_stride=CAT_B * CAT_BINS)
+                loss_out=loss, max_entropy_out=mx, dlogits=dlogits, dlogits_row_stride=CAT_LD,
+                dlogits_twin_stride=CAT_B * CAT_LD)
 
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MB > L2
     for _ in range(max(args.warmup, 3)):
@@ -526,14 +532,15 @@ def run_categorical(args) -> dict:
                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
                         "algorithmic_bytes": categorical_bytes(), "peak_source": f"{src} hbm_gbs"},
            "config": {"workload": "cfg4 categorical projection + CE + gradient, B 65536, 101 atoms on [-10, 10], "
-                                  "both twins", "l2": "L2 flushed (256 MB write) before every timed launch",
+                                  "both twins", "layout": "logits and gradient rows padded to 104 floats",
+                      "l2": "L2 flushed (256 MB write) before every timed launch",
                       "timing": "median of per-launch CUDA-event times"}}
     if not args.no_cpu_baseline:
         import numpy as np
 
         from oracle import flashsac_np as fs
 
-        xs = {k: v.cpu().numpy() for k, v in x.items()}
+        xs = {k: (v[:, :, :CAT_BINS] if v.dim() == 3 else v).cpu().numpy() for k, v in x.items()}
         t0 = time.perf_counter()
         tl = xs["target"] - np.log(np.exp(xs["target"]).sum(-1, keepdims=True))
         q = (np.exp(tl) * fs.support(CAT_BINS, -10.0, 10.0)).sum(-1)
