@@ -40,6 +40,9 @@ int rl2_abi_version(void);
  * operand planes: derived copies that feed the tensor-core products.
  * Either h16 (fp16, multiplied by *scale when scale is set, overflow -> *found_inf = 1)
  * or hi + lo (fp32 pair, hi exact in tf32, hi + lo = value). ld / twin_stride in elements.
+ * A GEMM that also writes its fp32 output may take lo alone (hi null): kind::tf32 products
+ * ignore the low 13 mantissa bits of their operands, so the fp32 output itself serves as
+ * the hi operand of a later product (same layout as the lo plane).
  * ------------------------------------------------------------------------- */
 typedef struct rl2_plane {
     void* h16;

@@ -842,7 +842,7 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
                         for (int r = 0; r < 32; ++r) {
                             if (full || r < vr) {
                                 const float h = tf32_hi(v[r]);
-                                pw.p.hi[o + static_cast<long long>(r) * pw.p.ld] = h;
+                                if (pw.p.hi) pw.p.hi[o + static_cast<long long>(r) * pw.p.ld] = h;
                                 pw.p.lo[o + static_cast<long long>(r) * pw.p.ld] = v[r] - h;
                             }
                         }
@@ -1089,8 +1089,10 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         set_error("GEMM operands / output must be non-null (kind 1 also needs a_lo and b_lo)");
         return nullptr;
     }
-    if (!plane_valid(&g->out_plane) || (plane_used(&g->out_plane) && (g->k_splits > 1 || g->accumulate))) {
-        set_error("GEMM output plane must be a valid fp16 or hi/lo plane, without split-K or accumulate");
+    if ((!plane_valid(&g->out_plane) && !(plane_lo_only(&g->out_plane) && g->d)) ||
+        (plane_used(&g->out_plane) && (g->k_splits > 1 || g->accumulate))) {
+        set_error("GEMM output plane must be a valid fp16 or hi/lo plane (lo alone only beside an fp32 output), "
+                  "without split-K or accumulate");
         return nullptr;
     }
     if ((g->a_major != 0 && g->a_major != 1) || (g->b_major != 0 && g->b_major != 1)) {

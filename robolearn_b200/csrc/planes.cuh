@@ -39,7 +39,13 @@ inline bool plane_valid(const rl2_plane* p) {
     return true;
 }
 
-inline bool plane_used(const rl2_plane* p) { return p && (p->h16 || p->hi); }
+inline bool plane_used(const rl2_plane* p) { return p && (p->h16 || p->hi || p->lo); }
+
+// A tf32 plane given as lo alone: the caller reads the operand's hi part from fp32 values
+// stored elsewhere in the same layout (the tensor cores ignore the low 13 mantissa bits of
+// a kind::tf32 operand, so raw fp32 serves as hi). Only GEMM outputs that also write the
+// fp32 result accept it.
+inline bool plane_lo_only(const rl2_plane* p) { return p && !p->h16 && !p->hi && p->lo; }
 
 #if defined(__CUDACC__)
 __device__ __forceinline__ float tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
@@ -52,16 +58,16 @@ struct PlaneWriter {
     __device__ __forceinline__ explicit PlaneWriter(const Plane& q) : p(q), scale(1.0f), overflow(false) {
         if (p.h16 && p.scale) scale = *p.scale;
     }
-    __device__ __forceinline__ bool active() const { return p.h16 != nullptr || p.hi != nullptr; }
+    __device__ __forceinline__ bool active() const { return p.h16 != nullptr || p.lo != nullptr; }
     __device__ __forceinline__ void store(int t, long long row, int col, float v) {
         const long long o = static_cast<long long>(t) * p.tstride + row * p.ld + col;
         if (p.h16) {
             const float s = v * scale;
             overflow |= !(fabsf(s) <= 65504.0f);
             p.h16[o] = __float2half_rn(s);
-        } else if (p.hi) {
+        } else if (p.lo) {
             const float h = tf32_hi(v);
-            p.hi[o] = h;
+            if (p.hi) p.hi[o] = h;
             p.lo[o] = v - h;
         }
     }
@@ -79,9 +85,9 @@ struct PlaneWriter {
             packed.x = *reinterpret_cast<const uint32_t*>(&lo2);
             packed.y = *reinterpret_cast<const uint32_t*>(&hi2);
             *reinterpret_cast<uint2*>(p.h16 + o) = packed;
-        } else if (p.hi) {
+        } else if (p.lo) {
             const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-            *reinterpret_cast<float4*>(p.hi + o) = h;
+            if (p.hi) *reinterpret_cast<float4*>(p.hi + o) = h;
             *reinterpret_cast<float4*>(p.lo + o) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
         }
     }

@@ -241,8 +241,10 @@ class WarpPPO:
         b = {"rows": rows, "G": G, "ldh": ldh,
              "x0": _PlanePair(1, rows, lo.kp[0], dev),
              "y": {i: torch.zeros(2, rows, lo.widths[i], **f32) for i in range(1, L)},
-             "yp": {i: _PlanePair(2, rows, lo.kp[i], dev) for i in range(1, L)},
              "head": torch.zeros(2, rows, ldh, **f32)}
+        # hidden activations as operands: hi = the fp32 activations themselves (kind::tf32
+        # products ignore the low 13 mantissa bits), lo = a separate plane in the same layout
+        b["yp"] = {i: _LoPlane(b["y"][i], lo.kp[i]) for i in range(1, L)}
         if backward:
             b["dz"] = {i: _PlanePair(2, rows, lo.kp[i + 1], dev) for i in range(L - 1)}
             b["dz"][L - 1] = _PlanePair(2, rows, ldh, dev)
@@ -253,7 +255,7 @@ class WarpPPO:
                                for k in ("log_probs", "values", "advantages", "returns")})
         return b
 
-    def _input_plane(self, b: dict, li: int) -> "_PlanePair":
+    def _input_plane(self, b: dict, li: int):
         return b["x0"] if li == 0 else b["yp"][li]
 
     # ------------------------------------------------------------------ programs
@@ -684,6 +686,32 @@ class WarpPPO:
         """Load an NPZ checkpoint into a model with the same architecture."""
         with np.load(path, allow_pickle=False) as state:
             self.load_state_dict(dict(state))
+
+
+class _LoPlane:
+    """tf32 operand [2][rows][ld] whose hi part is an fp32 array of that layout (the tensor
+    cores read raw fp32 as tf32 by ignoring the low mantissa bits); only lo is stored."""
+
+    def __init__(self, values: torch.Tensor, ld: int):
+        twins, rows, width = values.shape
+        if width != ld:
+            raise ValueError("the fp32 activations must have the operand row stride")
+        self.twins, self.rows, self.ld = twins, rows, ld
+        self.values = values
+        self.lo_t = torch.zeros_like(values)
+        self.hi, self.lo = values.data_ptr(), self.lo_t.data_ptr()
+        self.tstride = rows * ld
+
+    def c(self) -> N.Plane:
+        return N.Plane(lo=self.lo, ld=self.ld, twin_stride=self.rows * self.ld)
+
+    def twin(self, z: int) -> tuple[int, int]:
+        off = 4 * z * self.rows * self.ld
+        return self.hi + off, self.lo + off
+
+    def value(self) -> torch.Tensor:
+        hi = (self.values.view(torch.int32) & -8192).view(torch.float32)
+        return hi + self.lo_t
 
 
 class _PlanePair:

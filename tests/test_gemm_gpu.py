@@ -367,3 +367,36 @@ def test_gemm_residual_and_accumulate_paths(kind, how, plane, tile_n, path):
     elif plane:
         hi_ref = (out.contiguous().view(torch.int32) & -8192).view(torch.float32)
         assert torch.equal(keep[0][:, :, :n], hi_ref) and torch.equal(keep[1][:, :, :n], out - hi_ref)
+
+
+def test_tf32_operands_read_raw_fp32_as_hi():
+    """kind::tf32 products ignore the low 13 mantissa bits: raw fp32 in the hi operand slot
+    gives bit-identical results to the truncated hi plane (the PPO activations rely on it),
+    and a GEMM given a lo-only plane writes lo = D - trunc(D) beside its fp32 output."""
+    from robolearn_b200 import _native as N
+
+    m, n, k, batch = 300, 256, 96, 2
+    plan, D, ref = _run(1, m, n, k, 0, 0, batch=batch, ldd=n)
+    lo = torch.zeros(batch, m, n, device="cuda")
+    plan2, D2, _ = _run(1, m, n, k, 0, 0, batch=batch, ldd=n,
+                        out_plane=N.Plane(lo=lo.data_ptr(), ld=n, twin_stride=m * n))
+    plan2._keep.append(lo)
+    plan.run()
+    plan2.run()
+    torch.cuda.synchronize()
+    assert torch.equal(D, D2)
+    hi = (D2.view(torch.int32) & -8192).view(torch.float32)
+    assert torch.equal(lo, D2 - hi)
+    # next product with the output as operand: (raw fp32, lo) == (truncated hi, lo)
+    w = torch.randn(batch, 64, n, device="cuda") / n**0.5
+    w_hi, w_lo = dense.tf32_split(w)
+    outs = []
+    for a_hi in (D2, hi):
+        out = torch.zeros(batch, m, 64, device="cuda")
+        p = dense.DensePlan(kind=1, m=m, n=64, k=n, a=a_hi, a_lo=lo, b=w_hi, b_lo=w_lo, lda=n, ldb=n, d=out, ldd=64,
+                            a_major=0, b_major=0, batch=batch, a_batch_stride=m * n, b_batch_stride=64 * n,
+                            d_batch_stride=m * 64)
+        p.run()
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
