@@ -109,6 +109,17 @@ typedef struct rl2_gemm_desc {
     int activation;
     const float* act_aux;
     long long ld_aux, aux_batch_stride;
+    /* evaluation-mode batch norm of the output columns (optional; transposed plans only,
+     * i.e. n >= 128 and a plan-chosen tile): out = (x - mean) * invstd * gamma + beta,
+     * then ReLU when bn_relu, then + residual (with bn the residual is added after the
+     * normalisation). Per-column arrays [batch][n] at bn_twin_stride; replaces
+     * rl_flash_bn_forward in evaluation mode (src/robolearn/cuda/flash_kernels.cuh:500-560). */
+    const float* bn_mean;
+    const float* bn_invstd;
+    const float* bn_gamma;
+    const float* bn_beta;
+    long long bn_twin_stride;
+    int bn_relu;
 } rl2_gemm_desc;
 
 void* rl2_gemm_create(const rl2_gemm_desc* desc);

@@ -47,6 +47,7 @@ class GemmDesc(ctypes.Structure):
         ("scale", P), ("k_splits", I), ("d_split_stride", LL), ("tile_n", I), ("health", P),
         ("out_plane", Plane),
         ("activation", I), ("act_aux", P), ("ld_aux", LL), ("aux_batch_stride", LL),
+        ("bn_mean", P), ("bn_invstd", P), ("bn_gamma", P), ("bn_beta", P), ("bn_twin_stride", LL), ("bn_relu", I),
     ]
 
 

@@ -75,6 +75,12 @@ struct Params {
     // tma_plane: fp16 plane map)
     bool tma_epi, tma_d, tma_plane;
     bool tma_reduce;   // store-engine epilogue adds into D in L2 (D += result: in-place residual / accumulate)
+    const float* bn_mean;  // evaluation-mode batch norm of the output columns (transposed plans)
+    const float* bn_invstd;
+    const float* bn_gamma;
+    const float* bn_beta;
+    long long bn_tstride;
+    int bn_relu;
     bool swap;         // accumulator holds D^T: kernel M = output columns, kernel N = output rows
     int out_m, out_n;  // output rows / columns (the kernel's N / M when swapped)
     int epi_bufs;      // staging boxes per warp and output (store-engine epilogue: 1 or 2)
@@ -737,6 +743,14 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
         const int n = col0 + lane;
         const bool col_ok = n < p.out_n;
         const float bv = (p.bias && col_ok) ? __ldg(p.bias + static_cast<long long>(w.z) * p.bias_bstride + n) : 0.0f;
+        float bn_mu = 0.0f, bn_is = 1.0f, bn_g = 1.0f, bn_b = 0.0f;
+        if (p.bn_mean && col_ok) {
+            const long long o = static_cast<long long>(w.z) * p.bn_tstride + n;
+            bn_mu = __ldg(p.bn_mean + o);
+            bn_is = __ldg(p.bn_invstd + o);
+            bn_g = __ldg(p.bn_gamma + o);
+            bn_b = __ldg(p.bn_beta + o);
+        }
         float* dcol = p.d ? p.d + static_cast<long long>(w.z) * p.d_bstride +
                                 static_cast<long long>(w.split) * p.d_split_stride + n
                           : nullptr;
@@ -772,6 +786,13 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
             for (int r = 0; r < 32; ++r) {
                 if (scaled) v[r] = v[r] * scale;
                 if (p.bias) v[r] = v[r] + bv;
+            }
+            if (p.bn_mean) {  // evaluation-mode batch norm (+ ReLU); a residual is added after it
+#pragma unroll
+                for (int r = 0; r < 32; ++r) {
+                    const float o = (v[r] - bn_mu) * bn_is * bn_g + bn_b;
+                    v[r] = p.bn_relu ? fmaxf(o, 0.0f) : o;
+                }
             }
             if (col_ok) {
                 if (add_src) {
@@ -1105,6 +1126,12 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         set_error("split-K GEMMs write plain partials: no bias/residual/accumulate/stats/activation, positive split stride");
         return nullptr;
     }
+    if (g->bn_mean && (!g->bn_invstd || !g->bn_gamma || !g->bn_beta || g->stat_mean || g->activation ||
+                       g->accumulate || g->k_splits > 1)) {
+        set_error("GEMM batch-norm epilogue needs mean, invstd, gamma and beta, and no statistics, "
+                  "activation, accumulate or split-K");
+        return nullptr;
+    }
     if (!g->stat_mean && g->stat_m2) {
         set_error("GEMM column statistics: stat_m2 needs stat_mean");
         return nullptr;
@@ -1125,8 +1152,12 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
                           !(g->accumulate && g->residual);
     const bool reduce_ok = in_place && !plane_used(&g->out_plane) && !g->stat_mean;
     const bool reduce_path = tma_store_enabled() && splits == 1 && reduce_ok && !g->activation && !g->act_aux &&
-                             outputs_tma_ok(g);
+                             !g->bn_mean && outputs_tma_ok(g);
     const bool swap = swap_enabled() && g->tile_n <= 0 && g->n >= 128 && !reduce_path;
+    if (g->bn_mean && !swap) {
+        set_error("GEMM batch-norm epilogue needs a transposed plan (n >= 128, plan-chosen tile width)");
+        return nullptr;
+    }
     rl2_gemm_desc sw = *g;
     if (swap) {
         sw.m = g->n;
@@ -1208,6 +1239,12 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     p.swap = swap;
     p.out_m = g->m;
     p.out_n = g->n;
+    p.bn_mean = g->bn_mean;
+    p.bn_invstd = g->bn_invstd;
+    p.bn_gamma = g->bn_gamma;
+    p.bn_beta = g->bn_beta;
+    p.bn_tstride = g->bn_twin_stride;
+    p.bn_relu = g->bn_relu;
     p.batch = g->batch;
     p.kblocks_total = (g->k + bk - 1) / bk;
     p.splits = std::min(splits, p.kblocks_total);

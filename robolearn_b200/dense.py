@@ -76,7 +76,11 @@ class DensePlan:
         act_aux=None,
         ld_aux: int = 0,
         aux_batch_stride: int = 0,
+        bn=None,
     ):
+        """``bn``: optional evaluation-mode batch norm of the output columns, a tuple
+        (mean, invstd, gamma, beta, twin_stride, relu) of device addresses / ints; the
+        residual is then added after the normalisation (transposed plans only)."""
         self._keep = [a, b, d, a_lo, b_lo, bias, residual, stat_mean, stat_m2, scale, health, out_plane, act_aux]
         A = N.addr
         desc = N.GemmDesc(
@@ -91,6 +95,9 @@ class DensePlan:
             health=A(health), out_plane=out_plane if out_plane is not None else N.Plane(),
             activation=activation, act_aux=A(act_aux), ld_aux=ld_aux, aux_batch_stride=aux_batch_stride,
         )
+        if bn is not None:
+            desc.bn_mean, desc.bn_invstd, desc.bn_gamma, desc.bn_beta = (A(v) for v in bn[:4])
+            desc.bn_twin_stride, desc.bn_relu = int(bn[4]), int(bn[5])
         self._lib = N.load()
         self.handle = N.created(self._lib.rl2_gemm_create(ctypes.byref(desc)), "create tcgen05 GEMM plan")
         self.tile_n = self._lib.rl2_gemm_tile_n(self.handle)

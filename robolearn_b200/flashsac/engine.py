@@ -451,6 +451,22 @@ class Run:
                          bias_batch_stride=lin.out if bias_addr else 0,
                          out_plane=out_plane.c() if out_plane is not None else None, **kw)
 
+    def _fwd_gemm_bn(self, lin: Linear, a: PlaneBuf, pre: str, out_plane: PlaneBuf, d=None, ldd: int = 0,
+                     residual=None):
+        """Evaluation-mode product with the following batch norm + ReLU (+ residual) fused into
+        its epilogue: out = residual + relu(BN_eval(a W^T)); no pre-normalisation output."""
+        net = self.net
+        bm, bl = net.plane_addr(lin)
+        kp = operand_ld(lin.inp, net.kind)
+        mean, inv = self._stats_ptrs(pre)
+        bn = (mean, inv, net.addr(pre + ".weight"), net.addr(pre + ".bias"), lin.out, 1)
+        return DensePlan(kind=net.kind, m=self.rows, n=lin.out, k=lin.inp, batch=self.T,
+                         a=a.main, a_lo=a.lo, a_major=0, lda=a.ld, a_batch_stride=a.tstride,
+                         b=bm, b_lo=bl, b_major=0, ldb=kp, b_batch_stride=lin.out * kp,
+                         d=d, ldd=ldd, d_batch_stride=self.rows * ldd if d is not None else 0,
+                         residual=residual, ldr=ldd, residual_batch_stride=self.rows * ldd if residual is not None else 0,
+                         out_plane=out_plane.c(), bn=bn)
+
     def _dx_gemm(self, lin: Linear, dplane: PlaneBuf, d_addr, ldd: int, residual=None, out_plane=None):
         net = self.net
         bm, bl = net.plane_addr(lin)
@@ -575,7 +591,13 @@ class Run:
             prog += [colstats, self._bn_stats("embedder.norm", Cin, src_part_shared=True)]
         prog.append(self._apply("embedder.norm", Cin, self.x_addr, self.ldx, 0, relu=False, plane=self.e))
         prog.append(self._fwd_gemm(net.linears["embed"], self.e, self.h[0], H, stats=False, out_plane=self.hp[0]))
+        fused_eval = not self.training and min(E, H) >= 128  # transposed plans take the BN epilogue
         for i in range(spec.blocks):
+            if fused_eval:
+                prog.append(self._fwd_gemm_bn(net.linears[f"w1.{i}"], self.hp[i], f"encoder.{i}.norm1", self.a1[i]))
+                prog.append(self._fwd_gemm_bn(net.linears[f"w2.{i}"], self.a1[i], f"encoder.{i}.norm2", self.hp[i + 1],
+                                              d=self.h[i + 1], ldd=H, residual=self.h[i]))
+                continue
             prog.append(self._fwd_gemm(net.linears[f"w1.{i}"], self.hp[i], self.t1[i], E, stats=self.training))
             if self.training:
                 prog.append(self._bn_stats(f"encoder.{i}.norm1", E, src_part_shared=False))

@@ -400,3 +400,40 @@ def test_tf32_operands_read_raw_fp32_as_hi():
         outs.append(out)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_gemm_eval_batch_norm_epilogue(kind):
+    """Evaluation-mode batch norm fused into a transposed plan's epilogue:
+    out = residual + relu((x - mean) * invstd * gamma + beta), plus the operand plane."""
+    from robolearn_b200 import _native as N
+
+    m, n, k, batch = 1000, 384, 160, 2
+    g = torch.Generator(device="cuda").manual_seed(11)
+    mean = torch.randn(batch, n, device="cuda", generator=g)
+    invstd = torch.rand(batch, n, device="cuda", generator=g) + 0.5
+    gamma = torch.randn(batch, n, device="cuda", generator=g)
+    beta = torch.randn(batch, n, device="cuda", generator=g)
+    res = torch.randn(batch, m, n, device="cuda", generator=g)
+    pld = dense.operand_ld(n, kind)
+    if kind == 0:
+        h16 = torch.zeros(batch, m, pld, device="cuda", dtype=torch.float16)
+        plane, keep = N.Plane(h16=h16.data_ptr(), ld=pld, twin_stride=m * pld), [h16]
+    else:
+        hi = torch.zeros(batch, m, pld, device="cuda")
+        lo = torch.zeros(batch, m, pld, device="cuda")
+        plane, keep = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld), [hi, lo]
+    bn = (mean.data_ptr(), invstd.data_ptr(), gamma.data_ptr(), beta.data_ptr(), n, 1)
+    plan, D, ref = _run(kind, m, n, k, 0, 0, batch=batch, ldd=n, residual=res, ldr=n, residual_batch_stride=m * n,
+                        out_plane=plane, bn=bn)
+    assert plan.transposed
+    plan.run()
+    torch.cuda.synchronize()
+    y = (ref - mean.double()[:, None]) * invstd.double()[:, None] * gamma.double()[:, None] + beta.double()[:, None]
+    expect = res.double() + torch.clamp(y, min=0)
+    tol = 2e-3 if kind == 0 else 2e-5
+    assert (D.double() - expect).abs().max().item() < tol * expect.abs().max().item()
+    if kind == 0:
+        assert torch.equal(keep[0][:, :, :n], D.half())
+    else:
+        assert torch.equal(keep[0][:, :, :n] + keep[1][:, :, :n], D)
