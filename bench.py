@@ -162,7 +162,8 @@ def count_launches(prog) -> int:
 
 
 def gemm_roofline(L, peak_tflops):
-    """Average tcgen05 GEMM throughput over one update's products, timed as one CUDA graph."""
+    """Average tcgen05 GEMM throughput over one update's products, timed as one CUDA graph
+    (algorithmic FLOPs: products computed twice count once; their time is included)."""
     import torch
 
     from robolearn_b200.dense import DensePlan
@@ -170,7 +171,7 @@ def gemm_roofline(L, peak_tflops):
     plans = []
     for phase in (True, False):
         plans += [f for f in L.programs[phase] if isinstance(f, DensePlan)]
-    flops = sum(p.flops for p in plans)
+    flops = sum(p.flops for p in plans if not p.recompute)  # algorithmic: a recomputed product counts once
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())

@@ -1106,7 +1106,8 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         set_error("GEMM requires kind 0/1 and positive m, n, k, batch");
         return nullptr;
     }
-    if (!g->a || !g->b || (!g->d && !plane_used(&g->out_plane)) || (g->kind == 1 && (!g->a_lo || !g->b_lo))) {
+    if (!g->a || !g->b || (!g->d && !plane_used(&g->out_plane) && !g->stat_mean) ||
+        (g->kind == 1 && (!g->a_lo || !g->b_lo))) {
         set_error("GEMM operands / output must be non-null (kind 1 also needs a_lo and b_lo)");
         return nullptr;
     }

@@ -105,6 +105,7 @@ class DensePlan:
         self.tma_store = mode == 1
         self.transposed = mode == 2
         self.flops = 2 * m * n * k * batch * (3 if kind == TF32X3 else 1)
+        self.recompute = False  # set by callers that compute the same product twice
 
     def run(self, stream=None) -> None:
         N.check(self._lib.rl2_gemm_run(self.handle, N.stream_ptr(stream)), "tcgen05 GEMM")

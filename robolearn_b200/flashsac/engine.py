@@ -369,6 +369,7 @@ class Run:
         self.update_running = update_running and training
         self.need_param_grads = need_param_grads
         self.need_input_grad = need_input_grad
+        self.backward_needed = need_param_grads or need_input_grad
         self.scaler = scaler or Scaler()
         spec = net.spec
         self.T, self.H, self.E = spec.twins, spec.hidden, spec.hidden * spec.expansion
@@ -447,7 +448,7 @@ class Run:
         return DensePlan(kind=net.kind, m=self.rows, n=lin.out, k=lin.inp, batch=self.T,
                          a=a.main, a_lo=a.lo, a_major=0, lda=a.ld, a_batch_stride=a.tstride,
                          b=bm, b_lo=bl, b_major=0, ldb=kp, b_batch_stride=lin.out * kp,
-                         d=d, ldd=ldd, d_batch_stride=self.rows * ldd, bias=bias_addr,
+                         d=d, ldd=ldd, d_batch_stride=self.rows * ldd if d is not None else 0, bias=bias_addr,
                          bias_batch_stride=lin.out if bias_addr else 0,
                          out_plane=out_plane.c() if out_plane is not None else None, **kw)
 
@@ -592,7 +593,23 @@ class Run:
         prog.append(self._apply("embedder.norm", Cin, self.x_addr, self.ldx, 0, relu=False, plane=self.e))
         prog.append(self._fwd_gemm(net.linears["embed"], self.e, self.h[0], H, stats=False, out_plane=self.hp[0]))
         fused_eval = not self.training and min(E, H) >= 128  # transposed plans take the BN epilogue
+        # training without a backward pass (the target critic): the wide pre-normalisation
+        # output is never stored; a statistics-only product, then the product again with the
+        # batch norm fused into its epilogue
+        recompute_wide = self.training and not self.backward_needed and E >= 128
         for i in range(spec.blocks):
+            if recompute_wide:
+                w1, pre1 = net.linears[f"w1.{i}"], f"encoder.{i}.norm1"
+                stats_pass = self._fwd_gemm(w1, self.hp[i], None, 0, stats=True)
+                stats_pass.recompute = True  # the product is computed twice: one counts as work
+                prog.append(stats_pass)
+                prog.append(self._bn_stats(pre1, E, src_part_shared=False))
+                prog.append(self._fwd_gemm_bn(w1, self.hp[i], pre1, self.a1[i]))
+                prog.append(self._fwd_gemm(net.linears[f"w2.{i}"], self.a1[i], self.t2[i], H, stats=True))
+                prog.append(self._bn_stats(f"encoder.{i}.norm2", H, src_part_shared=False))
+                prog.append(self._apply(f"encoder.{i}.norm2", H, self.t2[i].data_ptr(), H, R * H, relu=True,
+                                        residual=self.h[i], y=self.h[i + 1], plane=self.hp[i + 1]))
+                continue
             if fused_eval:
                 prog.append(self._fwd_gemm_bn(net.linears[f"w1.{i}"], self.hp[i], f"encoder.{i}.norm1", self.a1[i]))
                 prog.append(self._fwd_gemm_bn(net.linears[f"w2.{i}"], self.a1[i], f"encoder.{i}.norm2", self.hp[i + 1],
