@@ -1180,8 +1180,9 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
         const int q = o.b_major ? chunk : 32;
         bn = std::min(256, (bn + q - 1) / q * q);
     }
-    // Fewer tiles than SMs: narrower tiles (down to 64) until the grid covers the SMs; with
-    // at most one tile per CTA a CTA's tile is all of its serial work.
+    // Fewer tiles than SMs: narrower tiles (down to 128) until the grid covers the SMs; with
+    // at most one tile per CTA a CTA's tile is all of its serial work. (64-wide tiles re-read
+    // the A tile from shared memory per 64 columns: slower on long-K products.)
     if (g->tile_n <= 0) {
         int dev = 0, nsm = 0;
         if (cudaGetDevice(&dev) == cudaSuccess &&
@@ -1190,7 +1191,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
             auto tiles_for = [&](int w) {
                 return static_cast<long long>((o.n + w - 1) / w) * ((o.m + kBM - 1) / kBM) * o.batch * splits;
             };
-            while (bn / 2 >= 64 && (bn / 2) % q == 0 && tiles_for(bn) < nsm) bn /= 2;
+            while (bn / 2 >= 128 && (bn / 2) % q == 0 && tiles_for(bn) < nsm) bn /= 2;
         }
     }
     if (bn % 16 != 0 || bn < 16 || bn > 256 || (o.b_major == 1 && bn % chunk != 0)) {

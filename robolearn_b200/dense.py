@@ -27,6 +27,18 @@ def operand_ld(cols: int, kind: int) -> int:
     return (cols + q - 1) // q * q
 
 
+def dw_splits(m: int, n: int, rows: int, batch: int, kind: int, sms: int = 148) -> int:
+    """K splits of a weight-gradient product dW[m][n] = sum over ``rows``: none when the
+    128 x 128 tiles already fill most SMs, else enough splits to approach one wave while
+    every split keeps at least 40 k-blocks (each split adds a partial output that the
+    fixed-order reduce reads back; short splits pay the pipeline fill for little work)."""
+    tiles = -(-m // 128) * -(-n // 128) * batch
+    if tiles * 3 >= 2 * sms:
+        return 1
+    kblocks = -(-rows // (64 if kind == FP16 else 32))
+    return max(1, min(32, kblocks // 40, -(-sms // tiles)))
+
+
 def tf32_split(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Exact split ``x = hi + lo`` with ``hi`` representable in tf32 (low 13 mantissa bits cleared)."""
     hi = (x.contiguous().view(torch.int32) & -8192).view(torch.float32)

@@ -27,7 +27,7 @@ import numpy as np
 import torch
 
 from .. import _native as N
-from ..dense import FP16, TF32X3, DensePlan, operand_ld, split_reduce
+from ..dense import FP16, TF32X3, DensePlan, dw_splits, operand_ld, split_reduce
 
 BN_EPS = 1e-5
 BN_MOMENTUM = 0.01
@@ -483,9 +483,7 @@ class Run:
         """dW[t] = dY[t]^T X[t] into the gradient arena, split over rows when the grid is small."""
         net = self.net
         n_out, k_in = lin.out, lin.inp
-        tiles = math.ceil(n_out / 128) * math.ceil(k_in / min(256, max(64, k_in))) * self.T
-        kblocks = math.ceil(self.rows / (64 if net.kind == FP16 else 32))
-        splits = max(1, min(math.ceil(2 * SM_COUNT / tiles), kblocks // 8, 16))
+        splits = dw_splits(n_out, k_in, self.rows, self.T, net.kind, SM_COUNT)
         d_addr = net.addr(grad_key, "grads")
         count = self.T * n_out * k_in
         common = dict(kind=net.kind, m=n_out, n=k_in, k=self.rows, batch=self.T,

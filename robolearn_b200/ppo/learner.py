@@ -297,6 +297,7 @@ class WarpPPO:
         n = lo.widths[li]
         dz, x = b["dz"][li], self._input_plane(b, li)
         batch = len(z_list)
+        # long K (24576 rows) over few small tiles: split up to 32 ways to fill the SMs
         tiles = math.ceil(m / 128) * math.ceil(n / min(256, max(32, n))) * batch
         kblocks = math.ceil(rows / 32)
         splits = max(1, min(math.ceil(2 * SM_COUNT / tiles), kblocks // 8, 32))
