@@ -3,8 +3,8 @@
 // One kernel per BN layer and direction. Block (slab of 32 columns, twin t), 8 warps:
 // the warps merge this rank's per-32-row-group partials (contiguous group ranges,
 // fixed order); warp 0 pushes the per-column entry into every rank's exchange slot
-// with plain peer stores, fences at system scope and raises one epoch flag per rank for
-// its slab, then polls its own slot's flags (acquire loads, bounded by wall-clock time)
+// with plain peer stores, raises one epoch flag per rank for its slab (system-scope release
+// after a warp barrier), then polls its own slot's flags (acquire loads, bounded by wall-clock time)
 // and merges the ranks' entries in rank order. Blocks never wait on one another, and a
 // wait that runs out records kHealthTimeout and returns.
 
@@ -58,7 +58,9 @@ __device__ bool exchange(const rl2_syncbn_exchange& ex, int twins, int t, int co
             dst[cols + c] = b;
         }
     }
-    __threadfence_system();
+    // The warp barrier orders every lane's pushes before the flag stores; each flag store is
+    // a system-scope release (cumulative over those pushes), so a peer that acquires the
+    // flag sees this rank's entries without a full system fence here.
     __syncwarp();
     if (lane < W) store_release(ex.peer_flags[lane] + flag_index + ex.rank, epoch);
     bool ok = true;
@@ -78,7 +80,7 @@ __device__ bool exchange(const rl2_syncbn_exchange& ex, int twins, int t, int co
         }
     }
     ok = __all_sync(0xffffffffu, ok);
-    __threadfence_system();
+    __syncwarp();  // every lane's reads of the entries follow the acquiring lanes' loads
     return ok;
 }
 
