@@ -54,16 +54,21 @@ __global__ void colstats_kernel(const float* __restrict__ x, long long ldx, long
 // range of groups in order, then warp 0 merges the 8 results in order (deterministic).
 // Group g of the partials lives at (g / gpr) * rs + (g % gpr) * cols: gpr groups per rank,
 // rank blocks rs floats apart (one rank: gpr = groups, rs = 0).
-__global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p,
+// Warps merge contiguous group ranges (eight groups loaded ahead of the merge), then a
+// fixed pairwise tree over the warps: with NT = 1024 a 256-group column takes 8 sequential
+// merges and 5 tree levels.
+template <int NT>
+__global__ void __launch_bounds__(NT) finalize_kernel(const float* __restrict__ mean_p, const float* __restrict__ m2_p,
                                                       long long pt, int gpr, long long rs, int twins, int rows,
                                                       int cols, float* mean, float* invstd, float* rm, float* rv,
                                                       float momentum, float eps, int update) {
-    __shared__ float sh[3][kT / 32][32];
+    constexpr int NW = NT / 32;
+    __shared__ float sh[3][NW][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     const int t = blockIdx.y;
     const int groups = (rows + 31) / 32;
-    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int per = (groups + NW - 1) / NW;
     const int g0 = warp * per, g1 = min(groups, g0 + per);
     float n = 0.0f, mu = 0.0f, m2 = 0.0f;
     if (c < cols) {
@@ -87,12 +92,17 @@ __global__ void __launch_bounds__(kT) finalize_kernel(const float* __restrict__ 
     sh[0][warp][lane] = n;
     sh[1][warp][lane] = mu;
     sh[2][warp][lane] = m2;
-    __syncthreads();
+#pragma unroll
+    for (int w = NW / 2; w >= 1; w >>= 1) {
+        __syncthreads();
+        if (warp < w) {
+            chan_merge(n, mu, m2, sh[0][warp + w][lane], sh[1][warp + w][lane], sh[2][warp + w][lane]);
+            sh[0][warp][lane] = n;
+            sh[1][warp][lane] = mu;
+            sh[2][warp][lane] = m2;
+        }
+    }
     if (warp != 0 || c >= cols) return;
-    n = sh[0][0][lane];
-    mu = sh[1][0][lane];
-    m2 = sh[2][0][lane];
-    for (int w = 1; w < kT / 32; ++w) chan_merge(n, mu, m2, sh[0][w][lane], sh[1][w][lane], sh[2][w][lane]);
     const int i = t * cols + c;
     const float var = m2 / static_cast<float>(rows);
     mean[i] = mu;
@@ -236,16 +246,18 @@ __global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
 }
 
 // grid (ceil(cols/32), twins), 8 warps over contiguous group ranges, fixed-order combine.
-__global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, const float* s2p, long long pt, int gpr,
+template <int NT>
+__global__ void __launch_bounds__(NT) bwd_finalize_kernel(const float* s1p, const float* s2p, long long pt, int gpr,
                                                           long long rs, int twins, int rows, int cols, float* dgamma,
                                                           float* dbeta, long long gts, int accumulate, float* coef1,
                                                           float* coef2) {
-    __shared__ float sh[2][kT / 32][32];
+    constexpr int NW = NT / 32;
+    __shared__ float sh[2][NW][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     const int t = blockIdx.y;
     const int groups = (rows + 31) / 32;
-    const int per = (groups + kT / 32 - 1) / (kT / 32);
+    const int per = (groups + NW - 1) / NW;
     const int g0 = warp * per, g1 = min(groups, g0 + per);
     float s1 = 0.0f, s2 = 0.0f;
     if (c < cols) {
@@ -270,14 +282,17 @@ __global__ void __launch_bounds__(kT) bwd_finalize_kernel(const float* s1p, cons
     }
     sh[0][warp][lane] = s1;
     sh[1][warp][lane] = s2;
-    __syncthreads();
-    if (warp != 0 || c >= cols) return;
-    s1 = 0.0f;
-    s2 = 0.0f;
-    for (int w = 0; w < kT / 32; ++w) {
-        s1 += sh[0][w][lane];
-        s2 += sh[1][w][lane];
+#pragma unroll
+    for (int w = NW / 2; w >= 1; w >>= 1) {
+        __syncthreads();
+        if (warp < w) {
+            s1 += sh[0][warp + w][lane];
+            s2 += sh[1][warp + w][lane];
+            sh[0][warp][lane] = s1;
+            sh[1][warp][lane] = s2;
+        }
     }
+    if (warp != 0 || c >= cols) return;
     const int i = t * cols + c;
     if (dgamma) dgamma[t * gts + c] = accumulate ? dgamma[t * gts + c] + s2 : s2;
     if (dbeta) dbeta[t * gts + c] = accumulate ? dbeta[t * gts + c] + s1 : s1;
@@ -476,9 +491,15 @@ extern "C" int rl2_bn_finalize_ranked(const float* mean_p, const float* m2_p, lo
         set_error("bn finalize: invalid buffers or shape (running update needs rows >= 2)");
         return -1;
     }
-    norm::finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
-        mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
-        update);
+    const dim3 grid((cols + 31) / 32, twins);
+    if ((rows + 31) / 32 >= 128)
+        norm::finalize_kernel<1024><<<grid, 1024, 0, as_stream(stream)>>>(
+            mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
+            update);
+    else
+        norm::finalize_kernel<norm::kT><<<grid, norm::kT, 0, as_stream(stream)>>>(
+            mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
+            update);
     return launch_status("batch-norm statistics");
 }
 
@@ -540,8 +561,13 @@ extern "C" int rl2_bn_backward_finalize_ranked(const float* s1p, const float* s2
         set_error("bn backward finalize: invalid arguments");
         return -1;
     }
-    norm::bwd_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kT, 0, as_stream(stream)>>>(
-        s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+    const dim3 grid((cols + 31) / 32, twins);
+    if ((rows + 31) / 32 >= 128)
+        norm::bwd_finalize_kernel<1024><<<grid, 1024, 0, as_stream(stream)>>>(
+            s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+    else
+        norm::bwd_finalize_kernel<norm::kT><<<grid, norm::kT, 0, as_stream(stream)>>>(
+            s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
     return launch_status("batch-norm backward finalize");
 }
 

@@ -84,9 +84,10 @@ __global__ void backward_kernel(const rl2_policy_args a, const Plane plane) {
     // each warp handles 32 consecutive rows (one column-sum group) at a time
     for (int g = blockIdx.x * kWarps + warp; g < groups; g += gridDim.x * kWarps) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};  // lanes own columns lane, lane+32, lane+64, lane+96 of 2A
+#pragma unroll 4
         for (int rr = 0; rr < 32; ++rr) {
             const long long row = static_cast<long long>(g) * 32 + rr;
-            if (row >= a.rows) break;
+            if (row >= a.rows) continue;
             const float* h = a.head + row * a.ld_head;
             const float* n = a.noise + row * a.ld_noise;
             const float dlp = row < a.grad_rows ? (a.d_log_pi ? a.d_log_pi[row] : dlp_val) : 0.0f;
@@ -228,10 +229,24 @@ __global__ void __launch_bounds__(kT) kernel(const rl2_actor_objective_args a, c
     __syncthreads();
     if (!last_block) return;
     __threadfence();
+    // all block rows summed by the last block's threads: thread i takes rows i, i + kT, ...
+    // in order, then a fixed pairwise tree over the threads (deterministic)
+    __shared__ float tree[5][kT];
+    {
+        float s[5] = {0, 0, 0, 0, 0};
+        for (unsigned b = threadIdx.x; b < gridDim.x; b += kT)
+            for (int i = 0; i < 5; ++i) s[i] += __ldcg(a.workspace + static_cast<long long>(b) * 5 + i);
+        for (int i = 0; i < 5; ++i) tree[i][threadIdx.x] = s[i];
+    }
+    __syncthreads();
+    for (int w = kT / 2; w >= 1; w >>= 1) {
+        if (threadIdx.x < w)
+            for (int i = 0; i < 5; ++i) tree[i][threadIdx.x] += tree[i][threadIdx.x + w];
+        __syncthreads();
+    }
     if (threadIdx.x == 0) {
-        float v[5] = {0, 0, 0, 0, 0};
-        for (unsigned b = 0; b < gridDim.x; ++b)
-            for (int i = 0; i < 5; ++i) v[i] += a.workspace[static_cast<long long>(b) * 5 + i];
+        float v[5];
+        for (int i = 0; i < 5; ++i) v[i] = tree[i][0];
         const float B = static_cast<float>(a.batch);
         const float q_abs = v[3] / B;
         float loss = v[0] / B;
