@@ -805,13 +805,23 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
                     for (int r = 0; r < 32; ++r)
                         if (full || r < vr) v[r] = v[r] + src[static_cast<long long>(r) * p.ldd];
                 }
-                if (actv) {
+                // the activation kind is uniform: one specialised loop each (no per-element
+                // selection between the ELU and tanh code)
+                if (actv == 1) {
                     if (acol) {
 #pragma unroll
-                        for (int r = 0; r < 32; ++r) v[r] = v[r] * act_grad(actv, aux[r]);
+                        for (int r = 0; r < 32; ++r) v[r] = v[r] * (aux[r] > 0.f ? 1.0f : aux[r] + 1.0f);
                     } else {
 #pragma unroll
-                        for (int r = 0; r < 32; ++r) v[r] = act_fwd(actv, v[r]);
+                        for (int r = 0; r < 32; ++r) v[r] = v[r] > 0.f ? v[r] : expf(v[r]) - 1.0f;
+                    }
+                } else if (actv == 2) {
+                    if (acol) {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) v[r] = v[r] * (1.0f - aux[r] * aux[r]);
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) v[r] = tanhf(v[r]);
                     }
                 }
             }

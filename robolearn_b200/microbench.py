@@ -36,6 +36,8 @@ def main() -> None:
     p.add_argument("--plane", action="store_true")
     p.add_argument("--residual", action="store_true")
     p.add_argument("--in-place", action="store_true", help="residual = the output itself")
+    p.add_argument("--act", type=int, choices=(0, 1, 2), default=0, help="epilogue activation: 1 ELU, 2 tanh")
+    p.add_argument("--lo-only", action="store_true", help="tf32 plane as lo alone beside the fp32 output")
     p.add_argument("--no-d", action="store_true", help="write only the operand plane")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
@@ -88,10 +90,16 @@ def main() -> None:
             keep.append(h)
             kw["out_plane"] = N.Plane(h16=h.data_ptr(), ld=pld, twin_stride=m * pld)
         else:
-            hi = torch.zeros(z, m, pld, device=dev)
-            lo = torch.zeros(z, m, pld, device=dev)
-            keep += [hi, lo]
-            kw["out_plane"] = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld)
+            lo = torch.zeros(z, m, ldd if a.lo_only else pld, device=dev)
+            keep.append(lo)
+            if a.lo_only:
+                kw["out_plane"] = N.Plane(lo=lo.data_ptr(), ld=ldd, twin_stride=m * ldd)
+            else:
+                hi = torch.zeros(z, m, pld, device=dev)
+                keep.append(hi)
+                kw["out_plane"] = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld)
+    if a.act:
+        kw["activation"] = a.act
     plan = dense.DensePlan(kind=kind, m=m, n=n, k=k, a=A, b=B, lda=lda, ldb=ldb, a_major=a.a_major,
                            b_major=a.b_major, batch=z, a_batch_stride=A[0].numel(), b_batch_stride=B[0].numel(),
                            tile_n=a.tile_n, **kw)
