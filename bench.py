@@ -309,17 +309,38 @@ def run_b200(args, rank, world, local_rank):
     host["rew"] = torch.randn(ENVS).pin_memory()
     host["term"] = (torch.rand(ENVS) < 0.01).float().pin_memory()
     host["trunc"] = torch.zeros(ENVS).pin_memory()
-    dev = {k: torch.empty(v.shape, device=device) for k, v in host.items()}
+    # two device staging sets: step i + 1's host->device copy runs on a copy stream while
+    # step i's ingest and update run (the copy into a set waits for the ingest that read it)
+    dev = [{k: torch.empty(v.shape, device=device) for k, v in host.items()} for _ in range(2)]
     loss_host = torch.zeros(1).pin_memory()
     h2d = sum(v.numel() * 4 for v in host.values())
+    main = torch.cuda.current_stream()
+    copy_stream = torch.cuda.Stream()
+    landed = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            if i >= 2:
+                copy_stream.wait_event(consumed[b])
+            for k in host:
+                dev[b][k].copy_(host[k], non_blocking=True)
+            landed[b].record(copy_stream)
+
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
+    upload(0)
     for i in range(args.steps):
-        for k in host:
-            dev[k].copy_(host[k], non_blocking=True)
-        R.add(dev["obs"], dev["act"], dev["rew"], dev["term"], dev["trunc"], dev["next_obs"])
+        b = i % 2
+        if i + 1 < args.steps:
+            upload(i + 1)
+        main.wait_event(landed[b])
+        d = dev[b]
+        R.add(d["obs"], d["act"], d["rew"], d["term"], d["trunc"], d["next_obs"])
+        consumed[b].record(main)
         step(i)
         loss_host.copy_(L.metrics[3:4], non_blocking=True)
     t1.record()
