@@ -440,16 +440,39 @@ def run_ppo(args) -> dict:
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    # end to end through the public API: rollout copied from pinned host memory, update, loss read back
+    # end to end through the public API: rollout copied from pinned host memory, update, loss
+    # read back. Update i + 1's rollout goes host -> device on a copy stream into one of two
+    # staging sets while update i runs; the update stream moves it into the agent's arrays.
     host = {k: v.cpu().pin_memory() for k, v in data.items()}
     loss_host = torch.zeros(4).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
+    stage = [{k: torch.empty_like(getattr(agent, k)) for k in host} for _ in range(2)]
+    main = torch.cuda.current_stream()
+    copy_stream = torch.cuda.Stream()
+    landed = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            if i >= 2:
+                copy_stream.wait_event(consumed[b])
+            for k, v in host.items():
+                stage[b][k].copy_(v, non_blocking=True)
+            landed[b].record(copy_stream)
+
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     t0.record()
-    for _ in range(args.steps):
-        for k, v in host.items():
-            getattr(agent, k).copy_(v, non_blocking=True)
+    upload(0)
+    for i in range(args.steps):
+        b = i % 2
+        if i + 1 < args.steps:
+            upload(i + 1)
+        main.wait_event(landed[b])
+        for k in host:
+            getattr(agent, k).copy_(stage[b][k])
+        consumed[b].record(main)
         agent.update()
         loss_host[:1].copy_(agent.loss, non_blocking=True)
         loss_host[1:].copy_(agent.metrics, non_blocking=True)
