@@ -594,7 +594,10 @@ class Run:
         # training without a backward pass (the target critic): the wide pre-normalisation
         # output is never stored; a statistics-only product, then the product again with the
         # batch norm fused into its epilogue
-        recompute_wide = self.training and not self.backward_needed and E >= 128
+        # (only where the product is cheap next to the bytes it saves: fp16 operands, K <= 512;
+        # a 3xTF32 product or a long K costs more than the stored output and the apply pass)
+        recompute_wide = (self.training and not self.backward_needed and E >= 128 and net.kind == FP16
+                          and H <= 512)
         for i in range(spec.blocks):
             if recompute_wide:
                 w1, pre1 = net.linears[f"w1.{i}"], f"encoder.{i}.norm1"
