@@ -703,6 +703,9 @@ class Run:
         return prog
 
     def _backward(self):
+        """Backward launch list; ``grad_marks`` records (position, arena offset) pairs: after
+        the launch at that position every parameter gradient from the offset on is final."""
+        self.grad_marks = []
         net, spec, lib = self.net, self.net.spec, _lib()
         T, H, E, R = self.T, self.H, self.E, self.rows
         pg = self.need_param_grads
@@ -737,6 +740,9 @@ class Run:
                                       self.dt1)
             if pg:
                 prog += self._dw_gemm(net.linears[f"w1.{i}"], self.dt1, self.hp[i], f"encoder.{i}.w1{wsuf}")
+                # every gradient from this block's first parameter to the end of the arena is
+                # final here (blocks, post-norm and head come after it in the arena)
+                self.grad_marks.append((len(prog), net.offsets[f"encoder.{i}.w1{wsuf}"]))
             # block 0's input gradient dh0 also feeds the embedder products as an operand plane
             emit = self.dh_plane.c(self.scaler.scale, self.scaler.found_inf) if i == 0 else None
             prog.append(self._dx_gemm(net.linears[f"w1.{i}"], self.dt1, self.dh, H, residual=self.dh, out_plane=emit))

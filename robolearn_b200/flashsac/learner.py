@@ -184,6 +184,8 @@ class Learner:
         self.metrics = torch.zeros(len(METRIC_KEYS), **f32)
         self.scratch = torch.zeros(8, **f32)  # [q_abs, d_log_pi, ...]
         self.health = torch.zeros(1, dtype=torch.int32, device=device)
+        # data parallel: gradient suffixes are averaged on this stream during the backward
+        self._grad_stream = torch.cuda.Stream(device) if (self.dp is not None and device.type == "cuda") else None
         self.counters = torch.zeros(4, dtype=torch.int64, device=device)  # [noise epoch, ...]
         self.noise_epoch = torch.zeros(1, dtype=torch.int64, device=device)
         self.support = torch.from_numpy(support(bins, cfg.critic_min_v, cfg.critic_max_v)).to(device)
@@ -224,7 +226,36 @@ class Learner:
                             rows=rows, act=self.act, actions=actions_addr, ld_actions=ld_actions,
                             log_pi=log_pi.data_ptr())
 
-    def _optimizer(self, name: str, net: Net, target: Net | None = None):
+    def _backward_with_exchange(self, run: Run, net: Net, apply_optimizer: bool):
+        """The run's backward launches; with data parallelism and an optimizer step, each
+        finished suffix of the gradient arena is averaged over the ranks on a side stream
+        while the earlier layers' backward continues. Returns (launches, prefix end): the
+        gradients below the prefix end are left to the optimizer launch."""
+        prog = list(run.backward_program)
+        dp = self.dp
+        if dp is None or not apply_optimizer or not dp.nccl or not run.grad_marks:
+            return prog, net.size
+        side = self._grad_stream
+        out, hi = [], net.size
+        marks = dict(run.grad_marks)
+        for i, f in enumerate(prog):
+            out.append(f)
+            if i + 1 in marks:
+                lo = marks[i + 1]
+
+                def bucket(lo=lo, hi=hi):
+                    side.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.stream(side):
+                        dp.all_reduce_mean(net.grads[lo:hi])
+
+                bucket.launches = 0
+                out.append(bucket)
+                hi = lo
+        return out, hi
+
+    def _optimizer(self, name: str, net: Net, target: Net | None = None, prefix: int | None = None):
+        """Fused optimizer pass; under data parallelism the gradients are averaged first
+        (only [0, prefix) here when the backward already averaged the rest on the side stream)."""
         cfg, lib = self.cfg, self.lib
         sc = self.scalers[name]
         prep = N.AdamPrepareArgs(
@@ -246,7 +277,12 @@ class Learner:
 
         def launch():
             if dp is not None:  # average the gradients of all ranks; skip the step on any rank's overflow
-                dp.all_reduce_mean(net.grads)
+                if prefix is not None and prefix < net.size:
+                    torch.cuda.current_stream().wait_stream(self._grad_stream)
+                    if prefix > 0:
+                        dp.all_reduce_mean(net.grads[:prefix])
+                else:
+                    dp.all_reduce_mean(net.grads)
                 if sc.found_inf is not None and self.kind == FP16:
                     dp.all_reduce_max(sc.found_inf)
             N.check(lib.rl2_adam_prepare(pref, N.stream_ptr()), f"{name} adam prepare")
@@ -308,9 +344,10 @@ class Learner:
                         "policy bias gradient")
 
             prog.append(bias_fin)
-            prog += self.actor_train.backward_program
+            bw, prefix = self._backward_with_exchange(self.actor_train, self.actor, apply_optimizer)
+            prog += bw
             if apply_optimizer:
-                prog.append(self._optimizer("actor", self.actor))
+                prog.append(self._optimizer("actor", self.actor, prefix=prefix))
             temp = N.TemperatureArgs(
                 log_temp=self.log_temp.data_ptr(), entropy=mi["actor/entropy"], target_entropy=self.target_entropy,
                 adam_state=self.temp_state.data_ptr(), beta1=0.9, beta2=0.999, eps=1e-8,
@@ -358,9 +395,10 @@ class Learner:
             co.dplane_row_stride = cr.dhead.ld
             co.dplane_twin_stride = cr.dhead.tstride
         prog.append(_wrap(lib.rl2_critic_objective, co, None, "critic objective"))
-        prog += self.critic_run.backward_program
+        bw, prefix = self._backward_with_exchange(self.critic_run, self.critic, apply_optimizer)
+        prog += bw
         if apply_optimizer:
-            prog.append(self._optimizer("critic", self.critic, target=self.target))
+            prog.append(self._optimizer("critic", self.critic, target=self.target, prefix=prefix))
         if self.dp is not None:  # reported metrics over the global batch
             mx = METRIC_KEYS.index("critic/max_entropy_bonus")
 
