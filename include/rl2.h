@@ -136,6 +136,12 @@ int rl2_gemm_uses_tma_store(void* plan);
 /* out[i] (+)= sum_s partial[s * split_stride + i], fixed order, i < count. */
 int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out, long long count,
                      int accumulate, void* stream);
+/* The same for batch independent reductions in one launch: reduction b reads
+ * partial + b * in_batch_stride and writes out + b * out_batch_stride (strides in floats,
+ * the output stride may be negative). */
+int rl2_split_reduce_batched(const float* partial, long long split_stride, int splits, float* out, long long count,
+                             int accumulate, int batch, long long in_batch_stride, long long out_batch_stride,
+                             void* stream);
 
 /* ---------------------------------------------------------------------------
  * fused categorical critic objective: min-Q twin selection + two-hot Bellman

@@ -156,6 +156,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_gemm_tile_n": ([P], I),
     "rl2_gemm_uses_tma_store": ([P], I),
     "rl2_split_reduce": ([P, LL, I, P, LL, I, P], I),
+    "rl2_split_reduce_batched": ([P, LL, I, P, LL, I, I, LL, LL, P], I),
     "rl2_categorical_workspace_floats": ([I, I], I),
     "rl2_categorical_counter_words": ([I, I], I),
     "rl2_critic_objective": ([ctypes.POINTER(CriticObjectiveArgs), P], I),

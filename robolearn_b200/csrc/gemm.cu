@@ -1422,7 +1422,10 @@ extern "C" int rl2_gemm_uses_tma_store(void* opaque) {
 namespace rl2 {
 namespace gemm {
 __global__ void split_reduce_kernel(const float* __restrict__ part, long long stride, int splits,
-                                    float* __restrict__ out, long long count, int accumulate, int allow_vec) {
+                                    float* __restrict__ out, long long count, int accumulate, int allow_vec,
+                                    long long in_bstride, long long out_bstride) {
+    part += blockIdx.y * in_bstride;  // grid.y: independent reductions of the same shape
+    out += blockIdx.y * out_bstride;
     const long long n4 = count / 4;
     const bool vec = allow_vec && (stride % 4 == 0) && ptx::aligned16(part) && ptx::aligned16(out);
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < (vec ? n4 : count);
@@ -1458,12 +1461,13 @@ __global__ void split_reduce_kernel(const float* __restrict__ part, long long st
 }  // namespace gemm
 }  // namespace rl2
 
-extern "C" int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out,
-                                long long count, int accumulate, void* stream) {
+extern "C" int rl2_split_reduce_batched(const float* partial, long long split_stride, int splits, float* out,
+                                        long long count, int accumulate, int batch, long long in_batch_stride,
+                                        long long out_batch_stride, void* stream) {
     using namespace rl2;
     clear_error();
-    if (!partial || !out || splits < 1 || count < 1 || split_stride < count) {
-        set_error("split reduce needs non-null buffers, splits >= 1 and split_stride >= count");
+    if (!partial || !out || splits < 1 || count < 1 || split_stride < count || batch < 1 || batch > 65535) {
+        set_error("split reduce needs non-null buffers, splits >= 1, split_stride >= count and 1..65535 batches");
         return -1;
     }
     // small outputs: one thread per element (more loads in flight than float4 threads);
@@ -1471,7 +1475,12 @@ extern "C" int rl2_split_reduce(const float* partial, long long split_stride, in
     const int vec = count > (1LL << 22) ? 1 : 0;
     const long long work = vec ? count / 4 + 1 : count;
     const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 148LL * 16));
-    gemm::split_reduce_kernel<<<blocks, 256, 0, as_stream(stream)>>>(partial, split_stride, splits, out, count,
-                                                                      accumulate, vec);
+    gemm::split_reduce_kernel<<<dim3(blocks, batch), 256, 0, as_stream(stream)>>>(
+        partial, split_stride, splits, out, count, accumulate, vec, in_batch_stride, out_batch_stride);
     return launch_status("split-K reduce");
+}
+
+extern "C" int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out,
+                                long long count, int accumulate, void* stream) {
+    return rl2_split_reduce_batched(partial, split_stride, splits, out, count, accumulate, 1, 0, 0, stream);
 }

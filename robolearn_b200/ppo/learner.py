@@ -319,13 +319,13 @@ class WarpPPO:
         plan = DensePlan(d=ws, k_splits=splits, d_split_stride=batch * count, **common)
         lib = self.lib
 
-        def reduce_launch():
-            s = N.stream_ptr()
-            for j, out in enumerate(outs):
-                N.check(lib.rl2_split_reduce(ws.data_ptr() + 4 * j * count, batch * count, splits, out, count, 0, s),
-                        "PPO weight-gradient reduce")
+        out_stride = (outs[1] - outs[0]) // 4 if batch == 2 else 0
 
-        reduce_launch.launches = batch
+        def reduce_launch():  # both twins in one launch (their outputs sit a fixed distance apart)
+            N.check(lib.rl2_split_reduce_batched(ws.data_ptr(), batch * count, splits, outs[0], count, 0, batch, count,
+                                                 out_stride, N.stream_ptr()), "PPO weight-gradient reduce")
+
+        reduce_launch.launches = 1
         return [plan, reduce_launch]
 
     def _backward_plans(self, b: dict) -> list:

@@ -437,3 +437,25 @@ def test_gemm_eval_batch_norm_epilogue(kind):
         assert torch.equal(keep[0][:, :, :n], D.half())
     else:
         assert torch.equal(keep[0][:, :, :n] + keep[1][:, :, :n], D)
+
+
+def test_split_reduce_batched_matches_per_batch_reduce():
+    """rl2_split_reduce_batched (one launch for several same-shape reductions, output stride
+    possibly negative) equals one rl2_split_reduce per batch, bit for bit."""
+    from robolearn_b200 import _native as N
+
+    lib = N.load()
+    splits, count, batch = 5, 3001, 2
+    part = torch.randn(splits, batch, count, device="cuda")
+    out = torch.zeros(2 * count + 17, device="cuda")
+    ref = torch.zeros_like(out)
+    s = torch.cuda.current_stream().cuda_stream
+    base1 = out.data_ptr() + 4 * (count + 17)  # batch 0 written after batch 1: negative stride
+    assert lib.rl2_split_reduce_batched(part.data_ptr(), batch * count, splits, base1, count, 0, batch, count,
+                                        -(count + 17), s) == 0
+    for b, off in ((0, count + 17), (1, 0)):
+        assert lib.rl2_split_reduce(part.data_ptr() + 4 * b * count, batch * count, splits, ref.data_ptr() + 4 * off,
+                                    count, 0, s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert torch.allclose(out[count + 17:], part[:, 0].sum(0), rtol=1e-5, atol=1e-5)
