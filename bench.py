@@ -329,6 +329,11 @@ def run_b200(args, rank, world, local_rank):
             landed[b].record(copy_stream)
 
     torch.cuda.synchronize()
+    if world > 1:  # every rank has its host buffers before the timed region (as for the device timing)
+        import torch.distributed as dist
+
+        dist.barrier()
+        torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
