@@ -1104,7 +1104,9 @@ int auto_tile_n(int n, int kind, int b_mn) {
 
 using rl2::gemm::Plan;
 
-extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
+// rebindable: the plan's output, bias and residual pointers are replaced at every launch
+// (rl2::gemm::run_rebound), so no epilogue form may bake them into a tensor map.
+static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
     using namespace rl2;
     using namespace rl2::gemm;
     clear_error();
@@ -1162,7 +1164,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
                                                       g->residual_batch_stride == g->d_batch_stride)) &&
                           !(g->accumulate && g->residual);
     const bool reduce_ok = in_place && !plane_used(&g->out_plane) && !g->stat_mean;
-    const bool reduce_path = tma_store_enabled() && splits == 1 && reduce_ok && !g->activation && !g->act_aux &&
+    const bool reduce_path = !rebindable && tma_store_enabled() && splits == 1 && reduce_ok && !g->activation && !g->act_aux &&
                              !g->bn_mean && outputs_tma_ok(g);
     const bool swap = swap_enabled() && g->tile_n <= 0 && g->n >= 128 && !reduce_path;
     if (g->bn_mean && !swap) {
@@ -1317,7 +1319,7 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     // when the product has no activation / split-K and the outputs satisfy the TMA rules.
     // D += result (accumulate, or a residual that is D itself) goes through TMA reduce-add
     // stores when nothing else needs the final values (reduce_ok).
-    if (!swap && tma_store_enabled() && p.splits == 1 && (!(g->residual || g->accumulate) || reduce_ok) &&
+    if (!rebindable && !swap && tma_store_enabled() && p.splits == 1 && (!(g->residual || g->accumulate) || reduce_ok) &&
         !g->activation && !g->act_aux && outputs_tma_ok(g)) {
         const bool plane_on = plane_used(&g->out_plane);
         bool mok = true;
@@ -1384,6 +1386,38 @@ extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) {
     }
     return plan;
 }
+
+extern "C" void* rl2_gemm_create(const rl2_gemm_desc* g) { return create_plan(g, false); }
+
+namespace rl2 {
+namespace gemm {
+
+void* create_rebindable(const rl2_gemm_desc* g) { return create_plan(g, true); }
+
+int run_rebound(void* opaque, float* d, const float* bias, const float* residual, int accumulate,
+                cudaStream_t stream) {
+    clear_error();
+    Plan* plan = static_cast<Plan*>(opaque);
+    if (!plan || plan->p.tma_epi || !d) {
+        set_error("rebound GEMM launch needs a rebindable plan and an output");
+        return -1;
+    }
+    Params p = plan->p;
+    p.d = d;
+    p.bias = bias;
+    p.residual = residual;
+    p.accumulate = accumulate;
+    p.vec_d = aligned(d, 16) && p.ldd % 4 == 0 && p.d_bstride % 4 == 0 && p.d_split_stride % 4 == 0;
+    p.vec_res = residual && aligned(residual, 16) && p.ldr % 4 == 0 && p.r_bstride % 4 == 0;
+    p.vec_bias = bias && aligned(bias, 16) && p.bias_bstride % 4 == 0;
+    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
+    fn<<<plan->grid, kThreads, plan->smem, stream>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, plan->td,
+                                                     plan->tp, p, plan->stages);
+    return launch_status("tcgen05 GEMM (rebound)");
+}
+
+}  // namespace gemm
+}  // namespace rl2
 
 extern "C" int rl2_gemm_run(void* opaque, void* stream) {
     using namespace rl2;
