@@ -323,7 +323,7 @@ def test_batch_norm_training_and_evaluation(lib):
     dw, db = torch.randn(C, generator=g).cuda(), torch.randn(C, generator=g).cuda()
     gmask = dy.double().cpu().numpy() * (y.double().cpu().numpy() > 0)
     dxr, dwr, dbr = O.bn_backward(gmask[None], cache)
-    exp_dx, exp_dw, exp_db = dx.double().cpu() + dxr[0], dw.double().cpu() + dwr[0], db.double().cpu() + dbr[0]
+    exp_dx, exp_dw, exp_db = (t.double().cpu() + torch.from_numpy(r[0]) for t, r in ((dx, dxr), (dw, dwr), (db, dbr)))
     _ok(lib, lib.rl_flash_bn_backward(x.data_ptr(), dy.data_ptr(), y.data_ptr(), w.data_ptr(), mean.data_ptr(),
                                       var.data_ptr(), partial.data_ptr(), sums.data_ptr(), dx.data_ptr(), dw.data_ptr(),
                                       db.data_ptr(), B, C, eps, 1, 1, _s()))
@@ -364,7 +364,7 @@ def test_rms_norm(lib):
     dx, dw = torch.randn(B, C, generator=g).cuda(), torch.randn(C, generator=g).cuda()
     partial = torch.zeros(((B + 255) // 256) * C, device="cuda")
     dxr, dwr = O.rms_backward(dy.double().cpu().numpy()[None], cache)
-    exp_dx, exp_dw = dx.double().cpu() + dxr[0], dw.double().cpu() + dwr[0]
+    exp_dx, exp_dw = dx.double().cpu() + torch.from_numpy(dxr[0]), dw.double().cpu() + torch.from_numpy(dwr[0])
     _ok(lib, lib.rl_flash_rms_backward(x.data_ptr(), dy.data_ptr(), w.data_ptr(), var.data_ptr(), partial.data_ptr(),
                                        dx.data_ptr(), dw.data_ptr(), B, C, eps, _s()))
     torch.cuda.synchronize()
