@@ -281,3 +281,115 @@ def test_categorical_heads_agree(libs, batch, bins):
         except AssertionError as e:
             raise AssertionError(f"{name}: {e}") from None
     assert ours[5].item() == ref[5].item()
+
+
+def test_reference_library_timing(libs):
+    """Times each entry-point family at cfg3 sizes in both libraries (CUDA events, 200 MB L2
+    flush before every timed call, median of 10 after 3 warm-up calls) and writes the table
+    as JSON to ``$RL2_REFOPS_OUT`` when that is set; asserts only that every call succeeds.
+    The reference library is the GPU baseline of the reference's native backend."""
+    import json
+    import os
+
+    g = torch.Generator().manual_seed(5)
+    flush = torch.empty(50 * 1024 * 1024, device="cuda")
+    rows, hidden, wide, bins = 8192, 512, 2048, 101
+
+    def timed(fn, reps=10, warm=3):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return float(np.median(ts))
+
+    x16 = torch.randn(rows, hidden, generator=g).half().cuda()
+    w16 = torch.randn(wide, hidden, generator=g).half().cuda()
+    x32, w32 = x16.float(), w16.float()
+    bias = torch.randn(wide, generator=g).cuda()
+    xb = torch.randn(rows, wide, generator=g).cuda()
+    dyb = torch.randn(rows, wide, generator=g).cuda()
+    wb, bb = torch.randn(wide, generator=g).cuda(), torch.randn(wide, generator=g).cuda()
+    xr, dyr, wr = xb[:, :hidden].contiguous(), dyb[:, :hidden].contiguous(), wb[:hidden].contiguous()
+    raw = torch.randn(rows, bins, generator=g).cuda()
+    cb, support = torch.randn(bins, generator=g).cuda(), torch.linspace(-10, 10, bins).cuda()
+    q = torch.randn(2, rows, generator=g).cuda()
+    lp_in = torch.log_softmax(torch.randn(2, rows, bins, generator=g), -1).cuda()
+    half = rows // 2
+    rew, term = torch.randn(half, generator=g).cuda(), torch.zeros(half, device="cuda")
+    disc, nlp, alpha = torch.full((half,), 0.99, device="cuda"), torch.randn(half, generator=g).cuda(), torch.tensor([0.05], device="cuda")
+    n_params = [wide * hidden] * 4 + [hidden * wide] * 4 + [wide] * 16 + [hidden * 160] * 2
+    params = [torch.randn(n, generator=g).cuda() for n in n_params]
+    table = {}
+
+    for name, lib in libs.items():
+        res = {}
+        # dense: Y^T (wide x rows) = W (wide x hidden) . X^T, column-major views of row-major X, W
+        for dtype, (xa, wa) in ((1, (x16, w16)), (0, (x32, w32))):
+            plan = lib.rl_plan_create_mixed(wide, rows, hidden, 1, 0, hidden, hidden, wide, 1, 0, dtype, 32 << 20)
+            assert plan, lib.rl_last_error().decode()
+            wsb = lib.rl_plan_workspace(plan)
+            ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
+            out = torch.empty(rows, wide, device="cuda")
+            res[f"dense_fp{16 if dtype else 32}_{wide}x{rows}x{hidden}"] = timed(lambda: _ok(lib, lib.rl_plan_run(
+                plan, wa.data_ptr(), xa.data_ptr(), None, out.data_ptr(), bias.data_ptr(), ws.data_ptr(), wsb, 0.0, _s())))
+            lib.rl_plan_destroy(plan)
+        chunks = (rows + 255) // 256
+        rm, rv = torch.zeros(wide, device="cuda"), torch.ones(wide, device="cuda")
+        mean, var = torch.zeros(wide, device="cuda"), torch.zeros(wide, device="cuda")
+        partial, sums = torch.zeros(2 * chunks * wide, device="cuda"), torch.zeros(2 * wide, device="cuda")
+        y, y16 = torch.empty_like(xb), torch.empty(rows, wide, dtype=torch.float16, device="cuda")
+        dx, dw, db = torch.zeros_like(xb), torch.zeros(wide, device="cuda"), torch.zeros(wide, device="cuda")
+        res[f"bn_forward_train_relu_{rows}x{wide}"] = timed(lambda: _ok(lib, lib.rl_flash_bn_forward_with_fp16(
+            xb.data_ptr(), wb.data_ptr(), bb.data_ptr(), rm.data_ptr(), rv.data_ptr(), mean.data_ptr(), var.data_ptr(),
+            partial.data_ptr(), y.data_ptr(), y16.data_ptr(), rows, wide, 1e-5, 0.01, 1, 1, _s())))
+        res[f"bn_backward_train_relu_{rows}x{wide}"] = timed(lambda: _ok(lib, lib.rl_flash_bn_backward(
+            xb.data_ptr(), dyb.data_ptr(), y.data_ptr(), wb.data_ptr(), mean.data_ptr(), var.data_ptr(),
+            partial.data_ptr(), sums.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), rows, wide, 1e-5, 1, 1,
+            _s())))
+        rvar, ry = torch.empty(rows, device="cuda"), torch.empty_like(xr)
+        rdx, rdw = torch.zeros_like(xr), torch.zeros(hidden, device="cuda")
+        rpart = torch.zeros(chunks * hidden, device="cuda")
+        res[f"rms_forward_{rows}x{hidden}"] = timed(lambda: _ok(lib, lib.rl_flash_rms_forward(
+            xr.data_ptr(), wr.data_ptr(), rvar.data_ptr(), ry.data_ptr(), rows, hidden, 1e-6, _s())))
+        res[f"rms_backward_{rows}x{hidden}"] = timed(lambda: _ok(lib, lib.rl_flash_rms_backward(
+            xr.data_ptr(), dyr.data_ptr(), wr.data_ptr(), rvar.data_ptr(), rpart.data_ptr(), rdx.data_ptr(),
+            rdw.data_ptr(), rows, hidden, 1e-6, _s())))
+        lp, val = torch.empty(rows, bins, device="cuda"), torch.empty(rows, device="cuda")
+        draw, dcb, scratch = torch.zeros(rows, bins, device="cuda"), torch.zeros(bins, device="cuda"), torch.empty(rows, bins, device="cuda")
+        res[f"categorical_forward_{rows}x{bins}"] = timed(lambda: _ok(lib, lib.rl_flash_categorical_forward(
+            raw.data_ptr(), cb.data_ptr(), support.data_ptr(), lp.data_ptr(), val.data_ptr(), rows, bins, _s())))
+        res[f"categorical_backward_{rows}x{bins}"] = timed(lambda: _ok(lib, lib.rl_flash_categorical_backward(
+            lp.data_ptr(), support.data_ptr(), raw.data_ptr(), val.data_ptr(), scratch.data_ptr(), draw.data_ptr(),
+            dcb.data_ptr(), rows, bins, _s())))
+        tgt, ment = torch.empty(half, bins, device="cuda"), torch.zeros(1, device="cuda")
+        res[f"categorical_target_{half}x{bins}"] = timed(lambda: _ok(lib, lib.rl_flash_categorical_target(
+            q.data_ptr(), lp_in.data_ptr(), rew.data_ptr(), term.data_ptr(), disc.data_ptr(), nlp.data_ptr(),
+            alpha.data_ptr(), tgt.data_ptr(), ment.data_ptr(), half, bins, -10.0, 10.0, _s())))
+        gr = [torch.randn_like(t) * 1e-3 for t in params]
+        m1, m2 = [torch.zeros_like(t) for t in params], [torch.zeros_like(t) for t in params]
+        ts, lr = torch.zeros(1, device="cuda"), torch.tensor([1e-4], device="cuda")
+        tab = lambda ts_: pointers([t.data_ptr() for t in ts_])  # noqa: E731
+        adam = lib.rl_adam_create(len(params), tab(params), tab(gr), tab(m1), tab(m2), sizes(n_params),
+                                  ts.data_ptr(), lr.data_ptr(), 0.9, 0.999, 1e-8)
+        assert adam
+        res[f"adam_{sum(n_params)}_params"] = timed(lambda: _ok(lib, lib.rl_adam_step(adam, _s())))
+        lib.rl_adam_destroy(adam)
+        targets = [t.clone() for t in params]
+        ema = lib.rl_flash_ema_create(len(params), tab(params), tab(targets), sizes(n_params), 0.005)
+        assert ema
+        res[f"ema_{sum(n_params)}_params"] = timed(lambda: _ok(lib, lib.rl_flash_ema_step(ema, _s())))
+        lib.rl_flash_ema_destroy(ema)
+        table[name] = res
+
+    out = {k: {"rl2_us": round(table["rl2"][k], 2), "reference_us": round(table["ref"][k], 2),
+               "reference_over_rl2": round(table["ref"][k] / table["rl2"][k], 2)} for k in table["rl2"]}
+    path = os.environ.get("RL2_REFOPS_OUT")
+    if path:
+        Path(path).write_text(json.dumps({"device": torch.cuda.get_device_name(0), "ops": out}, indent=1) + "\n")
