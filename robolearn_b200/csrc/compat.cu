@@ -13,6 +13,7 @@
 #include "../../include/rl2.h"
 #include "../../include/rl_compat.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -257,21 +258,34 @@ int grid_for(size_t work, int per_block) {
 }
 
 // db[c] += sum over rows of dy[row][c]: 32 channels per block (coalesced row segments),
-// 8 row lanes per channel, a fixed-order combine of the 8 lane sums.
-__global__ void __launch_bounds__(kT) column_sum_kernel(const float* __restrict__ dy, float* db, int batch,
-                                                        int channels) {
-    __shared__ float part[kT / 32][33];
+// 32 row lanes per channel (one warp each, four independent partial sums for memory-level
+// parallelism), then a fixed-order combine of the 32 lane sums.
+constexpr int kColT = 1024;
+
+__global__ void __launch_bounds__(kColT) column_sum_kernel(const float* __restrict__ dy, float* db, int batch,
+                                                           int channels) {
+    __shared__ float part[kColT / 32][33];
     const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
-    float s = 0.0f;
-    if (c < channels)
-        for (int r = grp; r < batch; r += kT / 32) s += dy[static_cast<long long>(r) * channels + c];
-    part[grp][lane] = s;
+    constexpr int G = kColT / 32;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    if (c < channels) {
+        const float* col = dy + c;
+        int r = grp;
+        for (; r + 3 * G < batch; r += 4 * G) {
+            s0 += col[static_cast<long long>(r) * channels];
+            s1 += col[static_cast<long long>(r + G) * channels];
+            s2 += col[static_cast<long long>(r + 2 * G) * channels];
+            s3 += col[static_cast<long long>(r + 3 * G) * channels];
+        }
+        for (; r < batch; r += G) s0 += col[static_cast<long long>(r) * channels];
+    }
+    part[grp][lane] = (s0 + s1) + (s2 + s3);
     __syncthreads();
     if (grp == 0 && c < channels) {
         float t = part[0][lane];
 #pragma unroll
-        for (int g = 1; g < kT / 32; ++g) t += part[g][lane];
+        for (int g = 1; g < G; ++g) t += part[g][lane];
         db[c] += t;
     }
 }
@@ -414,7 +428,7 @@ extern "C" int rl_bias_grad(const void* dy, void* db, int batch, int channels, v
         set_error("Bias gradient requires FP32 buffers and positive batch/channels.");
         return -1;
     }
-    compat::column_sum_kernel<<<(channels + 31) / 32, compat::kT, 0, as_stream(stream)>>>(
+    compat::column_sum_kernel<<<(channels + 31) / 32, compat::kColT, 0, as_stream(stream)>>>(
         static_cast<const float*>(dy), static_cast<float*>(db), batch, channels);
     return launch_status("Run bias gradient");
 }
@@ -1054,21 +1068,81 @@ __global__ void __launch_bounds__(kT) bn_merge_kernel(const float* __restrict__ 
     }
 }
 
+// Channel-parallel row loops for the element-wise passes: a thread owns V consecutive
+// channels (V = 4 when rows start 16-byte aligned), keeps their constants in registers and
+// walks a slab of rows, so no per-element index division or constant reload is needed.
+template <int V>
+__device__ __forceinline__ void ld_v(const float* p, float (&o)[V]) {
+    if constexpr (V == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(p);
+        o[0] = t.x, o[1] = t.y, o[2] = t.z, o[3] = t.w;
+    } else {
+        o[0] = *p;
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void st_v(float* p, const float (&o)[V]) {
+    if constexpr (V == 4)
+        *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+    else
+        *p = o[0];
+}
+
+template <int V>
+__device__ __forceinline__ void st_h(__half* p, const float (&o)[V]) {
+    if constexpr (V == 4) {
+        reinterpret_cast<__half2*>(p)[0] = __floats2half2_rn(o[0], o[1]);
+        reinterpret_cast<__half2*>(p)[1] = __floats2half2_rn(o[2], o[3]);
+    } else {
+        *p = __float2half_rn(o[0]);
+    }
+}
+
+struct Slab {
+    dim3 grid;
+    int rows;  // rows per block
+};
+
+Slab slab(int batch, int channels, int v) {
+    const int gx = (channels + kT * v - 1) / (kT * v);
+    int gy = std::max(1, std::min(batch, 592 / gx));
+    const int rows = (batch + gy - 1) / gy;
+    gy = (batch + rows - 1) / rows;
+    return {dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), rows};
+}
+
 // y = (x - mean) / sqrt(var + eps) * w + b (w, b optional), ReLU optional, optional fp16 copy.
+template <int V>
 __global__ void __launch_bounds__(kT) bn_apply_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                       const float* __restrict__ b, const float* __restrict__ mean,
                                                       const float* __restrict__ var, float* __restrict__ y,
-                                                      __half* __restrict__ y16, long long total, int channels,
-                                                      float eps, bool relu) {
-    for (long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * kT) {
-        const int c = static_cast<int>(i % channels);
-        float v = (x[i] - __ldg(mean + c)) / sqrtf(__ldg(var + c) + eps);
-        if (w) v *= __ldg(w + c);
-        if (b) v += __ldg(b + c);
-        if (relu && v <= 0.0f) v = 0.0f;
-        y[i] = v;
-        if (y16) y16[i] = __float2half_rn(v);
+                                                      __half* __restrict__ y16, int batch, int channels, float eps,
+                                                      bool relu, int rows) {
+    const int c0 = (blockIdx.x * kT + threadIdx.x) * V;
+    if (c0 >= channels) return;
+    float mu[V], sd[V], wv[V], bv[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        mu[v] = mean[c0 + v];
+        sd[v] = sqrtf(var[c0 + v] + eps);
+        wv[v] = w ? w[c0 + v] : 1.0f;
+        bv[v] = b ? b[c0 + v] : 0.0f;
+    }
+    const int r1 = min(batch, static_cast<int>(blockIdx.y + 1) * rows);
+    for (int r = blockIdx.y * rows; r < r1; ++r) {
+        const long long o = static_cast<long long>(r) * channels + c0;
+        float t[V];
+        ld_v<V>(x + o, t);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            float q = (t[v] - mu[v]) / sd[v];
+            if (w) q *= wv[v];
+            if (b) q += bv[v];
+            t[v] = relu && q <= 0.0f ? 0.0f : q;
+        }
+        st_v<V>(y + o, t);
+        if (y16) st_h<V>(y16 + o, t);
     }
 }
 
@@ -1123,23 +1197,40 @@ __global__ void __launch_bounds__(kT) bn_grad_merge_kernel(const float* __restri
 }
 
 // dx (+)= w / sqrt(var + eps) * (g - [training] (mean(g) + xhat * mean(g xhat)))
-template <bool kOverwrite>
+template <int V, bool kOverwrite>
 __global__ void __launch_bounds__(kT) bn_dx_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                                                    const float* __restrict__ y, const float* __restrict__ w,
                                                    const float* __restrict__ mean, const float* __restrict__ var,
-                                                   const float* __restrict__ sums, float* dx, __half* dx16,
-                                                   long long total, int channels, float eps, bool training,
-                                                   bool relu) {
-    for (long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * kT) {
-        const int c = static_cast<int>(i % channels);
-        const float inv = 1.0f / sqrtf(__ldg(var + c) + eps);
-        float g = relu && y[i] <= 0.0f ? 0.0f : dy[i];
-        if (training) g = g - __ldg(sums + c) - (x[i] - __ldg(mean + c)) * inv * __ldg(sums + channels + c);
-        const float contrib = (w ? __ldg(w + c) : 1.0f) * inv * g;
-        const float v = kOverwrite ? contrib : dx[i] + contrib;
-        dx[i] = v;
-        if (dx16) dx16[i] = __float2half_rn(v);
+                                                   const float* __restrict__ sums, float* dx, __half* dx16, int batch,
+                                                   int channels, float eps, bool training, bool relu, int rows) {
+    const int c0 = (blockIdx.x * kT + threadIdx.x) * V;
+    if (c0 >= channels) return;
+    float mu[V], inv[V], wi[V], mg[V], mgx[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        inv[v] = 1.0f / sqrtf(var[c0 + v] + eps);
+        wi[v] = (w ? w[c0 + v] : 1.0f) * inv[v];
+        mu[v] = training ? mean[c0 + v] : 0.0f;
+        mg[v] = training ? sums[c0 + v] : 0.0f;
+        mgx[v] = training ? sums[channels + c0 + v] : 0.0f;
+    }
+    const int r1 = min(batch, static_cast<int>(blockIdx.y + 1) * rows);
+    for (int r = blockIdx.y * rows; r < r1; ++r) {
+        const long long o = static_cast<long long>(r) * channels + c0;
+        float g[V], old[V], xv[V], yv[V];
+        ld_v<V>(dy + o, g);
+        if (relu) ld_v<V>(y + o, yv);
+        if (training) ld_v<V>(x + o, xv);
+        if (!kOverwrite) ld_v<V>(dx + o, old);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            float q = relu && yv[v] <= 0.0f ? 0.0f : g[v];
+            if (training) q = q - mg[v] - (xv[v] - mu[v]) * inv[v] * mgx[v];
+            const float c = wi[v] * q;
+            g[v] = kOverwrite ? c : old[v] + c;
+        }
+        st_v<V>(dx + o, g);
+        if (dx16) st_h<V>(dx16 + o, g);
     }
 }
 
@@ -1264,56 +1355,54 @@ __device__ __forceinline__ void atomic_max_float(float* addr, float v) {
     }
 }
 
-// One warp per row, the row's target in shared memory. Every lane computes the two-hot split
-// of its atoms; the contributions are then added by lane 0 in atom order (lower before
-// upper), so the result does not depend on scheduling.
+// One thread per row. The block's rows sit in shared memory exactly as in the output
+// ([rows][bins], contiguous), so zeroing and the copy-out are block-wide coalesced passes,
+// while each thread adds its row's two-hot contributions in atom order (lower before upper):
+// the result does not depend on scheduling. The running maximum of alpha * next_log_probs
+// is reduced over the warp before one atomic per warp.
 __global__ void cat_target_kernel(const float* __restrict__ q, const float* __restrict__ log_probs,
                                   const float* __restrict__ reward, const float* __restrict__ terminated,
                                   const float* __restrict__ discount, const float* __restrict__ next_log_probs,
                                   const float* __restrict__ alpha, float* target, float* maximum_entropy, int batch,
                                   int bins, float min_v, float max_v) {
-    extern __shared__ float rows[];
-    const int wpb = blockDim.x >> 5;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * wpb + warp;
-    if (row >= batch) return;
-    float* t = rows + static_cast<long long>(warp) * bins;
-    for (int j = lane; j < bins; j += 32) t[j] = 0.0f;
-    __syncwarp();
-    const float ent = alpha[0] * next_log_probs[row];
-    const int twin = q[3LL * batch + row] < q[static_cast<long long>(batch) + row] ? 1 : 0;
-    const float* lp = log_probs + (static_cast<long long>(twin) * 2 * batch + batch + row) * bins;
-    const float width = (max_v - min_v) / static_cast<float>(bins - 1);
-    const float r = reward[row], disc = discount[row], live = 1.0f - terminated[row];
-    for (int j0 = 0; j0 < bins; j0 += 32) {
-        const int j = j0 + lane;
-        int lo = 0, up = 0;
-        float wl = 0.0f, wu = 0.0f;
-        if (j < bins) {
+    extern __shared__ float rows_s[];
+    const int row0 = blockIdx.x * blockDim.x;
+    const int nrows = min(static_cast<int>(blockDim.x), batch - row0);
+    const int count = nrows * bins;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) rows_s[i] = 0.0f;
+    __syncthreads();
+    const int row = row0 + static_cast<int>(threadIdx.x);
+    float ent = -INFINITY;
+    if (static_cast<int>(threadIdx.x) < nrows) {
+        float* t = rows_s + threadIdx.x * bins;
+        ent = alpha[0] * next_log_probs[row];
+        const int twin = q[3LL * batch + row] < q[static_cast<long long>(batch) + row] ? 1 : 0;
+        const float* lp = log_probs + (static_cast<long long>(twin) * 2 * batch + batch + row) * bins;
+        const float width = (max_v - min_v) / static_cast<float>(bins - 1);
+        const float r = reward[row], disc = discount[row], live = 1.0f - terminated[row];
+        for (int j = 0; j < bins; ++j) {
             const float z = min_v + static_cast<float>(j) * width;
             const float v = r + disc * (z - ent) * live;
             const float loc = (fminf(fmaxf(v, min_v), max_v) - min_v) / width;
-            lo = min(max(static_cast<int>(floorf(loc)), 0), bins - 1);
-            up = min(lo + 1, bins - 1);
+            const int lo = min(max(static_cast<int>(floorf(loc)), 0), bins - 1);
+            const int up = min(lo + 1, bins - 1);
             const float frac = loc - static_cast<float>(lo);
             const float p = expf(lp[j]);
-            wl = p * (1.0f - frac);
-            wu = p * frac;
-        }
-        const int n = min(32, bins - j0);
-        for (int s = 0; s < n; ++s) {
-            const int l_s = __shfl_sync(0xffffffffu, lo, s), u_s = __shfl_sync(0xffffffffu, up, s);
-            const float a_s = __shfl_sync(0xffffffffu, wl, s), b_s = __shfl_sync(0xffffffffu, wu, s);
-            if (lane == 0) {
-                t[l_s] += a_s;
-                t[u_s] += b_s;
-            }
+            t[lo] += p * (1.0f - frac);
+            t[up] += p * frac;
         }
     }
-    __syncwarp();
-    float* out = target + static_cast<long long>(row) * bins;
-    for (int j = lane; j < bins; j += 32) out[j] = t[j];
-    if (lane == 0) atomic_max_float(maximum_entropy, ent);
+    if (blockDim.x % 32 == 0) {
+        float m = ent;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0 && m > -INFINITY) atomic_max_float(maximum_entropy, m);
+    } else if (ent > -INFINITY) {
+        atomic_max_float(maximum_entropy, ent);
+    }
+    __syncthreads();
+    float* out = target + static_cast<long long>(row0) * bins;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) out[i] = rows_s[i];
 }
 
 bool norm_dims(int batch, int channels, float eps) {
@@ -1345,10 +1434,14 @@ int bn_forward(const float* x, const float* w, const float* b, float* running_me
         bn_merge_kernel<<<(channels + kT - 1) / kT, kT, 0, s>>>(partial, mean, var, running_mean, running_var, batch,
                                                                channels, chunks, momentum);
     }
-    const long long total = static_cast<long long>(batch) * channels;
-    bn_apply_kernel<<<grid_for(total, kT * 4), kT, 0, s>>>(x, w, b, training ? mean : running_mean,
-                                                            training ? var : running_var, y, y16, total, channels, eps,
-                                                            relu != 0);
+    const bool v4 = channels % 4 == 0 && aligned(x, 16) && aligned(y, 16) && (!y16 || aligned(y16, 8));
+    const Slab sl = slab(batch, channels, v4 ? 4 : 1);
+    const float* mu = training ? mean : running_mean;
+    const float* va = training ? var : running_var;
+    if (v4)
+        bn_apply_kernel<4><<<sl.grid, kT, 0, s>>>(x, w, b, mu, va, y, y16, batch, channels, eps, relu != 0, sl.rows);
+    else
+        bn_apply_kernel<1><<<sl.grid, kT, 0, s>>>(x, w, b, mu, va, y, y16, batch, channels, eps, relu != 0, sl.rows);
     return launch_status("Run FlashSAC BatchNorm forward");
 }
 
@@ -1373,14 +1466,22 @@ int bn_backward(const float* x, const float* dy, const float* y, const float* w,
         bn_grad_merge_kernel<<<(channels + kT - 1) / kT, kT, 0, s>>>(partial, sums, dw, db, batch, channels, chunks);
     }
     if (dx) {
-        const long long total = static_cast<long long>(batch) * channels;
-        const int grid = grid_for(total, kT * 4);
-        if (overwrite)
-            bn_dx_kernel<true><<<grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, total, channels, eps,
-                                                   training != 0, relu != 0);
+        const bool v4 = channels % 4 == 0 && aligned(x, 16) && aligned(dy, 16) && aligned(y, 16) && aligned(dx, 16) &&
+                        (!dx16 || aligned(dx16, 8));
+        const Slab sl = slab(batch, channels, v4 ? 4 : 1);
+        const bool tr = training != 0, rl = relu != 0;
+        if (v4 && overwrite)
+            bn_dx_kernel<4, true><<<sl.grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, batch, channels, eps,
+                                                         tr, rl, sl.rows);
+        else if (v4)
+            bn_dx_kernel<4, false><<<sl.grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, batch, channels, eps,
+                                                          tr, rl, sl.rows);
+        else if (overwrite)
+            bn_dx_kernel<1, true><<<sl.grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, batch, channels, eps,
+                                                         tr, rl, sl.rows);
         else
-            bn_dx_kernel<false><<<grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, total, channels, eps,
-                                                    training != 0, relu != 0);
+            bn_dx_kernel<1, false><<<sl.grid, kT, 0, s>>>(x, dy, y, w, mean, var, sums, dx, dx16, batch, channels,
+                                                          eps, tr, rl, sl.rows);
     }
     return launch_status("Run FlashSAC BatchNorm backward");
 }
@@ -1506,7 +1607,7 @@ extern "C" int rl_flash_categorical_backward(const void* log_probs, const void* 
         dbias ? static_cast<float*>(scratch) : nullptr, static_cast<float*>(draw), batch, bins);
     if (launch_status("Categorical backward")) return -1;
     if (dbias)
-        compat::column_sum_kernel<<<(bins + 31) / 32, compat::kT, 0, s>>>(static_cast<const float*>(scratch),
+        compat::column_sum_kernel<<<(bins + 31) / 32, compat::kColT, 0, s>>>(static_cast<const float*>(scratch),
                                                                           static_cast<float*>(dbias), batch, bins);
     return launch_status("Categorical bias backward");
 }
@@ -1522,9 +1623,9 @@ extern "C" int rl_flash_categorical_target(const void* q, const void* log_probs,
         set_error("Categorical target requires FP32 buffers, valid support and 2..4096 bins.");
         return -1;
     }
-    // warps per block: as many rows as fit 48 KB of shared memory, at most 8
-    const int wpb = std::max(1, std::min(8, static_cast<int>((48 * 1024) / (static_cast<size_t>(bins) * 4))));
-    compat::cat_target_kernel<<<(batch + wpb - 1) / wpb, 32 * wpb, static_cast<size_t>(wpb) * bins * 4,
+    // rows per block: one warp, or as many rows as fit 48 KB of shared memory
+    const int rpb = std::max(1, std::min(32, static_cast<int>((48 * 1024) / (static_cast<size_t>(bins) * 4))));
+    compat::cat_target_kernel<<<(batch + rpb - 1) / rpb, rpb, static_cast<size_t>(rpb) * bins * 4,
                                 as_stream(stream)>>>(
         static_cast<const float*>(q), static_cast<const float*>(log_probs), static_cast<const float*>(reward),
         static_cast<const float*>(terminated), static_cast<const float*>(discount),
