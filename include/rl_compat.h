@@ -109,7 +109,8 @@ int rl_flash_rms_forward(const float* x, const float* w, float* var, float* y, i
 int rl_flash_rms_backward(const float* x, const float* dy, const float* w, const float* var, float* partial,
                           float* dx, float* dw, int batch, int channels, float eps, void* stream);
 
-/* Categorical heads (categorical_kernels.cuh:126-178). */
+/* Categorical heads (categorical_kernels.cuh:126-178). backward: scratch ([batch][bins], needed
+ * with dbias) holds intermediate sums on return, not the per-row gradients. */
 int rl_flash_categorical_forward(const void* raw, const void* bias, const void* support, void* log_probs,
                                  void* values, int batch, int bins, void* stream);
 int rl_flash_categorical_backward(const void* log_probs, const void* support, const void* dlog_probs,

@@ -263,7 +263,7 @@ int grid_for(size_t work, int per_block) {
 constexpr int kColT = 1024;
 
 __global__ void __launch_bounds__(kColT) column_sum_kernel(const float* __restrict__ dy, float* db, int batch,
-                                                           int channels) {
+                                                           int channels, long long ld) {
     __shared__ float part[kColT / 32][33];
     const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -273,12 +273,12 @@ __global__ void __launch_bounds__(kColT) column_sum_kernel(const float* __restri
         const float* col = dy + c;
         int r = grp;
         for (; r + 3 * G < batch; r += 4 * G) {
-            s0 += col[static_cast<long long>(r) * channels];
-            s1 += col[static_cast<long long>(r + G) * channels];
-            s2 += col[static_cast<long long>(r + 2 * G) * channels];
-            s3 += col[static_cast<long long>(r + 3 * G) * channels];
+            s0 += col[static_cast<long long>(r) * ld];
+            s1 += col[static_cast<long long>(r + G) * ld];
+            s2 += col[static_cast<long long>(r + 2 * G) * ld];
+            s3 += col[static_cast<long long>(r + 3 * G) * ld];
         }
-        for (; r < batch; r += G) s0 += col[static_cast<long long>(r) * channels];
+        for (; r < batch; r += G) s0 += col[static_cast<long long>(r) * ld];
     }
     part[grp][lane] = (s0 + s1) + (s2 + s3);
     __syncthreads();
@@ -287,6 +287,28 @@ __global__ void __launch_bounds__(kColT) column_sum_kernel(const float* __restri
 #pragma unroll
         for (int g = 1; g < G; ++g) t += part[g][lane];
         db[c] += t;
+    }
+}
+
+// First pass of a column sum over many rows whose source may be overwritten: block
+// (channel tile, row slab) sums its slab's rows (8 row lanes per channel, fixed-order
+// combine) and stores the sum over the slab's FIRST row, which no other block reads. The
+// slab sums are then added by column_sum_kernel over rows strided by the slab height.
+__global__ void __launch_bounds__(kT) slab_sum_kernel(float* src, int batch, int channels, int rows) {
+    __shared__ float part[kT / 32][33];
+    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const int r0 = blockIdx.y * rows, r1 = min(batch, r0 + rows);
+    float s = 0.0f;
+    if (c < channels)
+        for (int r = r0 + grp; r < r1; r += kT / 32) s += src[static_cast<long long>(r) * channels + c];
+    part[grp][lane] = s;
+    __syncthreads();
+    if (grp == 0 && c < channels) {
+        float t = part[0][lane];
+#pragma unroll
+        for (int g = 1; g < kT / 32; ++g) t += part[g][lane];
+        src[static_cast<long long>(r0) * channels + c] = t;
     }
 }
 
@@ -429,7 +451,7 @@ extern "C" int rl_bias_grad(const void* dy, void* db, int batch, int channels, v
         return -1;
     }
     compat::column_sum_kernel<<<(channels + 31) / 32, compat::kColT, 0, as_stream(stream)>>>(
-        static_cast<const float*>(dy), static_cast<float*>(db), batch, channels);
+        static_cast<const float*>(dy), static_cast<float*>(db), batch, channels, channels);
     return launch_status("Run bias gradient");
 }
 
@@ -1355,54 +1377,72 @@ __device__ __forceinline__ void atomic_max_float(float* addr, float v) {
     }
 }
 
-// One thread per row. The block's rows sit in shared memory exactly as in the output
-// ([rows][bins], contiguous), so zeroing and the copy-out are block-wide coalesced passes,
-// while each thread adds its row's two-hot contributions in atom order (lower before upper):
-// the result does not depend on scheduling. The running maximum of alpha * next_log_probs
-// is reduced over the warp before one atomic per warp.
-__global__ void cat_target_kernel(const float* __restrict__ q, const float* __restrict__ log_probs,
-                                  const float* __restrict__ reward, const float* __restrict__ terminated,
-                                  const float* __restrict__ discount, const float* __restrict__ next_log_probs,
-                                  const float* __restrict__ alpha, float* target, float* maximum_entropy, int batch,
-                                  int bins, float min_v, float max_v) {
+// Adds v into t[key] for every run of equal keys across the warp's lanes: a segmented
+// inclusive scan (runs found from lane-order key changes, so any key sequence is handled)
+// leaves each run's sum in its last lane, which commits it. The keys of one row are monotone
+// in the atom index (the two-hot location is a monotone function of the support value), so
+// every key has at most one run per call and the sums do not depend on scheduling.
+__device__ __forceinline__ void run_commit(float* t, int key, float v, int lane) {
+    const int kprev = __shfl_up_sync(0xffffffffu, key, 1);
+    const bool head = lane == 0 || kprev != key;
+    const unsigned heads = __ballot_sync(0xffffffffu, head);
+    const int run = __popc(heads & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float vo = __shfl_up_sync(0xffffffffu, v, o);
+        const int ro = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o && ro == run) v += vo;
+    }
+    const int rnext = __shfl_down_sync(0xffffffffu, run, 1);
+    if ((lane == 31 || rnext != run) && key >= 0) atomicAdd(t + key, v);
+}
+
+// One warp per row, the row's target in shared memory: lanes compute the two-hot split of
+// 32 atoms at a time, then the lower and the upper contributions are committed by runs.
+__global__ void __launch_bounds__(kT) cat_target_kernel(const float* __restrict__ q, const float* __restrict__ log_probs,
+                                                        const float* __restrict__ reward,
+                                                        const float* __restrict__ terminated,
+                                                        const float* __restrict__ discount,
+                                                        const float* __restrict__ next_log_probs,
+                                                        const float* __restrict__ alpha, float* target,
+                                                        float* maximum_entropy, int batch, int bins, float min_v,
+                                                        float max_v) {
     extern __shared__ float rows_s[];
-    const int row0 = blockIdx.x * blockDim.x;
-    const int nrows = min(static_cast<int>(blockDim.x), batch - row0);
-    const int count = nrows * bins;
-    for (int i = threadIdx.x; i < count; i += blockDim.x) rows_s[i] = 0.0f;
-    __syncthreads();
-    const int row = row0 + static_cast<int>(threadIdx.x);
-    float ent = -INFINITY;
-    if (static_cast<int>(threadIdx.x) < nrows) {
-        float* t = rows_s + threadIdx.x * bins;
-        ent = alpha[0] * next_log_probs[row];
-        const int twin = q[3LL * batch + row] < q[static_cast<long long>(batch) + row] ? 1 : 0;
-        const float* lp = log_probs + (static_cast<long long>(twin) * 2 * batch + batch + row) * bins;
-        const float width = (max_v - min_v) / static_cast<float>(bins - 1);
-        const float r = reward[row], disc = discount[row], live = 1.0f - terminated[row];
-        for (int j = 0; j < bins; ++j) {
+    const int wpb = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * wpb + warp;
+    if (row >= batch) return;  // warp-uniform
+    float* t = rows_s + static_cast<long long>(warp) * bins;
+    for (int j = lane; j < bins; j += 32) t[j] = 0.0f;
+    __syncwarp();
+    const float ent = alpha[0] * next_log_probs[row];
+    const int twin = q[3LL * batch + row] < q[static_cast<long long>(batch) + row] ? 1 : 0;
+    const float* lp = log_probs + (static_cast<long long>(twin) * 2 * batch + batch + row) * bins;
+    const float width = (max_v - min_v) / static_cast<float>(bins - 1);
+    const float r = reward[row], disc = discount[row], live = 1.0f - terminated[row];
+    for (int j0 = 0; j0 < bins; j0 += 32) {
+        const int j = j0 + lane;
+        int lo = -1, up = -1;
+        float wl = 0.0f, wu = 0.0f;
+        if (j < bins) {
             const float z = min_v + static_cast<float>(j) * width;
             const float v = r + disc * (z - ent) * live;
             const float loc = (fminf(fmaxf(v, min_v), max_v) - min_v) / width;
-            const int lo = min(max(static_cast<int>(floorf(loc)), 0), bins - 1);
-            const int up = min(lo + 1, bins - 1);
+            lo = min(max(static_cast<int>(floorf(loc)), 0), bins - 1);
+            up = min(lo + 1, bins - 1);
             const float frac = loc - static_cast<float>(lo);
             const float p = expf(lp[j]);
-            t[lo] += p * (1.0f - frac);
-            t[up] += p * frac;
+            wl = p * (1.0f - frac);
+            wu = p * frac;
         }
+        run_commit(t, lo, wl, lane);
+        __syncwarp();
+        run_commit(t, up, wu, lane);
+        __syncwarp();
     }
-    if (blockDim.x % 32 == 0) {
-        float m = ent;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if ((threadIdx.x & 31) == 0 && m > -INFINITY) atomic_max_float(maximum_entropy, m);
-    } else if (ent > -INFINITY) {
-        atomic_max_float(maximum_entropy, ent);
-    }
-    __syncthreads();
-    float* out = target + static_cast<long long>(row0) * bins;
-    for (int i = threadIdx.x; i < count; i += blockDim.x) out[i] = rows_s[i];
+    float* out = target + static_cast<long long>(row) * bins;
+    for (int j = lane; j < bins; j += 32) out[j] = t[j];
+    if (lane == 0) atomic_max_float(maximum_entropy, ent);
 }
 
 bool norm_dims(int batch, int channels, float eps) {
@@ -1606,9 +1646,16 @@ extern "C" int rl_flash_categorical_backward(const void* log_probs, const void* 
         static_cast<const float*>(dlog_probs), static_cast<const float*>(dvalues),
         dbias ? static_cast<float*>(scratch) : nullptr, static_cast<float*>(draw), batch, bins);
     if (launch_status("Categorical backward")) return -1;
-    if (dbias)
-        compat::column_sum_kernel<<<(bins + 31) / 32, compat::kColT, 0, s>>>(static_cast<const float*>(scratch),
-                                                                          static_cast<float*>(dbias), batch, bins);
+    if (dbias) {  // the per-row gradients in scratch are summed in two fixed-order passes
+        const int tiles = (bins + 31) / 32;
+        const int slabs = std::max(1, std::min((batch + 31) / 32, 600 / tiles));
+        const int rows = (batch + slabs - 1) / slabs;
+        const int used = (batch + rows - 1) / rows;
+        float* sc = static_cast<float*>(scratch);
+        compat::slab_sum_kernel<<<dim3(tiles, used), compat::kT, 0, s>>>(sc, batch, bins, rows);
+        compat::column_sum_kernel<<<tiles, compat::kColT, 0, s>>>(sc, static_cast<float*>(dbias), used, bins,
+                                                                 static_cast<long long>(rows) * bins);
+    }
     return launch_status("Categorical bias backward");
 }
 
@@ -1623,9 +1670,9 @@ extern "C" int rl_flash_categorical_target(const void* q, const void* log_probs,
         set_error("Categorical target requires FP32 buffers, valid support and 2..4096 bins.");
         return -1;
     }
-    // rows per block: one warp, or as many rows as fit 48 KB of shared memory
-    const int rpb = std::max(1, std::min(32, static_cast<int>((48 * 1024) / (static_cast<size_t>(bins) * 4))));
-    compat::cat_target_kernel<<<(batch + rpb - 1) / rpb, rpb, static_cast<size_t>(rpb) * bins * 4,
+    // warps per block: as many rows as fit 48 KB of shared memory, at most 8
+    const int wpb = std::max(1, std::min(8, static_cast<int>((48 * 1024) / (static_cast<size_t>(bins) * 4))));
+    compat::cat_target_kernel<<<(batch + wpb - 1) / wpb, 32 * wpb, static_cast<size_t>(wpb) * bins * 4,
                                 as_stream(stream)>>>(
         static_cast<const float*>(q), static_cast<const float*>(log_probs), static_cast<const float*>(reward),
         static_cast<const float*>(terminated), static_cast<const float*>(discount),
