@@ -470,6 +470,7 @@ struct AdamTensor {
     float* m1;
     float* m2;
     size_t n;
+    int vec;  // all four arrays 16-byte aligned: float4 accesses (chunks start at multiples of 4096)
 };
 
 // block b works on tensor i with first[i] <= b < first[i + 1] (first[count] = blocks)
@@ -537,14 +538,38 @@ __global__ void __launch_bounds__(kT) adam_kernel(const AdamTensor* __restrict__
     const size_t off = static_cast<size_t>(blockIdx.x - first[i]) * kAdamChunk;
     const size_t len = t.n - off < kAdamChunk ? t.n - off : kAdamChunk;
     const float c1 = s.corr[0], c2 = s.corr[1], lr = s.lr[0];
-    for (size_t j = threadIdx.x; j < len; j += kT) {
+    auto one = [&](float g, float& m1, float& m2, float& p) {
+        m1 = beta1 * m1 + omb1 * g;
+        m2 = beta2 * m2 + omb2 * (g * g);
+        p -= lr * ((m1 * c1) / (sqrtf(m2 * c2) + eps));
+    };
+    size_t j0 = 0;
+    if (t.vec) {
+        const size_t quads = len / 4;
+        float4* p4 = reinterpret_cast<float4*>(t.p + off);
+        const float4* g4 = reinterpret_cast<const float4*>(t.g + off);
+        float4* a4 = reinterpret_cast<float4*>(t.m1 + off);
+        float4* b4 = reinterpret_cast<float4*>(t.m2 + off);
+        for (size_t q = threadIdx.x; q < quads; q += kT) {
+            const float4 g = g4[q];
+            float4 a = a4[q], b = b4[q], pv = p4[q];
+            one(g.x, a.x, b.x, pv.x);
+            one(g.y, a.y, b.y, pv.y);
+            one(g.z, a.z, b.z, pv.z);
+            one(g.w, a.w, b.w, pv.w);
+            a4[q] = a;
+            b4[q] = b;
+            p4[q] = pv;
+        }
+        j0 = quads * 4;
+    }
+    for (size_t j = j0 + threadIdx.x; j < len; j += kT) {
         const size_t o = off + j;
-        const float g = t.g[o];
-        const float m = beta1 * t.m1[o] + omb1 * g;
-        const float v = beta2 * t.m2[o] + omb2 * (g * g);
-        t.m1[o] = m;
-        t.m2[o] = v;
-        t.p[o] -= lr * ((m * c1) / (sqrtf(v * c2) + eps));
+        float a = t.m1[o], b = t.m2[o], pv = t.p[o];
+        one(t.g[o], a, b, pv);
+        t.m1[o] = a;
+        t.m2[o] = b;
+        t.p[o] = pv;
     }
 }
 
@@ -651,7 +676,29 @@ struct EmaSpan {
 __global__ void __launch_bounds__(kT) ema_kernel(const EmaSpan* __restrict__ spans, float tau) {
     const EmaSpan e = spans[blockIdx.x];
     const float keep = 1.0f - tau;
-    for (unsigned i = threadIdx.x; i < e.len; i += kT) {
+    unsigned i0 = 0;
+    const bool vec = ptx::aligned16(e.src) && ptx::aligned16(e.dst) && (!e.shadow || (reinterpret_cast<uintptr_t>(e.shadow) & 7u) == 0);
+    if (vec) {
+        const unsigned quads = e.len / 4;
+        const float4* s4 = reinterpret_cast<const float4*>(e.src);
+        float4* d4 = reinterpret_cast<float4*>(e.dst);
+        for (unsigned q = threadIdx.x; q < quads; q += kT) {
+            const float4 a = s4[q];
+            float4 d = d4[q];
+            d.x = keep * d.x + tau * a.x;
+            d.y = keep * d.y + tau * a.y;
+            d.z = keep * d.z + tau * a.z;
+            d.w = keep * d.w + tau * a.w;
+            d4[q] = d;
+            if (e.shadow) {
+                __half2* h = reinterpret_cast<__half2*>(e.shadow + 4 * q);
+                h[0] = __floats2half2_rn(d.x, d.y);
+                h[1] = __floats2half2_rn(d.z, d.w);
+            }
+        }
+        i0 = quads * 4;
+    }
+    for (unsigned i = i0 + threadIdx.x; i < e.len; i += kT) {
         const float v = keep * e.dst[i] + tau * e.src[i];
         e.dst[i] = v;
         if (e.shadow) e.shadow[i] = __float2half_rn(v);
@@ -804,7 +851,9 @@ extern "C" void* rl_adam_create(size_t count, const void* const* parameters, con
         tensors.push_back({static_cast<float*>(const_cast<void*>(parameters[i])),
                            static_cast<float*>(const_cast<void*>(gradients[i])),
                            static_cast<float*>(const_cast<void*>(m1[i])), static_cast<float*>(const_cast<void*>(m2[i])),
-                           sizes[i]});
+                           sizes[i],
+                           aligned(parameters[i], 16) && aligned(gradients[i], 16) && aligned(m1[i], 16) &&
+                               aligned(m2[i], 16)});
     }
     first.push_back(static_cast<unsigned>(blocks));
     AdamPlan* p = new (std::nothrow) AdamPlan();
