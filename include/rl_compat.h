@@ -19,8 +19,9 @@
  *    or without allow_tf32; rl_plan_workspace returns 0 (operand staging is plan-owned);
  *    rl_plan_autotune validates its preconditions and freezes the single plan-chosen
  *    candidate, which rl_plan_tuning_metadata describes.
- *  - per-row categorical projections add their contributions in atom order (deterministic),
- *    where the reference adds them with shared-memory atomics.
+ *  - per-row categorical projections sum their contributions by runs of equal atom index in
+ *    a fixed order (deterministic), where the reference adds them with shared-memory atomics;
+ *    the categorical backward leaves intermediate sums in its scratch buffer.
  */
 #ifndef RL_COMPAT_H
 #define RL_COMPAT_H
