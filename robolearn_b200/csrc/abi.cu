@@ -1,7 +1,5 @@
 // Library-wide ABI: error buffer and version.
 #include "common.cuh"
-
-#include <cstdlib>
 #include "../../include/rl2.h"
 
 namespace rl2 {
@@ -19,14 +17,6 @@ void set_error(const char* format, ...) noexcept {
 void clear_error() noexcept { g_last_error[0] = '\0'; }
 
 const char* last_error() noexcept { return g_last_error; }
-
-bool pdl_enabled() noexcept {
-    static const bool on = [] {
-        const char* e = std::getenv("RL2_PDL");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
 }  // namespace rl2
 
 extern "C" const char* rl2_last_error(void) { return rl2::last_error(); }

@@ -140,7 +140,6 @@ __device__ __forceinline__ void scatter_runs(const int (&key)[E], const float (&
 
 template <int E>
 __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a) {
-    grid_dependency_begin();
     constexpr int P = pitch<E>();
     __shared__ float z_s[8 * E];
     __shared__ float p_s[kWarps][kRowsPerWarp][P];  // selected target distribution (strided write, blocked read)
@@ -480,13 +479,13 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
     cudaStream_t s = as_stream(stream);
     const int e = (g->bins + 7) / 8;
     if (e <= 4)
-        launch(cat::critic_objective_kernel<4>, grid, cat::kThreads, 0, s, a);
+        cat::critic_objective_kernel<4><<<grid, cat::kThreads, 0, s>>>(a);
     else if (e <= 8)
-        launch(cat::critic_objective_kernel<8>, grid, cat::kThreads, 0, s, a);
+        cat::critic_objective_kernel<8><<<grid, cat::kThreads, 0, s>>>(a);
     else if (e <= 13)
-        launch(cat::critic_objective_kernel<13>, grid, cat::kThreads, 0, s, a);
+        cat::critic_objective_kernel<13><<<grid, cat::kThreads, 0, s>>>(a);
     else
-        launch(cat::critic_objective_kernel<16>, grid, cat::kThreads, 0, s, a);
+        cat::critic_objective_kernel<16><<<grid, cat::kThreads, 0, s>>>(a);
     return launch_status("critic objective");
 }
 

@@ -273,33 +273,5 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
-// Programmatic dependent launch. Every kernel started through launch() first waits for the
-// grids it depends on to complete and their memory to be visible (griddepcontrol.wait, a
-// no-op without the launch attribute), then lets its own dependents be scheduled: they
-// become resident as this grid's CTAs retire and wait in turn, which hides the launch gap.
-// The ordering guarantees are those of plain stream order.
-__device__ __forceinline__ void grid_dependency_begin() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// RL2_PDL=0 launches every kernel without the attribute (plain stream serialisation).
-bool pdl_enabled() noexcept;
-
-template <typename... P, typename... A>
-inline void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, A&&... args) {
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);  // errors reach launch_status()
-}
-
 }  // namespace rl2
 #endif

@@ -896,7 +896,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ CUtensorMap tma_a_lo, const __grid_constant__ CUtensorMap tma_b_lo,
                 const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_p, const Params p,
                 const int stages) {
-    grid_dependency_begin();
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
     const uint32_t stage_bytes = (kBM * 128 + static_cast<uint32_t>(p.BN) * 128) * kPlanes;
 
@@ -1412,8 +1411,8 @@ int run_rebound(void* opaque, float* d, const float* bias, const float* residual
     p.vec_res = residual && aligned(residual, 16) && p.ldr % 4 == 0 && p.r_bstride % 4 == 0;
     p.vec_bias = bias && aligned(bias, 16) && p.bias_bstride % 4 == 0;
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
-    launch(fn, plan->grid, kThreads, plan->smem, stream, plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, plan->td,
-           plan->tp, p, plan->stages);
+    fn<<<plan->grid, kThreads, plan->smem, stream>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, plan->td,
+                                                     plan->tp, p, plan->stages);
     return launch_status("tcgen05 GEMM (rebound)");
 }
 
@@ -1430,8 +1429,8 @@ extern "C" int rl2_gemm_run(void* opaque, void* stream) {
     }
     Plan* plan = static_cast<Plan*>(opaque);
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
-    launch(fn, plan->grid, kThreads, plan->smem, as_stream(stream), plan->ta, plan->tb, plan->ta_lo, plan->tb_lo,
-           plan->td, plan->tp, plan->p, plan->stages);
+    fn<<<plan->grid, kThreads, plan->smem, as_stream(stream)>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo,
+                                                               plan->td, plan->tp, plan->p, plan->stages);
     return launch_status("tcgen05 GEMM");
 }
 
@@ -1459,7 +1458,6 @@ namespace gemm {
 __global__ void split_reduce_kernel(const float* __restrict__ part, long long stride, int splits,
                                     float* __restrict__ out, long long count, int accumulate, int allow_vec,
                                     long long in_bstride, long long out_bstride) {
-    grid_dependency_begin();
     part += blockIdx.y * in_bstride;  // grid.y: independent reductions of the same shape
     out += blockIdx.y * out_bstride;
     const long long n4 = count / 4;
@@ -1511,8 +1509,8 @@ extern "C" int rl2_split_reduce_batched(const float* partial, long long split_st
     const int vec = count > (1LL << 22) ? 1 : 0;
     const long long work = vec ? count / 4 + 1 : count;
     const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 148LL * 16));
-    launch(gemm::split_reduce_kernel, dim3(blocks, batch), 256, 0, as_stream(stream), partial, split_stride, splits,
-           out, count, accumulate, vec, in_batch_stride, out_batch_stride);
+    gemm::split_reduce_kernel<<<dim3(blocks, batch), 256, 0, as_stream(stream)>>>(
+        partial, split_stride, splits, out, count, accumulate, vec, in_batch_stride, out_batch_stride);
     return launch_status("split-K reduce");
 }
 

@@ -30,7 +30,6 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 // grid (ceil(cols/kT), G, twins)
 __global__ void colstats_kernel(const float* __restrict__ x, long long ldx, long long xt, int rows, int cols,
                                 float* __restrict__ mean_p, float* __restrict__ m2_p, long long pt) {
-    grid_dependency_begin();
     const int c = blockIdx.x * kT + threadIdx.x;
     const int g = blockIdx.y;
     const int t = blockIdx.z;
@@ -63,7 +62,6 @@ __global__ void __launch_bounds__(NT) finalize_kernel(const float* __restrict__ 
                                                       long long pt, int gpr, long long rs, int twins, int rows,
                                                       int cols, float* mean, float* invstd, float* rm, float* rv,
                                                       float momentum, float eps, int update) {
-    grid_dependency_begin();
     constexpr int NW = NT / 32;
     __shared__ float sh[3][NW][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -118,7 +116,6 @@ __global__ void __launch_bounds__(NT) finalize_kernel(const float* __restrict__ 
 
 __global__ void eval_prepare_kernel(const float* rm, const float* rv, long long count, float eps, float* mean,
                                     float* invstd) {
-    grid_dependency_begin();
     const long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x;
     if (i >= count) return;
     mean[i] = rm[i];
@@ -126,7 +123,6 @@ __global__ void eval_prepare_kernel(const float* rm, const float* rv, long long 
 }
 
 __global__ void apply_kernel(const rl2_bn_apply_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     const long long per_twin = static_cast<long long>(a.rows) * a.cols;
     const long long total = per_twin * a.twins;
@@ -151,7 +147,6 @@ __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast
 
 // Vectorised apply: four columns per thread, 32-bit index math, grid.y = twin.
 __global__ void __launch_bounds__(kT) apply_vec4_kernel(const rl2_bn_apply_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     const int t = blockIdx.y;
     const int c4n = a.cols >> 2;
@@ -181,7 +176,6 @@ __global__ void __launch_bounds__(kT) apply_vec4_kernel(const rl2_bn_apply_args 
 
 // Vectorised backward apply (twins kept separate, or summed into one output when sum_twins).
 __global__ void __launch_bounds__(kT) bwd_apply_vec4_kernel(const rl2_bn_backward_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     const int to = blockIdx.y;
     const int c4n = a.cols >> 2;
@@ -232,7 +226,6 @@ __device__ __forceinline__ float masked_dbn(const rl2_bn_backward_args& a, int t
 
 // grid (ceil(cols/kT), G, twins)
 __global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
-    grid_dependency_begin();
     const int c = blockIdx.x * kT + threadIdx.x;
     const int g = blockIdx.y;
     const int t = blockIdx.z;
@@ -258,7 +251,6 @@ __global__ void __launch_bounds__(NT) bwd_finalize_kernel(const float* s1p, cons
                                                           long long rs, int twins, int rows, int cols, float* dgamma,
                                                           float* dbeta, long long gts, int accumulate, float* coef1,
                                                           float* coef2) {
-    grid_dependency_begin();
     constexpr int NW = NT / 32;
     __shared__ float sh[2][NW][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -309,7 +301,6 @@ __global__ void __launch_bounds__(NT) bwd_finalize_kernel(const float* s1p, cons
 }
 
 __global__ void bwd_apply_kernel(const rl2_bn_backward_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     const int twins_out = a.sum_twins ? 1 : a.twins;
     const long long per_twin = static_cast<long long>(a.rows) * a.cols;
@@ -344,7 +335,6 @@ __global__ void bwd_apply_kernel(const rl2_bn_backward_args a, const Plane plane
 __global__ void rms_forward_kernel(const float* __restrict__ h, long long ldh, long long ht, int twins, int rows,
                                    int cols, const float* __restrict__ gamma, float eps, float* __restrict__ r_out,
                                    float* __restrict__ u, long long ldu, long long ut, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (kT / 32);
@@ -371,7 +361,6 @@ __global__ void rms_backward_kernel(const float* __restrict__ du, long long lddu
                                     const float* __restrict__ h, long long ldh, long long ht,
                                     const float* __restrict__ rv, const float* __restrict__ gamma, int twins, int rows,
                                     int cols, float* __restrict__ dh, long long lddh, long long dht) {
-    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (kT / 32);
     for (long long w = blockIdx.x * static_cast<long long>(kT / 32) + (threadIdx.x >> 5); w < static_cast<long long>(twins) * rows;
@@ -395,7 +384,6 @@ __global__ void rms_backward_kernel(const float* __restrict__ du, long long lddu
 __global__ void rms_dgamma_kernel(const float* __restrict__ du, long long lddu, long long dut,
                                   const float* __restrict__ h, long long ldh, long long ht,
                                   const float* __restrict__ rv, int rows, int cols, float* __restrict__ part) {
-    grid_dependency_begin();
     const int c = blockIdx.x * kT + threadIdx.x;
     const int g = blockIdx.y;
     const int t = blockIdx.z;
@@ -419,7 +407,6 @@ constexpr int kColsumThreads = 1024;
 __global__ void __launch_bounds__(kColsumThreads) colsum_finalize_kernel(const float* part, int twins, int groups,
                                                                         int cols, float* out, long long ots,
                                                                         int accumulate) {
-    grid_dependency_begin();
     constexpr int kW = kColsumThreads / 32;
     __shared__ float sh[kW][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -490,7 +477,7 @@ extern "C" int rl2_colstats(const float* x, long long ldx, long long xt, int twi
         return -1;
     }
     const dim3 grid((cols + norm::kT - 1) / norm::kT, (rows + 31) / 32, twins);
-    launch(norm::colstats_kernel, grid, norm::kT, 0, as_stream(stream), x, ldx, xt, rows, cols, mean_p, m2_p, pt);
+    norm::colstats_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(x, ldx, xt, rows, cols, mean_p, m2_p, pt);
     return launch_status("column statistics");
 }
 
@@ -506,11 +493,13 @@ extern "C" int rl2_bn_finalize_ranked(const float* mean_p, const float* m2_p, lo
     }
     const dim3 grid((cols + 31) / 32, twins);
     if ((rows + 31) / 32 >= 128)
-        launch(norm::finalize_kernel<1024>, grid, 1024, 0, as_stream(stream), mean_p, m2_p, pt, groups_per_rank,
-               rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update);
+        norm::finalize_kernel<1024><<<grid, 1024, 0, as_stream(stream)>>>(
+            mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
+            update);
     else
-        launch(norm::finalize_kernel<norm::kT>, grid, norm::kT, 0, as_stream(stream), mean_p, m2_p, pt,
-               groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps, update);
+        norm::finalize_kernel<norm::kT><<<grid, norm::kT, 0, as_stream(stream)>>>(
+            mean_p, m2_p, pt, groups_per_rank, rank_stride, twins, rows, cols, mean, invstd, rm, rv, momentum, eps,
+            update);
     return launch_status("batch-norm statistics");
 }
 
@@ -528,8 +517,8 @@ extern "C" int rl2_bn_eval_prepare(const float* rm, const float* rv, long long c
         set_error("bn eval prepare: invalid buffers");
         return -1;
     }
-    launch(norm::eval_prepare_kernel, static_cast<int>((count + norm::kT - 1) / norm::kT), norm::kT, 0,
-           as_stream(stream), rm, rv, count, eps, mean, invstd);
+    norm::eval_prepare_kernel<<<static_cast<int>((count + norm::kT - 1) / norm::kT), norm::kT, 0,
+                                as_stream(stream)>>>(rm, rv, count, eps, mean, invstd);
     return launch_status("batch-norm eval statistics");
 }
 
@@ -544,11 +533,10 @@ extern "C" int rl2_bn_apply(const rl2_bn_apply_args* a, void* stream) {
     if (norm::apply_vec4(*a)) {
         const long long per_twin = static_cast<long long>(a->rows) * (a->cols / 4);
         const int blocks = std::max(1, norm::stream_blocks(per_twin) / a->twins);
-        launch(norm::apply_vec4_kernel, dim3(blocks, a->twins), norm::kT, 0, as_stream(stream), *a,
-               to_plane(&a->plane));
+        norm::apply_vec4_kernel<<<dim3(blocks, a->twins), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
         return launch_status("batch-norm apply");
     }
-    launch(norm::apply_kernel, norm::stream_blocks(work), norm::kT, 0, as_stream(stream), *a, to_plane(&a->plane));
+    norm::apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
     return launch_status("batch-norm apply");
 }
 
@@ -560,7 +548,7 @@ extern "C" int rl2_bn_backward_reduce(const rl2_bn_backward_args* a, void* strea
         return -1;
     }
     const dim3 grid((a->cols + norm::kT - 1) / norm::kT, (a->rows + 31) / 32, a->twins);
-    launch(norm::bwd_reduce_kernel, grid, norm::kT, 0, as_stream(stream), *a);
+    norm::bwd_reduce_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(*a);
     return launch_status("batch-norm backward reduce");
 }
 
@@ -575,11 +563,11 @@ extern "C" int rl2_bn_backward_finalize_ranked(const float* s1p, const float* s2
     }
     const dim3 grid((cols + 31) / 32, twins);
     if ((rows + 31) / 32 >= 128)
-        launch(norm::bwd_finalize_kernel<1024>, grid, 1024, 0, as_stream(stream), s1p, s2p, pt, groups_per_rank,
-               rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+        norm::bwd_finalize_kernel<1024><<<grid, 1024, 0, as_stream(stream)>>>(
+            s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
     else
-        launch(norm::bwd_finalize_kernel<norm::kT>, grid, norm::kT, 0, as_stream(stream), s1p, s2p, pt,
-               groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
+        norm::bwd_finalize_kernel<norm::kT><<<grid, norm::kT, 0, as_stream(stream)>>>(
+            s1p, s2p, pt, groups_per_rank, rank_stride, twins, rows, cols, dgamma, dbeta, gts, accumulate, coef1, coef2);
     return launch_status("batch-norm backward finalize");
 }
 
@@ -604,11 +592,10 @@ extern "C" int rl2_bn_backward_apply(const rl2_bn_backward_args* a, void* stream
         const int outs = a->sum_twins ? 1 : a->twins;
         const long long per_twin = static_cast<long long>(a->rows) * (a->cols / 4);
         const int blocks = std::max(1, norm::stream_blocks(per_twin) / outs);
-        launch(norm::bwd_apply_vec4_kernel, dim3(blocks, outs), norm::kT, 0, as_stream(stream), *a,
-               to_plane(&a->plane));
+        norm::bwd_apply_vec4_kernel<<<dim3(blocks, outs), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
         return launch_status("batch-norm backward apply");
     }
-    launch(norm::bwd_apply_kernel, norm::stream_blocks(work), norm::kT, 0, as_stream(stream), *a, to_plane(&a->plane));
+    norm::bwd_apply_kernel<<<norm::stream_blocks(work), norm::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->plane));
     return launch_status("batch-norm backward apply");
 }
 
@@ -622,8 +609,8 @@ extern "C" int rl2_rms_forward(const float* h, long long ldh, long long ht, int 
         return -1;
     }
     const long long warps = static_cast<long long>(twins) * rows;
-    launch(norm::rms_forward_kernel, norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream), h, ldh, ht,
-           twins, rows, cols, gamma, eps, r_out, u, ldu, ut, to_plane(plane));
+    norm::rms_forward_kernel<<<norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream)>>>(
+        h, ldh, ht, twins, rows, cols, gamma, eps, r_out, u, ldu, ut, to_plane(plane));
     return launch_status("rms forward");
 }
 
@@ -636,13 +623,13 @@ extern "C" int rl2_rms_backward(const float* du, long long lddu, long long dut, 
         return -1;
     }
     const long long warps = static_cast<long long>(twins) * rows;
-    launch(norm::rms_backward_kernel, norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream), du, lddu, dut,
-           h, ldh, ht, r, gamma, twins, rows, cols, dh, lddh, dht);
+    norm::rms_backward_kernel<<<norm::stream_blocks(warps * 32), norm::kT, 0, as_stream(stream)>>>(
+        du, lddu, dut, h, ldh, ht, r, gamma, twins, rows, cols, dh, lddh, dht);
     if (launch_status("rms backward")) return -1;
     if (dgamma_part) {
         const dim3 grid((cols + norm::kT - 1) / norm::kT, (rows + 31) / 32, twins);
-        launch(norm::rms_dgamma_kernel, grid, norm::kT, 0, as_stream(stream), du, lddu, dut, h, ldh, ht, r, rows, cols,
-               dgamma_part);
+        norm::rms_dgamma_kernel<<<grid, norm::kT, 0, as_stream(stream)>>>(du, lddu, dut, h, ldh, ht, r, rows, cols,
+                                                                        dgamma_part);
     }
     return launch_status("rms weight gradient");
 }
@@ -654,7 +641,7 @@ extern "C" int rl2_colsum_finalize(const float* part, int twins, int groups, int
         set_error("colsum finalize: invalid arguments");
         return -1;
     }
-    launch(norm::colsum_finalize_kernel, dim3((cols + 31) / 32, twins), norm::kColsumThreads, 0, as_stream(stream),
-           part, twins, groups, cols, out, ots, accumulate);
+    norm::colsum_finalize_kernel<<<dim3((cols + 31) / 32, twins), norm::kColsumThreads, 0, as_stream(stream)>>>(
+        part, twins, groups, cols, out, ots, accumulate);
     return launch_status("column-sum finalize");
 }

@@ -27,7 +27,6 @@ constexpr int kPer = 16;  // elements per thread kept in registers -> rows up to
 // state layout (floats): [0] attempts, [1] successful steps, [2] step_size, [3] bc2_sqrt,
 // [4] lr, [5] skip flag, [6] loss scale, [7] growth tracker, [8] attempts skipped
 __global__ void prepare_kernel(const rl2_adam_prepare_args a) {
-    grid_dependency_begin();
     float* st = a.state;
     const bool skip = a.found_inf && *a.found_inf != 0;
     const double attempts = static_cast<double>(st[0]);
@@ -109,7 +108,6 @@ __device__ __forceinline__ void plane_write(const Plane& p, long long off, float
 }
 
 __global__ void __launch_bounds__(kT) step_kernel(const rl2_adam_args a, const Plane wp, const Plane tp) {
-    grid_dependency_begin();
     __shared__ float sh[32];
     const rl2_segment seg = a.segments[blockIdx.x];
     const float* st = a.state;
@@ -204,7 +202,7 @@ extern "C" int rl2_adam_prepare(const rl2_adam_prepare_args* a, void* stream) {
         set_error("adam prepare: invalid arguments");
         return -1;
     }
-    launch(optim::prepare_kernel, 1, 1, 0, as_stream(stream), *a);
+    optim::prepare_kernel<<<1, 1, 0, as_stream(stream)>>>(*a);
     return launch_status("adam prepare");
 }
 
@@ -215,8 +213,8 @@ extern "C" int rl2_adam_step(const rl2_adam_args* a, void* stream) {
         set_error("adam step: invalid arguments");
         return -1;
     }
-    launch(optim::step_kernel, a->count, optim::kT, 0, as_stream(stream), *a, to_plane(&a->weight_plane),
-           to_plane(&a->target_plane));
+    optim::step_kernel<<<a->count, optim::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->weight_plane),
+                                                                       to_plane(&a->target_plane));
     return launch_status("fused adam / projection / EMA");
 }
 

@@ -42,7 +42,6 @@ __device__ __forceinline__ Sample sample(float mean, float s, float eps) {
 
 // one warp per row
 __global__ void sample_kernel(const rl2_policy_args a) {
-    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     for (long long row = blockIdx.x * static_cast<long long>(kWarps) + (threadIdx.x >> 5); row < a.rows;
          row += static_cast<long long>(gridDim.x) * kWarps) {
@@ -64,7 +63,6 @@ __global__ void sample_kernel(const rl2_policy_args a) {
 }
 
 __global__ void deterministic_kernel(const rl2_policy_args a) {
-    grid_dependency_begin();
     const long long total = static_cast<long long>(a.rows) * a.act;
     for (long long i = blockIdx.x * static_cast<long long>(kT) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * kT) {
@@ -76,7 +74,6 @@ __global__ void deterministic_kernel(const rl2_policy_args a) {
 
 // one warp per row; dgrad columns [0,A) = d mean, [A,2A) = d pre-tanh log-std
 __global__ void backward_kernel(const rl2_policy_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     __shared__ float part[kWarps][2 * 64];
     const int lane = threadIdx.x & 31;
@@ -141,7 +138,6 @@ constexpr int kWarps = 8;
 constexpr int kT = kWarps * 32;
 
 __global__ void __launch_bounds__(kT) kernel(const rl2_actor_objective_args a, const Plane plane) {
-    grid_dependency_begin();
     PlaneWriter pw(plane);
     __shared__ float z_s[128];
     __shared__ float red[kWarps][5];
@@ -271,7 +267,6 @@ __global__ void __launch_bounds__(kT) kernel(const rl2_actor_objective_args a, c
 // ---------------------------------------------------------------------------
 namespace temp {
 __global__ void kernel(const rl2_temperature_args a) {
-    grid_dependency_begin();
     const float log_t = a.log_temp[0];
     const float value = expf(log_t);
     if (a.update) {
@@ -325,10 +320,10 @@ extern "C" int rl2_policy_sample(const rl2_policy_args* a, int deterministic, vo
     if (deterministic) {
         const long long work = static_cast<long long>(a->rows) * a->act;
         const int blocks = static_cast<int>(std::min<long long>((work + policy::kT - 1) / policy::kT, 148 * 16));
-        launch(policy::deterministic_kernel, blocks, policy::kT, 0, as_stream(stream), *a);
+        policy::deterministic_kernel<<<blocks, policy::kT, 0, as_stream(stream)>>>(*a);
     } else {
         const int blocks = std::min((a->rows + policy::kWarps - 1) / policy::kWarps, 148 * 16);
-        launch(policy::sample_kernel, blocks, policy::kT, 0, as_stream(stream), *a);
+        policy::sample_kernel<<<blocks, policy::kT, 0, as_stream(stream)>>>(*a);
     }
     return launch_status("policy sample");
 }
@@ -342,7 +337,7 @@ extern "C" int rl2_policy_backward(const rl2_policy_args* a, void* stream) {
     }
     const int groups = (a->rows + 31) / 32;
     const int blocks = std::min((groups + policy::kWarps - 1) / policy::kWarps, 148 * 8);
-    launch(policy::backward_kernel, blocks, policy::kT, 0, as_stream(stream), *a, to_plane(&a->d_plane));
+    policy::backward_kernel<<<blocks, policy::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
     return launch_status("policy backward");
 }
 
@@ -359,7 +354,7 @@ extern "C" int rl2_actor_objective(const rl2_actor_objective_args* a, void* stre
         return -1;
     }
     const int blocks = std::min((a->batch + actor_obj::kWarps - 1) / actor_obj::kWarps, 148 * 8);
-    launch(actor_obj::kernel, blocks, actor_obj::kT, 0, as_stream(stream), *a, to_plane(&a->d_logits));
+    actor_obj::kernel<<<blocks, actor_obj::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_logits));
     return launch_status("actor objective");
 }
 
@@ -369,6 +364,6 @@ extern "C" int rl2_temperature_step(const rl2_temperature_args* a, void* stream)
         set_error("temperature step: invalid arguments");
         return -1;
     }
-    launch(temp::kernel, 1, 1, 0, as_stream(stream), *a);
+    temp::kernel<<<1, 1, 0, as_stream(stream)>>>(*a);
     return launch_status("temperature step");
 }

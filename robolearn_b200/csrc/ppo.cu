@@ -42,7 +42,6 @@ __device__ __forceinline__ Step gae_step(const rl2_ppo_gae_args& a, long long k,
 // Lane layout: S consecutive lanes per environment (S | 32), lane c of a group owns
 // times [c L, min((c + 1) L, T)).
 __global__ void gae_kernel(const rl2_ppo_gae_args a, int S, int L) {
-    grid_dependency_begin();
     const long long tid = static_cast<long long>(blockIdx.x) * kT + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const int c = lane % S;
@@ -131,7 +130,6 @@ inline int sum_blocks(long long n) {
 // mode 0: stats[0] = sum x; mode 1: stats[1] = sum (x - mean)^2 with mean = stats[0] / n
 __global__ void adv_moment_kernel(const float* __restrict__ x, int n, int mode, double* stats, double* partials,
                                   int* counter) {
-    grid_dependency_begin();
     const double mean = mode ? __ldcg(stats) / n : 0.0;
     double v = 0.0;
     for (long long i = static_cast<long long>(blockIdx.x) * kT + threadIdx.x; i < n;
@@ -148,7 +146,6 @@ __global__ void adv_moment_kernel(const float* __restrict__ x, int n, int mode, 
 }
 
 __global__ void adv_normalize_kernel(float* __restrict__ x, int n, int sample_std, const double* stats) {
-    grid_dependency_begin();
     const double nn = static_cast<double>(n);
     const double mean = stats[0] / nn;
     const double denom = sample_std ? sqrt(stats[1] / (nn - 1.0 > 1.0 ? nn - 1.0 : 1.0)) + 1.0e-8
@@ -187,7 +184,6 @@ __device__ __forceinline__ uint32_t feistel(uint32_t x, int half, const uint32_t
 
 __global__ void permutation_kernel(uint64_t seed, const unsigned long long* epoch, int n, int half, int* out,
                                    int* fail) {
-    grid_dependency_begin();
     const int i = blockIdx.x * kT + threadIdx.x;
     if (i >= n) return;
     const unsigned long long e = epoch ? *epoch : 0ull;
@@ -213,7 +209,6 @@ __global__ void permutation_kernel(uint64_t seed, const unsigned long long* epoc
 // minibatch gather (one warp per row)
 // ---------------------------------------------------------------------------
 __global__ void gather_kernel(const rl2_ppo_gather_args a, const Plane obs_plane) {
-    grid_dependency_begin();
     const int warp = (blockIdx.x * kT + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= a.rows) return;
@@ -252,7 +247,6 @@ __device__ __forceinline__ float action_log_std(const rl2_ppo_loss_args& a, int 
 }
 
 __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
-    grid_dependency_begin();
     __shared__ double sh[kT / 32][loss_slots(kMaxAct)];
     const int row = blockIdx.x * kT + threadIdx.x;
     const int A = a.act;
@@ -374,7 +368,6 @@ __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
 __global__ void kl_kernel(const float* mean, long long ld_mean, const float* std_param, const float* old_means,
                           const float* old_stds, int rows, int act, int std_type, float std_min, float std_max,
                           float desired_kl, float* kl, float* learning_rate, double* partials, int* counter) {
-    grid_dependency_begin();
     const int row = blockIdx.x * kT + threadIdx.x;
     double v = 0.0;
     if (row < rows) {
@@ -411,7 +404,6 @@ __global__ void kl_kernel(const float* mean, long long ld_mean, const float* std
 // ---------------------------------------------------------------------------
 __global__ void sumsq_kernel(const float* __restrict__ g, long long na, long long nc, long long n, int separate,
                              float max_norm, float* norms, double* partials, int* counter) {
-    grid_dependency_begin();
     double s[3] = {0.0, 0.0, 0.0};  // actor, critic, std
     for (long long i = static_cast<long long>(blockIdx.x) * kT + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * kT) {
@@ -438,7 +430,6 @@ __global__ void sumsq_kernel(const float* __restrict__ g, long long na, long lon
 }
 
 __global__ void scale_kernel(float* __restrict__ g, long long na, long long nc, long long n, const float* norms) {
-    grid_dependency_begin();
     const float ca = norms[3], cc = norms[4];
     for (long long i = static_cast<long long>(blockIdx.x) * kT + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * kT)
@@ -449,7 +440,6 @@ __global__ void scale_kernel(float* __restrict__ g, long long na, long long nc, 
 // rollout side: sample actions, store one step
 // ---------------------------------------------------------------------------
 __global__ void sample_kernel(const rl2_ppo_sample_args a) {
-    grid_dependency_begin();
     const int i = blockIdx.x * kT + threadIdx.x;
     if (i >= a.rows) return;
     float log_prob = 0.0f;
@@ -470,7 +460,6 @@ __global__ void sample_kernel(const rl2_ppo_sample_args a) {
 }
 
 __global__ void store_kernel(const rl2_ppo_store_args a) {
-    grid_dependency_begin();
     const int i = blockIdx.x * kT + threadIdx.x;
     if (i >= a.num_envs) return;
     const long long k = static_cast<long long>(a.step) * a.num_envs + i;
@@ -519,7 +508,7 @@ extern "C" int rl2_ppo_gae(const rl2_ppo_gae_args* a, void* stream) {
         set_error("rl2_ppo_gae: too many environments");
         return -1;
     }
-    launch(ppo::gae_kernel, static_cast<unsigned>(blocks), ppo::kT, 0, as_stream(stream), *a, S, L);
+    ppo::gae_kernel<<<static_cast<unsigned>(blocks), ppo::kT, 0, as_stream(stream)>>>(*a, S, L);
     return launch_status("rl2_ppo_gae");
 }
 
@@ -532,9 +521,9 @@ extern "C" int rl2_ppo_normalize_advantages(float* adv, int n, int sample_std, d
     }
     const int blocks = ppo::sum_blocks(n);
     cudaStream_t s = as_stream(stream);
-    launch(ppo::adv_moment_kernel, blocks, ppo::kT, 0, s, adv, n, 0, stats, partials, counter);
-    launch(ppo::adv_moment_kernel, blocks, ppo::kT, 0, s, adv, n, 1, stats, partials, counter);
-    launch(ppo::adv_normalize_kernel, blocks, ppo::kT, 0, s, adv, n, sample_std, stats);
+    ppo::adv_moment_kernel<<<blocks, ppo::kT, 0, s>>>(adv, n, 0, stats, partials, counter);
+    ppo::adv_moment_kernel<<<blocks, ppo::kT, 0, s>>>(adv, n, 1, stats, partials, counter);
+    ppo::adv_normalize_kernel<<<blocks, ppo::kT, 0, s>>>(adv, n, sample_std, stats);
     return launch_status("rl2_ppo_normalize_advantages");
 }
 
@@ -551,8 +540,8 @@ extern "C" int rl2_ppo_permutation(unsigned long long seed, const unsigned long 
         set_error("rl2_ppo_permutation: n must be below 2^30");
         return -1;
     }
-    launch(ppo::permutation_kernel, (n + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream), seed, epoch, n, half,
-           indices, health);
+    ppo::permutation_kernel<<<(n + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream)>>>(seed, epoch, n, half,
+                                                                                           indices, health);
     return launch_status("rl2_ppo_permutation");
 }
 
@@ -566,8 +555,8 @@ extern "C" int rl2_ppo_gather(const rl2_ppo_gather_args* a, void* stream) {
         return -1;
     }
     const long long threads = static_cast<long long>(a->rows) * 32;
-    launch(ppo::gather_kernel, static_cast<unsigned>((threads + ppo::kT - 1) / ppo::kT), ppo::kT, 0, as_stream(stream),
-           *a, to_plane(&a->obs_plane));
+    ppo::gather_kernel<<<static_cast<unsigned>((threads + ppo::kT - 1) / ppo::kT), ppo::kT, 0, as_stream(stream)>>>(
+        *a, to_plane(&a->obs_plane));
     return launch_status("rl2_ppo_gather");
 }
 
@@ -581,7 +570,7 @@ extern "C" int rl2_ppo_loss(const rl2_ppo_loss_args* a, void* stream) {
         return -1;
     }
     const int blocks = (a->rows + ppo::kT - 1) / ppo::kT;
-    launch(ppo::loss_kernel, blocks, ppo::kT, 0, as_stream(stream), *a, to_plane(&a->d_plane));
+    ppo::loss_kernel<<<blocks, ppo::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
     return launch_status("rl2_ppo_loss");
 }
 
@@ -595,8 +584,9 @@ extern "C" int rl2_ppo_kl(const float* mean, long long ld_mean, const float* std
         return -1;
     }
     const int blocks = (rows + ppo::kT - 1) / ppo::kT;
-    launch(ppo::kl_kernel, blocks, ppo::kT, 0, as_stream(stream), mean, ld_mean, std_param, old_means, old_stds, rows,
-           act, std_type, std_min, std_max, desired_kl, kl, learning_rate, partials, counter);
+    ppo::kl_kernel<<<blocks, ppo::kT, 0, as_stream(stream)>>>(mean, ld_mean, std_param, old_means, old_stds, rows, act,
+                                                             std_type, std_min, std_max, desired_kl, kl,
+                                                             learning_rate, partials, counter);
     return launch_status("rl2_ppo_kl");
 }
 
@@ -612,9 +602,9 @@ extern "C" int rl2_ppo_clip_gradients(float* grads, long long actor_count, long 
     }
     const int blocks = ppo::sum_blocks(n);
     cudaStream_t s = as_stream(stream);
-    launch(ppo::sumsq_kernel, blocks, ppo::kT, 0, s, grads, actor_count, critic_count, n, separate, max_norm,
-           norms_out, partials, counter);
-    launch(ppo::scale_kernel, blocks, ppo::kT, 0, s, grads, actor_count, critic_count, n, norms_out);
+    ppo::sumsq_kernel<<<blocks, ppo::kT, 0, s>>>(grads, actor_count, critic_count, n, separate, max_norm, norms_out,
+                                                 partials, counter);
+    ppo::scale_kernel<<<blocks, ppo::kT, 0, s>>>(grads, actor_count, critic_count, n, norms_out);
     return launch_status("rl2_ppo_clip_gradients");
 }
 
@@ -624,7 +614,7 @@ extern "C" int rl2_ppo_sample(const rl2_ppo_sample_args* a, void* stream) {
         set_error("rl2_ppo_sample: invalid arguments");
         return -1;
     }
-    launch(ppo::sample_kernel, (a->rows + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream), *a);
+    ppo::sample_kernel<<<(a->rows + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream)>>>(*a);
     return launch_status("rl2_ppo_sample");
 }
 
@@ -638,6 +628,6 @@ extern "C" int rl2_ppo_store(const rl2_ppo_store_args* a, void* stream) {
         set_error("rl2_ppo_store: invalid arguments");
         return -1;
     }
-    launch(ppo::store_kernel, (a->num_envs + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream), *a);
+    ppo::store_kernel<<<(a->num_envs + ppo::kT - 1) / ppo::kT, ppo::kT, 0, as_stream(stream)>>>(*a);
     return launch_status("rl2_ppo_store");
 }

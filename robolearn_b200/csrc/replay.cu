@@ -33,7 +33,6 @@ using rl2::philox;
 
 __global__ void sample_kernel(uint64_t seed, const unsigned long long* epoch, const long long* population,
                               long long fixed_population, int batch, int* out, int* health) {
-    grid_dependency_begin();
     const int i = blockIdx.x * kT + threadIdx.x;
     if (i >= batch) return;
     const uint32_t n = static_cast<uint32_t>(population ? *population : fixed_population);
@@ -60,8 +59,7 @@ __global__ void sample_kernel(uint64_t seed, const unsigned long long* epoch, co
     if (health) atomicOr(health, kHealthTimeout);
 }
 
-__global__ void advance_kernel(unsigned long long* epoch, unsigned long long by) {
-    grid_dependency_begin(); *epoch += by; }
+__global__ void advance_kernel(unsigned long long* epoch, unsigned long long by) { *epoch += by; }
 
 // Standard normal samples by the Box-Muller transform of two Philox uniforms per pair.
 // Elements e0 .. e0 + rows * cols - 1 of the row-major [*, cols] stream (element i comes
@@ -69,7 +67,6 @@ __global__ void advance_kernel(unsigned long long* epoch, unsigned long long by)
 // global array reproduces exactly the values a single launch over all rows would give.
 __global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, long long e0, int rows, int cols,
                               float* out, long long ld) {
-    grid_dependency_begin();
     const long long total = static_cast<long long>(rows) * cols;
     const unsigned long long e = epoch ? *epoch : 0ull;
     const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
@@ -100,7 +97,6 @@ __global__ void normal_kernel(uint64_t seed, const unsigned long long* epoch, lo
 
 // one warp per sampled row
 __global__ void gather_kernel(const rl2_replay_gather_args a) {
-    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     const int B = a.batch;
     float rscale = 1.0f;
@@ -158,8 +154,8 @@ extern "C" int rl2_replay_sample(unsigned long long seed, const unsigned long lo
         set_error("replay sample: invalid arguments");
         return -1;
     }
-    launch(replay::sample_kernel, (batch + replay::kT - 1) / replay::kT, replay::kT, 0, as_stream(stream), seed, epoch,
-           population, fixed_population, batch, indices, health);
+    replay::sample_kernel<<<(batch + replay::kT - 1) / replay::kT, replay::kT, 0, as_stream(stream)>>>(
+        seed, epoch, population, fixed_population, batch, indices, health);
     return launch_status("replay sample");
 }
 
@@ -169,7 +165,7 @@ extern "C" int rl2_counter_advance(unsigned long long* epoch, unsigned long long
         set_error("counter advance: null counter");
         return -1;
     }
-    launch(replay::advance_kernel, 1, 1, 0, as_stream(stream), epoch, by);
+    replay::advance_kernel<<<1, 1, 0, as_stream(stream)>>>(epoch, by);
     return launch_status("counter advance");
 }
 
@@ -183,7 +179,7 @@ extern "C" int rl2_normal_noise_rows(unsigned long long seed, const unsigned lon
     const long long e0 = row0 * cols;
     const long long quads = (e0 + static_cast<long long>(rows) * cols + 3) / 4 - e0 / 4;
     const int blocks = static_cast<int>(std::min<long long>((quads + replay::kT - 1) / replay::kT, 148 * 8));
-    launch(replay::normal_kernel, blocks, replay::kT, 0, as_stream(stream), seed, epoch, e0, rows, cols, out, ld);
+    replay::normal_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(seed, epoch, e0, rows, cols, out, ld);
     return launch_status("normal noise");
 }
 
@@ -200,7 +196,7 @@ extern "C" int rl2_replay_gather(const rl2_replay_gather_args* a, void* stream) 
         return -1;
     }
     const int blocks = std::min((a->batch + 7) / 8, 148 * 16);
-    launch(replay::gather_kernel, blocks, replay::kT, 0, as_stream(stream), *a);
+    replay::gather_kernel<<<blocks, replay::kT, 0, as_stream(stream)>>>(*a);
     return launch_status("replay gather");
 }
 
@@ -231,7 +227,6 @@ constexpr int kT = 256;
 // one warp per environment: stage this step, then (from step n-1 on) commit the
 // n-step transition that starts n-1 steps ago into the replay ring
 __global__ void stage_commit_kernel(const rl2_replay_ingest_args a) {
-    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     const long long step = a.counters[0];
     const int n = a.n_step;
@@ -291,7 +286,6 @@ __global__ void stage_commit_kernel(const rl2_replay_ingest_args a) {
 }
 
 __global__ void advance_kernel(long long* counters, int n_step, long long num_envs, long long capacity) {
-    grid_dependency_begin();
     if (counters[0] >= n_step - 1) {
         counters[1] = (counters[1] + num_envs) % capacity;
         counters[2] = counters[2] + num_envs < capacity ? counters[2] + num_envs : capacity;
@@ -305,7 +299,6 @@ __global__ void advance_kernel(long long* counters, int n_step, long long num_en
 __global__ void reward_stats_kernel(const float* reward, const float* term, const float* trunc,
                                     const unsigned char* term_u8, const unsigned char* trunc_u8, float* g_r,
                                     int num_envs, float gamma, float* state, float epsilon) {
-    grid_dependency_begin();
     __shared__ double red[3][kT];
     double s = 0.0, mx = 0.0;
     for (int i = threadIdx.x; i < num_envs; i += kT) {
@@ -368,9 +361,9 @@ extern "C" int rl2_replay_ingest(const rl2_replay_ingest_args* a, void* stream) 
         return -1;
     }
     const int blocks = static_cast<int>(std::min<long long>((a->num_envs + 7) / 8, 148 * 16));
-    launch(ingest::stage_commit_kernel, blocks, ingest::kT, 0, as_stream(stream), *a);
+    ingest::stage_commit_kernel<<<blocks, ingest::kT, 0, as_stream(stream)>>>(*a);
     if (launch_status("replay ingest")) return -1;
-    launch(ingest::advance_kernel, 1, 1, 0, as_stream(stream), a->counters, a->n_step, a->num_envs, a->capacity);
+    ingest::advance_kernel<<<1, 1, 0, as_stream(stream)>>>(a->counters, a->n_step, a->num_envs, a->capacity);
     return launch_status("replay advance");
 }
 
@@ -385,7 +378,7 @@ extern "C" int rl2_reward_stats_update(const float* reward, const float* termina
         set_error("reward stats: invalid arguments");
         return -1;
     }
-    launch(ingest::reward_stats_kernel, 1, ingest::kT, 0, as_stream(stream), reward, terminated, truncated,
-           terminated_u8, truncated_u8, g_r, num_envs, gamma, state, epsilon);
+    ingest::reward_stats_kernel<<<1, ingest::kT, 0, as_stream(stream)>>>(
+        reward, terminated, truncated, terminated_u8, truncated_u8, g_r, num_envs, gamma, state, epsilon);
     return launch_status("reward statistics");
 }
