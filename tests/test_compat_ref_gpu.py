@@ -86,6 +86,71 @@ def test_dense_plans_agree(libs, m, n, k, ta, tb, dtype, bias, beta):
     _close(ours, ref, 1e-4 if dtype == 0 else 1e-5)
 
 
+def _linear_specs(batch, fan_in, fan_out):
+    """The three plans the reference's CudaLinear makes per layer (cuda/linear.py:178-186):
+    Y^T = W X^T (+ bias), dX^T += W^T dY^T and dW^T += X^T dY on row-major arrays."""
+    return (
+        (fan_out, batch, fan_in, 1, 0, fan_in, fan_in, fan_out, 1),
+        (fan_in, batch, fan_out, 0, 0, fan_in, fan_out, fan_in, 0),
+        (fan_in, fan_out, batch, 0, 1, fan_in, fan_out, fan_in, 0),
+    )
+
+
+def _linear_step(lib, dtype, specs, x, w, dy, bias, dx0, dw0, timer=None):
+    """Forward, input-gradient and weight-gradient plans of one layer, as CudaLinear runs them."""
+    plans, out = [], {}
+    try:
+        for spec in specs:
+            h = (lib.rl_plan_create_mixed(*spec, 0, 1, 32 << 20) if dtype == 1
+                 else lib.rl_plan_create(*spec, 0, 32 << 20))
+            assert h, lib.rl_last_error().decode()
+            plans.append(h)
+        ws_bytes = max(lib.rl_plan_workspace(h) for h in plans)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+        y = torch.empty(x.shape[0], w.shape[0], device="cuda")
+        dx, dw = dx0.clone(), dw0.clone()
+        calls = {
+            "forward": lambda: lib.rl_plan_run(plans[0], w.data_ptr(), x.data_ptr(), None, y.data_ptr(),
+                                               bias.data_ptr(), ws.data_ptr(), ws_bytes, 0.0, _s()),
+            "input_gradient": lambda: lib.rl_plan_run(plans[1], w.data_ptr(), dy.data_ptr(), dx.data_ptr(),
+                                                      dx.data_ptr(), None, ws.data_ptr(), ws_bytes, 1.0, _s()),
+            "weight_gradient": lambda: lib.rl_plan_run(plans[2], x.data_ptr(), dy.data_ptr(), dw.data_ptr(),
+                                                       dw.data_ptr(), None, ws.data_ptr(), ws_bytes, 1.0, _s()),
+        }
+        for name, call in calls.items():
+            _ok(lib, call())
+        torch.cuda.synchronize()
+        out = {"y": y, "dx": dx, "dw": dw}
+        if timer is not None:
+            for name, call in calls.items():
+                out[name] = timer(lambda call=call: _ok(lib, call()))
+    finally:
+        for h in plans:
+            lib.rl_plan_destroy(h)
+    return out
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("fan_in,fan_out", [(512, 2048), (2048, 512)])
+def test_linear_layer_plans_agree(libs, dtype, fan_in, fan_out):
+    g = torch.Generator().manual_seed(fan_in + 3 * fan_out + dtype)
+    B = 8192
+    dt = torch.float16 if dtype else torch.float32
+    x = torch.randn(B, fan_in, generator=g).to(dt).cuda()
+    w = (torch.randn(fan_out, fan_in, generator=g) / fan_in ** 0.5).to(dt).cuda()
+    dy = (torch.randn(B, fan_out, generator=g) / B).to(dt).cuda()
+    bias = torch.randn(fan_out, generator=g).cuda()
+    dx0 = torch.randn(B, fan_in, generator=g).cuda()
+    dw0 = torch.randn(fan_out, fan_in, generator=g).cuda()
+    specs = _linear_specs(B, fan_in, fan_out)
+    ours, ref = _both(libs, lambda lib: _linear_step(lib, dtype, specs, x, w, dy, bias, dx0, dw0))
+    for name in ("y", "dx", "dw"):
+        try:
+            _close(ours[name], ref[name], 1e-4 if dtype == 0 else 5e-5)
+        except AssertionError as e:
+            raise AssertionError(f"{name}: {e}") from None
+
+
 def test_cast_bias_grad_zero_agree(libs):
     g = torch.Generator().manual_seed(1)
     x = (torch.randn(100003, generator=g) * 5000).cuda()
@@ -340,6 +405,12 @@ def test_reference_library_timing(libs):
             res[f"dense_fp{16 if dtype else 32}_{wide}x{rows}x{hidden}"] = timed(lambda: _ok(lib, lib.rl_plan_run(
                 plan, wa.data_ptr(), xa.data_ptr(), None, out.data_ptr(), bias.data_ptr(), ws.data_ptr(), wsb, 0.0, _s())))
             lib.rl_plan_destroy(plan)
+        for dtype, (xa, wa) in ((1, (x16, w16)), (0, (x32, w32))):
+            dy_l = torch.randn(rows, wide, generator=g).to(xa.dtype).cuda()
+            dx_l, dw_l = torch.zeros(rows, hidden, device="cuda"), torch.zeros(wide, hidden, device="cuda")
+            t = _linear_step(lib, dtype, _linear_specs(rows, hidden, wide), xa, wa, dy_l, bias, dx_l, dw_l, timed)
+            for part in ("forward", "input_gradient", "weight_gradient"):
+                res[f"linear_{part}_fp{16 if dtype else 32}_{rows}x{hidden}->{wide}"] = t[part]
         chunks = (rows + 255) // 256
         rm, rv = torch.zeros(wide, device="cuda"), torch.ones(wide, device="cuda")
         mean, var = torch.zeros(wide, device="cuda"), torch.zeros(wide, device="cuda")
