@@ -27,6 +27,8 @@ namespace gemm {
 void* create_rebindable(const rl2_gemm_desc* g);
 int run_rebound(void* plan, float* d, const float* bias, const float* residual, int accumulate,
                 cudaStream_t stream);
+int run_rebound_ab(void* plan, const void* a, const void* b, float* d, const float* bias, const float* residual,
+                   int accumulate, cudaStream_t stream);
 }  // namespace gemm
 }  // namespace rl2
 
@@ -99,6 +101,7 @@ struct DensePlan {
     float *a_hi = nullptr, *a_lo = nullptr, *b_hi = nullptr, *b_lo = nullptr;  // kernel view: A' = op(B)^T, B' = op(A)
     __half *a16 = nullptr, *b16 = nullptr;
     void* gemm = nullptr;
+    bool direct = false;  // fp16 operands read in place by TMA (no staging): leading dimensions multiples of 8
     bool tuned = false, used = false;
     std::string metadata;
 
@@ -121,7 +124,8 @@ void describe(DensePlan& p, float beta) {
                   "\"default_candidate_index\":0,\"selected_candidate_index\":0,\"selected_workspace_bytes\":0,"
                   "\"candidates\":[{\"heuristic_index\":0,\"tile_n\":%d,\"epilogue_form\":%d,\"workspace_bytes\":0,"
                   "\"status\":0,\"samples_ms\":[],\"median_ms\":null}]}",
-                  p.tuned ? "true" : "false", beta_s, p.dtype == 1 ? "fp16" : "tf32x3", rl2_gemm_tile_n(p.gemm),
+                  p.tuned ? "true" : "false", beta_s,
+                  p.dtype == 1 ? (p.direct ? "fp16 in place" : "fp16 staged") : "tf32x3 staged", rl2_gemm_tile_n(p.gemm),
                   rl2_gemm_uses_tma_store(p.gemm));
     p.metadata = buf;
 }
@@ -162,47 +166,65 @@ void* create_dense(int m, int n, int k, int transa, int transb, int lda, int ldb
     p->m = m, p->n = n, p->k = k, p->transa = transa, p->transb = transb, p->lda = lda, p->ldb = ldb, p->ldd = ldd;
     p->bias = use_bias != 0;
     p->dtype = input_dtype;
-    // staged rows are K-contiguous with a 16-byte row pitch (TMA stride rule)
-    p->kp = input_dtype == 1 ? (k + 7) / 8 * 8 : (k + 3) / 4 * 4;
-    const size_t elem = input_dtype == 1 ? 2 : 4;
-    auto region = [&](long long rows) { return (static_cast<size_t>(rows) * p->kp * elem + 255) / 256 * 256; };
-    const size_t ra = region(n), rb = region(m);
-    const size_t total = input_dtype == 1 ? ra + rb : 2 * (ra + rb);
-    if (cudaMalloc(&p->stage, total) != cudaSuccess) {
-        cudaGetLastError();
-        set_error("Allocate dense operand staging (%zu bytes)", total);
-        delete p;
-        return nullptr;
-    }
-    char* base = static_cast<char*>(p->stage);
     rl2_gemm_desc g;
     std::memset(&g, 0, sizeof(g));
-    if (input_dtype == 1) {
-        p->a16 = reinterpret_cast<__half*>(base);
-        p->b16 = reinterpret_cast<__half*>(base + ra);
+    p->direct = input_dtype == 1 && lda % 8 == 0 && ldb % 8 == 0;
+    if (p->direct) {
+        // kernel view read in place: A'[j][kk] = op(B)(kk, j), B'[i][kk] = op(A)(i, kk); the
+        // operand addresses are bound at every launch (a 256-byte placeholder until then)
+        if (cudaMalloc(&p->stage, 256) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("Allocate dense plan placeholder");
+            delete p;
+            return nullptr;
+        }
         g.kind = 0;
-        g.a = p->a16;
-        g.b = p->b16;
+        g.a = g.b = p->stage;
+        g.a_major = transb ? 1 : 0;
+        g.lda = ldb;
+        g.b_major = transa ? 0 : 1;
+        g.ldb = lda;
     } else {
-        p->a_hi = reinterpret_cast<float*>(base);
-        p->a_lo = reinterpret_cast<float*>(base + ra);
-        p->b_hi = reinterpret_cast<float*>(base + 2 * ra);
-        p->b_lo = reinterpret_cast<float*>(base + 2 * ra + rb);
-        g.kind = 1;
-        g.a = p->a_hi;
-        g.a_lo = p->a_lo;
-        g.b = p->b_hi;
-        g.b_lo = p->b_lo;
+        // staged rows are K-contiguous with a 16-byte row pitch (TMA stride rule)
+        p->kp = input_dtype == 1 ? (k + 7) / 8 * 8 : (k + 3) / 4 * 4;
+        const size_t elem = input_dtype == 1 ? 2 : 4;
+        auto region = [&](long long rows) { return (static_cast<size_t>(rows) * p->kp * elem + 255) / 256 * 256; };
+        const size_t ra = region(n), rb = region(m);
+        const size_t total = input_dtype == 1 ? ra + rb : 2 * (ra + rb);
+        if (cudaMalloc(&p->stage, total) != cudaSuccess) {
+            cudaGetLastError();
+            set_error("Allocate dense operand staging (%zu bytes)", total);
+            delete p;
+            return nullptr;
+        }
+        char* base = static_cast<char*>(p->stage);
+        if (input_dtype == 1) {
+            p->a16 = reinterpret_cast<__half*>(base);
+            p->b16 = reinterpret_cast<__half*>(base + ra);
+            g.kind = 0;
+            g.a = p->a16;
+            g.b = p->b16;
+        } else {
+            p->a_hi = reinterpret_cast<float*>(base);
+            p->a_lo = reinterpret_cast<float*>(base + ra);
+            p->b_hi = reinterpret_cast<float*>(base + 2 * ra);
+            p->b_lo = reinterpret_cast<float*>(base + 2 * ra + rb);
+            g.kind = 1;
+            g.a = p->a_hi;
+            g.a_lo = p->a_lo;
+            g.b = p->b_hi;
+            g.b_lo = p->b_lo;
+        }
+        g.a_major = 0;
+        g.lda = p->kp;
+        g.b_major = 0;
+        g.ldb = p->kp;
     }
     g.m = n;
     g.n = m;
     g.k = k;
     g.batch = 1;
-    g.a_major = 0;
-    g.lda = p->kp;
-    g.b_major = 0;
-    g.ldb = p->kp;
-    g.d = reinterpret_cast<float*>(base);  // placeholder: the output is bound at every launch
+    g.d = static_cast<float*>(p->stage);  // placeholder: the output is bound at every launch
     g.ldd = ldd;
     g.ldr = ldd;
     g.k_splits = 1;
@@ -402,8 +424,8 @@ extern "C" int rl_plan_run(void* opaque, const void* a, const void* b, const voi
     const cudaStream_t s = as_stream(stream);
     p->used = true;
     // kernel view: A'[j][kk] = op(B)(kk, j), B'[i][kk] = op(A)(i, kk)
-    if (compat::pack(*p, b, p->transb == 1, p->ldb, p->n, p->a_hi, p->a_lo, p->a16, s) ||
-        compat::pack(*p, a, p->transa == 0, p->lda, p->m, p->b_hi, p->b_lo, p->b16, s))
+    if (!p->direct && (compat::pack(*p, b, p->transb == 1, p->ldb, p->n, p->a_hi, p->a_lo, p->a16, s) ||
+                       compat::pack(*p, a, p->transa == 0, p->lda, p->m, p->b_hi, p->b_lo, p->b16, s)))
         return -1;
     float* dst = static_cast<float*>(d);
     const float* cc = static_cast<const float*>(c);
@@ -420,8 +442,9 @@ extern "C" int rl_plan_run(void* opaque, const void* a, const void* b, const voi
         if (launch_status("Scale dense C")) return -1;
         accumulate = 1;
     }
-    return gemm::run_rebound(p->gemm, dst, p->bias ? static_cast<const float*>(bias) : nullptr, residual, accumulate,
-                             s);
+    const float* bv = p->bias ? static_cast<const float*>(bias) : nullptr;
+    if (p->direct) return gemm::run_rebound_ab(p->gemm, b, a, dst, bv, residual, accumulate, s);
+    return gemm::run_rebound(p->gemm, dst, bv, residual, accumulate, s);
 }
 
 extern "C" int rl_plan_destroy(void* opaque) {

@@ -1394,14 +1394,25 @@ namespace gemm {
 
 void* create_rebindable(const rl2_gemm_desc* g) { return create_plan(g, true); }
 
-int run_rebound(void* opaque, float* d, const float* bias, const float* residual, int accumulate,
-                cudaStream_t stream) {
-    clear_error();
-    Plan* plan = static_cast<Plan*>(opaque);
-    if (!plan || plan->p.tma_epi || !d) {
-        set_error("rebound GEMM launch needs a rebindable plan and an output");
-        return -1;
-    }
+namespace {
+
+typedef CUresult (*ReplaceAddress)(CUtensorMap*, void*);
+
+ReplaceAddress replacer() {
+    static ReplaceAddress fn = [] {
+        void* q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        return cudaGetDriverEntryPoint("cuTensorMapReplaceAddress", &q, cudaEnableDefault, &r) == cudaSuccess &&
+                       r == cudaDriverEntryPointSuccess
+                   ? reinterpret_cast<ReplaceAddress>(q)
+                   : nullptr;
+    }();
+    return fn;
+}
+
+int launch_rebound(const Plan* plan, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
+                   const CUtensorMap& tb_lo, float* d, const float* bias, const float* residual, int accumulate,
+                   cudaStream_t stream) {
     Params p = plan->p;
     p.d = d;
     p.bias = bias;
@@ -1411,9 +1422,51 @@ int run_rebound(void* opaque, float* d, const float* bias, const float* residual
     p.vec_res = residual && aligned(residual, 16) && p.ldr % 4 == 0 && p.r_bstride % 4 == 0;
     p.vec_bias = bias && aligned(bias, 16) && p.bias_bstride % 4 == 0;
     KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
-    fn<<<plan->grid, kThreads, plan->smem, stream>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, plan->td,
-                                                     plan->tp, p, plan->stages);
+    fn<<<plan->grid, kThreads, plan->smem, stream>>>(ta, tb, ta_lo, tb_lo, plan->td, plan->tp, p, plan->stages);
     return launch_status("tcgen05 GEMM (rebound)");
+}
+
+}  // namespace
+
+int run_rebound(void* opaque, float* d, const float* bias, const float* residual, int accumulate,
+                cudaStream_t stream) {
+    clear_error();
+    const Plan* plan = static_cast<const Plan*>(opaque);
+    if (!plan || plan->p.tma_epi || !d) {
+        set_error("rebound GEMM launch needs a rebindable plan and an output");
+        return -1;
+    }
+    return launch_rebound(plan, plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, d, bias, residual, accumulate, stream);
+}
+
+// The same with the operands rebound too (fp16 plans): a and b in the descriptor's view, their
+// layouts (majors, leading dimensions, extents) those the plan was created with; the plan's
+// tensor maps are copied and given the new base addresses (cuTensorMapReplaceAddress).
+int run_rebound_ab(void* opaque, const void* a, const void* b, float* d, const float* bias, const float* residual,
+                   int accumulate, cudaStream_t stream) {
+    clear_error();
+    const Plan* plan = static_cast<const Plan*>(opaque);
+    if (!plan || plan->p.tma_epi || !d || plan->kind != 0) {
+        set_error("operand-rebound GEMM launch needs a rebindable fp16 plan and an output");
+        return -1;
+    }
+    const ReplaceAddress rep = replacer();
+    if (!rep) {
+        set_error("cuTensorMapReplaceAddress is unavailable from the driver");
+        return -1;
+    }
+    if (!a || !b || !aligned(a, 16) || !aligned(b, 16)) {
+        set_error("GEMM operand base addresses must be 16-byte aligned");
+        return -1;
+    }
+    CUtensorMap ta = plan->ta, tb = plan->tb;
+    const void* ka = plan->p.swap ? b : a;  // kernel view of a swapped plan: A' = B, B' = A
+    const void* kb = plan->p.swap ? a : b;
+    if (rep(&ta, const_cast<void*>(ka)) != CUDA_SUCCESS || rep(&tb, const_cast<void*>(kb)) != CUDA_SUCCESS) {
+        set_error("cuTensorMapReplaceAddress failed");
+        return -1;
+    }
+    return launch_rebound(plan, ta, tb, ta, tb, d, bias, residual, accumulate, stream);
 }
 
 }  // namespace gemm
