@@ -16,7 +16,8 @@
  * Differences that a caller can observe (everything else matches):
  *  - dense plans run on the library's tcgen05 kernels, not cuBLASLt: fp32 products use
  *    three tf32 tensor-core products per step (error ~1e-6 relative, fp32 storage), with
- *    or without allow_tf32; rl_plan_workspace returns 0 (operand staging is plan-owned);
+ *    or without allow_tf32; fp16 operands are read in place when lda and ldb are multiples
+ *    of 8, else staged; rl_plan_workspace returns 0 (any staging is plan-owned);
  *    rl_plan_autotune validates its preconditions and freezes the single plan-chosen
  *    candidate, which rl_plan_tuning_metadata describes.
  *  - per-row categorical projections sum their contributions by runs of equal atom index in
