@@ -43,7 +43,7 @@ namespace rl2 {
 namespace gemm {
 
 constexpr int kBM = 128;
-constexpr int kEpiWarps = 12;                 // three per TMEM lane quarter
+constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxSmem = 232448;           // dynamic shared memory one CTA may use
 
