@@ -4,9 +4,15 @@ same argument and result kinds, and argument errors are reported the reference's
 (-1 / NULL / SIZE_MAX and a message in ``rl_last_error``) before any device work."""
 
 import ctypes
+import json
 import re
+import subprocess
+import sys
 from pathlib import Path
 
+import pytest
+
+from oracle import build_ref
 from tests._rl_abi import TABLE, bound_library, ints, pointers, sizes
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -116,3 +122,22 @@ def test_argument_errors_follow_reference_convention():
     assert lib.rl_zero_step(None, None) == -1
     for destroy in ("rl_adam_destroy", "rl_flash_projection_destroy", "rl_flash_ema_destroy", "rl_zero_destroy"):
         assert getattr(lib, destroy)(None) == 0
+
+
+def test_fixture_is_what_the_reference_declares():
+    """Re-records the ctypes declarations from the reference's own code (where its sources
+    are present) and compares them with the committed fixture."""
+    src = build_ref.reference_root() / "src"
+    if not (src / "robolearn" / "cuda" / "_runtime.py").is_file():
+        pytest.skip("reference sources absent")
+    code = ("import json, sys; from pathlib import Path; sys.path.insert(0, 'tests/golden'); "
+            "import make_rl_abi as m; print(json.dumps(m.record(Path(sys.argv[1]))))")
+    done = subprocess.run([sys.executable, "-c", code, str(src)], cwd=ROOT, capture_output=True, text=True,
+                          timeout=120)
+    assert done.returncode == 0, done.stderr
+    assert json.loads(done.stdout.strip().splitlines()[-1]) == TABLE
+
+
+def test_reference_library_build_skips_without_sources(tmp_path, monkeypatch):
+    monkeypatch.setenv("RL2_REFERENCE_ROOT", str(tmp_path))
+    assert build_ref.build() is None
