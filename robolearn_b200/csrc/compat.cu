@@ -169,6 +169,11 @@ void* create_dense(int m, int n, int k, int transa, int transb, int lda, int ldb
     rl2_gemm_desc g;
     std::memset(&g, 0, sizeof(g));
     p->direct = input_dtype == 1 && lda % 8 == 0 && ldb % 8 == 0;
+    if (!p->direct && (k + 31) / 32 > 65535) {  // the staging kernel's grid.y covers K in 32-wide tiles
+        set_error("Dense K above 2097120 needs fp16 operands with leading dimensions that are multiples of 8.");
+        delete p;
+        return nullptr;
+    }
     if (p->direct) {
         // kernel view read in place: A'[j][kk] = op(B)(kk, j), B'[i][kk] = op(A)(i, kk); the
         // operand addresses are bound at every launch (a 256-byte placeholder until then)

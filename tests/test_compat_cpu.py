@@ -75,6 +75,8 @@ def test_argument_errors_follow_reference_convention():
     assert "leading dimension" in _err(lib)
     assert lib.rl_plan_create_mixed(4, 4, 4, 0, 0, 4, 4, 4, 0, 1, 1, 0) is None
     assert _err(lib) == "TF32 applies only to FP32 inputs."
+    assert lib.rl_plan_create(4, 4, 3_000_000, 0, 0, 4, 3_000_000, 4, 0, 0, 0) is None  # staging grid limit
+    assert "K above" in _err(lib)
     assert lib.rl_plan_workspace(None) == ctypes.c_size_t(-1).value
     assert lib.rl_plan_tuning_metadata(None) is None
     assert lib.rl_plan_run(None, None, None, None, None, None, None, 0, 0.0, None) == -1
