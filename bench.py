@@ -54,7 +54,9 @@ CFG5_BATCH = 32768
 def parse():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default 400 for the FlashSAC headline, about one second so the clock "
+                        "sampler sees several samples; 40 for the other workloads and the reference arm)")
     p.add_argument("--warmup", type=int, default=6)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
@@ -64,7 +66,10 @@ def parse():
                    help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms); "
                         "categorical: the cfg4 objective microbench; cfg5: the data-parallel FP32 config "
                         "(global batch 32768 split over --gpus ranks)")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.steps is None:
+        args.steps = 400 if args.workload == "flashsac" and args.impl == "b200" else 40
+    return args
 
 
 class Clocks:
