@@ -441,3 +441,76 @@ def test_categorical_target_projection(lib, batch, bins):
     _close(target, ref, 1e-5)
     np.testing.assert_allclose(target.sum(-1).cpu().numpy(), np.exp(sel.astype(np.float64)).sum(-1), rtol=1e-5)
     assert max_ent.item() == float(ent.max())
+
+
+def test_entry_points_are_deterministic_and_capture_equals_eager(lib):
+    """Every family run twice on the same inputs gives bitwise equal results (fixed-order sums,
+    no scheduling-dependent atomics), and a CUDA-graph replay of a dense plan equals the eager
+    call bitwise (the reference's diagnostics hold capture to eager within 2e-6,
+    examples/diagnose_cuda_flashsac.py:250-256)."""
+    g = _gen(21)
+    B, C, K = 1000, 96, 101
+    x = (1.0 + torch.randn(B, C, generator=g)).cuda()
+    w, b = torch.randn(C, generator=g).cuda(), torch.randn(C, generator=g).cuda()
+    dy = torch.randn(B, C, generator=g).cuda()
+    q = torch.randn(2, 2 * B, generator=g).cuda()
+    lp = torch.log_softmax(torch.randn(2, 2 * B, K, generator=g), -1).cuda()
+    rew, term = torch.randn(B, generator=g).cuda(), (torch.rand(B, generator=g) < 0.1).float().cuda()
+    disc, nlp, alpha = torch.full((B,), 0.99, device="cuda"), torch.randn(B, generator=g).cuda(), torch.tensor([0.1], device="cuda")
+    support = torch.linspace(-10, 10, K).cuda()
+    A = torch.randn(300, 256, generator=g).half().cuda()  # column-major 256 x 300 (lda 256)
+    Bm = torch.randn(512, 300, generator=g).half().cuda()  # column-major 300 x 512 (ldb 300, staged)
+
+    def run():
+        chunks = (B + 255) // 256
+        mean, var = torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
+        rm, rv = torch.zeros(C, device="cuda"), torch.ones(C, device="cuda")
+        partial, sums = torch.zeros(2 * chunks * C, device="cuda"), torch.zeros(2 * C, device="cuda")
+        y = torch.empty_like(x)
+        _ok(lib, lib.rl_flash_bn_forward(x.data_ptr(), w.data_ptr(), b.data_ptr(), rm.data_ptr(), rv.data_ptr(),
+                                         mean.data_ptr(), var.data_ptr(), partial.data_ptr(), y.data_ptr(), B, C,
+                                         1e-5, 0.01, 1, 1, _s()))
+        dx, dw, db = torch.zeros_like(x), torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
+        _ok(lib, lib.rl_flash_bn_backward(x.data_ptr(), dy.data_ptr(), y.data_ptr(), w.data_ptr(), mean.data_ptr(),
+                                          var.data_ptr(), partial.data_ptr(), sums.data_ptr(), dx.data_ptr(),
+                                          dw.data_ptr(), db.data_ptr(), B, C, 1e-5, 1, 1, _s()))
+        tgt, ment = torch.empty(B, K, device="cuda"), torch.tensor([-1e30], device="cuda")
+        _ok(lib, lib.rl_flash_categorical_target(q.data_ptr(), lp.data_ptr(), rew.data_ptr(), term.data_ptr(),
+                                                 disc.data_ptr(), nlp.data_ptr(), alpha.data_ptr(), tgt.data_ptr(),
+                                                 ment.data_ptr(), B, K, -10.0, 10.0, _s()))
+        logp, val = torch.empty(B, K, device="cuda"), torch.empty(B, device="cuda")
+        _ok(lib, lib.rl_flash_categorical_forward(tgt.data_ptr(), support.data_ptr(), support.data_ptr(),
+                                                  logp.data_ptr(), val.data_ptr(), B, K, _s()))
+        draw, dcb, scratch = torch.zeros(B, K, device="cuda"), torch.zeros(K, device="cuda"), torch.empty(B, K, device="cuda")
+        _ok(lib, lib.rl_flash_categorical_backward(logp.data_ptr(), support.data_ptr(), tgt.data_ptr(),
+                                                   val.data_ptr(), scratch.data_ptr(), draw.data_ptr(),
+                                                   dcb.data_ptr(), B, K, _s()))
+        torch.cuda.synchronize()
+        return [y, mean, var, dx, dw, db, tgt, ment, logp, val, draw, dcb]
+
+    first, second = run(), run()
+    for t1, t2 in zip(first, second):
+        assert torch.equal(t1, t2)
+
+    plans = [lib.rl_plan_create_mixed(256, 512, 300, 0, 0, 256, 300, 256, 0, 0, 1, 0),  # fp16 staged (ldb 300)
+             lib.rl_plan_create_mixed(256, 512, 296, 0, 1, 256, 512, 256, 0, 0, 1, 0)]  # fp16 in place
+    try:
+        assert all(plans), lib.rl_last_error().decode()
+        Bt = torch.randn(296, 512, generator=g).half().cuda()  # column-major 512 x 296 (ldb 512)
+        operands = [(A, Bm), (A, Bt)]
+        for plan, (a, bb) in zip(plans, operands):
+            eager, replay = torch.empty(512, 256, device="cuda"), torch.empty(512, 256, device="cuda")
+            _ok(lib, lib.rl_plan_run(plan, a.data_ptr(), bb.data_ptr(), None, eager.data_ptr(), None, None, 0, 0.0,
+                                     _s()))
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                _ok(lib, lib.rl_plan_run(plan, a.data_ptr(), bb.data_ptr(), None, replay.data_ptr(), None, None, 0,
+                                         0.0, _s()))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(eager, replay)
+            del graph
+    finally:
+        for plan in plans:
+            lib.rl_plan_destroy(plan)
