@@ -590,7 +590,11 @@ class Run:
             prog += [colstats, self._bn_stats("embedder.norm", Cin, src_part_shared=True)]
         prog.append(self._apply("embedder.norm", Cin, self.x_addr, self.ldx, 0, relu=False, plane=self.e))
         prog.append(self._fwd_gemm(net.linears["embed"], self.e, self.h[0], H, stats=False, out_plane=self.hp[0]))
-        fused_eval = not self.training and min(E, H) >= 128  # transposed plans take the BN epilogue
+        # evaluation-mode BN + ReLU (+ residual) in the product epilogue (transposed plans, so
+        # both widths >= 128); the pre-normalisation outputs t1 / t2 are then not stored, so a
+        # run whose backward needs them (the frozen critic's action gradient rebuilds its ReLU
+        # masks from them) keeps the separate products and apply passes
+        fused_eval = not self.training and not self.backward_needed and min(E, H) >= 128
         # training without a backward pass (the target critic): the wide pre-normalisation
         # output is never stored; a statistics-only product, then the product again with the
         # batch norm fused into its epilogue
