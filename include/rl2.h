@@ -201,6 +201,9 @@ typedef struct rl2_critic_objective_args {
 
 int rl2_categorical_workspace_floats(int batch, int bins);
 int rl2_categorical_counter_words(int batch, int bins);
+/* With 16-byte aligned logits and row / twin strides that are multiples of four floats the
+ * logits rows are copied into shared memory whole, padding after the last atom included:
+ * the full stride of every row read must be allocated. */
 int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
 
 /* Allocation-free variant of rl2_critic_objective (no counterpart in the reference).
@@ -209,9 +212,13 @@ int rl2_critic_objective(const rl2_critic_objective_args* args, void* stream);
  * device memory is owned by another framework's pool. args->workspace and args->counter
  * are ignored: the kernel uses a file-scope device array (about 0.65 MB per GPU, held
  * until process exit). Limits: batch <= 65536, bins <= 128; larger sizes return -1.
- * The first call on each device looks up that array's address (make it before any
- * stream capture). All calls share the array: calls that overlap on the GPU race,
- * so issue them in order on one stream. Nothing is allocated or freed. */
+ * Every call outside stream capture looks up that array's address in the current
+ * driver context; a call during capture reuses the address found by the last such
+ * call in the same context, so make one call per device (and again after a
+ * cudaDeviceReset or in any other context the host makes current) before capturing.
+ * The stream must belong to the current device, or -1 is returned. All calls share
+ * the array: calls that overlap on the GPU race, so issue them in order on one
+ * stream. Nothing is allocated or freed. */
 int rl2_critic_objective_noalloc(const rl2_critic_objective_args* args, void* stream);
 
 /* ---------------------------------------------------------------------------

@@ -8,11 +8,11 @@ reference's own flags (``src/robolearn/cuda/_runtime.py:41,64``: ``-std=c++17 -O
 
 Only the tests use the result: ``tests/test_compat_ref_gpu.py`` runs the same inputs
 through the reference's library and through librl2's ``rl_*`` entry points. Nothing in the
-product loads it. The reference tree is located by ``RL2_REFERENCE_ROOT`` (default: the
-reference checkout of the build container); where it is absent the build is skipped and
-the comparison tests skip.
+product loads it. The reference tree is given by ``--root``, else ``RL2_REFERENCE_ROOT``,
+else a checkout named ``reference`` beside this repository's directory; where it is absent
+the build is skipped and the comparison tests skip.
 
-Usage: ``python oracle/build_ref.py`` (also run by ``__graft_entry__.build()``).
+Usage: ``python oracle/build_ref.py [--root PATH]`` (also run by ``__graft_entry__.build()``).
 """
 
 from __future__ import annotations
@@ -29,8 +29,13 @@ FLAGS = ["-std=c++17", "-O3", "--shared", "-Xcompiler=-fPIC", "--fmad=false", "-
          "arch=compute_100,code=sm_100"]
 
 
-def reference_root() -> Path:
-    return Path(os.environ.get("RL2_REFERENCE_ROOT", "/root/reference"))
+def reference_root(root: str | Path | None = None) -> Path:
+    """The reference project's root: ``root`` when given, else ``RL2_REFERENCE_ROOT``, else a
+    checkout named ``reference`` beside this repository's directory."""
+    if root is not None:
+        return Path(root)
+    env = os.environ.get("RL2_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parents[1] / "reference"
 
 
 def _sources(root: Path) -> list[Path]:
@@ -38,9 +43,9 @@ def _sources(root: Path) -> list[Path]:
     return [cuda / "kernels.cu", *sorted(cuda.glob("*.cuh"))]
 
 
-def build(verbose: bool = False) -> Path | None:
+def build(verbose: bool = False, root: str | Path | None = None) -> Path | None:
     """Compile the reference library when its sources are present; returns the path or None."""
-    root = reference_root()
+    root = reference_root(root)
     srcs = _sources(root)
     if not srcs[0].is_file():
         return None
@@ -66,6 +71,10 @@ def build(verbose: bool = False) -> Path | None:
 
 
 if __name__ == "__main__":
-    path = build(verbose=True)
+    import argparse
+
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--root", default=None, help="the reference project's root directory")
+    path = build(verbose=True, root=parser.parse_args().root)
     if path is None:
         print("reference sources absent: nothing built")

@@ -138,180 +138,167 @@ __device__ __forceinline__ void scatter_runs(const int (&key)[E], const float (&
     }
 }
 
+// One row per group of eight lanes (lane group rg of a warp): target-twin selection,
+// projection, cross-entropy and logits gradient. t0 / t1 and o0 / o1 point at the row's
+// next-observation target logits and current-observation online logits of twins 0 / 1, in
+// global memory or in a shared-memory stage; they are read only when rv.
 template <int E>
-__global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a) {
-    constexpr int P = pitch<E>();
-    __shared__ float z_s[8 * E];
-    __shared__ float p_s[kWarps][kRowsPerWarp][P];  // selected target distribution (strided write, blocked read)
-    __shared__ float t_s[kWarps][kRowsPerWarp][P];  // projected target
-    __shared__ float red_s[kWarps][2 * 8 * E + 2];
-    __shared__ bool last_s;
+__device__ __forceinline__ void row_work(const Args& a, const float* t0, const float* t1, const float* o0,
+                                         const float* o1, int row, bool rv, const float* z_s, float* pw, float* tw, float alpha,
+                                         float scale16, float (&bias_acc)[2][E], float& loss_acc, float& ent_max,
+                                         bool& overflow) {
+    const int sub = threadIdx.x & 7;
+    const int bins = a.bins;
+    const float width = a.width;
+    // ---- target twins at the next-observation row: softmax and expected value; twin 0's
+    // probabilities go to shared memory and twin 1's replace them when its value is lower
+    float q0 = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float* src = t == 0 ? t0 : t1;
+        float e[E];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            const int k = sub + 8 * s;
+            e[s] = (rv && k < bins) ? src[k] : -INFINITY;
+            mx = fmaxf(mx, e[s]);
+        }
+        mx = gmax(mx);
+        float se = 0.0f;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            e[s] = (sub + 8 * s < bins) ? __expf(e[s] - mx) : 0.0f;
+            se += e[s];
+        }
+        const float inv = 1.0f / gsum(se);
+        float qq = 0.0f;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            e[s] = e[s] * inv;  // probabilities
+            qq += e[s] * z_s[sub + 8 * s];
+        }
+        qq = gsum(qq);
+        if (t == 0) {
+            q0 = qq;
+#pragma unroll
+            for (int s = 0; s < E; ++s) {
+                pw[sub + 8 * s] = e[s];
+                tw[sub + 8 * s] = 0.0f;
+            }
+        } else if (qq < q0) {  // min-Q twin, ties keep twin 0
+#pragma unroll
+            for (int s = 0; s < E; ++s) pw[sub + 8 * s] = e[s];
+        }
+    }
+    __syncwarp();
 
+    // ---- projection of the selected distribution (blocked layout j = E sub + s)
+    const float r = rv ? a.reward[row] : 0.0f;
+    const float done = rv ? a.terminated[row] : 0.0f;
+    const float g = rv ? a.discount[row] : 0.0f;
+    const float ent = rv ? __fmul_rn(alpha, a.next_log_pi[row]) : -INFINITY;
+    ent_max = fmaxf(ent_max, ent);
+    const float cont = __fsub_rn(1.0f, done);
+    int kl[E], ku[E];
+    float ml[E], mu[E];
+#pragma unroll
+    for (int s = 0; s < E; ++s) {
+        const int j = E * sub + s;
+        if (rv && j < bins) {
+            float v = __fadd_rn(r, __fmul_rn(__fmul_rn(g, __fsub_rn(z_s[j], ent)), cont));
+            v = fminf(fmaxf(v, a.min_v), a.max_v);
+            const float b = __fdiv_rn(__fsub_rn(v, a.min_v), width);
+            const int lower = static_cast<int>(floorf(b));
+            const int upper = min(max(lower + 1, 0), bins - 1);
+            const float frac = __fsub_rn(b, static_cast<float>(lower));
+            const float p = pw[j];
+            kl[s] = lower;
+            ku[s] = upper;
+            ml[s] = __fmul_rn(p, __fsub_rn(1.0f, frac));
+            mu[s] = __fmul_rn(p, frac);
+        } else {
+            kl[s] = INT_MAX;
+            ku[s] = INT_MAX;
+            ml[s] = 0.0f;
+            mu[s] = 0.0f;
+        }
+    }
+    scatter_runs<E>(kl, ml, tw, bins, false);
+    __syncwarp();
+    scatter_runs<E>(ku, mu, tw, bins, true);
+    __syncwarp();
+    float tgt[E];
+    float tsum = 0.0f;
+#pragma unroll
+    for (int s = 0; s < E; ++s) {
+        const int k = sub + 8 * s;
+        tgt[s] = k < bins ? tw[k] : 0.0f;
+        tsum += tgt[s];
+        if (a.target_out && rv && k < bins) a.target_out[static_cast<long long>(row) * a.target_row + k] = tgt[s];
+    }
+    tsum = gsum(tsum);
+
+    // ---- online twins at the current-observation row: CE and logits gradient
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float* src = t == 0 ? o0 : o1;
+        float x[E];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            const int k = sub + 8 * s;
+            x[s] = (rv && k < bins) ? src[k] : -INFINITY;
+            mx = fmaxf(mx, x[s]);
+        }
+        mx = gmax(mx);
+        float ex[E];
+        float se = 0.0f;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            ex[s] = (sub + 8 * s < bins) ? __expf(x[s] - mx) : 0.0f;
+            se += ex[s];
+        }
+        se = gsum(se);
+        const float lse = mx + logf(se);
+        const float inv = 1.0f / se;
+        if (!rv) continue;
+        float ce = 0.0f;
+#pragma unroll
+        for (int s = 0; s < E; ++s) {
+            const int k = sub + 8 * s;
+            if (k >= bins) continue;
+            const float lp = x[s] - lse;
+            ce -= tgt[s] * lp;
+            const float grad = (ex[s] * inv * tsum - tgt[s]) * a.loss_weight;
+            bias_acc[t][s] += grad;
+            if (a.dlogits) a.dlogits[t * a.d_twin + static_cast<long long>(row) * a.d_row + k] = grad;
+            if (a.d16) {
+                const float sv = grad * scale16;
+                overflow |= !(fabsf(sv) <= 65504.0f);
+                a.d16[t * a.d16_twin + static_cast<long long>(row) * a.d16_row + k] = __float2half_rn(sv);
+            }
+            if (a.d_hi) {
+                const float hi = __uint_as_float(__float_as_uint(grad) & 0xFFFFE000u);
+                const long long o = t * a.dp_twin + static_cast<long long>(row) * a.dp_row + k;
+                a.d_hi[o] = hi;
+                a.d_lo[o] = grad - hi;
+            }
+        }
+        loss_acc += ce;
+    }
+}
+
+// Block partial row of the head-bias gradient [2][bins], loss and entropy maximum, then the
+// two-level fixed-order cross-block reduction (groups of kGroup blocks by ticket).
+template <int E>
+__device__ __forceinline__ void finish(const Args& a, float (&bias_acc)[2][E], float loss_acc, float ent_max,
+                                       bool overflow, float (*red_s)[2 * 8 * E + 2], bool& last_s) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int sub = lane & 7;
     const int rg = lane >> 3;
     const int bins = a.bins;
-    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
-    __syncthreads();
-    float* pw = p_s[warp][rg];
-    float* tw = t_s[warp][rg];
-
-    const float alpha = a.alpha[0];
-    const float scale16 = a.d16 ? a.d16_scale[0] : 1.0f;
-    const float width = a.width;
-    float bias_acc[2][E];
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int s = 0; s < E; ++s) bias_acc[t][s] = 0.0f;
-    float loss_acc = 0.0f;
-    float ent_max = -INFINITY;
-    bool overflow = false;
-
-    for (int base = (blockIdx.x * kWarps + warp) * kRowsPerWarp; base < a.batch;
-         base += gridDim.x * kRowsPerBlock) {
-        const int row = base + rg;
-        const bool rv = row < a.batch;
-        // ---- target twins at the next-observation row: softmax and expected value; twin 0's
-        // probabilities go to shared memory and twin 1's replace them when its value is lower
-        float q0 = 0.0f;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const float* src = a.target_logits + t * a.t_twin + static_cast<long long>(a.t_row0 + row) * a.t_row;
-            float e[E];
-            float mx = -INFINITY;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                const int k = sub + 8 * s;
-                e[s] = (rv && k < bins) ? src[k] : -INFINITY;
-                mx = fmaxf(mx, e[s]);
-            }
-            mx = gmax(mx);
-            float se = 0.0f;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                e[s] = (sub + 8 * s < bins) ? __expf(e[s] - mx) : 0.0f;
-                se += e[s];
-            }
-            const float inv = 1.0f / gsum(se);
-            float qq = 0.0f;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                e[s] = e[s] * inv;  // probabilities
-                qq += e[s] * z_s[sub + 8 * s];
-            }
-            qq = gsum(qq);
-            if (t == 0) {
-                q0 = qq;
-#pragma unroll
-                for (int s = 0; s < E; ++s) {
-                    pw[sub + 8 * s] = e[s];
-                    tw[sub + 8 * s] = 0.0f;
-                }
-            } else if (qq < q0) {  // min-Q twin, ties keep twin 0
-#pragma unroll
-                for (int s = 0; s < E; ++s) pw[sub + 8 * s] = e[s];
-            }
-        }
-        __syncwarp();
-
-        // ---- projection of the selected distribution (blocked layout j = E sub + s)
-        const float r = rv ? a.reward[row] : 0.0f;
-        const float done = rv ? a.terminated[row] : 0.0f;
-        const float g = rv ? a.discount[row] : 0.0f;
-        const float ent = rv ? __fmul_rn(alpha, a.next_log_pi[row]) : -INFINITY;
-        ent_max = fmaxf(ent_max, ent);
-        const float cont = __fsub_rn(1.0f, done);
-        int kl[E], ku[E];
-        float ml[E], mu[E];
-#pragma unroll
-        for (int s = 0; s < E; ++s) {
-            const int j = E * sub + s;
-            if (rv && j < bins) {
-                float v = __fadd_rn(r, __fmul_rn(__fmul_rn(g, __fsub_rn(z_s[j], ent)), cont));
-                v = fminf(fmaxf(v, a.min_v), a.max_v);
-                const float b = __fdiv_rn(__fsub_rn(v, a.min_v), width);
-                const int lower = static_cast<int>(floorf(b));
-                const int upper = min(max(lower + 1, 0), bins - 1);
-                const float frac = __fsub_rn(b, static_cast<float>(lower));
-                const float p = pw[j];
-                kl[s] = lower;
-                ku[s] = upper;
-                ml[s] = __fmul_rn(p, __fsub_rn(1.0f, frac));
-                mu[s] = __fmul_rn(p, frac);
-            } else {
-                kl[s] = INT_MAX;
-                ku[s] = INT_MAX;
-                ml[s] = 0.0f;
-                mu[s] = 0.0f;
-            }
-        }
-        scatter_runs<E>(kl, ml, tw, bins, false);
-        __syncwarp();
-        scatter_runs<E>(ku, mu, tw, bins, true);
-        __syncwarp();
-        float tgt[E];
-        float tsum = 0.0f;
-#pragma unroll
-        for (int s = 0; s < E; ++s) {
-            const int k = sub + 8 * s;
-            tgt[s] = k < bins ? tw[k] : 0.0f;
-            tsum += tgt[s];
-            if (a.target_out && rv && k < bins) a.target_out[static_cast<long long>(row) * a.target_row + k] = tgt[s];
-        }
-        tsum = gsum(tsum);
-
-        // ---- online twins at the current-observation row: CE and logits gradient
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const float* src = a.online_logits + t * a.o_twin + static_cast<long long>(row) * a.o_row;
-            float x[E];
-            float mx = -INFINITY;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                const int k = sub + 8 * s;
-                x[s] = (rv && k < bins) ? src[k] : -INFINITY;
-                mx = fmaxf(mx, x[s]);
-            }
-            mx = gmax(mx);
-            float ex[E];
-            float se = 0.0f;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                ex[s] = (sub + 8 * s < bins) ? __expf(x[s] - mx) : 0.0f;
-                se += ex[s];
-            }
-            se = gsum(se);
-            const float lse = mx + logf(se);
-            const float inv = 1.0f / se;
-            if (!rv) continue;
-            float ce = 0.0f;
-#pragma unroll
-            for (int s = 0; s < E; ++s) {
-                const int k = sub + 8 * s;
-                if (k >= bins) continue;
-                const float lp = x[s] - lse;
-                ce -= tgt[s] * lp;
-                const float grad = (ex[s] * inv * tsum - tgt[s]) * a.loss_weight;
-                bias_acc[t][s] += grad;
-                if (a.dlogits) a.dlogits[t * a.d_twin + static_cast<long long>(row) * a.d_row + k] = grad;
-                if (a.d16) {
-                    const float sv = grad * scale16;
-                    overflow |= !(fabsf(sv) <= 65504.0f);
-                    a.d16[t * a.d16_twin + static_cast<long long>(row) * a.d16_row + k] = __float2half_rn(sv);
-                }
-                if (a.d_hi) {
-                    const float hi = __uint_as_float(__float_as_uint(grad) & 0xFFFFE000u);
-                    const long long o = t * a.dp_twin + static_cast<long long>(row) * a.dp_row + k;
-                    a.d_hi[o] = hi;
-                    a.d_lo[o] = grad - hi;
-                }
-            }
-            loss_acc += ce;
-        }
-        __syncwarp();  // the next rows overwrite this warp's shared rows
-    }
     if (overflow && a.health) atomicOr(a.health, kHealthOverflow);
 
     // ---- block partial row: bias gradient [2][bins], loss, max entropy
@@ -406,6 +393,179 @@ __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a
     if (threadIdx.x == 0) a.counter[0] = 0u;
 }
 
+template <int E>
+__global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a) {
+    constexpr int P = pitch<E>();
+    __shared__ float z_s[8 * E];
+    __shared__ float p_s[kWarps][kRowsPerWarp][P];  // selected target distribution (strided write, blocked read)
+    __shared__ float t_s[kWarps][kRowsPerWarp][P];  // projected target
+    __shared__ float red_s[kWarps][2 * 8 * E + 2];
+    __shared__ bool last_s;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rg = lane >> 3;
+    const int bins = a.bins;
+    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
+    __syncthreads();
+    float* pw = p_s[warp][rg];
+    float* tw = t_s[warp][rg];
+    const float alpha = a.alpha[0];
+    const float scale16 = a.d16 ? a.d16_scale[0] : 1.0f;
+    float bias_acc[2][E];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int s = 0; s < E; ++s) bias_acc[t][s] = 0.0f;
+    float loss_acc = 0.0f;
+    float ent_max = -INFINITY;
+    bool overflow = false;
+    for (int base = (blockIdx.x * kWarps + warp) * kRowsPerWarp; base < a.batch;
+         base += gridDim.x * kRowsPerBlock) {
+        const int row = base + rg;
+        const float* tr = a.target_logits + static_cast<long long>(a.t_row0 + row) * a.t_row;
+        const float* orow = a.online_logits + static_cast<long long>(row) * a.o_row;
+        row_work<E>(a, tr, tr + a.t_twin, orow, orow + a.o_twin, row, row < a.batch, z_s, pw, tw, alpha, scale16, bias_acc, loss_acc, ent_max,
+                    overflow);
+        __syncwarp();  // the next rows overwrite this warp's shared rows
+    }
+    finish<E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
+}
+
+// Staged variant: one CTA per SM walks 32-row tiles (8 warps x 4 rows); one thread
+// copies each tile's four logits blocks (target twins 0 / 1 at the next-observation rows,
+// online twins 0 / 1 at the current rows: contiguous row ranges) into a shared-memory
+// stage with 1-D bulk asynchronous copies completing on the stage's mbarrier, kStages
+// tiles ahead, so HBM reads stay in flight while the warps compute on an earlier stage.
+// Row work and reduction are those of critic_objective_kernel (the same per-row results;
+// the block sums visit rows in another fixed order, so they are deterministic but not
+// bit-identical to that kernel's). Needs 16-byte aligned logits bases and row / twin
+// strides that are multiples of four floats, and reads every row with its full stride
+// (padding included); rl2_critic_objective falls back to critic_objective_kernel otherwise.
+// Every mbarrier wait is bounded: on a timeout the health word records it, the block
+// waits (bounded again) for its copies in flight, contributes what it has and returns.
+constexpr int kStages = 3;
+constexpr int kStageRows = kRowsPerBlock;  // 32
+
+inline size_t staged_smem_bytes(long long t_row, long long o_row) {
+    return static_cast<size_t>(kStages) * kStageRows * 2 * static_cast<size_t>(t_row + o_row) * sizeof(float);
+}
+
+template <int E>
+__global__ void __launch_bounds__(kThreads, 1) critic_objective_staged_kernel(const Args a, int tiles) {
+    constexpr int P = pitch<E>();
+    extern __shared__ __align__(128) float stage_s[];  // [kStages][target twin 0 | 1 | online twin 0 | 1][32 rows]
+    __shared__ float z_s[8 * E];
+    __shared__ float p_s[kWarps][kRowsPerWarp][P];
+    __shared__ float t_s[kWarps][kRowsPerWarp][P];
+    __shared__ float red_s[kWarps][2 * 8 * E + 2];
+    __shared__ __align__(8) uint64_t full_s[kStages];
+    __shared__ bool last_s;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rg = lane >> 3;
+    const int bins = a.bins;
+    const int tr = static_cast<int>(a.t_row), orr = static_cast<int>(a.o_row);
+    const int stage_floats = kStageRows * 2 * (tr + orr);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) ptx::mbar_init(&full_s[s], 1);
+        ptx::fence_barrier_init();
+    }
+    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
+    __syncthreads();
+
+    // thread 0: arm stage i % kStages and copy local tile i into it
+    auto issue = [&](int i) {
+        const int r0 = (blockIdx.x + i * static_cast<int>(gridDim.x)) * kStageRows;
+        const int rows = min(kStageRows, a.batch - r0);
+        float* st = stage_s + (i % kStages) * stage_floats;
+        const uint32_t tb = static_cast<uint32_t>(rows * tr) * 4u, ob = static_cast<uint32_t>(rows * orr) * 4u;
+        uint64_t* bar = &full_s[i % kStages];
+        ptx::mbar_arrive_expect_tx(bar, 2u * (tb + ob));
+        const float* t = a.target_logits + static_cast<long long>(a.t_row0 + r0) * tr;
+        const float* o = a.online_logits + static_cast<long long>(r0) * orr;
+        ptx::bulk_load(st, t, tb, bar);
+        ptx::bulk_load(st + kStageRows * tr, t + a.t_twin, tb, bar);
+        ptx::bulk_load(st + 2 * kStageRows * tr, o, ob, bar);
+        ptx::bulk_load(st + 2 * kStageRows * tr + kStageRows * orr, o + a.o_twin, ob, bar);
+    };
+    const int mine = blockIdx.x < tiles ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                                        : 0;
+    int issued = 0;
+    if (threadIdx.x == 0)
+        for (; issued < min(kStages, mine); ++issued) issue(issued);
+
+    float* pw = p_s[warp][rg];
+    float* tw = t_s[warp][rg];
+    const float alpha = a.alpha[0];
+    const float scale16 = a.d16 ? a.d16_scale[0] : 1.0f;
+    float bias_acc[2][E];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int s = 0; s < E; ++s) bias_acc[t][s] = 0.0f;
+    float loss_acc = 0.0f;
+    float ent_max = -INFINITY;
+    bool overflow = false;
+    int done = 0;
+    for (int i = 0; i < mine; ++i) {
+        const int s = i % kStages;
+        const bool got = ptx::mbar_wait(&full_s[s], static_cast<uint32_t>((i / kStages) & 1), a.health);
+        if (!__syncthreads_and(got)) break;
+        const float* st = stage_s + s * stage_floats;
+        const int lr = warp * kRowsPerWarp + rg;
+        const int row = (blockIdx.x + i * static_cast<int>(gridDim.x)) * kStageRows + lr;
+        const float* t0 = st + lr * tr;
+        const float* o0 = st + 2 * kStageRows * tr + lr * orr;
+        row_work<E>(a, t0, t0 + kStageRows * tr, o0, o0 + kStageRows * orr, row, row < a.batch, z_s, pw, tw, alpha,
+                    scale16, bias_acc, loss_acc, ent_max, overflow);
+        done = i + 1;
+        __syncthreads();  // every warp is done with stage s (and with its shared rows)
+        if (threadIdx.x == 0 && issued < mine) {
+            ptx::fence_proxy_async_smem();
+            issue(issued++);
+        }
+    }
+    // copies armed but not consumed (only after a timeout) land before the block exits
+    if (threadIdx.x == 0) {
+        for (int i = done; i < issued; ++i)
+            ptx::mbar_wait(&full_s[i % kStages], static_cast<uint32_t>((i / kStages) & 1), nullptr);
+    }
+    __syncthreads();
+    finish<E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
+}
+
+constexpr size_t kSmemPerBlock = 232448;  // opt-in dynamic + static shared memory one CTA may use
+
+inline int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// The staged kernel reads whole row ranges with bulk copies: 16-byte aligned bases and
+// strides that are multiples of four floats, and stages that fit next to the static arrays.
+inline bool staged_ok(const rl2_critic_objective_args* g) {
+    const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!a16(g->target_logits) || !a16(g->online_logits)) return false;
+    if (g->target_row_stride % 4 || g->online_row_stride % 4 || g->target_twin_stride % 4 ||
+        g->online_twin_stride % 4 || g->target_row_stride < g->bins || g->online_row_stride < g->bins)
+        return false;
+    return staged_smem_bytes(g->target_row_stride, g->online_row_stride) + 48 * 1024 <= kSmemPerBlock;
+}
+
+template <int E>
+inline int launch_staged(const Args& a, int grid, int tiles, size_t smem, cudaStream_t s) {
+    if (cudaFuncSetAttribute(critic_objective_staged_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess) {
+        set_error("critic objective: cannot reserve %zu bytes of shared memory", smem);
+        return -1;
+    }
+    critic_objective_staged_kernel<E><<<grid, kThreads, smem, s>>>(a, tiles);
+    return launch_status("critic objective (staged)");
+}
+
 }  // namespace cat
 }  // namespace rl2
 
@@ -478,6 +638,18 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
     const int grid = cat::grid_for(g->batch);
     cudaStream_t s = as_stream(stream);
     const int e = (g->bins + 7) / 8;
+    if (cat::staged_ok(g)) {
+        const int tiles = (g->batch + cat::kStageRows - 1) / cat::kStageRows;
+        const int sg = std::min(tiles, cat::sm_count());
+        const size_t smem = cat::staged_smem_bytes(g->target_row_stride, g->online_row_stride);
+        if (e <= 4)
+            return cat::launch_staged<4>(a, sg, tiles, smem, s);
+        if (e <= 8)
+            return cat::launch_staged<8>(a, sg, tiles, smem, s);
+        if (e <= 13)
+            return cat::launch_staged<13>(a, sg, tiles, smem, s);
+        return cat::launch_staged<16>(a, sg, tiles, smem, s);
+    }
     if (e <= 4)
         cat::critic_objective_kernel<4><<<grid, cat::kThreads, 0, s>>>(a);
     else if (e <= 8)
@@ -501,13 +673,17 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
 // library holds until the process exits (about 0.65 MB).
 //
 // Limits: batch <= kNoAllocMaxBatch rows and bins <= 128 atoms; larger sizes are
-// rejected with an error. The first call on a device looks up the array's device
-// address (cudaGetSymbolAddress) with that device current; make that first call
-// before any stream capture. All calls share the one array and it keeps the last
-// call's contents: the counters are cleared at the start of every call (the partials
-// are fully rewritten before they are read), and calls that overlap on the GPU
-// (concurrent streams, or concurrent host threads) race on it, so issue them in
-// order on one stream.
+// rejected with an error. The array's device address is looked up
+// (cudaGetSymbolAddress) with the caller's device current on every call made outside
+// stream capture, and remembered per driver context; a call made while its stream is
+// being captured uses the address remembered for the current context, so make one
+// call on each device (and again after a cudaDeviceReset, or in any other context
+// the host makes current) before capturing a stream. The stream must belong to the
+// current device; a stream of another device is rejected. All calls share the one
+// array and it keeps the last call's contents: the counters are cleared at the start
+// of every call (the partials are fully rewritten before they are read), and calls
+// that overlap on the GPU (concurrent streams, or concurrent host threads) race on
+// it, so issue them in order on one stream.
 // ===========================================================================
 #include <mutex>
 
@@ -516,29 +692,75 @@ namespace cat {
 
 constexpr int kNoAllocMaxBatch = 65536;
 constexpr int kNoAllocGroups = (kMaxGrid + kGroup - 1) / kGroup;  // same grid rule as rl2_critic_objective
-constexpr int kNoAllocFloats = (kMaxGrid + kNoAllocGroups) * (2 * kMaxBins + 2);  // 162,282 floats of partial rows
-constexpr int kNoAllocCounterPad = 64;  // counter words (1 + groups <= 64), 256-byte aligned
+// partial rows (162,282 floats), rounded up to 64 floats so the counter words that
+// follow start on a 256-byte boundary like the array itself
+constexpr int kNoAllocFloats = ((kMaxGrid + kNoAllocGroups) * (2 * kMaxBins + 2) + 63) / 64 * 64;
+constexpr int kNoAllocCounterPad = 64;  // counter words (1 + groups <= 64)
+static_assert(kNoAllocFloats % 64 == 0, "counter words must start 256-byte aligned");
+static_assert(1 + kNoAllocGroups <= kNoAllocCounterPad, "counter pad too small");
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats + kNoAllocCounterPad];
 
 namespace {
+using CtxGetCurrent = int (*)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[256] = {};
+struct NoAllocEntry {
+    void* context;
+    void* address;
+};
+NoAllocEntry g_noalloc_cache[64] = {};
+int g_noalloc_next = 0;
+
+CtxGetCurrent ctx_get_current() {
+    static CtxGetCurrent fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<CtxGetCurrent>(nullptr);
+        return reinterpret_cast<CtxGetCurrent>(p);
+    }();
+    return fn;
+}
 }  // namespace
 
-// Device address of the scratch array for the current device (looked up once per device).
-static float* noalloc_scratch(int device) {
+// Device address of the scratch array in the current driver context. Outside capture
+// the address is looked up afresh (so a reset device or another context never gets a
+// stale address) and remembered for the context; during capture the remembered one is
+// used, as no lookup may run then.
+static float* noalloc_scratch(bool capturing) {
+    void* ctx = nullptr;
+    const CtxGetCurrent get = ctx_get_current();
+    if (!get || get(&ctx) != 0 || !ctx) {
+        set_error("critic objective (no-alloc): no current CUDA context");
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_addr[device]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) {
-            set_error("critic objective (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    NoAllocEntry* slot = nullptr;
+    for (auto& e : g_noalloc_cache)
+        if (e.context == ctx) slot = &e;
+    if (capturing) {
+        if (!slot) {
+            set_error("critic objective (no-alloc): the first call in this CUDA context was made during stream "
+                      "capture; make one call outside capture first");
             return nullptr;
         }
-        g_noalloc_addr[device] = p;
+        return static_cast<float*>(slot->address);
     }
-    return static_cast<float*>(g_noalloc_addr[device]);
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+        set_error("critic objective (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return nullptr;
+    }
+    if (!slot) {
+        slot = &g_noalloc_cache[g_noalloc_next];
+        g_noalloc_next = (g_noalloc_next + 1) % 64;
+    }
+    slot->context = ctx;
+    slot->address = p;
+    return static_cast<float*>(p);
 }
 
 }  // namespace cat
@@ -556,12 +778,23 @@ extern "C" int rl2_critic_objective_noalloc(const rl2_critic_objective_args* g, 
                   cat::kNoAllocMaxBatch, cat::kMaxBins, g->batch, g->bins);
         return -1;
     }
-    int device = -1;
-    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 256) {
+    int device = -1, stream_device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0) {
         set_error("critic objective (no-alloc): no current CUDA device");
         return -1;
     }
-    float* scratch = cat::noalloc_scratch(device);
+    if (cudaStreamGetDevice(as_stream(stream), &stream_device) != cudaSuccess || stream_device != device) {
+        cudaGetLastError();
+        set_error("critic objective (no-alloc): the stream belongs to device %d, not to the current device %d",
+                  stream_device, device);
+        return -1;
+    }
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(as_stream(stream), &capture) != cudaSuccess) {
+        set_error("critic objective (no-alloc): cannot query the stream's capture status");
+        return -1;
+    }
+    float* scratch = cat::noalloc_scratch(capture != cudaStreamCaptureStatusNone);
     if (!scratch) return -1;
     unsigned* counter = reinterpret_cast<unsigned*>(scratch + cat::kNoAllocFloats);
     if (cudaMemsetAsync(counter, 0, sizeof(unsigned) * (1 + cat::kNoAllocGroups), as_stream(stream)) != cudaSuccess) {

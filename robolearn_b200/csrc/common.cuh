@@ -101,6 +101,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* he
     return false;
 }
 
+// 1-D bulk copy from global memory into this CTA's shared memory, completing on `bar`
+// (no multicast). Both addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // 2D / 3D tiled TMA load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
     asm volatile(

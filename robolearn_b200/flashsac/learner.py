@@ -108,8 +108,6 @@ def _init_reference_weights(obs_a: int, obs_c: int, act: int, cfg: FlashSACConfi
                 b = params[k[: -len("weight")] + "bias"]
                 f = math.sqrt(v.shape[-1]) * torch.rsqrt((v * v + b * b).sum(-1, keepdim=True) + 1e-8)
                 out[k], out[k[: -len("weight")] + "bias"] = v * f, b * f
-            elif k == "post_norm.weight":
-                out[k] = v * (math.sqrt(v.shape[-1]) * torch.rsqrt((v * v).sum(-1, keepdim=True) + 1e-8))
             elif k.endswith("weight") and "norm" not in k:
                 out[k] = F.normalize(v, dim=-1, eps=1e-8)
             elif k not in out:

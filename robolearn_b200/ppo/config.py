@@ -8,7 +8,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 
-@dataclass
+@dataclass(frozen=True)
 class PPOConfig:
     hidden_dims: tuple[int, ...] = (64, 64)
     learning_rate: float = 3e-4

@@ -2,7 +2,8 @@
 
 Small cases compare with the golden tensors of the reference's own functions
 (``updates.py:19-80,248-257``) and with the pinned oracle; the full cfg4 size
-(65,536 rows x 101 atoms) is checked through size-independent properties: mass
+(65,536 rows x 101 atoms, config 4's distributions) is checked against the oracle at the
+same tolerances as the small cases, and through size-independent properties: mass
 conservation of the projected target, zero-sum logits gradients, bias gradient =
 column sums, and bitwise run-to-run determinism.
 """
@@ -19,14 +20,19 @@ pytestmark = pytest.mark.gpu
 from robolearn_b200.categorical import CriticObjective, support  # noqa: E402
 
 
-def _launch(target_lp, online_logits, reward, done, discount, next_lp, alpha, min_v, max_v, outputs=("fp32",)):
-    """target_lp: [2, B, bins] next-half distributions; online_logits: [2, 2B, bins]."""
+def _launch(target_lp, online_logits, reward, done, discount, next_lp, alpha, min_v, max_v, outputs=("fp32",),
+            padded=False):
+    """target_lp: [2, B, bins] next-half distributions; online_logits: [2, 2B, bins].
+    ``padded``: logits rows padded to a multiple of four floats (16-byte rows, the layout the
+    critic head product writes), which takes the shared-memory staged kernel."""
     twins, B, bins = target_lp.shape
     dev = "cuda"
-    # the kernel reads the next half at rows B..2B-1 of a [2, 2B, bins] target tensor
-    tgt_full = torch.zeros(2, 2 * B, bins, device=dev)
-    tgt_full[:, B:] = torch.as_tensor(target_lp, device=dev)
-    onl = torch.as_tensor(online_logits, device=dev).contiguous()
+    ld = (bins + 3) // 4 * 4 if padded else bins
+    # the kernel reads the next half at rows B..2B-1 of a [2, 2B, ld] target tensor
+    tgt_full = torch.zeros(2, 2 * B, ld, device=dev)
+    tgt_full[:, B:, :bins] = torch.as_tensor(target_lp, device=dev)
+    onl = torch.zeros(2, 2 * B, ld, device=dev)
+    onl[:, :, :bins] = torch.as_tensor(online_logits, device=dev)
     obj = CriticObjective(B, bins, min_v, max_v)
     out = dict(
         loss=torch.zeros(1, device=dev), ent=torch.zeros(1, device=dev),
@@ -43,8 +49,8 @@ def _launch(target_lp, online_logits, reward, done, discount, next_lp, alpha, mi
         out["lo"] = torch.zeros(2, 2 * B, bins, device=dev)
         kw.update(d_hi=out["hi"], d_lo=out["lo"], dplane_row_stride=bins, dplane_twin_stride=2 * B * bins)
     t = lambda x: torch.as_tensor(np.asarray(x, dtype=np.float32), device=dev)  # noqa: E731
-    obj.run(target_logits=tgt_full, target_row_stride=bins, target_twin_stride=2 * B * bins, target_row_offset=B,
-            online_logits=onl, online_row_stride=bins, online_twin_stride=2 * B * bins, reward=t(reward),
+    obj.run(target_logits=tgt_full, target_row_stride=ld, target_twin_stride=2 * B * ld, target_row_offset=B,
+            online_logits=onl, online_row_stride=ld, online_twin_stride=2 * B * ld, reward=t(reward),
             terminated=t(done), discount=t(discount), next_log_pi=t(next_lp), alpha=t([alpha]),
             loss_weight=1.0 / (2 * B), loss_out=out["loss"], max_entropy_out=out["ent"], bias_grad_out=out["bias"],
             dlogits=out["dlogits"], dlogits_row_stride=bins, dlogits_twin_stride=2 * B * bins,
@@ -87,8 +93,10 @@ def test_matches_golden_and_oracle(case):
     np.testing.assert_allclose(out["bias"], d.sum(axis=1), rtol=1e-4, atol=1e-8)
 
 
-@pytest.mark.parametrize("B,bins,min_v,max_v", [(4096, 101, -10.0, 10.0), (999, 51, -5.0, 5.0), (257, 128, -1.0, 3.0)])
-def test_random_against_oracle(B, bins, min_v, max_v):
+@pytest.mark.parametrize("padded", [False, True])
+@pytest.mark.parametrize("B,bins,min_v,max_v", [(4096, 101, -10.0, 10.0), (999, 51, -5.0, 5.0), (257, 128, -1.0, 3.0),
+                                               (37, 11, -5.0, 5.0)])
+def test_random_against_oracle(B, bins, min_v, max_v, padded):
     rng = np.random.default_rng(B + bins)
     tl = rng.standard_normal((2, B, bins)).astype(np.float32)
     target_lp = tl - np.log(np.exp(tl).sum(-1, keepdims=True))
@@ -98,7 +106,7 @@ def test_random_against_oracle(B, bins, min_v, max_v):
     discount = np.full(B, 0.99, np.float32)
     next_lp = rng.standard_normal(B).astype(np.float32)
     args = (target_lp.astype(np.float32), online, reward, done, discount, next_lp, 0.01, min_v, max_v)
-    out = _launch(*args, outputs=("fp32", "fp16", "tf32"))
+    out = _launch(*args, outputs=("fp32", "fp16", "tf32"), padded=padded)
     tgt, loss, d, ent = _oracle(*args)
     np.testing.assert_allclose(out["target"], tgt, rtol=2e-5, atol=2e-7)
     assert abs(out["loss"][0] - loss) <= 1e-5 * abs(loss)
@@ -108,7 +116,8 @@ def test_random_against_oracle(B, bins, min_v, max_v):
     np.testing.assert_allclose(d16[:, :B], out["dlogits"][:, :B], rtol=2e-3, atol=1e-7)
 
 
-def test_full_size_properties_and_determinism():
+@pytest.mark.parametrize("padded", [False, True])
+def test_full_size_against_oracle_properties_and_determinism(padded):
     B, bins = 65536, 101
     g = torch.Generator(device="cuda").manual_seed(4)
     tl = torch.log_softmax(torch.randn(2, B, bins, device="cuda", generator=g), -1)
@@ -117,8 +126,8 @@ def test_full_size_properties_and_determinism():
     done = (torch.rand(B, device="cuda", generator=g) < 0.01).float()
     args = (tl.cpu().numpy(), online.cpu().numpy(), reward.cpu().numpy(), done.cpu().numpy(),
             np.full(B, 0.99, np.float32), torch.randn(B, generator=None).numpy(), 0.01, -10.0, 10.0)
-    first = _launch(*args)
-    second = _launch(*args)
+    first = _launch(*args, padded=padded)
+    second = _launch(*args, padded=padded)
     for k in ("target", "loss", "dlogits", "bias", "ent"):
         np.testing.assert_array_equal(first[k], second[k])
     np.testing.assert_allclose(first["target"].sum(-1), 1.0, atol=2e-6)
@@ -126,6 +135,11 @@ def test_full_size_properties_and_determinism():
     assert np.all(first["dlogits"][:, B:] == 0)
     np.testing.assert_allclose(first["bias"], first["dlogits"].astype(np.float64).sum(1), rtol=1e-3, atol=1e-7)
     assert np.isfinite(first["loss"]).all()
+    tgt, loss, d, ent = _oracle(*args)
+    np.testing.assert_allclose(first["target"], tgt, rtol=2e-5, atol=2e-7)
+    assert abs(first["loss"][0] - loss) <= 1e-5 * abs(loss)
+    np.testing.assert_allclose(first["dlogits"], d, rtol=1e-4, atol=1e-9)
+    assert abs(first["ent"][0] - ent) <= 1e-7 * max(1.0, abs(ent))
 
 
 def test_support_matches_oracle_rule():

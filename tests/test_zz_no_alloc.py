@@ -82,3 +82,14 @@ def test_no_alloc_rejects_sizes_beyond_its_limit():
     a.batch = 65537
     assert lib.rl2_critic_objective_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == -1
     assert b"batch must be in [1, 65536]" in lib.rl2_last_error()
+
+
+def test_no_alloc_rejects_a_stream_of_another_device():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    lib = N.load()
+    a, _ = _args(16, 11, seed=1)
+    with torch.cuda.device(1):
+        other = torch.cuda.Stream()
+    assert lib.rl2_critic_objective_noalloc(ctypes.byref(a), other.cuda_stream) == -1
+    assert b"belongs to device 1" in lib.rl2_last_error()
