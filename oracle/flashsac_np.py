@@ -126,7 +126,7 @@ def bn_buffer_prefixes(blocks: int) -> list[str]:
 # ----------------------------------------------------------------------------
 
 
-def bn_forward(x, w, b, rm, rv, training, eps=BN_EPS, momentum=BN_MOMENTUM):
+def _bn_forward_cols(x, w, b, rm, rv, training, eps=BN_EPS, momentum=BN_MOMENTUM):
     """Batch norm over rows of ``x[T,R,C]`` (``layers.py:32-55,189-214``).
 
     Training uses the biased variance and moves running statistics by
@@ -149,7 +149,7 @@ def bn_forward(x, w, b, rm, rv, training, eps=BN_EPS, momentum=BN_MOMENTUM):
     return y, (xhat, inv, w, training), new_rm, new_rv
 
 
-def bn_backward(dy, cache):
+def _bn_backward_cols(dy, cache):
     """Adjoint of :func:`bn_forward`; returns ``(dx, dw, db)``."""
     xhat, inv, w, training = cache
     dw = (dy * xhat).sum(axis=1)
@@ -159,6 +159,71 @@ def bn_backward(dy, cache):
         dx = inv * (g - g.mean(axis=1, keepdims=True) - xhat * (g * xhat).mean(axis=1, keepdims=True))
     else:
         dx = g * inv
+    return dx, dw, db
+
+
+# Host threads for the column-independent batch-norm passes (off by default; the CPU
+# baseline turns them on). Every column is computed by the same expressions whichever
+# thread runs it, so the result does not depend on the thread count.
+_THREADS = {"n": 1, "pool": None}
+
+
+def set_threads(n: int) -> None:
+    """Run the batch-norm passes of large arrays over ``n`` host threads (numpy releases
+    the interpreter lock inside its array loops)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    n = max(1, int(n))
+    if _THREADS["pool"] is not None:
+        _THREADS["pool"].shutdown()
+    _THREADS.update(n=n, pool=ThreadPoolExecutor(n) if n > 1 else None)
+
+
+def _col_chunks(cols: int):
+    n = _THREADS["n"]
+    step = -(-cols // n)
+    return [(c, min(c + step, cols)) for c in range(0, cols, step)]
+
+
+def bn_forward(x, w, b, rm, rv, training, eps=BN_EPS, momentum=BN_MOMENTUM):
+    """Batch norm over rows of ``x[T,R,C]`` (see :func:`_bn_forward_cols`), over column
+    chunks on the host threads of :func:`set_threads` for large arrays."""
+    pool = _THREADS["pool"]
+    if pool is None or x.size < (1 << 20):
+        return _bn_forward_cols(x, w, b, rm, rv, training, eps, momentum)
+    T, _, C = x.shape
+    dt = np.result_type(x, w)
+    y, xhat = np.empty(x.shape, dt), np.empty(x.shape, dt)
+    inv = np.empty((T, 1, C), dt)
+    nrm, nrv = np.empty(rm.shape, np.result_type(rm, x)), np.empty(rv.shape, np.result_type(rv, x))
+
+    def work(c):
+        sl = slice(*c)
+        yy, (xh, iv, _, _), r1, r2 = _bn_forward_cols(x[..., sl], w[:, sl], b[:, sl], rm[:, sl], rv[:, sl], training,
+                                                     eps, momentum)
+        y[..., sl], xhat[..., sl], inv[..., sl] = yy, xh, np.broadcast_to(iv, (T, 1, c[1] - c[0]))
+        nrm[..., sl], nrv[..., sl] = r1, r2
+
+    list(pool.map(work, _col_chunks(C)))
+    return y, (xhat, inv, w, training), nrm, nrv
+
+
+def bn_backward(dy, cache):
+    """Adjoint of :func:`bn_forward` (see :func:`_bn_backward_cols`), column-chunked like it."""
+    pool = _THREADS["pool"]
+    if pool is None or dy.size < (1 << 20):
+        return _bn_backward_cols(dy, cache)
+    xhat, inv, w, training = cache
+    T, _, C = dy.shape
+    dt = np.result_type(dy, xhat)
+    dx, dw, db = np.empty(dy.shape, dt), np.empty((T, C), dt), np.empty((T, C), dt)
+
+    def work(c):
+        sl = slice(*c)
+        dx[..., sl], dw[:, sl], db[:, sl] = _bn_backward_cols(dy[..., sl], (xhat[..., sl], inv[..., sl], w[:, sl],
+                                                                             training))
+
+    list(pool.map(work, _col_chunks(C)))
     return dx, dw, db
 
 
@@ -200,15 +265,34 @@ _ROUND = {"mode": "fp32", "scale": 1.0}
 
 
 def set_operand_rounding(mode: str = "fp32", scale: float = 1.0) -> None:
-    if mode not in ("fp32", "fp16"):
+    """Round every dense-product operand as a CUDA recipe does before its tensor-core
+    products: "fp16" (operands rounded to fp16, gradient operands carrying ``scale``), or
+    "tf32x3" (the FP32 recipe's split: the fp32 value's high part with the low 13 mantissa
+    bits cleared, plus the remainder as the tensor core reads it, truncated to tf32; the
+    model multiplies the two rounded sums, so it keeps the lo x lo term the recipe drops,
+    about 2^-22 of each product). "fp32" leaves operands exact."""
+    if mode not in ("fp32", "fp16", "tf32x3"):
         raise ValueError(mode)
     _ROUND["mode"], _ROUND["scale"] = mode, float(scale)
+
+
+def _tf32_trunc(v32):
+    return (np.asarray(v32, np.float32).view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+def _tf32x3(x):
+    x32 = np.asarray(x, np.float32)
+    hi = _tf32_trunc(x32)
+    lo = _tf32_trunc(x32 - hi)
+    return hi.astype(np.float64) + lo.astype(np.float64)
 
 
 def _rf(x):
     """forward / weight operand"""
     if _ROUND["mode"] == "fp16":
         return np.asarray(x).astype(np.float16).astype(np.float64)
+    if _ROUND["mode"] == "tf32x3":
+        return _tf32x3(x)
     return x
 
 
@@ -217,6 +301,8 @@ def _rg(x):
     if _ROUND["mode"] == "fp16":
         s = _ROUND["scale"]
         return (np.asarray(x) * s).astype(np.float16).astype(np.float64) / s
+    if _ROUND["mode"] == "tf32x3":
+        return _tf32x3(x)
     return x
 
 
@@ -238,21 +324,104 @@ def sigmoid(x):
 
 
 _MARGIN = [np.inf]
+# ReLU sites are numbered in call order since the last reset; a near-kink element is
+# (site, flat index) with |pre-activation| below _KINK["margin"]; _KINK["flips"] holds
+# the elements whose decision is evaluated the other way (the pre-activation's sign is
+# flipped there, so the forward value and the backward mask both take the other branch);
+# _KINK["adopt"] maps a site to another evaluation's pre-normalisation output, whose
+# decisions (rebuilt with this evaluation's batch-norm statistics) are taken wherever
+# they differ from this one's
+_KINK = {"site": 0, "margin": 0.0, "near": [], "flips": set(), "adopt": {}, "adopted": 0, "track": False,
+         "keep": False, "pre": {}}
 
 
-def _note_margin(pre_relu) -> None:
-    """Track the smallest |pre-activation| seen by a ReLU (how close a mask decision is to the kink)."""
-    _MARGIN[0] = min(_MARGIN[0], float(np.abs(pre_relu).min()))
+def _kink(pre_relu, bn=None):
+    """Note how close this ReLU's decisions are to the kink, record near-kink elements and
+    apply requested decision flips. ``bn`` = (pre-normalisation input, mean, invstd,
+    weight, bias) of the batch norm that produced ``pre_relu``, used to rebuild adopted
+    decisions. Returns the pre-activation to feed the ReLU."""
+    site = _KINK["site"]
+    _KINK["site"] += 1
+    if not _KINK["track"]:  # no reset since import: plain evaluation, nothing recorded
+        return pre_relu
+    a = np.abs(pre_relu)
+    _MARGIN[0] = min(_MARGIN[0], float(a.min()))
+    if _KINK["margin"] > 0:
+        for i in np.flatnonzero(a.ravel() < _KINK["margin"]):
+            _KINK["near"].append((site, int(i)))
+    flip = np.zeros(pre_relu.size, dtype=bool)
+    mine = [i for (s_, i) in _KINK["flips"] if s_ == site]
+    flip[mine] = True
+    if _KINK["keep"] and bn is not None:
+        _KINK["pre"][site] = np.array(bn[0], copy=True)
+    other = _KINK["adopt"].get(site)
+    if other is not None and bn is not None:
+        _, mean, inv, w, b = bn
+        if isinstance(other, tuple):
+            # (pre-normalisation output, mean, invstd) of a float32 evaluation: its decision
+            # is the sign of fma((x - mean) * invstd, weight, bias) with float32 roundings of
+            # the difference and the product; the fused multiply-add's sign is that of the
+            # exact value, which float64 holds exactly for float32 factors
+            ox, om, oi = (np.asarray(v, np.float32) for v in other)
+            f32 = np.float32
+            xh = ((ox.reshape(pre_relu.shape) - om[:, None, :]).astype(f32) * oi[:, None, :]).astype(f32)
+            rebuilt = xh.astype(np.float64) * w.astype(f32)[:, None, :].astype(np.float64) \
+                + b.astype(f32)[:, None, :].astype(np.float64)
+        else:
+            rebuilt = (np.asarray(other, np.float64).reshape(pre_relu.shape) - mean) * inv * w[:, None, :] + b[:, None, :]
+        differ = ((rebuilt > 0) != (pre_relu > 0)).ravel()
+        _KINK["adopted"] += int(differ.sum())
+        flip ^= differ
+    if flip.any():
+        pre_relu = np.array(pre_relu, copy=True)
+        flat = pre_relu.reshape(-1)
+        flat[flip] = -flat[flip]
+    return pre_relu
 
 
-def relu_margin_reset() -> None:
+def relu_margin_reset(record_below: float = 0.0, flips=(), adopt=None, keep_pre: bool = False) -> None:
+    """Start a new update: reset the margin and the site counter; record elements whose
+    |pre-activation| is below ``record_below``; evaluate the decisions of ``flips``
+    ((site, flat index) pairs from :func:`relu_near_kinks`) the other way; take the
+    decisions of another evaluation at the sites of ``adopt`` (site -> its
+    pre-normalisation output, same shape as this evaluation's, rebuilt with this
+    evaluation's statistics; or a float32 evaluation's (output, mean [T,C], invstd [T,C]),
+    rebuilt with its own statistics and float32 roundings); with ``keep_pre`` keep
+    this evaluation's own pre-normalisation outputs (:func:`relu_pre_outputs`)."""
     _MARGIN[0] = np.inf
+    _KINK.update(site=0, margin=float(record_below), near=[], flips=set(flips), adopt=dict(adopt or {}), adopted=0,
+                 track=True, keep=bool(keep_pre), pre={})
+
+
+def relu_near_kinks() -> list[tuple[int, int]]:
+    """(site, flat index) of the pre-activations below the recording margin since the reset."""
+    return list(_KINK["near"])
+
+
+def relu_pre_outputs() -> dict:
+    """Site -> pre-normalisation output kept since a ``keep_pre`` reset."""
+    return dict(_KINK["pre"])
+
+
+def relu_adopted() -> int:
+    """How many decisions were taken from the other evaluation since the reset."""
+    return _KINK["adopted"]
 
 
 def relu_margin() -> float:
-    """Smallest |pre-ReLU| value since the last reset; a decision closer to 0 than the
-    arithmetic's rounding is not determined by fp32 evaluation order."""
+    """Smallest |pre-ReLU| value since the last reset (tracking starts at the first reset);
+    a decision closer to 0 than the arithmetic's rounding is not determined by fp32
+    evaluation order."""
     return _MARGIN[0]
+
+
+def _bn_ctx(x, cache, running_mean, bias):
+    """(input, mean, invstd, weight, bias) of a batch norm, for rebuilding decisions."""
+    if not (_KINK["adopt"] or _KINK["keep"]):
+        return None
+    _, inv, w, training = cache
+    mean = x.mean(axis=1, keepdims=True) if training else running_mean[:, None, :]
+    return x, mean, inv, w, bias
 
 
 def _stack(p: dict, key: str, twin: bool) -> np.ndarray:
@@ -286,15 +455,15 @@ def backbone_forward(p, x, blocks, training, twin, dtype):
             t1, g(f"encoder.{i}.norm1.weight"), g(f"encoder.{i}.norm1.bias"),
             g(f"encoder.{i}.norm1.running_mean"), g(f"encoder.{i}.norm1.running_var"), training,
         )
+        n1 = _kink(n1, _bn_ctx(t1, c1, g(f"encoder.{i}.norm1.running_mean"), g(f"encoder.{i}.norm1.bias")))
         a1 = relu(n1)
-        _note_margin(n1)
         t2 = linear(_rf(a1), _rf(w2))
         n2, c2, rm2, rv2 = bn_forward(
             t2, g(f"encoder.{i}.norm2.weight"), g(f"encoder.{i}.norm2.bias"),
             g(f"encoder.{i}.norm2.running_mean"), g(f"encoder.{i}.norm2.running_var"), training,
         )
+        n2 = _kink(n2, _bn_ctx(t2, c2, g(f"encoder.{i}.norm2.running_mean"), g(f"encoder.{i}.norm2.bias")))
         a2 = relu(n2)
-        _note_margin(n2)
         stats[f"encoder.{i}.norm1"] = (rm1, rv1)
         stats[f"encoder.{i}.norm2"] = (rm2, rv2)
         caches.append(("block", h, w1, w2, c1, n1, a1, c2, n2))

@@ -118,6 +118,20 @@ def normalize_advantages(adv, sample_std: bool = False) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # parameters and MLP
 # ---------------------------------------------------------------------------
+# Working floating-point type of the MLP, loss and optimiser arithmetic: float64 for the
+# parity checks (default), float32 for timing the update as the reference's Torch
+# restatement computes it. GAE keeps its own float32 operation order either way.
+_WORK = {"dtype": np.float64}
+
+
+def set_dtype(dtype) -> None:
+    _WORK["dtype"] = np.dtype(dtype).type
+
+
+def _FT():
+    return _WORK["dtype"]
+
+
 def init_mlp(in_dim: int, out_dim: int, hidden: tuple, rng: np.random.Generator) -> list[np.ndarray]:
     widths = (in_dim, *hidden, out_dim)
     params = []
@@ -150,12 +164,12 @@ def _act_grad(y, kind):
 
 
 def mlp_forward(net: list, x, activation: str):
-    h = np.asarray(x, np.float64)
+    h = np.asarray(x, _FT())
     acts = [h]
     layers = len(net) // 2
     for li in range(layers):
-        w = net[2 * li].astype(np.float64)
-        b = net[2 * li + 1].astype(np.float64).reshape(-1)
+        w = net[2 * li].astype(_FT())
+        b = net[2 * li + 1].astype(_FT()).reshape(-1)
         h = h @ w.T + b
         if li < layers - 1:
             h = _act(h, activation)
@@ -166,13 +180,13 @@ def mlp_forward(net: list, x, activation: str):
 def mlp_backward(net: list, acts: list, dout, activation: str) -> list[np.ndarray]:
     layers = len(net) // 2
     grads = [None] * len(net)
-    d = np.asarray(dout, np.float64)
+    d = np.asarray(dout, _FT())
     for li in range(layers - 1, -1, -1):
         x = acts[li]
         grads[2 * li] = d.T @ x
         grads[2 * li + 1] = d.sum(0).reshape(-1, 1)
         if li > 0:
-            d = (d @ net[2 * li].astype(np.float64)) * _act_grad(acts[li], activation)
+            d = (d @ net[2 * li].astype(_FT())) * _act_grad(acts[li], activation)
     return grads
 
 
@@ -180,7 +194,7 @@ def mlp_backward(net: list, acts: list, dout, activation: str) -> list[np.ndarra
 # loss and its adjoint
 # ---------------------------------------------------------------------------
 def _action_log_std(param, h: PPOHyper):
-    p = np.asarray(param, np.float64)
+    p = np.asarray(param, _FT())
     if h.std_type == "scalar":
         lo, hi = h.std_range
         inside = (p >= lo) & (p <= hi)
@@ -190,13 +204,13 @@ def _action_log_std(param, h: PPOHyper):
 
 def ppo_loss(mean, value, std_param, actions, old_log_probs, old_values, advantages, returns, h: PPOHyper):
     """Returns (loss, metrics[policy, value, entropy], d_mean, d_value, d_std_param)."""
-    mean = np.asarray(mean, np.float64)
-    value = np.asarray(value, np.float64).reshape(-1)
-    a = np.asarray(actions, np.float64)
-    olp = np.asarray(old_log_probs, np.float64)
-    ov = np.asarray(old_values, np.float64)
-    adv = np.asarray(advantages, np.float64)
-    ret = np.asarray(returns, np.float64)
+    mean = np.asarray(mean, _FT())
+    value = np.asarray(value, _FT()).reshape(-1)
+    a = np.asarray(actions, _FT())
+    olp = np.asarray(old_log_probs, _FT())
+    ov = np.asarray(old_values, _FT())
+    adv = np.asarray(advantages, _FT())
+    ret = np.asarray(returns, _FT())
     M = mean.shape[0]
     s, ds_dp = _action_log_std(std_param, h)
     r = (a - mean) * np.exp(-s)
@@ -287,7 +301,7 @@ class PPOState:
 
     @staticmethod
     def fresh(params: list, lr: float) -> "PPOState":
-        p = [np.asarray(x, np.float64) for x in params]
+        p = [np.asarray(x, _FT()) for x in params]
         return PPOState(p, [np.zeros_like(x) for x in p], [np.zeros_like(x) for x in p], 0, lr)
 
 
@@ -296,7 +310,7 @@ def returns_and_advantages(data: dict, horizon: int, num_envs: int, h: PPOHyper)
                    horizon, num_envs, h.gamma, h.gae_lambda, h.timeout_bootstrap == "current")
     if h.normalize_advantages:
         adv = normalize_advantages(adv, h.advantage_sample_std)
-    return np.asarray(adv, np.float64), np.asarray(ret, np.float64)
+    return np.asarray(adv, _FT()), np.asarray(ret, _FT())
 
 
 def minibatch_step(state: PPOState, batch: dict, h: PPOHyper) -> dict:

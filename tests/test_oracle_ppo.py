@@ -143,3 +143,40 @@ def test_clip_coefficient_and_adam_formula():
     # first step: m1 c1 = g, m2 c2 = g^2 -> p - lr * g / (|g| + eps)
     assert abs(p[0] - (1.0 - 0.1 * 0.5 / (0.5 + 1e-8))) < 1e-12
     assert math.isclose(m1[0], 0.05) and math.isclose(m2[0], 0.001 * 0.25)
+
+
+def test_oracle_matches_reference_torch_controlled_update():
+    """The reference's controlled PPO update check (examples/diagnose_ppo_update.py, run by
+    tests/golden/make_ppo_golden.py with the oracle standing in for Warp PPO): its Torch half's
+    final parameters, Adam moments and adaptive learning rate after 5 epochs x 4 minibatches
+    (adaptive KL, scalar std, separate clipping, timeout bootstrap 'current', sample-std
+    advantages) are matched by the oracle within that check's thresholds (maximum absolute
+    error 2e-4 for parameters and moments, 1e-7 for the learning rate)."""
+    import numpy as np
+
+    from oracle import ppo_np as P
+    from robolearn_b200.ppo.config import PPOConfig
+    from tests import _golden as G
+
+    g = G.load("ppo_controlled_update.npz")
+    cfg = PPOConfig(hidden_dims=(16, 8), activation="elu", std_type="scalar", epochs=5, num_mini_batches=4,
+                    learning_rate=1.0e-3, schedule="adaptive", desired_kl=0.01, value_coefficient=1.0,
+                    value_loss_scale=1.0, entropy_coefficient=0.008, advantage_sample_std=True,
+                    timeout_bootstrap="current", separate_grad_clipping=True)
+    h = P.PPOHyper(**{k: getattr(cfg, k) for k in P.PPOHyper.__dataclass_fields__})
+    n = len([k for k in g if k.startswith("initial.")])
+    initial = [g[f"initial.{i}"] for i in range(n)]
+    np.testing.assert_array_equal(np.concatenate([x.ravel() for x in initial]),
+                                  np.concatenate([x.ravel() for x in P.init_params(7, 3, h, seed=cfg.seed)]))
+    data = {k[len("data."):]: v for k, v in g.items() if k.startswith("data.")}
+    state = P.PPOState.fresh(initial, cfg.learning_rate)
+    P.update(state, data, 4, 16, h, permutation=g["permutation"])
+    assert abs(state.lr - float(g["torch.learning_rate"])) < 1e-7
+    for i in range(n):
+        ref = g[f"torch.parameter.{i}"].reshape(-1)
+        assert np.abs(state.params[i].reshape(-1) - ref).max() < 2e-4, i
+        assert np.abs(state.m1[i].reshape(-1) - g[f"torch.exp_avg.{i}"].reshape(-1)).max() < 2e-4, i
+        assert np.abs(state.m2[i].reshape(-1) - g[f"torch.exp_avg_sq.{i}"].reshape(-1)).max() < 2e-4, i
+    # the reference's own check passed on the oracle when the fixture was made
+    assert float(g["report.torch_warp_parameters_max_abs_error"]) < 2e-4
+    assert float(g["report.returns_max_abs_error"]) < 1e-5 and float(g["report.advantages_max_abs_error"]) < 1e-5

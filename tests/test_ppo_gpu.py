@@ -274,3 +274,50 @@ def test_act_and_store():
     np.testing.assert_allclose(agent.values[rows].cpu().numpy(), v[:, 0], rtol=1e-5, atol=1e-6)
     with pytest.raises(ValueError):
         agent.store(3, obs, torch.ones(8), torch.zeros(8), torch.zeros(8), nxt)
+
+
+def test_cfg2_update_matches_oracle_at_the_reference_protocol_tolerances():
+    """Config 2 at full size: WarpPPO(48, 12, 4096 envs, 24 steps), actor / critic 512-256-128
+    ELU, 5 epochs x 4 minibatches of 24576 rows (split-K weight gradients, the large
+    minibatch gathers), clip 0.2, value coefficient 1.0, entropy 0.01, lr 1e-3, through the
+    captured update graph. Rollout with the config-2 distributions (obs ~N(0,1), actions =
+    initial means + N(0,1), rewards ~N(0,1), terminated ~Bernoulli(0.005), next values from
+    the critic on next observations ~N(0,1)). The float64 oracle runs the same update with
+    the device's own permutation; the thresholds are those of the reference's controlled
+    update check (examples/diagnose_ppo_update.py:197-206, maximum absolute errors): returns
+    and advantages 1e-5, every parameter and Adam moment 2e-4."""
+    cfg = PPOConfig(hidden_dims=(512, 256, 128), activation="elu", epochs=5, num_mini_batches=4, clip_ratio=0.2,
+                    value_coefficient=1.0, entropy_coefficient=0.01, learning_rate=1e-3, gamma=0.99, gae_lambda=0.95)
+    agent = WarpPPO(48, 12, 4096, 24, cfg)
+    initial = [p.detach().cpu().numpy().copy() for p in agent.parameters]
+    rng = np.random.default_rng(2026)
+    B, O, A = agent.batch_size, 48, 12
+    actor, critic, _ = P.split(initial, cfg.hidden_dims)
+    obs = rng.standard_normal((B, O)).astype(np.float32)
+    means, _ = P.mlp_forward(actor, obs, "elu")
+    values, _ = P.mlp_forward(critic, obs, "elu")
+    next_values, _ = P.mlp_forward(critic, rng.standard_normal((B, O)).astype(np.float32), "elu")
+    actions = (means + rng.standard_normal(means.shape)).astype(np.float32)
+    data = dict(observations=obs, actions=actions, means=means.astype(np.float32), stds=np.ones((B, A), np.float32),
+                values=values[:, 0].astype(np.float32), next_values=next_values[:, 0].astype(np.float32),
+                log_probs=(-0.5 * ((actions - means) ** 2 + np.log(2 * np.pi))).sum(1).astype(np.float32),
+                rewards=rng.standard_normal(B).astype(np.float32),
+                terminated=(rng.random(B) < 0.005).astype(np.int32), truncated=np.zeros(B, np.int32))
+    for k, v in data.items():
+        getattr(agent, k).copy_(torch.from_numpy(v))
+    agent.update()  # captured graph (first call: eager warm pass, capture, replay)
+    torch.cuda.synchronize()
+    perm = agent._perm.cpu().numpy()
+    assert np.array_equal(np.sort(perm), np.arange(B))
+    state = P.PPOState.fresh(initial, cfg.learning_rate)
+    out = P.update(state, data, agent.horizon, agent.num_envs, _hyper(cfg), permutation=perm)
+    assert np.abs(agent.advantages.cpu().numpy() - out["advantages"]).max() < 1e-5
+    assert np.abs(agent.returns.cpu().numpy() - out["returns"]).max() < 1e-5
+    sd = agent.state_dict()
+    for i, (got, ref) in enumerate(zip(agent.parameters, state.params)):
+        err = np.abs(got.detach().cpu().numpy().astype(np.float64).reshape(ref.shape) - ref).max()
+        assert err < 2e-4, ("parameter", i, err)
+        for name, moments in (("adam_m1", state.m1), ("adam_m2", state.m2)):
+            m_err = np.abs(sd[f"{name}_{i}"].reshape(ref.shape).astype(np.float64) - moments[i]).max()
+            assert m_err < 2e-4, (name, i, m_err)
+    assert agent.health_metrics()["optimizer_updates"] == 20
