@@ -19,13 +19,25 @@ learner data-parallel: every rank processes 4096 rows of the N x 4096 global bat
 ranks and gradients averaged with NCCL before Adam; ``value`` counts N x 4096-row
 updates per second (weak scaling).
 
-``--workload cfg5`` times config 5 instead (critic 1024 x 3 blocks, actor 128 x 2,
-FP32 recipe, a global batch of 32768 split over the ranks: strong scaling);
-``--workload ppo`` the config-2 WarpPPO update; ``--workload categorical`` the
-config-4 objective microbench. Only the JSON line goes to stdout.
+``optimizer_updates_per_s`` is the learner's optimizer-update rate (steps / s) beside
+that weak-scaled ``value``.
 
-``--impl reference`` times the CPU restatement of the reference update (the
-reference is Python/Torch and cannot travel to the GPU box) on all host cores.
+Extra keys of the FlashSAC line (``--no-extras`` leaves them out): ``cfg5``, config 5 of
+BASELINE.json (critic 1024 x 3 blocks, actor 128 x 2, FP32 recipe, a global batch of
+32768 split over the ranks: strong scaling) timed on every rank count with its own
+roofline, clocks and end-to-end figure; at N = 1 also ``ppo`` (the config-2 WarpPPO
+update with its CPU baseline) and ``cfg4`` (the config-4 categorical objective, HBM
+roofline, CPU baseline). ``cpu_baseline`` (N = 1) is the numpy restatement of the
+reference update on all host cores: one actor + critic and one critic update at batch
+4096, no extrapolation.
+
+``--workload cfg5 | ppo | categorical`` time one of those alone; ``--workload gemm`` one
+product shape of the update in isolation (the small case for ncu captures). Only the
+JSON line goes to stdout.
+
+``--impl reference`` times the CPU restatement of the reference update (the reference is
+Python/Torch and cannot travel to the GPU box) on all host cores: real batch-4096
+updates, at most six timed.
 """
 
 from __future__ import annotations
@@ -49,6 +61,13 @@ METRIC = "FlashSAC updates/s (obs123/act37, batch 4096)"
 # (strong scaling), critics 1024 x 3 blocks, actor 128 x 2 (defaults), FP32 recipe
 CFG5_METRIC = "FlashSAC cfg5 updates/s (obs123/act37, global batch 32768, critic 1024x3, FP32)"
 CFG5_BATCH = 32768
+CFG5_STEPS = 5  # timed cfg5 updates in the headline line's summary (about 1 s on one GPU)
+# DRAM traffic of the GEMM family over one cfg3 update pair: the per-launch
+# dram__bytes_read.sum + dram__bytes_write.sum of every product of one actor + critic
+# update pair, summed (ncu launch list with those metrics; see the profiles directory).
+# None until that capture exists.
+GEMM_TRAFFIC_PER_PAIR = None
+GEMM_TRAFFIC_SOURCE = "not captured"
 
 
 def parse():
@@ -62,13 +81,33 @@ def parse():
     p.add_argument("--precision", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ppo", action="store_true", help="leave the PPO summary out of the FlashSAC line")
-    p.add_argument("--workload", choices=("flashsac", "ppo", "categorical", "cfg5"), default="flashsac",
+    p.add_argument("--workload", choices=("flashsac", "ppo", "categorical", "cfg5", "gemm"), default="flashsac",
                    help="flashsac: the headline FlashSAC update; ppo: the cfg2 WarpPPO update (ms); "
                         "categorical: the cfg4 objective microbench; cfg5: the data-parallel FP32 config "
-                        "(global batch 32768 split over --gpus ranks)")
+                        "(global batch 32768 split over --gpus ranks); gemm: one tcgen05 product shape in "
+                        "isolation (the small case for ncu captures)")
+    p.add_argument("--no-extras", action="store_true",
+                   help="leave the ppo / cfg4 / cfg5 summaries out of the FlashSAC line")
+    g = p.add_argument_group("gemm workload: D[z] = A[z] B[z]^T with the update's forward epilogue")
+    g.add_argument("--gemm-m", type=int, default=8192)
+    g.add_argument("--gemm-n", type=int, default=2048)
+    g.add_argument("--gemm-k", type=int, default=512)
+    g.add_argument("--gemm-batch", type=int, default=2)
+    g.add_argument("--gemm-kind", type=int, choices=(0, 1), default=0, help="0 fp16 operands, 1 3xTF32")
+    g.add_argument("--gemm-a-major", type=int, choices=(0, 1), default=0)
+    g.add_argument("--gemm-b-major", type=int, choices=(0, 1), default=0)
+    g.add_argument("--gemm-tile-n", type=int, default=0)
+    g.add_argument("--gemm-splits", type=int, default=1)
+    g.add_argument("--gemm-stats", action="store_true", help="32-row column moments in the epilogue")
+    g.add_argument("--gemm-plane", action="store_true", help="fp16 / tf32 operand-plane copy of the output")
+    g.add_argument("--gemm-residual", action="store_true")
+    g.add_argument("--gemm-in-place", action="store_true", help="residual = the output itself")
+    g.add_argument("--gemm-act", type=int, choices=(0, 1, 2), default=0, help="epilogue activation: 1 ELU, 2 tanh")
     args = p.parse_args()
     if args.steps is None:
         args.steps = 400 if args.workload == "flashsac" and args.impl == "b200" else 40
+    if args.no_ppo:
+        args.no_extras = True
     return args
 
 
@@ -202,18 +241,35 @@ def gemm_roofline(L, peak_tflops):
             "flops_per_pair": flops, "ms_per_pair": round(sec * 1e3, 4)}
 
 
-def cpu_update_rate(batch: int, pairs: int = 1, critic=(512, 2), actor=(256, 2)):
-    """CPU restatement of the reference update (oracle, float32, all host cores): updates/s at ``batch``.
+def cpu_threads() -> int:
+    """Size the host thread pools of the CPU restatement to every core this process may run
+    on: BLAS (the products) and the oracle's column-chunked batch-norm passes, which never
+    run at the same time (so the cores are not oversubscribed). Returns the core count."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
 
-    Returns (updates_per_s_at_batch, seconds, cores). Used by the cpu_baseline field
-    and by ``--impl reference``; the oracle is the checker, never the product path.
-    """
+    from oracle import flashsac_np as fs
+
+    cores = len(os.sched_getaffinity(0))
+    np.ones((8, 8), np.float32) @ np.ones((8, 8), np.float32)  # load BLAS so its pool can be sized
+    threadpool_limits(limits=cores)
+    fs.set_threads(cores)
+    return cores
+
+
+def cpu_update_rate(batch: int, updates: int = 2, critic=(512, 2), actor=(256, 2)):
+    """CPU restatement of the reference update (oracle, float32, all host cores): ``updates``
+    real updates at ``batch`` rows, alternating actor + critic and critic-only phases like
+    ``update()`` with ``actor_update_period`` = 2. Returns (updates/s, seconds, cores).
+    Used by the cpu_baseline field and by ``--impl reference``; the oracle is the checker,
+    never the product path."""
     import numpy as np
 
     from oracle import flashsac_np as fs
     from robolearn_b200.flashsac.config import FlashSACConfig
     from robolearn_b200.flashsac.learner import _init_reference_weights
 
+    cores = cpu_threads()
     d = fs.Dims(obs=OBS, act=ACT, actor_hidden=actor[0], actor_blocks=actor[1], critic_hidden=critic[0],
                 critic_blocks=critic[1], bins=101, min_v=-10.0, max_v=10.0)
     a0, c0, lt = _init_reference_weights(OBS, OBS, ACT, FlashSACConfig(
@@ -243,24 +299,17 @@ def cpu_update_rate(batch: int, pairs: int = 1, critic=(512, 2), actor=(256, 2))
     nn = rng.standard_normal((B, ACT)).astype(np.float32)
     h = fs.Hyper(tau=0.005, lr_end=3e-4, target_entropy=float(0.5 * ACT * np.log(2 * np.pi * np.e * 0.15**2)))
     t0 = time.perf_counter()
-    for i in range(2 * pairs):
+    for i in range(updates):
         st, _ = fs.update_networks(st, bt, an, nn, d, h, do_actor=(i % 2 == 0), dtype=np.float32)
     sec = time.perf_counter() - t0
-    return 2 * pairs / sec, sec, len(os.sched_getaffinity(0))
+    return updates / sec, sec, cores
 
 
-def cpu_update_seconds(full_batch: int, b1: int, b2: int, critic=(512, 2), actor=(256, 2)):
-    """Seconds per update of the CPU restatement at ``full_batch`` rows from one update pair at
-    ``b1`` rows and one at ``b2``: t(B) = t(b2) + (B - b2) (t(b2) - t(b1)) / (b2 - b1). The
-    parameter-sized work (Adam, projection, EMA) is the intercept and the row work the
-    slope, so the intercept is not multiplied up. Returns (seconds, measured seconds, cores)."""
-    _, s1, cores = cpu_update_rate(b1, 1, critic, actor)
-    _, s2, _ = cpu_update_rate(b2, 1, critic, actor)
-    t1, t2 = s1 / 2, s2 / 2
-    return t2 + max(t2 - t1, 0.0) / (b2 - b1) * (full_batch - b2), s1 + s2, cores
-
-
-def run_b200(args, rank, world, local_rank):
+def run_flashsac(workload: str, precision: str, steps: int, warmup: int, world: int, local_rank: int):
+    """Device-timed and end-to-end FlashSAC updates. ``workload`` "cfg3": batch 4096 per rank
+    (weak scaling), ``precision`` as given; "cfg5": global batch 32768 split over the ranks,
+    critic 1024 x 3, actor 128 x 2, FP32 recipe (strong scaling). Returns (learner, device
+    seconds, end-to-end seconds, host->device bytes per step, launches, clocks)."""
     import torch
 
     device = torch.device("cuda", local_rank)
@@ -270,12 +319,12 @@ def run_b200(args, rank, world, local_rank):
         from robolearn_b200.flashsac.dp import DataParallel
 
         dp = DataParallel()
-    if args.workload == "cfg5":
+    if workload == "cfg5":
         if CFG5_BATCH % world:
             raise SystemExit("cfg5 needs a rank count that divides 32768")
         L, R, feed = build("fp32", device, seed=0, dp=dp, batch=CFG5_BATCH // world, critic=(1024, 3), actor=(128, 2))
     else:
-        L, R, feed = build(args.precision, device, seed=0, dp=dp)
+        L, R, feed = build(precision, device, seed=0, dp=dp)
     for phase in (True, False):  # one eager pass loads every kernel module before capture
         for f in feed:
             f()
@@ -287,7 +336,7 @@ def run_b200(args, rank, world, local_rank):
     def step(i):
         graphs[i % period == 0].replay()
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     if world > 1:
@@ -298,13 +347,13 @@ def run_b200(args, rank, world, local_rank):
     with Clocks(local_rank) as clocks:
         torch.cuda.synchronize()
         e0.record()
-        for i in range(args.steps):
-            step(args.warmup + i)
+        for i in range(steps):
+            step(warmup + i)
         e1.record()
         torch.cuda.synchronize()
     sec = e0.elapsed_time(e1) / 1e3
-    launches = sum(count_launches(feed) + count_launches(L.programs[(args.warmup + i) % period == 0])
-                   for i in range(args.steps))
+    launches = sum(count_launches(feed) + count_launches(L.programs[(warmup + i) % period == 0])
+                   for i in range(steps))
     # ---- end to end through the public replay + learner API with host buffers:
     # each step copies one vector-environment step of transitions from pinned host
     # memory, ingests it, runs the update and reads the critic loss back to the host.
@@ -343,9 +392,9 @@ def run_b200(args, rank, world, local_rank):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     upload(0)
-    for i in range(args.steps):
+    for i in range(steps):
         b = i % 2
-        if i + 1 < args.steps:
+        if i + 1 < steps:
             upload(i + 1)
         main.wait_event(landed[b])
         d = dev[b]
@@ -356,6 +405,8 @@ def run_b200(args, rank, world, local_rank):
     t1.record()
     torch.cuda.synchronize()
     e2e_sec = t0.elapsed_time(t1) / 1e3
+    for gr in graphs.values():  # graphs holding NCCL calls go before the process group does
+        gr.reset()
     return L, sec, e2e_sec, h2d, launches, clocks.summary()
 
 
@@ -408,24 +459,38 @@ def ppo_rollout(agent, seed: int = 0) -> dict:
     return data
 
 
-def ppo_cpu_minibatch_seconds() -> tuple[float, int]:
-    """One oracle minibatch step (24576 rows, forward + loss + backward + clip + Adam) on the host."""
+def ppo_cpu_update_seconds() -> tuple[float, int]:
+    """One full cfg2 update of the oracle restatement in float32 on all host cores: GAE and
+    advantage normalisation over 4096 x 24 steps, then 5 epochs x 4 minibatches of 24576
+    rows (forward, loss, backward, clipping, Adam), the cfg2 rollout distributions."""
     import numpy as np
 
     from oracle import ppo_np as P
 
+    cores = cpu_threads()
     h = P.PPOHyper(hidden_dims=PPO_HIDDEN, activation="elu", epochs=5, num_mini_batches=4, clip_ratio=0.2,
                    value_coefficient=1.0, entropy_coefficient=0.01, learning_rate=1e-3)
-    params = P.init_params(PPO_OBS, PPO_ACT, h, seed=42)
-    M = PPO_ENVS * PPO_T // 4
+    n = PPO_ENVS * PPO_T
     rng = np.random.default_rng(0)
-    batch = dict(observations=rng.normal(size=(M, PPO_OBS)), actions=rng.normal(size=(M, PPO_ACT)),
-                 means=np.zeros((M, PPO_ACT)), stds=np.ones((M, PPO_ACT)), log_probs=rng.normal(-15, 1, size=M),
-                 values=rng.normal(size=M), advantages=rng.normal(size=M), returns=rng.normal(size=M))
-    state = P.PPOState.fresh(params, 1e-3)
-    t0 = time.perf_counter()
-    P.minibatch_step(state, batch, h)
-    return time.perf_counter() - t0, len(os.sched_getaffinity(0))
+    f32 = lambda x: np.asarray(x, np.float32)  # noqa: E731
+    means = f32(0.1 * rng.standard_normal((n, PPO_ACT)))
+    actions = f32(means + rng.standard_normal((n, PPO_ACT)))
+    data = dict(observations=f32(rng.standard_normal((n, PPO_OBS))), actions=actions, means=means,
+                stds=np.ones((n, PPO_ACT), np.float32),
+                log_probs=f32((-0.5 * ((actions - means) ** 2 + 1.8378770664093453)).sum(1)),
+                values=f32(rng.standard_normal(n)), rewards=f32(rng.standard_normal(n)),
+                next_values=f32(rng.standard_normal(n)), terminated=(rng.random(n) < 0.005).astype(np.int32),
+                truncated=np.zeros(n, np.int32))
+    perm = rng.permutation(n)
+    P.set_dtype(np.float32)
+    try:
+        state = P.PPOState.fresh(P.init_params(PPO_OBS, PPO_ACT, h, seed=42), h.learning_rate)
+        t0 = time.perf_counter()
+        P.update(state, data, PPO_T, PPO_ENVS, h, permutation=perm)
+        sec = time.perf_counter() - t0
+    finally:
+        P.set_dtype(np.float64)
+    return sec, cores
 
 
 def run_ppo(args) -> dict:
@@ -504,9 +569,10 @@ def run_ppo(args) -> dict:
                                   "5 epochs x 4 minibatches)", "global_batch": agent.batch_size,
                       "parallelism": "single", "l2": "rollout + activations > 126 MB L2 (no flush needed)"}}
     if not args.no_cpu_baseline:
-        sec, cores = ppo_cpu_minibatch_seconds()
-        out["cpu_baseline"] = {"value": sec * 20 * 1e3, "unit": "ms/update", "cores": cores, "kind": "port",
-                               "sample": f"one minibatch step of 24576 rows ({sec:.1f} s, numpy), x20 minibatches"}
+        sec, cores = ppo_cpu_update_seconds()
+        out["cpu_baseline"] = {"value": sec * 1e3, "unit": "ms/update", "cores": cores, "kind": "port",
+                               "sample": "one full update (GAE + 5 epochs x 4 minibatches of 24576 rows) of the "
+                                         "numpy restatement, float32, no extrapolation"}
     return out
 
 
@@ -610,6 +676,103 @@ def run_categorical(args) -> dict:
     return out
 
 
+# ---------------------------------------------------------------------------
+# one tcgen05 product shape in isolation (the small, self-contained ncu case)
+# ---------------------------------------------------------------------------
+def run_gemm(args) -> dict:
+    """Times ``--steps`` launches of one product ``D[z] = A[z] B[z]^T`` with the forward
+    epilogue the update uses (bias, optional residual, 32-row column moments, operand-plane
+    copy of the output), CUDA events on the launching stream after ``--warmup`` launches."""
+    import torch
+
+    from robolearn_b200 import _native as N
+    from robolearn_b200 import dense
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    m, n, k, z, kind = args.gemm_m, args.gemm_n, args.gemm_k, args.gemm_batch, args.gemm_kind
+    dt = torch.float16 if kind == 0 else torch.float32
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def operand(rows: int, major: int):
+        inner, outer = (k, rows) if major == 0 else (rows, k)
+        ld = dense.operand_ld(inner, kind)
+        t = torch.zeros(z, outer, ld, device=dev, dtype=dt)
+        t[:, :, :inner] = (torch.randn(z, outer, inner, device=dev, generator=g) / k**0.5).to(dt)
+        return t, ld
+
+    A, lda = operand(m, args.gemm_a_major)
+    B, ldb = operand(n, args.gemm_b_major)
+    kw = {}
+    if kind == 1:
+        A, a_lo = dense.tf32_split(A)
+        B, b_lo = dense.tf32_split(B)
+        kw.update(a_lo=a_lo, b_lo=b_lo)
+    ldd = dense.operand_ld(n, 1)
+    splits = max(1, args.gemm_splits)
+    D = torch.zeros(splits, z, m, ldd, device=dev)
+    kw.update(d=D, ldd=ldd, d_batch_stride=m * ldd)
+    if splits > 1:
+        kw.update(k_splits=splits, d_split_stride=z * m * ldd)
+    else:
+        kw.update(bias=torch.randn(z, n, device=dev, generator=g), bias_batch_stride=n)
+    if args.gemm_in_place and splits == 1:
+        kw.update(residual=D[0], ldr=ldd, residual_batch_stride=m * ldd)
+    elif args.gemm_residual and splits == 1:
+        kw.update(residual=torch.randn(z, m, n, device=dev, generator=g), ldr=n, residual_batch_stride=m * n)
+    groups = (m + 31) // 32
+    if args.gemm_stats and splits == 1:
+        kw.update(stat_mean=torch.zeros(z, groups, n, device=dev), stat_m2=torch.zeros(z, groups, n, device=dev),
+                  stat_batch_stride=groups * n)
+    keep = []
+    if args.gemm_plane and splits == 1:
+        pld = dense.operand_ld(n, kind)
+        if kind == 0:
+            h = torch.zeros(z, m, pld, device=dev, dtype=torch.float16)
+            keep.append(h)
+            kw["out_plane"] = N.Plane(h16=h.data_ptr(), ld=pld, twin_stride=m * pld)
+        else:
+            hi, lo = torch.zeros(z, m, pld, device=dev), torch.zeros(z, m, pld, device=dev)
+            keep += [hi, lo]
+            kw["out_plane"] = N.Plane(hi=hi.data_ptr(), lo=lo.data_ptr(), ld=pld, twin_stride=m * pld)
+    if args.gemm_act:
+        kw["activation"] = args.gemm_act
+    plan = dense.DensePlan(kind=kind, m=m, n=n, k=k, a=A, b=B, lda=lda, ldb=ldb, a_major=args.gemm_a_major,
+                           b_major=args.gemm_b_major, batch=z, a_batch_stride=A[0].numel(),
+                           b_batch_stride=B[0].numel(), tile_n=args.gemm_tile_n, **kw)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        plan.run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        plan.run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / max(args.steps, 1)
+    el = 2 if kind == 0 else 8
+    out_bytes = z * m * n * 4 * splits + (z * m * n * el if args.gemm_plane and splits == 1 else 0)
+    in_bytes = z * (m + n) * k * el + (z * m * n * 4 if args.gemm_residual and splits == 1 else 0)
+    flops = 2.0 * z * m * n * k * (1 if kind == 0 else 3)
+    pk, src = peaks()
+    peak = pk["bf16_tflops"] if kind == 0 else pk["bf16_tflops"] / 2
+    tflops = flops / us / 1e6
+    del keep
+    return {"metric": f"tcgen05 GEMM us/launch (M {m}, N {n}, K {k}, batch {z}, {'fp16' if kind == 0 else '3xTF32'})",
+            "value": us, "unit": "us/launch", "higher_is_better": False, "ms_per_step": us / 1e3,
+            "gpu_launches": args.steps, "dtype": "fp16" if kind == 0 else "f32 (tf32x3)",
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "traffic": None, "algorithmic_bytes": in_bytes + out_bytes,
+                         "peak_source": f"{src} bf16_tflops" + (" / 2 (tf32 dense rate; FLOPs per tf32 pass)"
+                                                                 if kind == 1 else " (burst)")},
+            "config": {"workload": "one product of the update in isolation", "tile_n": plan.tile_n,
+                       "splits": splits, "stats": args.gemm_stats, "plane": args.gemm_plane,
+                       "residual": args.gemm_residual or args.gemm_in_place, "activation": args.gemm_act,
+                       "a_major": args.gemm_a_major, "b_major": args.gemm_b_major,
+                       "l2": "operands resident (launch-to-launch timing of one shape)"}}
+
+
 _JSON_OUT = None
 
 
@@ -619,6 +782,100 @@ def emit(line: str) -> None:
     out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
     out.write(line + "\n")
     out.flush()
+
+
+REF_MAX_STEPS = 6  # timed CPU updates of the reference arm (about 10 s each at batch 4096 on 16 cores)
+
+
+def reference_line(args, base) -> dict:
+    """``--impl reference``: the CPU restatement of the reference path on all host cores, on
+    the same workload, metric and unit as the b200 arm. FlashSAC cfg3: real updates at batch
+    4096 (alternating actor + critic and critic-only phases, as ``update()`` does), one
+    warm-up update and at most ``REF_MAX_STEPS`` timed. cfg5 (30 TFLOP per update, beyond a
+    bounded CPU sample): one update pair at 1024 and at 2048 rows, time extrapolated
+    linearly in the rows to 32768, labelled as such. PPO: one full cfg2 update. The CPU
+    path has no warm-up to do (no compilation, no caches to fill at these sizes)."""
+    if args.workload == "ppo":
+        sec, cores = ppo_cpu_update_seconds()
+        value = sec * 1e3
+        return {"metric": PPO_METRIC, "impl": "reference", "value": value, "unit": "ms/update",
+                "higher_is_better": False, "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": value,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "cfg2 WarpPPO update, CPU restatement of the reference (oracle port)"},
+                "cpu_baseline": {"value": value, "unit": "ms/update", "cores": cores, "kind": "port",
+                                 "sample": "one full update (GAE + 5 epochs x 4 minibatches of 24576 rows), float32"},
+                "e2e": {"value": value, "unit": "ms/update", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "cfg5":
+        rates = []
+        for rows in (1024, 2048):
+            r, sec, cores = cpu_update_rate(rows, 2, critic=(1024, 3), actor=(128, 2))
+            rates.append((rows, 1.0 / r))
+        (b1, t1), (b2, t2) = rates
+        per_update = t2 + max(t2 - t1, 0.0) / (b2 - b1) * (CFG5_BATCH - b2)
+        value = 1.0 / per_update
+        return dict(base, metric=CFG5_METRIC, scaling="strong", impl="reference", value=value, steps=2, warmup=0,
+                    ms_per_step=per_update * 1e3, dtype="f32",
+                    config={"workload": "cfg5 FlashSAC update, CPU restatement of the reference (oracle port)",
+                            "global_batch": CFG5_BATCH, "parallelism": "cpu"},
+                    cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
+                                  "sample": f"one actor+critic update pair at {b1} rows and one at {b2} "
+                                            f"(EXTRAPOLATED linearly in the rows to {CFG5_BATCH})"},
+                    e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+    steps = min(args.steps, REF_MAX_STEPS)
+    value, sec, cores = cpu_update_rate(BATCH, steps)  # the CPU path has nothing to warm up
+    return dict(base, impl="reference", value=value, steps=steps, warmup=0, steps_requested=args.steps,
+                ms_per_step=1e3 / value, dtype="f32",
+                config={"workload": "cfg3 FlashSAC update, CPU restatement of the reference (oracle port)",
+                        "global_batch": BATCH, "parallelism": "cpu"},
+                cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
+                              "sample": f"{steps} real updates at batch {BATCH} (alternating actor + critic "
+                                        "and critic-only, no extrapolation), float32"},
+                e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+
+
+def flashsac_summary(workload: str, precision: str, steps: int, warmup: int, world: int, local_rank: int) -> dict:
+    """One FlashSAC workload timed on every rank (device time and end-to-end: max over ranks)
+    with its GEMM-family roofline; the learner is released before returning."""
+    import torch
+
+    L, sec, e2e_sec, h2d, launches, clocks = run_flashsac(workload, precision, steps, warmup, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([sec, e2e_sec], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec, e2e_sec = t.tolist()
+    pk, src = peaks()
+    if workload == "cfg5":
+        # three tf32 tensor passes per product (counted in the executed FLOPs) at the dense
+        # tf32 rate, half the bf16 rate
+        roof = gemm_roofline(L, pk["bf16_tflops"] / 2)
+        roof["peak_source"] = f"{src} bf16_tflops / 2 (dense tf32 rate; FLOPs counted per tf32 pass, 3 per product)"
+        rows, scaling, dtype = CFG5_BATCH, "strong", "f32 (3xTF32 products)"
+        workload_name = ("cfg5 data-parallel FlashSAC update (obs 123, act 37, global batch 32768 split over the "
+                         "ranks, critic 1024x3, actor 128x2, 101 atoms, FP32 recipe)")
+        value = steps / sec  # global-batch updates per second
+    else:
+        roof = gemm_roofline(L, pk["bf16_tflops"])
+        roof["peak_source"] = f"{src} bf16_tflops (burst; fp16 dense rate taken equal)"
+        roof["traffic"] = GEMM_TRAFFIC_PER_PAIR
+        roof["traffic_source"] = GEMM_TRAFFIC_SOURCE
+        rows, scaling, dtype = BATCH * world, "weak", precision
+        workload_name = ("cfg3 FlashSAC update (obs 123, act 37, batch 4096 per GPU, critic 512x2, actor 256x2, "
+                         "101 atoms)")
+        value = world * steps / sec  # 4096-row batches per second over all ranks
+    out = {"value": value, "optimizer_updates_per_s": steps / sec, "ms_per_step": sec / steps * 1e3,
+           "steps": steps, "warmup": warmup, "scaling": scaling, "dtype": dtype, "gpu_launches": launches,
+           "clocks": clocks, "roofline": roof,
+           "config": {"workload": workload_name, "global_batch": rows, "seq_len": None,
+                      "parallelism": f"dp{world}" if world > 1 else "single",
+                      "l2": "working set > 126 MB L2 (no flush needed)"},
+           "e2e": {"value": value * sec / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": 4}}
+    del L
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -633,72 +890,15 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     base = {"metric": METRIC, "unit": "updates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"}
-    if args.workload == "categorical":
-        if rank != 0:
-            return
-        out = dict(n_gpus=1, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None, data="synthetic",
-                   impl="b200", **run_categorical(args))
-        emit(json.dumps(out))
-        return
-    if args.workload == "ppo":
-        if rank != 0:
-            return
-        if args.impl == "reference":
-            sec, cores = ppo_cpu_minibatch_seconds()
-            value = sec * 20 * 1e3
-            emit(json.dumps({"metric": PPO_METRIC, "impl": "reference", "value": value, "unit": "ms/update",
-                              "higher_is_better": False, "n_gpus": args.gpus, "steps": 1, "warmup": 0,
-                              "ms_per_step": value, "dtype": "f64", "data": "synthetic",
-                              "config": {"workload": "cfg2 WarpPPO update, CPU restatement (oracle port)"},
-                              "cpu_baseline": {"value": value, "unit": "ms/update", "cores": cores, "kind": "port",
-                                               "sample": "one minibatch step of 24576 rows, x20 minibatches"},
-                              "e2e": {"value": value, "unit": "ms/update", "h2d_bytes_per_step": 0,
-                                      "d2h_bytes_per_step": 0}}))
-            return
-        out = dict(n_gpus=args.gpus, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None,
-                   data="synthetic", impl="b200", **run_ppo(args))
-        emit(json.dumps(out))
-        return
-    if args.impl == "reference" and args.workload == "cfg5":
-        if rank != 0:
-            return
-        b1, b2 = 64, 256
-        times = []
-        for i in range(min(args.warmup, 1) + min(args.steps, 3)):  # about 15 s of CPU work each
-            sec, _, cores = cpu_update_seconds(CFG5_BATCH, b1, b2, critic=(1024, 3), actor=(128, 2))
-            if i >= min(args.warmup, 1):
-                times.append(sec)
-        per_update = statistics.median(times)
-        value = 1.0 / per_update
-        out = dict(base, metric=CFG5_METRIC, scaling="strong", impl="reference", value=value,
-                   ms_per_step=per_update * 1e3, dtype="f32",
-                   config={"workload": "cfg5 FlashSAC update, CPU restatement of the reference (oracle port)",
-                           "global_batch": CFG5_BATCH, "parallelism": "cpu"},
-                   cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
-                                 "sample": f"one actor+critic update pair at batch {b1} and one at {b2} per step, "
-                                           f"time extrapolated linearly in the batch to {CFG5_BATCH}"},
-                   e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
-        emit(json.dumps(out))
-        return
+    common = dict(n_gpus=1, steps=args.steps, warmup=args.warmup, scaling="weak", vs_baseline=None, data="synthetic")
     if args.impl == "reference":
-        if rank != 0:
-            return
-        b1, b2 = BATCH // 8, BATCH // 4
-        times = []
-        for i in range(args.warmup + args.steps):
-            sec, _, cores = cpu_update_seconds(BATCH, b1, b2)
-            if i >= args.warmup:
-                times.append(sec)
-        per_update = statistics.median(times)
-        value = 1.0 / per_update
-        out = dict(base, impl="reference", value=value, ms_per_step=per_update * 1e3, dtype="f32",
-                   config={"workload": "cfg3 FlashSAC update, CPU restatement of the reference (oracle port)",
-                           "global_batch": BATCH, "parallelism": "cpu"},
-                   cpu_baseline={"value": value, "unit": "updates/s", "cores": cores, "kind": "port",
-                                 "sample": f"one actor+critic update pair at batch {b1} and one at {b2} per step, "
-                                           f"time extrapolated linearly in the batch to {BATCH}"},
-                   e2e={"value": value, "unit": "updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
-        emit(json.dumps(out))
+        if rank == 0:  # the CPU arm runs once per job; other ranks exit without work
+            emit(json.dumps(reference_line(args, base)))
+        return
+    if args.workload in ("categorical", "gemm", "ppo"):
+        if rank == 0:
+            run = {"categorical": run_categorical, "gemm": run_gemm, "ppo": run_ppo}[args.workload]
+            emit(json.dumps(dict(common, impl="b200", **run(args))))
         return
     import torch
 
@@ -709,60 +909,35 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    L, sec, e2e_sec, h2d, launches, clocks = run_b200(args, rank, world, local_rank)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([sec, e2e_sec], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        sec, e2e_sec = t.tolist()
-    pk, src = peaks()
     if args.workload == "cfg5":
-        # three tf32 tensor passes per product (counted in the executed FLOPs) at the dense
-        # tf32 rate, half the bf16 rate
-        roof = gemm_roofline(L, pk["bf16_tflops"] / 2)
-        roof["peak_source"] = f"{src} bf16_tflops / 2 (dense tf32 rate; FLOPs counted per tf32 pass, 3 per product)"
-        out = dict(base, metric=CFG5_METRIC, scaling="strong", impl="b200", value=args.steps / sec,
-                   ms_per_step=sec / args.steps * 1e3, dtype="f32 (3xTF32 products)", gpu_launches=launches,
-                   clocks=clocks, roofline=roof,
-                   config={"workload": "cfg5 data-parallel FlashSAC update (obs 123, act 37, global batch 32768 "
-                                       "split over the ranks, critic 1024x3, actor 128x2, 101 atoms, FP32 recipe)",
-                           "global_batch": CFG5_BATCH, "seq_len": None,
-                           "parallelism": f"dp{world}" if world > 1 else "single",
-                           "l2": "working set > 126 MB L2 (no flush needed)"},
-                   e2e={"value": args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": 4})
-        if rank == 0:
-            emit(json.dumps(out))
-        if world > 1:
-            import torch.distributed as dist
+        head = flashsac_summary("cfg5", "fp32", args.steps, args.warmup, world, local_rank)
+        out = dict(base, impl="b200", metric=CFG5_METRIC, **head)
+    else:
+        head = flashsac_summary("cfg3", args.precision, args.steps, args.warmup, world, local_rank)
+        out = dict(base, impl="b200", **head)
+        if not args.no_extras:
+            # config 5 (strong scaling of the global batch 32768) on every rank count
+            c5 = flashsac_summary("cfg5", "fp32", CFG5_STEPS, 3, world, local_rank)
+            out["cfg5"] = dict(metric=CFG5_METRIC, unit="updates/s", **c5)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            rate, csec, cores = cpu_update_rate(BATCH, 2)
+            out["cpu_baseline"] = {"value": rate, "unit": "updates/s", "cores": cores, "kind": "port",
+                                   "sample": f"one actor + critic update and one critic update at batch {BATCH} "
+                                             f"({csec:.1f} s, numpy restatement in float32, no extrapolation)"}
+        if rank == 0 and world == 1 and not args.no_extras:
+            import types
 
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-    roof = gemm_roofline(L, pk["bf16_tflops"])
-    roof["peak_source"] = f"{src} bf16_tflops (burst; fp16 dense rate taken equal)"
-    out = dict(base, impl="b200", value=world * args.steps / sec, ms_per_step=sec / args.steps * 1e3,
-               dtype=args.precision, gpu_launches=launches, clocks=clocks, roofline=roof,
-               config={"workload": "cfg3 FlashSAC update (obs 123, act 37, batch 4096 per GPU, critic 512x2, "
-                                   "actor 256x2, 101 atoms)", "global_batch": BATCH * world, "seq_len": None,
-                       "parallelism": f"dp{world}" if world > 1 else "single",
-                       "l2": "working set > 126 MB L2 (no flush needed)"},
-               e2e={"value": world * args.steps / e2e_sec, "unit": "updates/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": 4})
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        b1, b2 = BATCH // 8, BATCH // 4
-        per_update, csec, cores = cpu_update_seconds(BATCH, b1, b2)
-        out["cpu_baseline"] = {"value": 1.0 / per_update, "unit": "updates/s", "cores": cores, "kind": "port",
-                               "sample": f"one actor+critic update pair at batch {b1} and one at {b2} "
-                                         f"({csec:.1f} s), time extrapolated linearly in the batch to {BATCH}"}
-    if rank == 0 and world == 1 and not args.no_ppo:
-        # the cfg2 PPO update beside the headline (full line: --workload ppo)
-        import types
-
-        pp = run_ppo(types.SimpleNamespace(steps=10, warmup=3, no_cpu_baseline=True))
-        out["ppo"] = {"metric": pp["metric"], "value": pp["value"], "unit": pp["unit"],
-                      "roofline_frac": pp["roofline"]["frac"], "e2e": pp["e2e"]["value"]}
+            sub = types.SimpleNamespace(steps=10, warmup=3, no_cpu_baseline=args.no_cpu_baseline)
+            pp = run_ppo(sub)
+            out["ppo"] = {k: pp[k] for k in ("metric", "value", "unit", "higher_is_better", "ms_per_step",
+                                             "gpu_launches", "clocks", "roofline", "e2e", "config")
+                          if k in pp}
+            if "cpu_baseline" in pp:
+                out["ppo"]["cpu_baseline"] = pp["cpu_baseline"]
+            sub = types.SimpleNamespace(steps=20, warmup=3, no_cpu_baseline=args.no_cpu_baseline)
+            cat = run_categorical(sub)
+            out["cfg4"] = {k: cat[k] for k in ("metric", "value", "unit", "higher_is_better", "roofline", "config",
+                                               "rows_per_s", "cpu_baseline") if k in cat}
     if rank == 0:
         emit(json.dumps(out))
     if world > 1:
