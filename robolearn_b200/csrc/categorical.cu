@@ -78,35 +78,36 @@ struct Args {
 inline int grid_for(int batch) { return std::max(1, std::min((batch + kRowsPerBlock - 1) / kRowsPerBlock, kMaxGrid)); }
 inline int groups_for(int grid) { return (grid + kGroup - 1) / kGroup; }
 
-// Row pitch of the per-row shared arrays: >= 8E and = 8 (mod 32), so that the strided
-// (k = sub + 8 s) and blocked (j = E sub + s) accesses of the four rows of a warp spread
-// over the banks.
-template <int E>
+// Row pitch of the per-row shared arrays: >= G E and = G (mod 32), so that the strided
+// (k = sub + G s) and blocked (j = E sub + s) accesses of the rows of a warp spread over
+// the banks.
+template <int G, int E>
 __host__ __device__ constexpr int pitch() {
-    return 8 * E + ((8 - (8 * E) % 32) + 32) % 32;
+    return G * E + ((G - (G * E) % 32) + 32) % 32;
 }
 
+// Sum / maximum over the G lanes of a row.
+template <int G>
 __device__ __forceinline__ float gsum(float v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 4);
+#pragma unroll
+    for (int d = 1; d < G; d <<= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
     return v;
 }
 
+template <int G>
 __device__ __forceinline__ float gmax(float v) {
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+#pragma unroll
+    for (int d = 1; d < G; d <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
     return v;
 }
 
 // Segmented inclusive scan over the blocked elements of a row (lane sub holds j = E sub + s)
 // with monotone non-decreasing keys: each run's total goes to out[key] at the run's last
 // element (out[key] += total when add). Keys outside [0, bins) are never written.
-template <int E>
+template <int G, int E>
 __device__ __forceinline__ void scatter_runs(const int (&key)[E], const float (&val)[E], float* out, int bins,
                                              bool add) {
-    const int sub = threadIdx.x & 7;
+    const int sub = threadIdx.x & (G - 1);
     float acc[E];
     acc[0] = val[0];
 #pragma unroll
@@ -115,39 +116,39 @@ __device__ __forceinline__ void scatter_runs(const int (&key)[E], const float (&
     float run = acc[E - 1];
     bool open = key[0] == key[E - 1];
 #pragma unroll
-    for (int d = 1; d < 8; d <<= 1) {
-        const int ok = __shfl_up_sync(0xffffffffu, tail, d, 8);
-        const float os = __shfl_up_sync(0xffffffffu, run, d, 8);
-        const int oo = __shfl_up_sync(0xffffffffu, static_cast<int>(open), d, 8);
+    for (int d = 1; d < G; d <<= 1) {
+        const int ok = __shfl_up_sync(0xffffffffu, tail, d, G);
+        const float os = __shfl_up_sync(0xffffffffu, run, d, G);
+        const int oo = __shfl_up_sync(0xffffffffu, static_cast<int>(open), d, G);
         if (sub >= d && open && ok == tail) {
             run = os + run;
             open = oo != 0;
         }
     }
-    const int prev_tail = __shfl_up_sync(0xffffffffu, tail, 1, 8);
-    const float prev_run = __shfl_up_sync(0xffffffffu, run, 1, 8);
+    const int prev_tail = __shfl_up_sync(0xffffffffu, tail, 1, G);
+    const float prev_run = __shfl_up_sync(0xffffffffu, run, 1, G);
     const float carry = (sub > 0 && prev_tail == key[0]) ? prev_run : 0.0f;
 #pragma unroll
     for (int s = 0; s < E; ++s)
         if (key[s] == key[0]) acc[s] = carry + acc[s];
-    const int next_head = __shfl_down_sync(0xffffffffu, key[0], 1, 8);
+    const int next_head = __shfl_down_sync(0xffffffffu, key[0], 1, G);
 #pragma unroll
     for (int s = 0; s < E; ++s) {
-        const int nk = s < E - 1 ? key[s + 1] : (sub < 7 ? next_head : INT_MAX - 1);
+        const int nk = s < E - 1 ? key[s + 1] : (sub < G - 1 ? next_head : INT_MAX - 1);
         if (key[s] != nk && key[s] >= 0 && key[s] < bins) out[key[s]] = add ? out[key[s]] + acc[s] : acc[s];
     }
 }
 
-// One row per group of eight lanes (lane group rg of a warp): target-twin selection,
+// One row per group of G lanes (lane group rg of a warp): target-twin selection,
 // projection, cross-entropy and logits gradient. t0 / t1 and o0 / o1 point at the row's
 // next-observation target logits and current-observation online logits of twins 0 / 1, in
 // global memory or in a shared-memory stage; they are read only when rv.
-template <int E>
+template <int G, int E>
 __device__ __forceinline__ void row_work(const Args& a, const float* t0, const float* t1, const float* o0,
                                          const float* o1, int row, bool rv, const float* z_s, float* pw, float* tw, float alpha,
                                          float scale16, float (&bias_acc)[2][E], float& loss_acc, float& ent_max,
                                          bool& overflow) {
-    const int sub = threadIdx.x & 7;
+    const int sub = threadIdx.x & (G - 1);
     const int bins = a.bins;
     const float width = a.width;
     // ---- target twins at the next-observation row: softmax and expected value; twin 0's
@@ -160,35 +161,35 @@ __device__ __forceinline__ void row_work(const Args& a, const float* t0, const f
         float mx = -INFINITY;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
-            const int k = sub + 8 * s;
+            const int k = sub + G * s;
             e[s] = (rv && k < bins) ? src[k] : -INFINITY;
             mx = fmaxf(mx, e[s]);
         }
-        mx = gmax(mx);
+        mx = gmax<G>(mx);
         float se = 0.0f;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
-            e[s] = (sub + 8 * s < bins) ? __expf(e[s] - mx) : 0.0f;
+            e[s] = (sub + G * s < bins) ? __expf(e[s] - mx) : 0.0f;
             se += e[s];
         }
-        const float inv = 1.0f / gsum(se);
+        const float inv = 1.0f / gsum<G>(se);
         float qq = 0.0f;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
             e[s] = e[s] * inv;  // probabilities
-            qq += e[s] * z_s[sub + 8 * s];
+            qq += e[s] * z_s[sub + G * s];
         }
-        qq = gsum(qq);
+        qq = gsum<G>(qq);
         if (t == 0) {
             q0 = qq;
 #pragma unroll
             for (int s = 0; s < E; ++s) {
-                pw[sub + 8 * s] = e[s];
-                tw[sub + 8 * s] = 0.0f;
+                pw[sub + G * s] = e[s];
+                tw[sub + G * s] = 0.0f;
             }
         } else if (qq < q0) {  // min-Q twin, ties keep twin 0
 #pragma unroll
-            for (int s = 0; s < E; ++s) pw[sub + 8 * s] = e[s];
+            for (int s = 0; s < E; ++s) pw[sub + G * s] = e[s];
         }
     }
     __syncwarp();
@@ -224,20 +225,20 @@ __device__ __forceinline__ void row_work(const Args& a, const float* t0, const f
             mu[s] = 0.0f;
         }
     }
-    scatter_runs<E>(kl, ml, tw, bins, false);
+    scatter_runs<G, E>(kl, ml, tw, bins, false);
     __syncwarp();
-    scatter_runs<E>(ku, mu, tw, bins, true);
+    scatter_runs<G, E>(ku, mu, tw, bins, true);
     __syncwarp();
     float tgt[E];
     float tsum = 0.0f;
 #pragma unroll
     for (int s = 0; s < E; ++s) {
-        const int k = sub + 8 * s;
+        const int k = sub + G * s;
         tgt[s] = k < bins ? tw[k] : 0.0f;
         tsum += tgt[s];
         if (a.target_out && rv && k < bins) a.target_out[static_cast<long long>(row) * a.target_row + k] = tgt[s];
     }
-    tsum = gsum(tsum);
+    tsum = gsum<G>(tsum);
 
     // ---- online twins at the current-observation row: CE and logits gradient
 #pragma unroll
@@ -247,26 +248,26 @@ __device__ __forceinline__ void row_work(const Args& a, const float* t0, const f
         float mx = -INFINITY;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
-            const int k = sub + 8 * s;
+            const int k = sub + G * s;
             x[s] = (rv && k < bins) ? src[k] : -INFINITY;
             mx = fmaxf(mx, x[s]);
         }
-        mx = gmax(mx);
+        mx = gmax<G>(mx);
         float ex[E];
         float se = 0.0f;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
-            ex[s] = (sub + 8 * s < bins) ? __expf(x[s] - mx) : 0.0f;
+            ex[s] = (sub + G * s < bins) ? __expf(x[s] - mx) : 0.0f;
             se += ex[s];
         }
-        se = gsum(se);
+        se = gsum<G>(se);
         const float lse = mx + logf(se);
         const float inv = 1.0f / se;
         if (!rv) continue;
         float ce = 0.0f;
 #pragma unroll
         for (int s = 0; s < E; ++s) {
-            const int k = sub + 8 * s;
+            const int k = sub + G * s;
             if (k >= bins) continue;
             const float lp = x[s] - lse;
             ce -= tgt[s] * lp;
@@ -291,33 +292,33 @@ __device__ __forceinline__ void row_work(const Args& a, const float* t0, const f
 
 // Block partial row of the head-bias gradient [2][bins], loss and entropy maximum, then the
 // two-level fixed-order cross-block reduction (groups of kGroup blocks by ticket).
-template <int E>
+template <int G, int E>
 __device__ __forceinline__ void finish(const Args& a, float (&bias_acc)[2][E], float loss_acc, float ent_max,
-                                       bool overflow, float (*red_s)[2 * 8 * E + 2], bool& last_s) {
+                                       bool overflow, float (*red_s)[2 * G * E + 2], bool& last_s) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int sub = lane & 7;
-    const int rg = lane >> 3;
+    const int sub = lane & (G - 1);
+    const int rg = lane / G;
     const int bins = a.bins;
     if (overflow && a.health) atomicOr(a.health, kHealthOverflow);
 
     // ---- block partial row: bias gradient [2][bins], loss, max entropy
-    // (the four row groups of a warp hold the same atoms: xor 8, 16 combine them)
+    // (the row groups of a warp hold the same atoms: xor G .. 16 combine them)
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int s = 0; s < E; ++s) {
             float v = bias_acc[t][s];
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            if (rg == 0) red_s[warp][t * 8 * E + sub + 8 * s] = v;
+#pragma unroll
+            for (int d = G; d < 32; d <<= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+            if (rg == 0) red_s[warp][t * G * E + sub + G * s] = v;
         }
     {
         const float l = warp_sum(loss_acc) * a.loss_weight;
         const float e = warp_max(ent_max);
         if (lane == 0) {
-            red_s[warp][2 * 8 * E] = l;
-            red_s[warp][2 * 8 * E + 1] = e;
+            red_s[warp][2 * G * E] = l;
+            red_s[warp][2 * G * E + 1] = e;
         }
     }
     __syncthreads();
@@ -331,13 +332,13 @@ __device__ __forceinline__ void finish(const Args& a, float (&bias_acc)[2][E], f
         if (i < 2 * bins) {
             const int t = i / bins, k = i % bins;
             s = 0.0f;
-            for (int w = 0; w < kWarps; ++w) s += red_s[w][t * 8 * E + k];
+            for (int w = 0; w < kWarps; ++w) s += red_s[w][t * G * E + k];
         } else if (i == 2 * bins) {
             s = 0.0f;
-            for (int w = 0; w < kWarps; ++w) s += red_s[w][2 * 8 * E];
+            for (int w = 0; w < kWarps; ++w) s += red_s[w][2 * G * E];
         } else {
             s = -INFINITY;
-            for (int w = 0; w < kWarps; ++w) s = fmaxf(s, red_s[w][2 * 8 * E + 1]);
+            for (int w = 0; w < kWarps; ++w) s = fmaxf(s, red_s[w][2 * G * E + 1]);
         }
         rows[static_cast<long long>(blockIdx.x) * W + i] = s;
     }
@@ -393,20 +394,21 @@ __device__ __forceinline__ void finish(const Args& a, float (&bias_acc)[2][E], f
     if (threadIdx.x == 0) a.counter[0] = 0u;
 }
 
-template <int E>
+template <int G, int E>
 __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a) {
-    constexpr int P = pitch<E>();
-    __shared__ float z_s[8 * E];
-    __shared__ float p_s[kWarps][kRowsPerWarp][P];  // selected target distribution (strided write, blocked read)
-    __shared__ float t_s[kWarps][kRowsPerWarp][P];  // projected target
-    __shared__ float red_s[kWarps][2 * 8 * E + 2];
+    constexpr int P = pitch<G, E>();
+    constexpr int R = 32 / G;  // rows per warp
+    __shared__ float z_s[G * E];
+    __shared__ float p_s[kWarps][R][P];  // selected target distribution (strided write, blocked read)
+    __shared__ float t_s[kWarps][R][P];  // projected target
+    __shared__ float red_s[kWarps][2 * G * E + 2];
     __shared__ bool last_s;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int rg = lane >> 3;
+    const int rg = lane / G;
     const int bins = a.bins;
-    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
+    for (int k = threadIdx.x; k < G * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
     __syncthreads();
     float* pw = p_s[warp][rg];
     float* tw = t_s[warp][rg];
@@ -420,51 +422,54 @@ __global__ void __launch_bounds__(kThreads) critic_objective_kernel(const Args a
     float loss_acc = 0.0f;
     float ent_max = -INFINITY;
     bool overflow = false;
-    for (int base = (blockIdx.x * kWarps + warp) * kRowsPerWarp; base < a.batch;
-         base += gridDim.x * kRowsPerBlock) {
+    for (int base = (blockIdx.x * kWarps + warp) * R; base < a.batch; base += gridDim.x * kWarps * R) {
         const int row = base + rg;
         const float* tr = a.target_logits + static_cast<long long>(a.t_row0 + row) * a.t_row;
         const float* orow = a.online_logits + static_cast<long long>(row) * a.o_row;
-        row_work<E>(a, tr, tr + a.t_twin, orow, orow + a.o_twin, row, row < a.batch, z_s, pw, tw, alpha, scale16, bias_acc, loss_acc, ent_max,
-                    overflow);
+        row_work<G, E>(a, tr, tr + a.t_twin, orow, orow + a.o_twin, row, row < a.batch, z_s, pw, tw, alpha, scale16,
+                       bias_acc, loss_acc, ent_max, overflow);
         __syncwarp();  // the next rows overwrite this warp's shared rows
     }
-    finish<E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
+    finish<G, E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
 }
 
-// Staged variant: one CTA per SM walks 32-row tiles (8 warps x 4 rows); one thread
-// copies each tile's four logits blocks (target twins 0 / 1 at the next-observation rows,
-// online twins 0 / 1 at the current rows: contiguous row ranges) into a shared-memory
-// stage with 1-D bulk asynchronous copies completing on the stage's mbarrier, kStages
-// tiles ahead, so HBM reads stay in flight while the warps compute on an earlier stage.
-// Row work and reduction are those of critic_objective_kernel (the same per-row results;
-// the block sums visit rows in another fixed order, so they are deterministic but not
-// bit-identical to that kernel's). Needs 16-byte aligned logits bases and row / twin
-// strides that are multiples of four floats, and reads every row with its full stride
-// (padding included); rl2_critic_objective falls back to critic_objective_kernel otherwise.
-// Every mbarrier wait is bounded: on a timeout the health word records it, the block
-// waits (bounded again) for its copies in flight, contributes what it has and returns.
-constexpr int kStages = 3;
-constexpr int kStageRows = kRowsPerBlock;  // 32
+// Staged variant: persistent CTAs (three per SM) walk 16-row tiles; one thread copies each tile's four
+// logits blocks (target twins 0 / 1 at the next-observation rows, online twins 0 / 1 at
+// the current rows: contiguous row ranges) into a shared-memory stage with 1-D bulk
+// asynchronous copies completing on the stage's mbarrier, kStages tiles ahead, so HBM
+// reads stay in flight while the warps compute on an earlier stage. Row work and
+// reduction are those of critic_objective_kernel (the same per-row results; the block
+// sums visit rows in another fixed order, so they are deterministic but not bit-identical
+// to that kernel's). Needs 16-byte aligned logits bases and row / twin strides that are
+// multiples of four floats, and reads every row with its full stride (padding included);
+// rl2_critic_objective falls back to critic_objective_kernel otherwise. Every mbarrier
+// wait is bounded: on a timeout the health word records it, the block waits (bounded
+// again) for its copies in flight, contributes what it has and returns.
+constexpr int kStages = 2;
+constexpr int kStageRows = 16;
+constexpr int kStagedBlocksPerSm = 3;  // 16-row stages keep three CTAs (24 warps) on an SM
 
 inline size_t staged_smem_bytes(long long t_row, long long o_row) {
     return static_cast<size_t>(kStages) * kStageRows * 2 * static_cast<size_t>(t_row + o_row) * sizeof(float);
 }
 
-template <int E>
-__global__ void __launch_bounds__(kThreads, 1) critic_objective_staged_kernel(const Args a, int tiles) {
-    constexpr int P = pitch<E>();
-    extern __shared__ __align__(128) float stage_s[];  // [kStages][target twin 0 | 1 | online twin 0 | 1][32 rows]
-    __shared__ float z_s[8 * E];
-    __shared__ float p_s[kWarps][kRowsPerWarp][P];
-    __shared__ float t_s[kWarps][kRowsPerWarp][P];
-    __shared__ float red_s[kWarps][2 * 8 * E + 2];
+template <int G, int E>
+__global__ void __launch_bounds__(kThreads, kStagedBlocksPerSm) critic_objective_staged_kernel(const Args a, int tiles) {
+    constexpr int P = pitch<G, E>();
+    constexpr int R = 32 / G;
+    constexpr int kPasses = kStageRows / (kWarps * R) > 0 ? kStageRows / (kWarps * R) : 1;
+    static_assert(kPasses * kWarps * R >= kStageRows, "every row of a stage is processed");
+    extern __shared__ __align__(128) float stage_s[];  // [kStages][target twin 0 | 1 | online twin 0 | 1][kStageRows]
+    __shared__ float z_s[G * E];
+    __shared__ float p_s[kWarps][R][P];
+    __shared__ float t_s[kWarps][R][P];
+    __shared__ float red_s[kWarps][2 * G * E + 2];
     __shared__ __align__(8) uint64_t full_s[kStages];
     __shared__ bool last_s;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int rg = lane >> 3;
+    const int rg = lane / G;
     const int bins = a.bins;
     const int tr = static_cast<int>(a.t_row), orr = static_cast<int>(a.o_row);
     const int stage_floats = kStageRows * 2 * (tr + orr);
@@ -472,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) critic_objective_staged_kernel(co
         for (int s = 0; s < kStages; ++s) ptx::mbar_init(&full_s[s], 1);
         ptx::fence_barrier_init();
     }
-    for (int k = threadIdx.x; k < 8 * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
+    for (int k = threadIdx.x; k < G * E; k += kThreads) z_s[k] = k < bins ? a.support[k] : 0.0f;
     __syncthreads();
 
     // thread 0: arm stage i % kStages and copy local tile i into it
@@ -514,26 +519,29 @@ __global__ void __launch_bounds__(kThreads, 1) critic_objective_staged_kernel(co
         const bool got = ptx::mbar_wait(&full_s[s], static_cast<uint32_t>((i / kStages) & 1), a.health);
         if (!__syncthreads_and(got)) break;
         const float* st = stage_s + s * stage_floats;
-        const int lr = warp * kRowsPerWarp + rg;
-        const int row = (blockIdx.x + i * static_cast<int>(gridDim.x)) * kStageRows + lr;
-        const float* t0 = st + lr * tr;
-        const float* o0 = st + 2 * kStageRows * tr + lr * orr;
-        row_work<E>(a, t0, t0 + kStageRows * tr, o0, o0 + kStageRows * orr, row, row < a.batch, z_s, pw, tw, alpha,
-                    scale16, bias_acc, loss_acc, ent_max, overflow);
+#pragma unroll 1
+        for (int pass = 0; pass < kPasses; ++pass) {
+            const int lr = (pass * kWarps + warp) * R + rg;
+            const int row = lr < kStageRows ? (blockIdx.x + i * static_cast<int>(gridDim.x)) * kStageRows + lr : a.batch;
+            const float* t0 = st + lr * tr;
+            const float* o0 = st + 2 * kStageRows * tr + lr * orr;
+            row_work<G, E>(a, t0, t0 + kStageRows * tr, o0, o0 + kStageRows * orr, row, row < a.batch, z_s, pw, tw,
+                           alpha, scale16, bias_acc, loss_acc, ent_max, overflow);
+            __syncwarp();  // the next pass overwrites this warp's shared rows
+        }
         done = i + 1;
-        __syncthreads();  // every warp is done with stage s (and with its shared rows)
+        __syncthreads();  // every warp is done with stage s
         if (threadIdx.x == 0 && issued < mine) {
             ptx::fence_proxy_async_smem();
             issue(issued++);
         }
     }
     // copies armed but not consumed (only after a timeout) land before the block exits
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0)
         for (int i = done; i < issued; ++i)
             ptx::mbar_wait(&full_s[i % kStages], static_cast<uint32_t>((i / kStages) & 1), nullptr);
-    }
     __syncthreads();
-    finish<E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
+    finish<G, E>(a, bias_acc, loss_acc, ent_max, overflow, red_s, last_s);
 }
 
 constexpr size_t kSmemPerBlock = 232448;  // opt-in dynamic + static shared memory one CTA may use
@@ -555,15 +563,42 @@ inline bool staged_ok(const rl2_critic_objective_args* g) {
     return staged_smem_bytes(g->target_row_stride, g->online_row_stride) + 48 * 1024 <= kSmemPerBlock;
 }
 
-template <int E>
-inline int launch_staged(const Args& a, int grid, int tiles, size_t smem, cudaStream_t s) {
-    if (cudaFuncSetAttribute(critic_objective_staged_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess) {
-        set_error("critic objective: cannot reserve %zu bytes of shared memory", smem);
-        return -1;
+template <int G, int E>
+inline int launch(const Args& a, const rl2_critic_objective_args* g, int grid, cudaStream_t s) {
+    if (staged_ok(g)) {
+        const int tiles = (g->batch + kStageRows - 1) / kStageRows;
+        // the caller's workspace holds grid_for(batch) partial rows
+        const int sg = std::min({tiles, kStagedBlocksPerSm * sm_count(), grid});
+        const size_t smem = staged_smem_bytes(g->target_row_stride, g->online_row_stride);
+        if (cudaFuncSetAttribute(critic_objective_staged_kernel<G, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)) != cudaSuccess) {
+            set_error("critic objective: cannot reserve %zu bytes of shared memory", smem);
+            return -1;
+        }
+        critic_objective_staged_kernel<G, E><<<sg, kThreads, smem, s>>>(a, tiles);
+        return launch_status("critic objective (staged)");
     }
-    critic_objective_staged_kernel<E><<<grid, kThreads, smem, s>>>(a, tiles);
-    return launch_status("critic objective (staged)");
+    critic_objective_kernel<G, E><<<grid, kThreads, 0, s>>>(a);
+    return launch_status("critic objective");
+}
+
+// Lanes per transition row: 16 (E = ceil(bins / 16) atoms per lane, fewer registers per
+// thread, so more warps per SM to hide the latency of the row's reductions and scans).
+constexpr int kLanes = 16;
+
+inline int dispatch(const Args& a, const rl2_critic_objective_args* g, int grid, cudaStream_t s) {
+    if (kLanes == 16) {
+        const int e = (g->bins + 15) / 16;
+        if (e <= 2) return launch<16, 2>(a, g, grid, s);
+        if (e <= 4) return launch<16, 4>(a, g, grid, s);
+        if (e <= 7) return launch<16, 7>(a, g, grid, s);
+        return launch<16, 8>(a, g, grid, s);
+    }
+    const int e = (g->bins + 7) / 8;
+    if (e <= 4) return launch<8, 4>(a, g, grid, s);
+    if (e <= 8) return launch<8, 8>(a, g, grid, s);
+    if (e <= 13) return launch<8, 13>(a, g, grid, s);
+    return launch<8, 16>(a, g, grid, s);
 }
 
 }  // namespace cat
@@ -635,30 +670,7 @@ extern "C" int rl2_critic_objective(const rl2_critic_objective_args* g, void* st
     a.bias_grad_out = g->bias_grad_out;
     a.bias_accumulate = g->bias_grad_accumulate;
     a.health = g->health;
-    const int grid = cat::grid_for(g->batch);
-    cudaStream_t s = as_stream(stream);
-    const int e = (g->bins + 7) / 8;
-    if (cat::staged_ok(g)) {
-        const int tiles = (g->batch + cat::kStageRows - 1) / cat::kStageRows;
-        const int sg = std::min(tiles, cat::sm_count());
-        const size_t smem = cat::staged_smem_bytes(g->target_row_stride, g->online_row_stride);
-        if (e <= 4)
-            return cat::launch_staged<4>(a, sg, tiles, smem, s);
-        if (e <= 8)
-            return cat::launch_staged<8>(a, sg, tiles, smem, s);
-        if (e <= 13)
-            return cat::launch_staged<13>(a, sg, tiles, smem, s);
-        return cat::launch_staged<16>(a, sg, tiles, smem, s);
-    }
-    if (e <= 4)
-        cat::critic_objective_kernel<4><<<grid, cat::kThreads, 0, s>>>(a);
-    else if (e <= 8)
-        cat::critic_objective_kernel<8><<<grid, cat::kThreads, 0, s>>>(a);
-    else if (e <= 13)
-        cat::critic_objective_kernel<13><<<grid, cat::kThreads, 0, s>>>(a);
-    else
-        cat::critic_objective_kernel<16><<<grid, cat::kThreads, 0, s>>>(a);
-    return launch_status("critic objective");
+    return cat::dispatch(a, g, cat::grid_for(g->batch), as_stream(stream));
 }
 
 // ===========================================================================

@@ -22,17 +22,19 @@ yardsticks the fixture script measured on the reference itself:
   layer's gradients by ~1e-3, and the first Adam step, ``lr g / (|g| + 1e-8)``, turns
   gradients near zero into a full ``+-lr`` step either way;
 * ``spread16``: the same with the inputs restated at fp16 precision (+-2^-11 relative);
-* ``tf32x3``: the float64 oracle run with the FP32 recipe's operand splits (each product
-  operand as the tensor cores read its 3xTF32 hi / lo parts: up to 2^-21 relative error per
-  operand, eight times float32's), i.e. where an exact-accumulation model of the recipe
-  lands.
+* ``spread17``: the same with the inputs moved by +-2^-17 relative, the forward precision
+  of the FP32 recipe: its 3xTF32 tensor-core products accumulate K terms in fp32 with an
+  error of about 7e-9 K relative (4e-6 at K = 512, 1.5e-5 at K = 2048, measured against
+  float64; the operand split alone is 3.5e-7, CPU float32 stays below 1e-6), so it takes
+  more ReLU decisions at the kink the other way than the reference's float32 does, and the
+  gradient-carrying tensors (Adam moments) move accordingly.
 
 Tolerances:
 
-* FP32 recipe: within ``max(1e-4, 3 floor, 2 spread, 2 tf32x3)`` of the reference's
+* FP32 recipe: within ``max(1e-4, 3 floor, 2 spread, 2 spread17)`` of the reference's
   float32 result: 1e-4 wherever the arithmetic determines the result to that level,
-  otherwise no farther from the reference than its own float32 evaluations are from each
-  other, or than the modelled recipe is.
+  otherwise no farther from the reference than the reference moves itself under
+  rounding-level changes of its inputs at float32 precision or at the recipe's precision.
 * FP16-operand recipe: within ``max(1e-2, 2 spread16)``: no farther from the reference's
   FP32 result than that result moves when its inputs are stated at fp16 precision.
 * Metrics: the same rules on each returned metric.
@@ -107,14 +109,14 @@ def _compare(g: dict, u: int, ours: dict, tol: float, fp16: bool) -> list[str]:
         floor = float(g[f"u{u}.{k}.floor"])
         spread = float(g[f"u{u}.{k}.spread"])
         spread16 = float(g[f"u{u}.{k}.spread16"])
-        model = float(g[f"u{u}.{k}.tf32x3"])
+        spread17 = float(g[f"u{u}.{k}.spread17"])
         if fp16:
             limit = max(tol, SPREAD_FACTOR * spread16)
         else:
-            limit = max(tol, FLOOR_FACTOR * floor, SPREAD_FACTOR * spread, SPREAD_FACTOR * model)
+            limit = max(tol, FLOOR_FACTOR * floor, SPREAD_FACTOR * spread, SPREAD_FACTOR * spread17)
         if not err <= limit:
             failures.append(f"{k}: {err:.2e} > {limit:.2e} (reference: float64 {floor:.2e}, float32 spread "
-                            f"{spread:.2e}, fp16-scale spread {spread16:.2e}, 3xTF32 model {model:.2e})")
+                            f"{spread:.2e}, 2^-17 spread {spread17:.2e}, fp16-scale spread {spread16:.2e})")
     return failures
 
 
@@ -158,7 +160,7 @@ def test_update_matches_reference_at_config_size(case, precision):
             else:
                 limit = max(tol * max(1.0, abs(r32)), FLOOR_FACTOR * abs(r64 - r32),
                             SPREAD_FACTOR * float(g[f"u{u}.metricspread.{k}"]),
-                            SPREAD_FACTOR * abs(float(g[f"u{u}.metrictf32x3.{k}"]) - r32))
+                            SPREAD_FACTOR * float(g[f"u{u}.metricspread17.{k}"]))
             if not abs(v - r32) <= limit:
                 report.append(f"update {u}: metric {k} = {v} vs reference {r32} (float64 {r64})")
         t32 = float(g[f"u{u}.temp32"][0])
