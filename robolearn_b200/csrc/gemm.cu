@@ -46,6 +46,10 @@ constexpr int kBM = 128;
 constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxSmem = 232448;           // dynamic shared memory one CTA may use
+// k-blocks per tensor-core accumulation chain of a 3xTF32 product (32 k each: 256 products,
+// about 2e-6 relative from the accumulation), folded with round-to-nearest fp32 additions
+// by the epilogue
+constexpr int kChainBlocks = 8;
 
 struct Params {
     int M, N, K;
@@ -85,6 +89,7 @@ struct Params {
     int out_m, out_n;  // output rows / columns (the kernel's N / M when swapped)
     int epi_bufs;      // staging boxes per warp and output (store-engine epilogue: 1 or 2)
     int stage_floats;  // per-warp staging floats (multiple of 256: 1 KB-aligned regions)
+    int kc_blocks;     // k-blocks per tensor-core accumulation chunk (0: one chain per tile)
 };
 
 // Epilogue activations. ELU (alpha 1) and tanh; derivatives from the stored outputs y.
@@ -241,46 +246,107 @@ __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem
     const uint32_t lay_mn = KIND == 0 ? 2u : 1u;
     int s = 0;
     uint32_t phase = 0;
-    int i = 0;
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+    int i = 0;  // accumulation chain counter: one per tile, or one per chunk of kc_blocks k-blocks
+    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
         const Tile w = decode(p, t);
-        const int buf = i & 1;
-        if (!wait_bar(&acc_empty[buf], ((i >> 1) & 1) ^ 1, p.health, abort_flag)) return;
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf) * buf_cols;
-        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
-            if (!wait_bar(&full[s], phase, p.health, abort_flag)) return;
+        const int span = p.kc_blocks > 0 ? p.kc_blocks : w.kb_end - w.kb_begin;
+        for (int c0 = w.kb_begin; c0 < w.kb_end; c0 += span, ++i) {
+            const int c1 = min(c0 + span, w.kb_end);
+            const int buf = i & 1;
+            if (!wait_bar(&acc_empty[buf], ((i >> 1) & 1) ^ 1, p.health, abort_flag)) return;
             ptx::tc_fence_after();
-            const uint32_t sa = ptx::smem_u32(smem + s * stage_bytes);
-            const uint32_t sb = sa + a_bytes * kPlanes;
-            const bool first = kb == w.kb_begin;
+            const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf) * buf_cols;
+            for (int kb = c0; kb < c1; ++kb) {
+                if (!wait_bar(&full[s], phase, p.health, abort_flag)) return;
+                ptx::tc_fence_after();
+                const uint32_t sa = ptx::smem_u32(smem + s * stage_bytes);
+                const uint32_t sb = sa + a_bytes * kPlanes;
+                const bool first = kb == c0;
 #pragma unroll
-            for (int j = 0; j < kBK / kUK; ++j) {
-                const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
-                const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
-                const uint64_t da = A_MN ? smem_desc(sa + a_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sa + a_off, 16, 1024);
-                const uint64_t db = B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
-                const uint32_t acc = (!first || j > 0) ? 1u : 0u;
-                if (KIND == 0) {
-                    ptx::mma_f16(d_tmem, da, db, idesc, acc);
-                } else {
-                    const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
-                                                : smem_desc(sa + a_bytes + a_off, 16, 1024);
-                    const uint64_t db_lo = B_MN ? smem_desc(sb + b_bytes + b_off, lbo_mn, sbo_mn, lay_mn)
-                                                : smem_desc(sb + b_bytes + b_off, 16, 1024);
-                    ptx::mma_tf32(d_tmem, da_lo, db, idesc, acc);
-                    ptx::mma_tf32(d_tmem, da, db_lo, idesc, 1u);
-                    ptx::mma_tf32(d_tmem, da, db, idesc, 1u);
+                for (int j = 0; j < kBK / kUK; ++j) {
+                    const uint32_t a_off = A_MN ? j * kUK * 128 : j * 32;
+                    const uint32_t b_off = B_MN ? j * kUK * 128 : j * 32;
+                    const uint64_t da =
+                        A_MN ? smem_desc(sa + a_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sa + a_off, 16, 1024);
+                    const uint64_t db =
+                        B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
+                    const uint32_t acc = (!first || j > 0) ? 1u : 0u;
+                    if (KIND == 0) {
+                        ptx::mma_f16(d_tmem, da, db, idesc, acc);
+                    } else {
+                        const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
+                                                    : smem_desc(sa + a_bytes + a_off, 16, 1024);
+                        const uint64_t db_lo = B_MN ? smem_desc(sb + b_bytes + b_off, lbo_mn, sbo_mn, lay_mn)
+                                                    : smem_desc(sb + b_bytes + b_off, 16, 1024);
+                        ptx::mma_tf32(d_tmem, da_lo, db, idesc, acc);
+                        ptx::mma_tf32(d_tmem, da, db_lo, idesc, 1u);
+                        ptx::mma_tf32(d_tmem, da, db, idesc, 1u);
+                    }
+                }
+                ptx::mma_commit(&empty[s]);
+                if (++s == stages) {
+                    s = 0;
+                    phase ^= 1;
                 }
             }
-            ptx::mma_commit(&empty[s]);
-            if (++s == stages) {
-                s = 0;
-                phase ^= 1;
-            }
+            ptx::mma_commit(&acc_full[buf]);
         }
-        ptx::mma_commit(&acc_full[buf]);
     }
+}
+
+// Chunked accumulation (p.kc_blocks > 0): the MMA issuer accumulates every kc_blocks
+// k-blocks of a tile into a fresh chain in TMEM buffer i & 1 (i counting chains). The
+// tensor cores add into an fp32 accumulator with an error that grows with the chain's
+// length (about 7e-9 K relative, measured), so chains stay short and the epilogue warps
+// add them with ordinary round-to-nearest fp32 additions: chains 0 .. n-2 into a running
+// sum in TMEM columns [2 buf_cols, 3 buf_cols), and the running sum into the last chain's
+// buffer, which the epilogue then reads as the tile's accumulator. Each warp folds its own
+// TMEM lane quarter and every other 16-column group (the two warps of a quarter); the
+// warps then meet on an mbarrier (bounded wait) before any of them reads the total. On
+// return, i indexes the tile's last chain.
+__device__ __forceinline__ bool fold_chunks(const Params& p, const Tile& w, uint64_t* acc_full, uint64_t* acc_empty,
+                                            uint64_t* epi_sync, uint32_t& epi_phase, uint32_t tmem, int& i,
+                                            volatile int* abort_flag) {
+    const int chains = (w.kb_end - w.kb_begin + p.kc_blocks - 1) / p.kc_blocks;
+    if (chains <= 1) return true;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = warp & 3;
+    const int slot = (warp - 2) >> 2;
+    const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t run = tmem + 2u * p.buf_cols + lanes;
+    const int groups = (p.BN + 15) / 16;
+    for (int c = 0; c < chains; ++c, ++i) {
+        const int buf = i & 1;
+        if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) return false;
+        ptx::tc_fence_after();
+        const uint32_t src = tmem + static_cast<uint32_t>(buf) * p.buf_cols + lanes;
+        const bool last = c == chains - 1;
+        for (int g = slot; g < groups; g += kEpiWarps / 4) {
+            float v[16];
+            ptx::tmem_ld16(src + 16u * g, v);
+            if (c > 0) {
+                float r[16];
+                ptx::tmem_ld16(run + 16u * g, r);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = __fadd_rn(r[e], v[e]);
+            }
+            ptx::tmem_st16(last ? src + 16u * g : run + 16u * g, v);
+        }
+        ptx::tmem_st_wait();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (!last) {
+            if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);  // this chain's buffer is free again
+        } else {
+            if (lane == 0) ptx::mbar_arrive(epi_sync);
+            if (!wait_bar(epi_sync, epi_phase, p.health, abort_flag)) return false;
+            epi_phase ^= 1u;
+            ptx::tc_fence_after();
+        }
+    }
+    --i;
+    return true;
 }
 
 // Staged 32 x 16 slice: rows of 16 floats, 16-byte chunk j of row r stored at chunk
@@ -344,8 +410,9 @@ __device__ __forceinline__ float4 pick4(const float4 (&v)[kMaxChunks], int k) {
     return r;
 }
 
-__device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
-                                      float* staging, volatile int* abort_flag) {
+__device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint64_t* epi_sync,
+                                      uint32_t tmem, float* staging, volatile int* abort_flag) {
+    uint32_t epi_phase = 0;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
@@ -364,6 +431,8 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
         const Tile w = decode(p, t);
+        if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
+            break;
         const int buf = i & 1;
         const int r0 = w.m_tile * kBM + q * 32;
         const int valid = min(max(p.M - r0, 0), 32);
@@ -642,8 +711,9 @@ struct TmaEpi {
 };
 
 __device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtensorMap* tma_p, const Params& p,
-                                          uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem, float* staging,
-                                          volatile int* abort_flag) {
+                                          uint64_t* acc_full, uint64_t* acc_empty, uint64_t* epi_sync, uint32_t tmem,
+                                          float* staging, volatile int* abort_flag) {
+    uint32_t epi_phase = 0;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
@@ -653,6 +723,8 @@ __device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtens
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
         const Tile w = decode(p, t);
+        if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
+            break;
         const int buf = i & 1;
         const int r0 = w.m_tile * kBM + q * 32;
         const int valid = min(max(p.M - r0, 0), 32);
@@ -723,8 +795,9 @@ __device__ __forceinline__ float sum32(const float (&x)[32]) {
 // activation outputs; the instance without them keeps the add / aux registers out of the
 // common path.
 template <bool kLoads>
-__device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
-                                           volatile int* abort_flag) {
+__device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, uint64_t* acc_empty,
+                                           uint64_t* epi_sync, uint32_t tmem, volatile int* abort_flag) {
+    uint32_t epi_phase = 0;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
@@ -738,6 +811,8 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
     int i = 0;
     for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
         const Tile w = decode(p, t);
+        if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
+            break;
         const int buf = i & 1;
         const int col0 = w.m_tile * kBM + q * 32;  // this warp's 32 output columns
         const int n = col0 + lane;
@@ -907,11 +982,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_full = empty + stages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* mma_done = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* epi_sync = mma_done + 1;  // epilogue warps meet here after folding a tile's chains
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_sync + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
-    const uint32_t tmem_cols = 2 * p.buf_cols;
+    // two accumulator buffers, plus a running-sum region when chains are folded (power of two)
+    const uint32_t tmem_cols = (p.kc_blocks > 0 ? 4 : 2) * p.buf_cols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -923,6 +1000,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
         }
         ptx::mbar_init(mma_done, 1);
+        ptx::mbar_init(epi_sync, kEpiWarps);
         *abort_flag = 0;
         ptx::fence_barrier_init();
     }
@@ -950,13 +1028,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (p.swap) {
         if (p.residual || p.accumulate || p.aux)
-            drain_swap<true>(p, acc_full, acc_empty, tmem, abort_flag);
+            drain_swap<true>(p, acc_full, acc_empty, epi_sync, tmem, abort_flag);
         else
-            drain_swap<false>(p, acc_full, acc_empty, tmem, abort_flag);
+            drain_swap<false>(p, acc_full, acc_empty, epi_sync, tmem, abort_flag);
     } else if (p.tma_epi) {
-        drain_tma(&tma_d, &tma_p, p, acc_full, acc_empty, tmem, staging, abort_flag);
+        drain_tma(&tma_d, &tma_p, p, acc_full, acc_empty, epi_sync, tmem, staging, abort_flag);
     } else {
-        drain(p, acc_full, acc_empty, tmem, staging, abort_flag);
+        drain(p, acc_full, acc_empty, epi_sync, tmem, staging, abort_flag);
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -1206,6 +1284,12 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
             while (bn / 2 >= 128 && (bn / 2) % q == 0 && tiles_for(bn) < nsm) bn /= 2;
         }
     }
+    // 3xTF32 products longer than one chain accumulate in chains of kChainBlocks k-blocks
+    // folded by the epilogue (fold_chunks); the running sum takes a third TMEM region, so
+    // such plans use tiles of at most 128 columns (four 128-column regions fill TMEM).
+    const int kblocks_tile = ((g->k + bk - 1) / bk + std::max(splits, 1) - 1) / std::max(splits, 1);
+    const bool chained = g->kind == 1 && kblocks_tile > kChainBlocks;
+    if (chained) bn = std::min(bn, 128);
     if (bn % 16 != 0 || bn < 16 || bn > 256 || (o.b_major == 1 && bn % chunk != 0)) {
         set_error("GEMM tile_n must be a multiple of 16 in [16, 256] (and of %d for an N-contiguous B)", chunk);
         return nullptr;
@@ -1265,6 +1349,7 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
     p.kblocks_per_split = (p.kblocks_total + p.splits - 1) / p.splits;
     p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;  // every split non-empty
     p.BN = bn;
+    p.kc_blocks = chained ? kChainBlocks : 0;
     p.a_batched = o.a_batch_stride != 0;
     p.b_batched = o.b_batch_stride != 0;
     p.d = g->d;
