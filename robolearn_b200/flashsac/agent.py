@@ -28,6 +28,7 @@ from typing import Any, MutableMapping
 import torch
 
 from .. import _native as N
+from ..categorical import support
 from .config import FlashSACConfig
 from .engine import Run
 from .learner import METRIC_KEYS, Learner
@@ -49,21 +50,39 @@ def truncated_zeta_cdf(mu: float, max_n: int) -> torch.Tensor:
     return torch.cumsum(pmf, dim=0)
 
 
-def _adam_state_dict(m: list[torch.Tensor], v: list[torch.Tensor], steps: float, lr: float, lr_init: float) -> dict:
+def _adam_state_dict(m: list[torch.Tensor], v: list[torch.Tensor], steps: float, lr: float, initial_lr: float) -> dict:
     """torch.optim.Adam state_dict layout for parameters 0..n-1 (one param group)."""
     state = {i: {"step": torch.tensor(float(steps)), "exp_avg": m[i].clone(), "exp_avg_sq": v[i].clone()}
              for i in range(len(m))} if steps > 0 else {}
+    # fused: the reference builds Adam(fused=True) on CUDA devices (agent.py:64-65)
     group = {"lr": lr, "betas": _BETAS, "eps": _EPS, "weight_decay": 0, "amsgrad": False, "maximize": False,
-             "foreach": None, "capturable": False, "differentiable": False, "fused": None, "decoupled_weight_decay": False,
-             "initial_lr": lr_init, "params": list(range(len(m)))}
+             "foreach": None, "capturable": False, "differentiable": False, "fused": True, "decoupled_weight_decay": False,
+             "initial_lr": initial_lr, "params": list(range(len(m)))}
     return {"state": state, "param_groups": [group]}
 
 
-def _scheduler_state_dict(attempts: float, lr: float, lr_init: float) -> dict:
+def _schedule_lr(cfg: FlashSACConfig, steps: float) -> float:
+    """The learning rate the reference's optimisers hold after ``steps`` scheduler steps:
+    LambdaLR multiplies the optimiser's initial rate (learning_rate_peak) by
+    warmup_cosine_decay_lr(steps) / learning_rate_peak (agent.py:64-69,
+    _utils/scheduler.py:43-65), in Python floats."""
+    k = int(steps)
+    init, peak, end = cfg.learning_rate_init, cfg.learning_rate_peak, cfg.learning_rate_end
+    w, d = cfg.learning_rate_warmup_step, cfg.learning_rate_decay_step
+    if k < w:
+        v = init + (peak - init) * (k / w)
+    elif k < d:
+        v = end + (peak - end) * 0.5 * (1 + math.cos(math.pi * ((k - w) / (d - w))))
+    else:
+        v = end
+    return peak * (v / peak)
+
+
+def _scheduler_state_dict(attempts: float, lr: float, base_lr: float) -> dict:
     """LambdaLR state_dict layout (the lambda itself is not serialised by torch either)."""
     n = int(attempts)
-    return {"base_lrs": [lr_init], "last_epoch": n, "_step_count": n + 1, "_get_lr_called_within_step": False,
-            "_last_lr": [lr], "lr_lambdas": [None]}
+    return {"base_lrs": [base_lr], "last_epoch": n, "_step_count": n + 1, "_is_initial": False,
+            "_get_lr_called_within_step": False, "_last_lr": [lr], "lr_lambdas": [None]}
 
 
 class FlashSAC:
@@ -224,25 +243,33 @@ class FlashSAC:
 
     # ------------------------------------------------------------------ checkpoints
     def _network_ckpt(self, net, optimised: bool) -> dict:
-        lr_init = self._cfg.learning_rate_init
-        ckpt = {"network_state_dict": net.state_dict(), "optimizer_state_dict": None, "scheduler_state_dict": None,
-                "update_step": 0}
+        peak = self._cfg.learning_rate_peak
+        # the reference's Network.update_step is never advanced by an update; it is whatever was
+        # loaded (0 for a fresh agent), and is written back as such
+        state = net.state_dict()
+        if net.spec.critic:  # the categorical head's support buffer (layers.py:289-292), saved by the reference
+            cfg = self._cfg
+            state["predictor.bin_values"] = torch.from_numpy(
+                support(cfg.critic_num_bins, cfg.critic_min_v, cfg.critic_max_v)).reshape(1, 1, -1)
+        ckpt = {"network_state_dict": state, "optimizer_state_dict": None, "scheduler_state_dict": None,
+                "update_step": getattr(net, "ckpt_update_step", 0)}
         if optimised:
             st = net.opt_state.cpu().tolist()
             m = [net.moment("m", k) for k in net.param_names]
             v = [net.moment("v", k) for k in net.param_names]
-            ckpt["optimizer_state_dict"] = _adam_state_dict(m, v, st[_STEPS], st[_LR] or lr_init, lr_init)
-            ckpt["scheduler_state_dict"] = _scheduler_state_dict(st[_ATTEMPTS], st[_LR] or lr_init, lr_init)
-            ckpt["update_step"] = int(st[_ATTEMPTS])
+            lr = _schedule_lr(self._cfg, st[_ATTEMPTS])
+            ckpt["optimizer_state_dict"] = _adam_state_dict(m, v, st[_STEPS], lr, peak)
+            ckpt["scheduler_state_dict"] = _scheduler_state_dict(st[_ATTEMPTS], lr, peak)
         return ckpt
 
     def _temperature_ckpt(self) -> dict:
-        lr_init = self._cfg.learning_rate_init
+        peak = self._cfg.learning_rate_peak
         step, m, v = self._learner.temp_state.cpu().tolist()
-        lr = lr_init  # the temperature shares the schedule; its value is recomputed from the step on load
+        lr = _schedule_lr(self._cfg, step)  # the temperature shares the schedule, one step per actor update
         return {"network_state_dict": {"log_temp": self._learner.log_temp.detach().clone()},
-                "optimizer_state_dict": _adam_state_dict([torch.tensor([m])], [torch.tensor([v])], step, lr, lr_init),
-                "scheduler_state_dict": _scheduler_state_dict(step, lr, lr_init), "update_step": int(step)}
+                "optimizer_state_dict": _adam_state_dict([torch.tensor([m])], [torch.tensor([v])], step, lr, peak),
+                "scheduler_state_dict": _scheduler_state_dict(step, lr, peak),
+                "update_step": getattr(self._learner, "temp_ckpt_update_step", 0)}
 
     def save(self, path: str) -> None:
         os.makedirs(path, exist_ok=True)
@@ -273,6 +300,8 @@ class FlashSAC:
     def _load_network(self, net, ckpt: dict, load_optimizer: bool) -> None:
         state = {k.removeprefix("_orig_mod."): v for k, v in ckpt["network_state_dict"].items()}
         net.load_state_dict(state)
+        if load_optimizer:
+            net.ckpt_update_step = int(ckpt.get("update_step", 0))
         opt = ckpt.get("optimizer_state_dict")
         if load_optimizer and opt is not None and getattr(net, "with_optimizer", False):
             for i, k in enumerate(net.param_names):
@@ -296,6 +325,8 @@ class FlashSAC:
         self._load_network(L.target, rd("target_critic.pt"), False)
         temp = rd("temperature.pt")
         L.log_temp.copy_(temp["network_state_dict"]["log_temp"].reshape(1))
+        if load_optimizer:
+            L.temp_ckpt_update_step = int(temp.get("update_step", 0))
         opt = temp.get("optimizer_state_dict")
         if load_optimizer and opt is not None and opt["state"]:
             s = opt["state"][0]
