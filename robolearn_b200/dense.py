@@ -118,6 +118,17 @@ class DensePlan:
         self.transposed = mode == 2
         self.flops = 2 * m * n * k * batch * (3 if kind == TF32X3 else 1)
         self.recompute = False  # set by callers that compute the same product twice
+        # algorithmic bytes of one launch (operands read once, outputs written once)
+        el = 2 if kind == 0 else 8  # fp16, or the tf32 hi + lo planes
+        plane = out_plane is not None and (out_plane.h16 or out_plane.hi or out_plane.lo)
+        self.bytes = batch * (m * k * el + n * k * el + (m * n * 4 * max(k_splits, 1) if d is not None else 0)
+                              + (m * n * el if plane else 0) + (m * n * 4 if residual is not None else 0)
+                              + (m * n * 4 if accumulate else 0)
+                              + ((m + 31) // 32 * n * 8 if stat_mean is not None else 0))
+        self.shape = dict(m=m, n=n, k=k, batch=batch, kind=kind, a_major=a_major, b_major=b_major, splits=k_splits,
+                          stats=stat_mean is not None, plane=bool(plane), residual=residual is not None,
+                          tile_n=self.tile_n, form="transposed" if self.transposed else
+                          ("tma-store" if self.tma_store else "register-store"))
 
     def run(self, stream=None) -> None:
         N.check(self._lib.rl2_gemm_run(self.handle, N.stream_ptr(stream)), "tcgen05 GEMM")
