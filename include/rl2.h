@@ -132,6 +132,11 @@ int rl2_gemm_tile_n(void* plan);
  * 1 = outputs written by TMA stores (no activation / split-K, a residual only if it is D
  * itself, 16-byte aligned fp32 output and fp16 plane); 0 = register stores. */
 int rl2_gemm_uses_tma_store(void* plan);
+/* 1 if the plan runs on CTA pairs (fp16 products with at least 512 kernel rows, a
+ * contraction of at least 16 k-blocks of 64 and a plan-chosen tile width: clusters of two
+ * CTAs computing 256-row tiles with tcgen05 cta_group::2, each CTA staging half of the
+ * operands). RL2_GEMM_PAIR=0 disables pairs, RL2_GEMM_PAIR=2 drops the length rule. */
+int rl2_gemm_cta_pair(void* plan);
 
 /* out[i] (+)= sum_s partial[s * split_stride + i], fixed order, i < count. */
 int rl2_split_reduce(const float* partial, long long split_stride, int splits, float* out, long long count,
@@ -419,12 +424,14 @@ int rl2_temperature_step(const rl2_temperature_args* args, void* stream);
  * rl_flash_ema_* (src/robolearn/cuda/flash_kernels.cuh:383-498) and the fp16
  * weight casts rl_cast_f32_f16 (kernels.cu:663-687).
  *
- * One segment = one projection unit, processed by one CTA:
+ * One segment = one projection unit, processed by one warp or one CTA (warp_segments):
  *   kind 0 plain vector (no projection: head / policy biases),
  *   kind 1 unit-linear weight row -> w / max(||w||, 1e-8),
  *   kind 2 BN (weight at offset, bias at offset2) -> both * sqrt(C)/sqrt(sum(w^2+b^2)+1e-8),
  *   kind 3 RMS scale -> w * sqrt(C)/sqrt(sum(w^2)+1e-8).
- * length <= rl2_segment_max_length() per vector. plane_offset >= 0 refreshes the
+ * length <= rl2_segment_max_length() per vector (rl2_segment_warp_max_length() for the
+ * leading warp_segments units). Units whose offsets and length are multiples of four
+ * floats move in 16-byte vectors. plane_offset >= 0 refreshes the
  * row's operand copy in weight_plane (and target_plane for the EMA target).
  * formula 0 = torch Adam (lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps)),
  * formula 1 = Warp-NN Adam (lr * m c1 / (sqrt(v c2) + eps)).
@@ -471,11 +478,14 @@ typedef struct rl2_adam_args {
     float* target_params;
     float tau;
     rl2_plane target_plane;
+    int warp_segments; /* the leading units, each <= rl2_segment_warp_max_length(), take one
+                          warp each (eight per CTA); the rest one CTA each. 0: a CTA per unit */
 } rl2_adam_args;
 
 int rl2_adam_prepare(const rl2_adam_prepare_args* args, void* stream);
 int rl2_adam_step(const rl2_adam_args* args, void* stream);
 int rl2_segment_max_length(void);
+int rl2_segment_warp_max_length(void);
 
 /* ---------------------------------------------------------------------------
  * replay sampling and gather. Replaces the Warp kernels _sample_indices and
@@ -809,6 +819,24 @@ int rl2_syncbn_backward(const float* s1_part, const float* s2_part, long long pa
 /* Bytes of one exchange slot's data and flag regions for (world, twins, cols). */
 long long rl2_syncbn_slot_data_bytes(int world, int twins, int cols);
 long long rl2_syncbn_slot_flag_bytes(int world, int twins, int cols);
+
+/* Small all-reduce of the learner's scalars over the same peer slots (one warp; a slot
+ * sized for twins = 1, cols = 32): mean[0 .. n_mean) averaged over the ranks (sum in
+ * rank order / world), then max[0 .. n_max) and the flags max_int[0 .. n_max_int)
+ * replaced by their maxima (max results written after the means, so max may point into
+ * mean). n_mean + n_max + n_max_int <= 64. Replaces the entropy average before the
+ * temperature step (src/robolearn/flashsac/updates.py), the overflow-flag maximum before
+ * each optimizer step and the reported-metrics reductions of data-parallel updates. */
+typedef struct rl2_peer_reduce_args {
+    float* mean;
+    int n_mean;
+    float* max;
+    int n_max;
+    int* max_int;
+    int n_max_int;
+} rl2_peer_reduce_args;
+
+int rl2_peer_reduce(const rl2_peer_reduce_args* args, const rl2_syncbn_exchange* ex, void* stream);
 
 #ifdef __cplusplus
 }

@@ -130,7 +130,7 @@ class AdamArgs(ctypes.Structure):
     _fields_ = [
         ("params", P), ("grads", P), ("m", P), ("v", P), ("segments", P), ("count", I), ("state", P),
         ("formula", I), ("beta1", F), ("beta2", F), ("eps", F), ("project", I), ("weight_plane", Plane),
-        ("target_params", P), ("tau", F), ("target_plane", Plane),
+        ("target_params", P), ("tau", F), ("target_plane", Plane), ("warp_segments", I),
     ]
 
 
@@ -155,6 +155,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_gemm_destroy": ([P], I),
     "rl2_gemm_tile_n": ([P], I),
     "rl2_gemm_uses_tma_store": ([P], I),
+    "rl2_gemm_cta_pair": ([P], I),
     "rl2_split_reduce": ([P, LL, I, P, LL, I, P], I),
     "rl2_split_reduce_batched": ([P, LL, I, P, LL, I, I, LL, LL, P], I),
     "rl2_categorical_workspace_floats": ([I, I], I),
@@ -178,6 +179,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "rl2_adam_prepare": ([ctypes.POINTER(AdamPrepareArgs), P], I),
     "rl2_adam_step": ([ctypes.POINTER(AdamArgs), P], I),
     "rl2_segment_max_length": ([], I),
+    "rl2_segment_warp_max_length": ([], I),
     "rl2_replay_sample": ([ctypes.c_ulonglong, P, P, LL, I, P, P, P], I),
     "rl2_counter_advance": ([P, ctypes.c_ulonglong, P], I),
     "rl2_replay_gather": ([ctypes.POINTER(ReplayGatherArgs), P], I),
@@ -239,6 +241,24 @@ def addr(x) -> int | None:
     if isinstance(x, int):
         return x
     return x.data_ptr()
+
+
+def segment_table(rows, device):
+    """Device table of optimizer units (offset, offset2, plane_offset, length, kind) for
+    ``rl2_adam_step``: units short enough for one warp first (in their given order), then
+    the rest. Returns (uint8 tensor, unit count, leading warp units)."""
+    import torch
+
+    lib = load()
+    longest, warp_max = lib.rl2_segment_max_length(), lib.rl2_segment_warp_max_length()
+    if any(r[3] > longest for r in rows):
+        raise ValueError(f"a projection unit is longer than {longest} elements")
+    ordered = [r for r in rows if r[3] <= warp_max] + [r for r in rows if r[3] > warp_max]
+    warp_units = sum(1 for r in rows if r[3] <= warp_max)
+    arr = (Segment * len(ordered))(*[Segment(offset=a, offset2=b, plane_offset=c, length=d, kind=e)
+                                     for a, b, c, d, e in ordered])
+    raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).clone()
+    return raw.to(device), len(ordered), warp_units
 
 
 def stream_ptr(stream=None) -> int:
@@ -354,6 +374,12 @@ SIGNATURES.update({
 })
 
 
+class PeerReduceArgs(ctypes.Structure):
+    """``rl2_peer_reduce_args`` (include/rl2.h)."""
+
+    _fields_ = [("mean", P), ("n_mean", I), ("max", P), ("n_max", I), ("max_int", P), ("n_max_int", I)]
+
+
 class SyncBNExchange(ctypes.Structure):
     """``rl2_syncbn_exchange`` (include/rl2.h)."""
 
@@ -364,6 +390,7 @@ class SyncBNExchange(ctypes.Structure):
 SIGNATURES.update({
     "rl2_syncbn_forward": ([P, P, LL, I, I, I, I, P, P, P, P, F, F, I, ctypes.POINTER(SyncBNExchange), P], I),
     "rl2_syncbn_backward": ([P, P, LL, I, I, I, P, P, LL, P, P, ctypes.POINTER(SyncBNExchange), P], I),
+    "rl2_peer_reduce": ([ctypes.POINTER(PeerReduceArgs), ctypes.POINTER(SyncBNExchange), P], I),
     "rl2_syncbn_slot_data_bytes": ([I, I, I], LL),
     "rl2_syncbn_slot_flag_bytes": ([I, I, I], LL),
 })

@@ -43,13 +43,17 @@ namespace rl2 {
 namespace gemm {
 
 constexpr int kBM = 128;
-constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter
+constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter (register- and TMA-store epilogues)
+constexpr int kEpiWarpsWide = 16;             // four per quarter: transposed-accumulator plans
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, epilogue warps
+__host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi; }
 constexpr int kMaxSmem = 232448;           // dynamic shared memory one CTA may use
 // k-blocks per tensor-core accumulation chain of a 3xTF32 product (32 k each: 256 products,
 // about 2e-6 relative from the accumulation), folded with round-to-nearest fp32 additions
 // by the epilogue
 constexpr int kChainBlocks = 8;
+// k-blocks per tile (64 each for fp16) from which a product runs on CTA pairs
+constexpr int kPairMinKBlocks = 16;
 
 struct Params {
     int M, N, K;
@@ -90,6 +94,9 @@ struct Params {
     int epi_bufs;      // staging boxes per warp and output (store-engine epilogue: 1 or 2)
     int stage_floats;  // per-warp staging floats (multiple of 256: 1 KB-aligned regions)
     int kc_blocks;     // k-blocks per tensor-core accumulation chunk (0: one chain per tile)
+    int epi_warps;     // epilogue warps of the launch (kEpiWarps, or kEpiWarpsWide for transposed plans)
+    bool pair;         // CTA pairs: 256-row tiles over two SMs (tcgen05 cta_group::2), tiles_m counts pairs
+    int bn_cta;        // rows of the B tile each CTA stages (BN, or BN / 2 in a pair)
 };
 
 // Epilogue activations. ELU (alpha 1) and tanh; derivatives from the stored outputs y.
@@ -140,11 +147,20 @@ struct Tile {
     int n_tile, m_tile, z, split, kb_begin, kb_end;
 };
 
+// Persistent walk over the work list: CTA b takes tiles b, b + gridDim.x, ...; in pair mode
+// the two CTAs of cluster c (blocks 2c, 2c + 1) take pair tiles c, c + gridDim.x / 2, ...
+__device__ __forceinline__ int tile_first(const Params& p) { return p.pair ? static_cast<int>(blockIdx.x >> 1) : blockIdx.x; }
+__device__ __forceinline__ int tile_step(const Params& p) { return p.pair ? static_cast<int>(gridDim.x >> 1) : gridDim.x; }
+
+// A pair tile covers kernel rows [256 m, 256 m + 256): each CTA of the pair owns the 128-row
+// half of its rank (its TMEM holds those rows of the accumulator), so decode() returns that
+// half as a 128-row m_tile and the epilogues are the same as for one CTA.
 __device__ __forceinline__ Tile decode(const Params& p, int t) {
     Tile w;
     w.n_tile = t % p.tiles_n;
     t /= p.tiles_n;
     w.m_tile = t % p.tiles_m;
+    if (p.pair) w.m_tile = 2 * w.m_tile + static_cast<int>(blockIdx.x & 1);
     t /= p.tiles_m;
     w.z = t / p.splits;
     w.split = t % p.splits;
@@ -153,7 +169,16 @@ __device__ __forceinline__ Tile decode(const Params& p, int t) {
     return w;
 }
 
-template <int KIND, int A_MN, int B_MN>
+// An epilogue warp is done with an accumulator buffer: arrive on the MMA issuer's barrier
+// (in a pair, the leader CTA's, which counts the warps of both CTAs).
+__device__ __forceinline__ void release_acc(const Params& p, uint64_t* bar) {
+    if (p.pair)
+        ptx::mbar_arrive_cluster(ptx::cluster_addr(bar, 0));
+    else
+        ptx::mbar_arrive(bar);
+}
+
+template <int KIND, int A_MN, int B_MN, bool PAIR>
 __device__ __forceinline__ void produce(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const CUtensorMap* tma_a_lo,
                                         const CUtensorMap* tma_b_lo, const Params& p, int stages, uint8_t* smem,
                                         uint32_t stage_bytes, uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
@@ -161,28 +186,34 @@ __device__ __forceinline__ void produce(const CUtensorMap* tma_a, const CUtensor
     constexpr int kBK = 128 / kElem;
     constexpr int kChunk = 128 / kElem;
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
-    const int BN = p.BN;
+    const int BNC = p.bn_cta;  // B rows this CTA stages
     const uint32_t a_bytes = kBM * 128;
-    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
+    const uint32_t b_bytes = static_cast<uint32_t>(BNC) * 128;
+    // In a pair, both CTAs' loads complete on the leader's full barrier, which the leader
+    // alone arms with the pair's bytes; each CTA waits on its own empty barrier (the MMA
+    // issuer commits to both).
+    const uint32_t rank = PAIR ? (blockIdx.x & 1u) : 0u;
+    const bool arms = !PAIR || rank == 0;
     ptx::prefetch_tensormap(tma_a);
     ptx::prefetch_tensormap(tma_b);
     int s = 0;
     uint32_t phase = 0;
     long long issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+    for (int t = tile_first(p); t < p.tiles_total && ok; t += tile_step(p)) {
         const Tile w = decode(p, t);
         const int za = p.a_batched ? w.z : 0;
         const int zb = p.b_batched ? w.z : 0;
         const int m0 = w.m_tile * kBM;
-        const int n0 = w.n_tile * BN;
+        const int n0 = w.n_tile * p.BN + static_cast<int>(rank) * BNC;
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
             if (!wait_bar(&empty[s], phase ^ 1, p.health, abort_flag)) {
                 ok = false;
                 break;
             }
-            ptx::mbar_arrive_expect_tx(&full[s], stage_bytes);
+            if (arms) ptx::mbar_arrive_expect_tx(&full[s], PAIR ? 2 * stage_bytes : stage_bytes);
             ++issued;
+            const uint32_t bar = PAIR ? ptx::cluster_addr(&full[s], 0) : 0u;
             uint8_t* sa = smem + s * stage_bytes;
             uint8_t* sb = sa + a_bytes * kPlanes;
             const int k0 = kb * kBK;
@@ -191,17 +222,21 @@ __device__ __forceinline__ void produce(const CUtensorMap* tma_a, const CUtensor
                 const CUtensorMap* mb = plane == 0 ? tma_b : tma_b_lo;
                 uint8_t* da = sa + plane * a_bytes;
                 uint8_t* db = sb + plane * b_bytes;
+                auto load = [&](uint8_t* dst, const CUtensorMap* map, int x, int y, int z) {
+                    if (PAIR)
+                        ptx::tma_load_3d_pair(dst, map, bar, x, y, z);
+                    else
+                        ptx::tma_load_3d(dst, map, &full[s], x, y, z);
+                };
                 if (A_MN) {
-                    for (int c = 0; c < kBM / kChunk; ++c)
-                        ptx::tma_load_3d(da + c * (kBK * 128), ma, &full[s], m0 + c * kChunk, k0, za);
+                    for (int c = 0; c < kBM / kChunk; ++c) load(da + c * (kBK * 128), ma, m0 + c * kChunk, k0, za);
                 } else {
-                    ptx::tma_load_3d(da, ma, &full[s], k0, m0, za);
+                    load(da, ma, k0, m0, za);
                 }
                 if (B_MN) {
-                    for (int c = 0; c < BN / kChunk; ++c)
-                        ptx::tma_load_3d(db + c * (kBK * 128), mb, &full[s], n0 + c * kChunk, k0, zb);
+                    for (int c = 0; c < BNC / kChunk; ++c) load(db + c * (kBK * 128), mb, n0 + c * kChunk, k0, zb);
                 } else {
-                    ptx::tma_load_3d(db, mb, &full[s], k0, n0, zb);
+                    load(db, mb, k0, n0, zb);
                 }
             }
             if (++s == stages) {
@@ -211,43 +246,59 @@ __device__ __forceinline__ void produce(const CUtensorMap* tma_a, const CUtensor
         }
     }
     // Before the CTA may exit (and free its shared memory), every armed stage must have
-    // landed, including loads nobody consumed after an abort (bounded waits).
+    // landed, including loads nobody consumed after an abort (bounded waits). In a pair the
+    // leader's barriers also count the follower's loads, and the follower leaves only
+    // after the leader (cluster barrier at the end of the kernel).
+    if (!arms) return;
     for (int st = 0; st < stages; ++st) {
-        const long long arms = issued > st ? (issued - 1 - st) / stages + 1 : 0;
-        if (arms > 0) {
+        const long long armed = issued > st ? (issued - 1 - st) / stages + 1 : 0;
+        if (armed > 0) {
             volatile int no_abort = 0;
-            wait_bar(&full[st], static_cast<uint32_t>((arms - 1) & 1), p.health, &no_abort);
+            wait_bar(&full[st], static_cast<uint32_t>((armed - 1) & 1), p.health, &no_abort);
         }
     }
 }
 
-// One elected thread issues every tcgen05.mma of the CTA. Local tile i accumulates into
-// TMEM buffer i & 1 once the epilogue has drained that buffer's previous tile.
-template <int KIND, int A_MN, int B_MN>
+// One elected thread issues every tcgen05.mma of the CTA (of the pair: the leader's).
+// Local tile i accumulates into TMEM buffer i & 1 once the epilogue has drained that
+// buffer's previous tile. In a pair the MMA spans both CTAs (M = 256: A rows 128 per CTA,
+// B rows BN / 2 per CTA at the same shared-memory offsets, accumulator rows in each CTA's
+// TMEM), and its completions are committed to the barriers of both CTAs.
+template <int KIND, int A_MN, int B_MN, bool PAIR>
 __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem, uint32_t stage_bytes, uint64_t* full,
                                       uint64_t* empty, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
                                       uint32_t buf_cols, volatile int* abort_flag) {
+    static_assert(!PAIR || KIND == 0, "CTA pairs run fp16 products");
     constexpr int kElem = KIND == 0 ? 2 : 4;
     constexpr int kBK = 128 / kElem;
     constexpr int kUK = 32 / kElem;
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
     const int BN = p.BN;
     const uint32_t a_bytes = kBM * 128;
-    const uint32_t b_bytes = static_cast<uint32_t>(BN) * 128;
+    const uint32_t b_bytes = static_cast<uint32_t>(p.bn_cta) * 128;
     const uint32_t fmt = KIND == 0 ? 0u : 2u;
+    const uint32_t mma_m = PAIR ? 2 * kBM : kBM;
     const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(A_MN) << 15) |
                            (static_cast<uint32_t>(B_MN) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                           (static_cast<uint32_t>(kBM >> 4) << 24);
+                           ((mma_m >> 4) << 24);
     // MN-major: LBO = distance between 128-byte MN chunks (one box), SBO = one swizzle
     // atom of K rows (8 rows = 1024 B for fp16; 4 rows = 512 B for the tf32 32-byte-granule
     // swizzle). K-major: SBO = 8 rows of 128 bytes, LBO unused (encoded as 16 bytes).
     const uint32_t lbo_mn = kBK * 128;
     const uint32_t sbo_mn = KIND == 0 ? 1024u : 512u;
     const uint32_t lay_mn = KIND == 0 ? 2u : 1u;
+    auto commit = [&](uint64_t* bar) {
+        if (PAIR) {
+            ptx::mma_commit_pair(ptx::cluster_addr(bar, 0));
+            ptx::mma_commit_pair(ptx::cluster_addr(bar, 1));
+        } else {
+            ptx::mma_commit(bar);
+        }
+    };
     int s = 0;
     uint32_t phase = 0;
     int i = 0;  // accumulation chain counter: one per tile, or one per chunk of kc_blocks k-blocks
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
+    for (int t = tile_first(p); t < p.tiles_total; t += tile_step(p)) {
         const Tile w = decode(p, t);
         const int span = p.kc_blocks > 0 ? p.kc_blocks : w.kb_end - w.kb_begin;
         for (int c0 = w.kb_begin; c0 < w.kb_end; c0 += span, ++i) {
@@ -271,7 +322,9 @@ __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem
                     const uint64_t db =
                         B_MN ? smem_desc(sb + b_off, lbo_mn, sbo_mn, lay_mn) : smem_desc(sb + b_off, 16, 1024);
                     const uint32_t acc = (!first || j > 0) ? 1u : 0u;
-                    if (KIND == 0) {
+                    if (PAIR) {
+                        ptx::mma_f16_pair(d_tmem, da, db, idesc, acc);
+                    } else if (KIND == 0) {
                         ptx::mma_f16(d_tmem, da, db, idesc, acc);
                     } else {
                         const uint64_t da_lo = A_MN ? smem_desc(sa + a_bytes + a_off, lbo_mn, sbo_mn, lay_mn)
@@ -283,13 +336,13 @@ __device__ __forceinline__ void issue(const Params& p, int stages, uint8_t* smem
                         ptx::mma_tf32(d_tmem, da, db, idesc, 1u);
                     }
                 }
-                ptx::mma_commit(&empty[s]);
+                commit(&empty[s]);
                 if (++s == stages) {
                     s = 0;
                     phase ^= 1;
                 }
             }
-            ptx::mma_commit(&acc_full[buf]);
+            commit(&acc_full[buf]);
         }
     }
 }
@@ -322,7 +375,7 @@ __device__ __forceinline__ bool fold_chunks(const Params& p, const Tile& w, uint
         ptx::tc_fence_after();
         const uint32_t src = tmem + static_cast<uint32_t>(buf) * p.buf_cols + lanes;
         const bool last = c == chains - 1;
-        for (int g = slot; g < groups; g += kEpiWarps / 4) {
+        for (int g = slot; g < groups; g += p.epi_warps / 4) {
             float v[16];
             ptx::tmem_ld16(src + 16u * g, v);
             if (c > 0) {
@@ -337,7 +390,7 @@ __device__ __forceinline__ bool fold_chunks(const Params& p, const Tile& w, uint
         ptx::tc_fence_before();
         __syncwarp();
         if (!last) {
-            if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);  // this chain's buffer is free again
+            if (lane == 0) release_acc(p, &acc_empty[buf]);  // this chain's buffer is free again
         } else {
             if (lane == 0) ptx::mbar_arrive(epi_sync);
             if (!wait_bar(epi_sync, epi_phase, p.health, abort_flag)) return false;
@@ -429,7 +482,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
     const int actv = p.activation;
     const int BN = p.BN;
     int i = 0;
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+    for (int t = tile_first(p); t < p.tiles_total; t += tile_step(p), ++i) {
         const Tile w = decode(p, t);
         if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
             break;
@@ -572,7 +625,7 @@ __device__ __forceinline__ void drain(const Params& p, uint64_t* acc_full, uint6
         }
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+        if (lane == 0) release_acc(p, &acc_empty[buf]);
     }
     pw.flush();
 }
@@ -721,7 +774,7 @@ __device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtens
     TmaEpi epi(tma_d, tma_p, p, staging + (warp - 2) * p.stage_floats, p.epi_bufs);
     const int BN = p.BN;
     int i = 0;
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+    for (int t = tile_first(p); t < p.tiles_total; t += tile_step(p), ++i) {
         const Tile w = decode(p, t);
         if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
             break;
@@ -764,7 +817,7 @@ __device__ __forceinline__ void drain_tma(const CUtensorMap* tma_d, const CUtens
         }
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+        if (lane == 0) release_acc(p, &acc_empty[buf]);
     }
     if (lane == 0) ptx::bulk_wait0();
     __syncwarp();
@@ -809,7 +862,7 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
     const int actv = p.activation;
     const int BN = p.BN;  // output rows per tile (a multiple of 32)
     int i = 0;
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++i) {
+    for (int t = tile_first(p); t < p.tiles_total; t += tile_step(p), ++i) {
         const Tile w = decode(p, t);
         if (p.kc_blocks > 0 && !fold_chunks(p, w, acc_full, acc_empty, epi_sync, epi_phase, tmem, i, abort_flag))
             break;
@@ -834,7 +887,7 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
         if (!wait_bar(&acc_full[buf], (i >> 1) & 1, p.health, abort_flag)) break;
         ptx::tc_fence_after();
         const uint32_t t_base = tmem + static_cast<uint32_t>(buf) * p.buf_cols + (static_cast<uint32_t>(q * 32) << 16);
-        for (int gl = slot; gl < BN / 32 && col0 < p.out_n; gl += kEpiSlots) {
+        for (int gl = slot; gl < BN / 32 && col0 < p.out_n; gl += p.epi_warps / 4) {
             const int m0 = w.n_tile * BN + 32 * gl;  // first output row of the group
             const int vr = min(32, p.out_m - m0);
             if (vr <= 0) break;  // warp-uniform
@@ -900,21 +953,35 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
                     }
                 }
             }
+            // (whole 32-row groups take unpredicated copies of the same arithmetic)
             if (p.stat_mean) {
                 float x[32];
+                float sum;
+                if (full) {
+                    sum = sum32(v);
+                } else {
 #pragma unroll
-                for (int r = 0; r < 32; ++r) x[r] = (full || r < vr) ? v[r] : 0.0f;
-                const float sum = sum32(x);
+                    for (int r = 0; r < 32; ++r) x[r] = r < vr ? v[r] : 0.0f;
+                    sum = sum32(x);
+                }
                 const long long idx =
                     static_cast<long long>(w.z) * p.stat_bstride + static_cast<long long>(m0 / 32) * p.out_n + n;
                 if (!p.stat_m2) {
                     if (col_ok) p.stat_mean[idx] = sum;
                 } else {
                     const float mean = sum * (full ? 0.03125f : 1.0f / static_cast<float>(vr));
+                    if (full) {
 #pragma unroll
-                    for (int r = 0; r < 32; ++r) {
-                        const float dv = v[r] - mean;
-                        x[r] = (full || r < vr) ? dv * dv : 0.0f;
+                        for (int r = 0; r < 32; ++r) {
+                            const float dv = v[r] - mean;
+                            x[r] = dv * dv;
+                        }
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r) {
+                            const float dv = v[r] - mean;
+                            x[r] = r < vr ? dv * dv : 0.0f;
+                        }
                     }
                     const float m2 = sum32(x);
                     if (col_ok) {
@@ -926,20 +993,37 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
             if (col_ok) {
                 if (dcol) {
                     float* dst = dcol + static_cast<long long>(m0) * p.ldd;
+                    const long long ld = p.ldd;
+                    if (full) {
 #pragma unroll
-                    for (int r = 0; r < 32; ++r)
-                        if (full || r < vr) dst[static_cast<long long>(r) * p.ldd] = v[r];
+                        for (int r = 0; r < 32; ++r) dst[r * ld] = v[r];
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < 32; ++r)
+                            if (r < vr) dst[r * ld] = v[r];
+                    }
                 }
                 if (plane_on) {
                     const long long o = static_cast<long long>(w.z) * pw.p.tstride + static_cast<long long>(m0) * pw.p.ld + n;
                     if (pw.p.h16) {
                         bool over = false;
+                        __half* dst = pw.p.h16 + o;
+                        const long long ld = pw.p.ld;
+                        if (full) {
 #pragma unroll
-                        for (int r = 0; r < 32; ++r) {
-                            if (full || r < vr) {
+                            for (int r = 0; r < 32; ++r) {
                                 const float s = v[r] * pw.scale;
                                 over |= !(fabsf(s) <= 65504.0f);
-                                pw.p.h16[o + static_cast<long long>(r) * pw.p.ld] = __float2half_rn(s);
+                                dst[r * ld] = __float2half_rn(s);
+                            }
+                        } else {
+#pragma unroll
+                            for (int r = 0; r < 32; ++r) {
+                                if (r < vr) {
+                                    const float s = v[r] * pw.scale;
+                                    over |= !(fabsf(s) <= 65504.0f);
+                                    dst[r * ld] = __float2half_rn(s);
+                                }
                             }
                         }
                         pw.overflow |= over;
@@ -958,26 +1042,27 @@ __device__ __forceinline__ void drain_swap(const Params& p, uint64_t* acc_full, 
         }
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+        if (lane == 0) release_acc(p, &acc_empty[buf]);
     }
     pw.flush();
 }
 
 // Persistent kernel: one CTA per SM walks the output tiles blockIdx.x, +gridDim.x, ...
+// (PAIR: clusters of two CTAs walk 256-row pair tiles, the leader issuing the MMAs).
 // Shared memory: [stage ring][epilogue staging kEpiWarps x 32 x 16 floats][barriers].
-template <int KIND, int A_MN, int B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KIND, int A_MN, int B_MN, bool PAIR, int EPI>
+__global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_a_lo, const __grid_constant__ CUtensorMap tma_b_lo,
                 const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_p, const Params p,
                 const int stages) {
     constexpr int kPlanes = KIND == 0 ? 1 : 2;
-    const uint32_t stage_bytes = (kBM * 128 + static_cast<uint32_t>(p.BN) * 128) * kPlanes;
+    const uint32_t stage_bytes = (kBM * 128 + static_cast<uint32_t>(p.bn_cta) * 128) * kPlanes;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* staging = reinterpret_cast<float*>(smem + stages * stage_bytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * p.stage_floats);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + EPI * p.stage_floats);
     uint64_t* empty = full + stages;
     uint64_t* acc_full = empty + stages;
     uint64_t* acc_empty = acc_full + 2;
@@ -987,6 +1072,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
+    const bool leader = !PAIR || (blockIdx.x & 1u) == 0;
     // two accumulator buffers, plus a running-sum region when chains are folded (power of two)
     const uint32_t tmem_cols = (p.kc_blocks > 0 ? 4 : 2) * p.buf_cols;
 
@@ -997,35 +1083,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(&acc_full[b], 1);
-            ptx::mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
+            ptx::mbar_init(&acc_empty[b], (PAIR ? 2 : 1) * EPI);  // one arrival per epilogue warp (of the pair)
         }
         ptx::mbar_init(mma_done, 1);
-        ptx::mbar_init(epi_sync, kEpiWarps);
+        ptx::mbar_init(epi_sync, EPI);
         *abort_flag = 0;
         ptx::fence_barrier_init();
     }
     if (warp == 1) {
-        ptx::tmem_alloc(tmem_slot, tmem_cols);
-        ptx::tmem_relinquish();
+        if (PAIR) {
+            ptx::tmem_alloc_pair(tmem_slot, tmem_cols);
+            ptx::tmem_relinquish_pair();
+        } else {
+            ptx::tmem_alloc(tmem_slot, tmem_cols);
+            ptx::tmem_relinquish();
+        }
     }
     ptx::tc_fence_before();
     __syncthreads();
+    if (PAIR) ptx::cluster_sync();  // the peer's barriers are initialised before any remote use
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
         if (ptx::elect_one())
-            produce<KIND, A_MN, B_MN>(&tma_a, &tma_b, &tma_a_lo, &tma_b_lo, p, stages, smem, stage_bytes, full, empty,
-                                      abort_flag);
+            produce<KIND, A_MN, B_MN, PAIR>(&tma_a, &tma_b, &tma_a_lo, &tma_b_lo, p, stages, smem, stage_bytes, full,
+                                            empty, abort_flag);
     } else if (warp == 1) {
         if (ptx::elect_one()) {
-            issue<KIND, A_MN, B_MN>(p, stages, smem, stage_bytes, full, empty, acc_full, acc_empty, tmem, p.buf_cols,
-                                    abort_flag);
-            // every issued MMA has completed before TMEM is released (also after an abort)
-            ptx::mma_commit(mma_done);
+            if (leader) {
+                issue<KIND, A_MN, B_MN, PAIR>(p, stages, smem, stage_bytes, full, empty, acc_full, acc_empty, tmem,
+                                              p.buf_cols, abort_flag);
+                // every issued MMA has completed before TMEM is released (also after an abort)
+                if (PAIR) {
+                    ptx::mma_commit_pair(ptx::cluster_addr(mma_done, 0));
+                    ptx::mma_commit_pair(ptx::cluster_addr(mma_done, 1));
+                } else {
+                    ptx::mma_commit(mma_done);
+                }
+            }
             volatile int no_abort = 0;
             wait_bar(mma_done, 0, p.health, &no_abort);
         }
+    } else if (EPI != kEpiWarps) {  // the wide instances serve transposed plans without row loads
+        drain_swap<false>(p, acc_full, acc_empty, epi_sync, tmem, abort_flag);
     } else if (p.swap) {
         if (p.residual || p.accumulate || p.aux)
             drain_swap<true>(p, acc_full, acc_empty, epi_sync, tmem, abort_flag);
@@ -1038,9 +1139,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::tc_fence_before();
     __syncthreads();
+    __syncwarp();
+    if (PAIR) ptx::cluster_sync();  // neither CTA leaves while the peer may still address its memory
     if (warp == 1) {
         ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, tmem_cols);
+        if (PAIR)
+            ptx::tmem_dealloc_pair(tmem, tmem_cols);
+        else
+            ptx::tmem_dealloc(tmem, tmem_cols);
     }
 }
 
@@ -1155,18 +1261,75 @@ struct Plan {
 typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                          const CUtensorMap, const Params, const int);
 
-KernelFn pick(int kind, int a_mn, int b_mn) {
+template <int EPI>
+KernelFn pick_for(int kind, int a_mn, int b_mn, bool pair) {
     const int key = kind * 4 + a_mn * 2 + b_mn;
-    switch (key) {
-        case 0: return gemm_kernel<0, 0, 0>;
-        case 1: return gemm_kernel<0, 0, 1>;
-        case 2: return gemm_kernel<0, 1, 0>;
-        case 3: return gemm_kernel<0, 1, 1>;
-        case 4: return gemm_kernel<1, 0, 0>;
-        case 5: return gemm_kernel<1, 0, 1>;
-        case 6: return gemm_kernel<1, 1, 0>;
-        default: return gemm_kernel<1, 1, 1>;
+    if (pair) {  // fp16 products only
+        switch (key & 3) {
+            case 0: return gemm_kernel<0, 0, 0, true, EPI>;
+            case 1: return gemm_kernel<0, 0, 1, true, EPI>;
+            case 2: return gemm_kernel<0, 1, 0, true, EPI>;
+            default: return gemm_kernel<0, 1, 1, true, EPI>;
+        }
     }
+    switch (key) {
+        case 0: return gemm_kernel<0, 0, 0, false, EPI>;
+        case 1: return gemm_kernel<0, 0, 1, false, EPI>;
+        case 2: return gemm_kernel<0, 1, 0, false, EPI>;
+        case 3: return gemm_kernel<0, 1, 1, false, EPI>;
+        case 4: return gemm_kernel<1, 0, 0, false, EPI>;
+        case 5: return gemm_kernel<1, 0, 1, false, EPI>;
+        case 6: return gemm_kernel<1, 1, 0, false, EPI>;
+        default: return gemm_kernel<1, 1, 1, false, EPI>;
+    }
+}
+
+KernelFn pick(const Plan* plan) {
+    return plan->p.epi_warps == kEpiWarpsWide ? pick_for<kEpiWarpsWide>(plan->kind, plan->a_mn, plan->b_mn, plan->p.pair)
+                                              : pick_for<kEpiWarps>(plan->kind, plan->a_mn, plan->b_mn, plan->p.pair);
+}
+
+// RL2_GEMM_EPI_WARPS=8 keeps every plan on eight epilogue warps (default: sixteen for
+// transposed plans without row loads).
+int swap_epi_warps() {
+    static const int w = [] {
+        const char* e = std::getenv("RL2_GEMM_EPI_WARPS");
+        return e && std::atoi(e) == kEpiWarps ? kEpiWarps : kEpiWarpsWide;
+    }();
+    return w;
+}
+
+// RL2_GEMM_PAIR=0 keeps every product on single-CTA tiles; 2 puts every eligible fp16
+// product on CTA pairs whatever its contraction length; unset or 1: long contractions.
+int pair_mode() {
+    static const int mode = [] {
+        const char* e = std::getenv("RL2_GEMM_PAIR");
+        return e && (e[0] == '0' || e[0] == '2') ? e[0] - '0' : 1;
+    }();
+    return mode;
+}
+
+// Launch of a plan's kernel: CTA-pair plans as clusters of two.
+cudaError_t launch(KernelFn fn, const Plan* plan, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
+                   const CUtensorMap& tb_lo, const Params& p, cudaStream_t stream) {
+    const int threads = threads_for(p.epi_warps);
+    if (!p.pair) {
+        fn<<<plan->grid, threads, plan->smem, stream>>>(ta, tb, ta_lo, tb_lo, plan->td, plan->tp, p, plan->stages);
+        return cudaSuccess;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = plan->grid;
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(plan->smem);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, ta, tb, ta_lo, tb_lo, plan->td, plan->tp, p, plan->stages);
 }
 
 int auto_tile_n(int n, int kind, int b_mn) {
@@ -1270,25 +1433,52 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
         const int q = o.b_major ? chunk : 32;
         bn = std::min(256, (bn + q - 1) / q * q);
     }
-    // Fewer tiles than SMs: narrower tiles (down to 128) until the grid covers the SMs; with
-    // at most one tile per CTA a CTA's tile is all of its serial work. (64-wide tiles re-read
-    // the A tile from shared memory per 64 columns: slower on long-K products.)
-    if (g->tile_n <= 0) {
-        int dev = 0, nsm = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && nsm > 0) {
-            const int q = o.b_major ? chunk : (swap ? 32 : 16);
-            auto tiles_for = [&](int w) {
-                return static_cast<long long>((o.n + w - 1) / w) * ((o.m + kBM - 1) / kBM) * o.batch * splits;
-            };
-            while (bn / 2 >= 128 && (bn / 2) % q == 0 && tiles_for(bn) < nsm) bn /= 2;
-        }
-    }
     // 3xTF32 products longer than one chain accumulate in chains of kChainBlocks k-blocks
     // folded by the epilogue (fold_chunks); the running sum takes a third TMEM region, so
     // such plans use tiles of at most 128 columns (four 128-column regions fill TMEM).
     const int kblocks_tile = ((g->k + bk - 1) / bk + std::max(splits, 1) - 1) / std::max(splits, 1);
     const bool chained = g->kind == 1 && kblocks_tile > kChainBlocks;
+    // fp16 products with at least 256 kernel rows run on CTA pairs: 256 x BN tiles whose
+    // operands each SM stages half of (A: its 128 rows, B: BN / 2 rows), so a pair reads
+    // (256 + BN) K operand rows from L2 where two single-CTA tiles read 2 (128 + BN).
+    // Pairs pay where the main loop dominates (long K) over at least two pair rows; a pair's
+    // MMAs also wait for the slower of its two epilogues, which costs more than the saved
+    // operand traffic on short-K products with wide fp32 outputs (measured: K = 512 slower,
+    // K >= 2048 faster, 256 kernel rows slower).
+    bool pair = pair_mode() > 0 && !rebindable && g->kind == 0 && g->tile_n <= 0 &&
+                (pair_mode() == 2 ? o.m >= 2 * kBM : o.m >= 4 * kBM && kblocks_tile >= kPairMinKBlocks);
+    // Fewer tiles than SMs: narrower tiles (down to 128) until the grid covers the SMs (a
+    // pair tile occupies two); with at most one tile per CTA a CTA's tile is all of its
+    // serial work. (64-wide tiles re-read the A tile from shared memory per 64 columns:
+    // slower on long-K products.)
+    int nsm = 0;
+    if (g->tile_n <= 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            nsm = 0;
+    }
+    auto narrowed = [&](int w, bool in_pairs) {
+        if (nsm <= 0) return w;
+        const int q = o.b_major ? chunk : (swap ? 32 : 16);
+        const int rows = in_pairs ? 2 * kBM : kBM;
+        const int units = in_pairs ? nsm / 2 : nsm;
+        auto tiles_for = [&](int x) {
+            return static_cast<long long>((o.n + x - 1) / x) * ((o.m + rows - 1) / rows) * o.batch * splits;
+        };
+        while (w / 2 >= 128 && (w / 2) % q == 0 && tiles_for(w) < units) w /= 2;
+        return w;
+    };
+    if (pair) {
+        // a pair stages BN / 2 rows of B per CTA: whole 16-row groups (whole 128-byte chunks
+        // of an N-contiguous B)
+        const int w = narrowed(bn, true);
+        if (w % 32 == 0 && (o.b_major == 0 || (w / 2) % chunk == 0))
+            bn = w;
+        else
+            pair = false;
+    }
+    if (!pair) bn = narrowed(bn, false);
     if (chained) bn = std::min(bn, 128);
     if (bn % 16 != 0 || bn < 16 || bn > 256 || (o.b_major == 1 && bn % chunk != 0)) {
         set_error("GEMM tile_n must be a multiple of 16 in [16, 256] (and of %d for an N-contiguous B)", chunk);
@@ -1318,7 +1508,7 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
         else
             ok = ok && make_map(ma, a, elem, o.m, o.k, a_batch, o.lda, o.a_batch_stride, chunk, bk, mn_swz);
         if (o.b_major == 0)
-            ok = ok && make_map(mb, b, elem, o.k, o.n, b_batch, o.ldb, o.b_batch_stride, bk, bn);
+            ok = ok && make_map(mb, b, elem, o.k, o.n, b_batch, o.ldb, o.b_batch_stride, bk, pair ? bn / 2 : bn);
         else
             ok = ok && make_map(mb, b, elem, o.n, o.k, b_batch, o.ldb, o.b_batch_stride, chunk, bk, mn_swz);
     }
@@ -1349,6 +1539,13 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
     p.kblocks_per_split = (p.kblocks_total + p.splits - 1) / p.splits;
     p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;  // every split non-empty
     p.BN = bn;
+    // sixteen epilogue warps (four per TMEM lane quarter) for transposed plans that read no
+    // rows besides the accumulator: twice the warps to hide the epilogue's dependent
+    // latency (its register work per 32-row group) within the 113 registers a thread gets
+    // (rebindable plans may gain a residual or an accumulate at launch: eight warps)
+    p.epi_warps = swap && !rebindable && !g->residual && !g->accumulate && !g->act_aux ? swap_epi_warps() : kEpiWarps;
+    p.pair = pair;
+    p.bn_cta = pair ? bn / 2 : bn;
     p.kc_blocks = chained ? kChainBlocks : 0;
     p.a_batched = o.a_batch_stride != 0;
     p.b_batched = o.b_batch_stride != 0;
@@ -1369,7 +1566,7 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
     p.health = g->health;
     p.out_plane = to_plane(&g->out_plane);
     const long long tiles_n = (o.n + bn - 1) / bn;
-    const long long tiles_m = (o.m + kBM - 1) / kBM;
+    const long long tiles_m = (o.m + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);  // pair tiles in a pair plan
     const long long tiles = tiles_n * tiles_m * g->batch * p.splits;
     if (tiles > 0x7FFFFFFFLL) {
         set_error("GEMM has too many output tiles");
@@ -1428,9 +1625,9 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
     // unless that costs the operand ring its fourth stage (RL2_GEMM_EPI_BUFS=1 or 2 forces).
     {
         const int planes = g->kind == 0 ? 1 : 2;
-        const int stage_bytes = (kBM * 128 + bn * 128) * planes;
+        const int stage_bytes = (kBM * 128 + p.bn_cta * 128) * planes;
         auto stages_for = [&](int stage_floats) {
-            return std::min(8, (kMaxSmem - (1024 + kEpiWarps * stage_floats * 4 + 256)) / stage_bytes);
+            return std::min(8, (kMaxSmem - (1024 + p.epi_warps * stage_floats * 4 + 256)) / stage_bytes);
         };
         auto tma_floats = [&](int nbuf) { return nbuf * (512 + (p.tma_plane ? 256 : 0)); };
         p.epi_bufs = 1;
@@ -1450,7 +1647,7 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
             delete plan;
             return nullptr;
         }
-        plan->smem = plan->stages * stage_bytes + 1024 + kEpiWarps * p.stage_floats * 4 + 256;
+        plan->smem = plan->stages * stage_bytes + 1024 + p.epi_warps * p.stage_floats * 4 + 256;
     }
     int device = 0, sms = 0;
     if (cudaGetDevice(&device) != cudaSuccess ||
@@ -1459,16 +1656,39 @@ static void* create_plan(const rl2_gemm_desc* g, bool rebindable) {
         delete plan;
         return nullptr;
     }
-    plan->grid = dim3(static_cast<unsigned>(std::min<long long>(tiles, sms)), 1, 1);
     // The limit is an attribute of the kernel function shared by every plan that uses
     // it, so it is always raised to the device maximum (never lowered by a small plan).
-    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
+    KernelFn fn = pick(plan);
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxSmem) != cudaSuccess) {
         set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", kMaxSmem);
         delete plan;
         return nullptr;
     }
+    if (!p.pair) {
+        plan->grid = dim3(static_cast<unsigned>(std::min<long long>(tiles, sms)), 1, 1);
+        return plan;
+    }
+    // one cluster of two CTAs per pair of SMs that can hold one at once
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * std::max(1, sms / 2)), 1, 1);
+    cfg.blockDim = dim3(threads_for(p.epi_warps), 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(plan->smem);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(fn), &cfg) != cudaSuccess ||
+        clusters < 1) {
+        set_error("no cluster of two GEMM CTAs fits the device");
+        delete plan;
+        return nullptr;
+    }
+    plan->grid = dim3(static_cast<unsigned>(2 * std::min<long long>(tiles, clusters)), 1, 1);
     return plan;
 }
 
@@ -1506,8 +1726,12 @@ int launch_rebound(const Plan* plan, const CUtensorMap& ta, const CUtensorMap& t
     p.vec_d = aligned(d, 16) && p.ldd % 4 == 0 && p.d_bstride % 4 == 0 && p.d_split_stride % 4 == 0;
     p.vec_res = residual && aligned(residual, 16) && p.ldr % 4 == 0 && p.r_bstride % 4 == 0;
     p.vec_bias = bias && aligned(bias, 16) && p.bias_bstride % 4 == 0;
-    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
-    fn<<<plan->grid, kThreads, plan->smem, stream>>>(ta, tb, ta_lo, tb_lo, plan->td, plan->tp, p, plan->stages);
+    KernelFn fn = pick(plan);
+    const cudaError_t e = launch(fn, plan, ta, tb, ta_lo, tb_lo, p, stream);
+    if (e != cudaSuccess) {
+        set_error("tcgen05 GEMM (rebound) launch: %s", cudaGetErrorString(e));
+        return -1;
+    }
     return launch_status("tcgen05 GEMM (rebound)");
 }
 
@@ -1566,9 +1790,12 @@ extern "C" int rl2_gemm_run(void* opaque, void* stream) {
         return -1;
     }
     Plan* plan = static_cast<Plan*>(opaque);
-    KernelFn fn = pick(plan->kind, plan->a_mn, plan->b_mn);
-    fn<<<plan->grid, kThreads, plan->smem, as_stream(stream)>>>(plan->ta, plan->tb, plan->ta_lo, plan->tb_lo,
-                                                               plan->td, plan->tp, plan->p, plan->stages);
+    KernelFn fn = pick(plan);
+    const cudaError_t e = launch(fn, plan, plan->ta, plan->tb, plan->ta_lo, plan->tb_lo, plan->p, as_stream(stream));
+    if (e != cudaSuccess) {
+        set_error("tcgen05 GEMM launch: %s", cudaGetErrorString(e));
+        return -1;
+    }
     return launch_status("tcgen05 GEMM");
 }
 
@@ -1581,6 +1808,8 @@ extern "C" int rl2_gemm_destroy(void* opaque) {
 extern "C" int rl2_gemm_tile_n(void* opaque) {
     return opaque ? static_cast<Plan*>(opaque)->p.BN : -1;
 }
+
+extern "C" int rl2_gemm_cta_pair(void* opaque) { return opaque && static_cast<Plan*>(opaque)->p.pair ? 1 : 0; }
 
 extern "C" int rl2_gemm_uses_tma_store(void* opaque) {
     if (!opaque) return 0;

@@ -229,6 +229,54 @@ __global__ void __launch_bounds__(kT) backward_kernel(const float* __restrict__ 
     finish_launch(ex, epoch);
 }
 
+// One warp: value v (0 .. 63) of this rank travels as entry v of the slot (lanes carry
+// v = lane and v = 32 + lane); every rank reduces all ranks' entries in rank order.
+__global__ void __launch_bounds__(32) small_reduce_kernel(const rl2_peer_reduce_args a, const rl2_syncbn_exchange ex) {
+    const int lane = threadIdx.x;
+    const unsigned long long epoch = launch_epoch(ex);
+    const int n1 = a.n_mean, n2 = n1 + a.n_max, n3 = n2 + a.n_max_int;
+    auto own = [&](int v) -> float {
+        if (v < n1) return a.mean[v];
+        if (v < n2) return a.max[v - n1];
+        if (v < n3) return __int_as_float(a.max_int[v - n2]);
+        return 0.0f;
+    };
+    const float x0 = own(lane), x1 = own(32 + lane);
+    const bool ok = exchange(ex, 1, 0, 32, lane, x0, x1, epoch);
+    float r[2];
+    const float* base = ex.peer_data[ex.rank];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int v = lane + 32 * h;
+        float acc = 0.0f;
+        int iacc = 0;
+        for (int q = 0; q < ex.world; ++q) {
+            const float e = ok ? __ldcv(base + static_cast<long long>(q) * 64 + v) : (h == 0 ? x0 : x1);
+            if (v < n1)
+                acc = q == 0 ? e : acc + e;
+            else if (v < n2)
+                acc = q == 0 ? e : fmaxf(acc, e);
+            else
+                iacc = q == 0 ? __float_as_int(e) : max(iacc, __float_as_int(e));
+            if (!ok) break;  // a timed-out exchange keeps this rank's own values
+        }
+        r[h] = v < n1 ? (ok ? acc / static_cast<float>(ex.world) : acc) : v < n2 ? acc : __int_as_float(iacc);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int v = lane + 32 * h;
+        if (v < n1) a.mean[v] = r[h];
+    }
+    __syncwarp();  // max results after the means (max may alias an entry of mean)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int v = lane + 32 * h;
+        if (v >= n1 && v < n2) a.max[v - n1] = r[h];
+        if (v >= n2 && v < n3) a.max_int[v - n2] = __float_as_int(r[h]);
+    }
+    finish_launch(ex, epoch);
+}
+
 }  // namespace syncbn
 }  // namespace rl2
 
@@ -280,4 +328,15 @@ extern "C" int rl2_syncbn_backward(const float* s1p, const float* s2p, long long
     syncbn::backward_kernel<<<dim3((cols + 31) / 32, twins), syncbn::kT, 0, as_stream(stream)>>>(
         s1p, s2p, pt, twins, rows, cols, dgamma, dbeta, gts, coef1, coef2, *ex);
     return launch_status("data-parallel batch-norm backward sums");
+}
+
+extern "C" int rl2_peer_reduce(const rl2_peer_reduce_args* a, const rl2_syncbn_exchange* ex, void* stream) {
+    clear_error();
+    if (!a || a->n_mean < 0 || a->n_max < 0 || a->n_max_int < 0 || a->n_mean + a->n_max + a->n_max_int > 64 ||
+        (a->n_mean && !a->mean) || (a->n_max && !a->max) || (a->n_max_int && !a->max_int) || !exchange_valid(ex)) {
+        set_error("peer reduce: invalid arguments");
+        return -1;
+    }
+    syncbn::small_reduce_kernel<<<1, 32, 0, as_stream(stream)>>>(*a, *ex);
+    return launch_status("data-parallel scalar reduction");
 }

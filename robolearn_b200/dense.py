@@ -116,6 +116,7 @@ class DensePlan:
         mode = self._lib.rl2_gemm_uses_tma_store(self.handle)
         self.tma_store = mode == 1
         self.transposed = mode == 2
+        self.cta_pair = bool(self._lib.rl2_gemm_cta_pair(self.handle))
         self.flops = 2 * m * n * k * batch * (3 if kind == TF32X3 else 1)
         self.recompute = False  # set by callers that compute the same product twice
         # algorithmic bytes of one launch (operands read once, outputs written once)
@@ -127,7 +128,7 @@ class DensePlan:
                               + ((m + 31) // 32 * n * 8 if stat_mean is not None else 0))
         self.shape = dict(m=m, n=n, k=k, batch=batch, kind=kind, a_major=a_major, b_major=b_major, splits=k_splits,
                           stats=stat_mean is not None, plane=bool(plane), residual=residual is not None,
-                          tile_n=self.tile_n, form="transposed" if self.transposed else
+                          tile_n=self.tile_n, pair=self.cta_pair, form="transposed" if self.transposed else
                           ("tma-store" if self.tma_store else "register-store"))
 
     def run(self, stream=None) -> None:

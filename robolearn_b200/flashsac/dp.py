@@ -14,7 +14,9 @@ src/robolearn/flashsac/updates.py):
   Adam; the fp16 recipe's overflow flags are combined with MAX so every rank skips the
   same steps;
 * the actor entropy feeding the temperature step is averaged, and the reported metrics
-  are averaged (``critic/max_entropy_bonus``: maximum).
+  are averaged (``critic/max_entropy_bonus``: maximum); on NVLink these scalars and the
+  overflow flags travel through one peer-memory kernel per sync point
+  (``scalar_reducer``) instead of NCCL calls.
 
 Each rank back-propagates its local loss (mean over its rows), so local gradients are
 ``world`` times their share of the global gradient; batch-norm backward coefficients
@@ -30,6 +32,8 @@ was most of the exchange time for these kilobyte-sized partials.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -73,6 +77,41 @@ class DataParallel:
     def all_reduce_max(self, t: torch.Tensor) -> None:
         if self.world > 1:
             self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+
+    def scalar_reducer(self, mean: torch.Tensor | None = None, max: torch.Tensor | None = None,
+                       max_int: torch.Tensor | None = None):
+        """A launch (callable, graph-capturable) that averages ``mean`` over the ranks and
+        replaces ``max`` (float) and ``max_int`` (int32 flags) by their maxima, the maxima
+        last (``max`` may be a view into ``mean``). One peer-memory kernel (``rl2_peer_reduce``)
+        when the peer exchange is on and a slot is left, else the same through collectives."""
+        views = [v for v in (mean, max, max_int) if v is not None]
+        if self.peer is not None and sum(v.numel() for v in views) <= 64:
+            ex = self.peer.try_slot(32, 1)
+            if ex is not None:
+                from .. import _native as N
+
+                lib = N.load()
+                args = N.PeerReduceArgs(mean=N.addr(mean), n_mean=mean.numel() if mean is not None else 0,
+                                        max=N.addr(max), n_max=max.numel() if max is not None else 0,
+                                        max_int=N.addr(max_int), n_max_int=max_int.numel() if max_int is not None else 0)
+
+                def launch():
+                    N.check(lib.rl2_peer_reduce(ctypes.byref(args), ctypes.byref(ex), N.stream_ptr()),
+                            "data-parallel scalar reduction")
+
+                launch.keep = (args, ex, views)
+                launch.launches = 1
+                return launch
+
+        def launch():
+            for v in (max, max_int):
+                if v is not None:
+                    self.all_reduce_max(v)
+            if mean is not None:
+                self.all_reduce_mean(mean)
+
+        launch.launches = 0
+        return launch
 
     # ---- batch-norm partials --------------------------------------------
     def all_gather(self, local: torch.Tensor, out: torch.Tensor) -> None:
@@ -134,6 +173,12 @@ class PeerExchange:
         self.health_ptr = health_ptr or None
         self.next = 0
         self._keep: list = []
+
+    def try_slot(self, cols: int, twins: int):
+        """``slot`` or None when every slot is taken or the slots are narrower."""
+        if self.next >= self.slots or cols > self.max_cols or twins > self.twins:
+            return None
+        return self.slot(cols, twins)
 
     def slot(self, cols: int, twins: int):
         """Exchange arguments of the next free slot (host struct; keep it alive while in use)."""

@@ -318,21 +318,15 @@ class Net:
                 C = shape[-1]
                 for t in range(T if len(shape) == 2 else 1):
                     rows.append((o + t * C, -1, -1, C, 0))
-        maxlen = _lib().rl2_segment_max_length()
-        if any(r[3] > maxlen for r in rows):
-            raise ValueError(f"a projection unit is longer than {maxlen} elements")
-        arr = (N.Segment * len(rows))(*[N.Segment(offset=a, offset2=b, plane_offset=c, length=d, kind=e)
-                                       for a, b, c, d, e in rows])
-        raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).clone()
-        self.segment_count = len(rows)
-        return raw.to(self.device)
+        table, self.segment_count, self.warp_segment_count = N.segment_table(rows, self.device)
+        return table
 
     def refresh_planes(self, project: bool = False) -> None:
         """Rewrite every weight operand plane from the fp32 parameters (and optionally project)."""
         a = N.AdamArgs(params=N.addr(self.params), grads=None, m=None, v=None, segments=N.addr(self.segments),
                        count=self.segment_count, state=None, formula=0, beta1=0.9, beta2=0.999, eps=1e-8,
                        project=int(project), weight_plane=self.plane_c(), target_params=None, tau=0.0,
-                       target_plane=N.Plane())
+                       target_plane=N.Plane(), warp_segments=self.warp_segment_count)
         N.check(_lib().rl2_adam_step(ctypes.byref(a), N.stream_ptr()), "refresh weight planes")
 
 

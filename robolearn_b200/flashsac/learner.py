@@ -197,8 +197,9 @@ class Learner:
         if self.dp is not None and self.dp.peer is None:
             # one peer-exchange slot per batch-norm sync point: forward + backward of the
             # actor and online critic, forward of the target critic
+            # (plus slots for the scalar reductions of the phase programs)
             la, lc = self.actor.bn_layers, self.critic.bn_layers
-            self.dp.enable_peer(device, 2 * len(la) + 3 * len(lc), max(C for _, C in la + lc),
+            self.dp.enable_peer(device, 2 * len(la) + 3 * len(lc) + 16, max([32] + [C for _, C in la + lc]),
                                 self.health.data_ptr())
         pa, pa_eval, pc, pc_eval = {}, {}, {}, {}
         sa, scc = self.scalers["actor"], self.scalers["critic"]
@@ -269,25 +270,29 @@ class Learner:
             formula=self.adam_formula, beta1=0.9, beta2=0.999, eps=1e-8, project=1, weight_plane=net.plane_c(),
             target_params=target.params.data_ptr() if target is not None else None,
             tau=cfg.critic_target_update_tau if target is not None else 0.0,
-            target_plane=target.plane_c() if target is not None else N.Plane())
+            target_plane=target.plane_c() if target is not None else N.Plane(),
+            warp_segments=net.warp_segment_count)
         pref, sref = ctypes.byref(prep), ctypes.byref(step)
         dp = self.dp
+        # skip the step on any rank's overflow
+        flags = dp.scalar_reducer(max_int=sc.found_inf) if (
+            dp is not None and sc.found_inf is not None and self.kind == FP16) else None
 
         def launch():
-            if dp is not None:  # average the gradients of all ranks; skip the step on any rank's overflow
+            if dp is not None:  # average the gradients of all ranks
                 if prefix is not None and prefix < net.size:
                     torch.cuda.current_stream().wait_stream(self._grad_stream)
                     if prefix > 0:
                         dp.all_reduce_mean(net.grads[:prefix])
                 else:
                     dp.all_reduce_mean(net.grads)
-                if sc.found_inf is not None and self.kind == FP16:
-                    dp.all_reduce_max(sc.found_inf)
+                if flags is not None:
+                    flags()
             N.check(lib.rl2_adam_prepare(pref, N.stream_ptr()), f"{name} adam prepare")
             N.check(lib.rl2_adam_step(sref, N.stream_ptr()), f"{name} adam step")
 
-        launch.keep = (prep, step)
-        launch.launches = 2
+        launch.keep = (prep, step, flags)
+        launch.launches = 2 + (flags.launches if flags is not None else 0)
         return launch
 
     def _program(self, actor_phase: bool, apply_optimizer: bool = True):
@@ -355,8 +360,7 @@ class Learner:
                 alpha_out=self.alpha.data_ptr())
             if self.dp is not None:
                 ent = self.metrics[METRIC_KEYS.index("actor/entropy"):METRIC_KEYS.index("actor/entropy") + 1]
-                prog.append(lambda ent=ent: self.dp.all_reduce_mean(ent))
-                prog[-1].launches = 0
+                prog.append(self.dp.scalar_reducer(mean=ent))
             if apply_optimizer:
                 prog.append(_wrap(lib.rl2_temperature_step, temp, None, "temperature step"))
         else:
@@ -399,13 +403,7 @@ class Learner:
             prog.append(self._optimizer("critic", self.critic, target=self.target, prefix=prefix))
         if self.dp is not None:  # reported metrics over the global batch
             mx = METRIC_KEYS.index("critic/max_entropy_bonus")
-
-            def metrics_exchange():
-                self.dp.all_reduce_max(self.metrics[mx:mx + 1])
-                self.dp.all_reduce_mean(self.metrics)
-
-            metrics_exchange.launches = 0
-            prog.append(metrics_exchange)
+            prog.append(self.dp.scalar_reducer(mean=self.metrics, max=self.metrics[mx:mx + 1]))
         return prog
 
     # ------------------------------------------------------------------

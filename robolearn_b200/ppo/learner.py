@@ -174,12 +174,9 @@ class WarpPPO:
         self.learning_rate = torch.full((1,), cfg.learning_rate, **f32)
         self._seed = torch.tensor([cfg.seed], dtype=torch.int64, device=dev)  # advanced like the reference's
         segs = lo.segments()
-        arr = (N.Segment * len(segs))(*[N.Segment(offset=a, offset2=b, plane_offset=c, length=d, kind=e)
-                                        for a, b, c, d, e in segs])
-        self._segments = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).clone().to(dev)
-        self._segment_count = len(segs)
         if max(s[3] for s in segs) > lib.rl2_segment_max_length():
             raise ValueError("a layer is wider than the optimizer's vector limit")
+        self._segments, self._segment_count, self._warp_segments = N.segment_table(segs, dev)
         # ---- scalars and reduction workspace (tickets start at zero and are left at zero)
         self.loss = torch.zeros(1, **f32)
         self.metrics = torch.zeros(3, **f32)
@@ -225,7 +222,7 @@ class WarpPPO:
         a = N.AdamArgs(params=self.params.data_ptr(), grads=None, m=None, v=None,
                        segments=self._segments.data_ptr(), count=self._segment_count, state=None, formula=1,
                        beta1=0.9, beta2=0.999, eps=1e-8, project=0, weight_plane=self._weight_plane(),
-                       target_params=None, tau=0.0, target_plane=N.Plane())
+                       target_params=None, tau=0.0, target_plane=N.Plane(), warp_segments=self._warp_segments)
         N.check(self.lib.rl2_adam_step(ctypes.byref(a), N.stream_ptr()), "refresh weight planes")
 
     def _weight_plane(self) -> N.Plane:
@@ -474,7 +471,8 @@ class WarpPPO:
         step = N.AdamArgs(params=self.params.data_ptr(), grads=self.grads.data_ptr(), m=self.m1.data_ptr(),
                           v=self.m2.data_ptr(), segments=self._segments.data_ptr(), count=self._segment_count,
                           state=self.opt_state.data_ptr(), formula=1, beta1=0.9, beta2=0.999, eps=1e-8, project=0,
-                          weight_plane=self._weight_plane(), target_params=None, tau=0.0, target_plane=N.Plane())
+                          weight_plane=self._weight_plane(), target_params=None, tau=0.0, target_plane=N.Plane(),
+                          warp_segments=self._warp_segments)
         self._keep += [prep, step]
         pref, sref = ctypes.byref(prep), ctypes.byref(step)
 

@@ -1,5 +1,6 @@
 """Host-side logic of data-parallel FlashSAC on CPU ranks (gloo, world size 2): the
-batch-norm partial all-gather layout, mean / max reductions and row slicing."""
+batch-norm partial all-gather layout, mean / max reductions, the scalar reducer's
+collective form (the peer-memory kernel's fallback) and row slicing."""
 
 import os
 import socket
@@ -40,6 +41,13 @@ def _worker(rank: int, world: int, port: int, out):
         dp.all_reduce_max(y)
         ok &= y.item() == world - 1
         ok &= dp.row_slice(8) == (4 * rank, 4)
+        # scalar reducer (collective form): means, then maxima over an aliasing view, flags
+        metrics = torch.tensor([float(rank), 2.0 * rank, 5.0 + rank])
+        flag = torch.tensor([rank], dtype=torch.int32)
+        dp.scalar_reducer(mean=metrics, max=metrics[2:3])()
+        dp.scalar_reducer(max_int=flag)()
+        ok &= torch.allclose(metrics, torch.tensor([0.5, 1.0, 6.0]))
+        ok &= flag.item() == world - 1
         out[rank] = bool(ok)
     finally:
         dist.destroy_process_group()

@@ -7,8 +7,12 @@ temperature of the 2-rank learner must match the single-GPU learner at the globa
 batch: FP32 recipe within 1e-4 relative to each tensor's largest magnitude (batch-norm
 buffers with a 1e-3 floor); FP16-operand recipe within 1e-2 in relative L2 norm (the
 two runs sum weight gradients in different orders and Adam's first steps amplify that
-for near-zero gradients). Both ranks must hold bit-identical parameters and report no
-health flag. Batch-norm statistics go through the NVLink peer-memory kernels
+for near-zero gradients). At config 5's widths (critic 1024 x 3, actor 128 x 2, 512 rows
+per rank, FP32 recipe) the gradients of both phases, averaged over the ranks, match the
+global batch's within 1e-4 of each tensor's largest magnitude (Adam's first steps turn
+rounding-level differences of near-zero gradients into whole learning-rate steps, so
+parameters are not the measure there). Both ranks must hold
+bit-identical parameters and report no health flag. Batch-norm statistics go through the NVLink peer-memory kernels
 (``RL2_DP_PEER=1``, the default) and, in one FP32 case, through NCCL all-gathers.
 Skipped with fewer than two GPUs.
 """
@@ -35,13 +39,15 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("precision,measure,tol,peer", [("fp32", 0, 1e-4, "1"), ("fp16", 1, 1e-2, "1"),
-                                                        ("fp32", 0, 1e-4, "0")])
-def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol, peer):
+@pytest.mark.parametrize("precision,measure,tol,peer,widths", [("fp32", 0, 1e-4, "1", "small"),
+                                                               ("fp16", 1, 1e-2, "1", "small"),
+                                                               ("fp32", 0, 1e-4, "0", "small"),
+                                                               ("fp32", 0, 1e-4, "1", "wide")])
+def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol, peer, widths):
     out = tmp_path / "dp.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(ROOT / "tests" / "_dp_worker.py"),
-           str(out), precision]
+           str(out), precision, widths]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", RL2_DP_PEER=peer)
     done = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert done.returncode == 0, done.stdout[-4000:] + done.stderr[-4000:]
@@ -52,3 +58,7 @@ def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol,
     for upd in report["updates"]:
         worst = max(upd["errors"].items(), key=lambda kv: kv[1][measure])
         assert worst[1][measure] < tol, (upd["phase"], worst)
+        if "metrics_dp" in upd:  # reported metrics reduced over the ranks (scalar reducer)
+            for got, want in zip(upd["metrics_dp"], upd["metrics_single"]):
+                assert abs(got - want) <= 1e-2 * max(abs(want), 1e-2), (upd["phase"], upd["metrics_dp"],
+                                                                         upd["metrics_single"])

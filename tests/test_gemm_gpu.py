@@ -459,3 +459,69 @@ def test_split_reduce_batched_matches_per_batch_reduce():
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     assert torch.allclose(out[count + 17:], part[:, 0].sum(0), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("with_residual", [True, False])
+@pytest.mark.parametrize("a_major,b_major", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", [(1000, 96, 1040), (600, 96, 1100), (512, 1000, 1030), (2048, 640, 1024)])
+def test_gemm_cta_pair_plans(a_major, b_major, m, n, k, with_residual):
+    """fp16 products with >= 512 kernel rows and >= 16 k-blocks run on CTA pairs (256-row
+    tiles over two SMs):
+    ragged pair tiles (a follower half partly or wholly outside M), both orientations
+    (n >= 128: transposed accumulator, kernel rows = n; without a residual such plans
+    take sixteen epilogue warps), all operand majors, bias (+ residual) + column moments,
+    against float64."""
+    batch = 2
+    groups = (m + 31) // 32
+    bias = torch.randn(batch, n, device="cuda")
+    res = torch.randn(batch, m, n, device="cuda") if with_residual else None
+    mean = torch.zeros(batch, groups, n, device="cuda")
+    m2 = torch.zeros(batch, groups, n, device="cuda")
+    plan, D, ref = _run(0, m, n, k, a_major, b_major, batch=batch, bias=bias, bias_batch_stride=n, residual=res,
+                        ldr=n if with_residual else 0, residual_batch_stride=m * n if with_residual else 0,
+                        stat_mean=mean, stat_m2=m2, stat_batch_stride=groups * n)
+    assert plan.cta_pair, plan.shape
+    plan.run()
+    torch.cuda.synchronize()
+    expect = ref + bias.double()[:, None, :] + (res.double() if with_residual else 0.0)
+    out = D[:, :, :n].double()
+    assert (out - expect).abs().max().item() < 2e-3 * expect.abs().max().item()
+    full = torch.zeros(batch, groups * 32, n, device="cuda", dtype=torch.float64)
+    full[:, :m] = out
+    rows = full.view(batch, groups, 32, n)
+    counts = torch.full((groups,), 32.0, device="cuda", dtype=torch.float64)
+    counts[-1] = m - 32 * (groups - 1)
+    mu = rows.sum(2) / counts[None, :, None]
+    assert torch.allclose(mean.double(), mu, atol=1e-4, rtol=1e-4)
+
+
+def test_gemm_cta_pair_split_k_and_graph_replay():
+    """A CTA-pair plan with split-K partials, replayed from a CUDA graph, equals its eager run."""
+    m, n, k, batch, splits = 512, 64, 2048, 2, 2
+    stride = batch * m * n
+    part = torch.zeros(splits, stride, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn(batch, m, k, device="cuda", generator=g).half().float()
+    B = (torch.randn(batch, n, k, device="cuda", generator=g) / k**0.5).half().float()
+    a_st, lda = _store(A, 0, 0)
+    b_st, ldb = _store(B, 0, 0)
+    plan = dense.DensePlan(kind=0, m=m, n=n, k=k, a=a_st, b=b_st, d=part, lda=lda, ldb=ldb, ldd=n, a_major=0,
+                           b_major=0, batch=batch, a_batch_stride=a_st[0].numel(), b_batch_stride=b_st[0].numel(),
+                           d_batch_stride=m * n, k_splits=splits, d_split_stride=stride)
+    assert plan.cta_pair
+    plan.run()
+    torch.cuda.synchronize()
+    eager = part.clone()
+    got = eager.view(splits, batch, m, n).sum(0).double()
+    ref = torch.einsum("zmk,znk->zmn", A.double(), B.double())
+    assert (got - ref).abs().max().item() < 2e-3 * ref.abs().max().item()
+    part.zero_()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+        plan.run()
+    torch.cuda.current_stream().wait_stream(s)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(part, eager)
