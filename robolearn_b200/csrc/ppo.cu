@@ -337,9 +337,15 @@ __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
         a.partials[static_cast<long long>(blockIdx.x) * nslot + v] = s;
     }
     if (last_block(a.counter)) {
-        for (int v = threadIdx.x; v < nslot; v += kT) {
+        // warp w sums slots w, w + 8, ...: lane l the blocks l, l + 32, ... in order, then a
+        // fixed shuffle tree (the partials were written by other SMs: L1 bypassed)
+        const int lane = threadIdx.x & 31;
+        for (int v = warp; v < nslot; v += kT / 32) {
             double s = 0.0;
-            for (int b = 0; b < static_cast<int>(gridDim.x); ++b) s += __ldcg(a.partials + static_cast<long long>(b) * nslot + v);
+            for (int b = lane; b < static_cast<int>(gridDim.x); b += 32)
+                s += __ldcg(a.partials + static_cast<long long>(b) * nslot + v);
+            s = warp_sum_d(s);
+            if (lane != 0) continue;
             if (v == 0) {
                 *a.loss = static_cast<float>(s);
             } else if (v < 4) {
