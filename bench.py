@@ -129,6 +129,11 @@ class Clocks:
             threading.Thread(target=self._read, daemon=True).start()
         except OSError:
             self.proc = None
+            return self
+        # the sampler's own start (driver initialisation) stays out of the timed region
+        deadline = time.time() + 5.0
+        while not self.rows and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
     def _read(self):
@@ -339,12 +344,12 @@ def run_flashsac(workload: str, precision: str, steps: int, warmup: int, world: 
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local_rank) as clocks:
+        if world > 1:  # every rank's sampler is up before the ranks start together
+            import torch.distributed as dist
+
+            dist.barrier()
         torch.cuda.synchronize()
         e0.record()
         for i in range(steps):
