@@ -838,6 +838,20 @@ typedef struct rl2_peer_reduce_args {
 
 int rl2_peer_reduce(const rl2_peer_reduce_args* args, const rl2_syncbn_exchange* ex, void* stream);
 
+/* Mean over the ranks of a float arena held in symmetric memory, in place on every rank
+ * (the data-parallel gradient average before each optimizer step: every rank then steps
+ * on the global batch's gradient, src/robolearn/flashsac/updates.py). ex->peer_data[q] =
+ * rank q's arena (16-byte aligned, the same count on every rank), ex->peer_flags[q] =
+ * rank q's flag region of this call site (rl2_peer_mean_flag_bytes(world) bytes, zeroed
+ * once), ex->epoch = this call site's two-word counter. One kernel of 148 blocks that must
+ * all be resident: launch it on a stream with no other waiting kernel beside it. Each rank
+ * averages 1/world of the arena (sum in rank order / world) and stores it into every
+ * rank's arena, so the ranks hold bit-identical results. A wait on a peer that runs out
+ * (ex->timeout_s) records the timeout in ex->health and leaves the arena partly averaged.
+ * count: floats, a multiple of 4. Replaces an NCCL all-reduce (AVG) of the arena. */
+long long rl2_peer_mean_flag_bytes(int world);
+int rl2_peer_mean(long long count, const rl2_syncbn_exchange* ex, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -393,4 +393,6 @@ SIGNATURES.update({
     "rl2_peer_reduce": ([ctypes.POINTER(PeerReduceArgs), ctypes.POINTER(SyncBNExchange), P], I),
     "rl2_syncbn_slot_data_bytes": ([I, I, I], LL),
     "rl2_syncbn_slot_flag_bytes": ([I, I, I], LL),
+    "rl2_peer_mean": ([LL, ctypes.POINTER(SyncBNExchange), P], I),
+    "rl2_peer_mean_flag_bytes": ([I], LL),
 })

@@ -277,6 +277,121 @@ __global__ void __launch_bounds__(32) small_reduce_kernel(const rl2_peer_reduce_
     finish_launch(ex, epoch);
 }
 
+// ---- gradient arena mean over the ranks ------------------------------------------------
+//
+// One launch per optimizer step. Every rank's arena lives in symmetric memory. Rank r owns
+// the float4 range [n4 * r / W, n4 * (r + 1) / W), split evenly over the blocks. Block b
+// of rank r: (1) entry barrier with block b of every rank (each rank's block b has started,
+// so that rank's backward kernels have finished writing its arena); (2) for each float4 of
+// its share, loads the W ranks' values, sums them in rank order, divides by W and stores
+// the mean into every rank's arena (this rank's share of the reduce-scatter and of the
+// all-gather in one pass, one copy of each value crossing each link per direction);
+// (3) exit barrier with block b of every rank (every rank's share is in this rank's arena
+// before the kernel ends). Flags of a call site: [2 (entry, exit)][blocks][W] u64 per rank.
+// Every value is computed by one rank only, so all ranks hold bit-identical means.
+
+constexpr int kGradT = 512;
+constexpr int kGradU = 2;         // float4 per thread and rank per iteration
+constexpr int kGradBlocks = 148;  // all resident on a B200 (one 512-thread block per SM)
+
+__device__ bool wait_epoch(const unsigned long long* f, unsigned long long epoch, const rl2_syncbn_exchange& ex) {
+    if (load_acquire(f) >= epoch) return true;
+    const uint64_t start = now_ns();
+    const uint64_t limit = static_cast<uint64_t>(ex.timeout_s * 1e9f);
+    for (uint32_t i = 1;; ++i) {
+        if (load_acquire(f) >= epoch) return true;
+        if ((i & 255u) == 0 && now_ns() - start > limit) {
+            if (ex.health) atomicOr(ex.health, kHealthTimeout);
+            return false;
+        }
+    }
+}
+
+// Block-wide barrier with block b of every rank on flag row `phase`; false on a timeout.
+__device__ bool rank_barrier(const rl2_syncbn_exchange& ex, int phase, unsigned long long epoch, int* s_ok) {
+    const int W = ex.world, t = threadIdx.x;
+    const long long row = (static_cast<long long>(phase) * gridDim.x + blockIdx.x) * W;
+    __syncthreads();  // every thread's earlier stores precede the release below
+    if (t == 0) *s_ok = 1;
+    if (t < W) store_release(ex.peer_flags[t] + row + ex.rank, epoch);
+    __syncthreads();
+    if (t < W && !wait_epoch(ex.peer_flags[ex.rank] + row + t, epoch, ex)) *s_ok = 0;
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+__device__ __forceinline__ float4 ld_peer(const float4* p) { return __ldcv(p); }
+
+__device__ __forceinline__ void add4(float4& a, const float4& b) {
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+}
+
+template <int W>  // W > 0: compile-time world; W == 0: runtime world
+__global__ void __launch_bounds__(kGradT) grad_mean_kernel(long long n4, const rl2_syncbn_exchange ex) {
+    __shared__ int s_ok;
+    __shared__ float4* s_ptr[32];
+    const int world = W > 0 ? W : ex.world;
+    const unsigned long long epoch = launch_epoch(ex);
+    if (threadIdx.x < world) s_ptr[threadIdx.x] = reinterpret_cast<float4*>(ex.peer_data[threadIdx.x]);
+    bool ok = rank_barrier(ex, 0, epoch, &s_ok);
+    if (ok) {
+        const long long lo = n4 * ex.rank / world, len = n4 * (ex.rank + 1) / world - lo;
+        const long long c0 = lo + len * blockIdx.x / gridDim.x, c1 = lo + len * (blockIdx.x + 1) / gridDim.x;
+        const float wf = static_cast<float>(world);
+        for (long long i = c0 + threadIdx.x; i < c1; i += static_cast<long long>(kGradT) * kGradU) {
+            float4 acc[kGradU];
+            if constexpr (W > 0) {
+                float4 x[W][kGradU];
+#pragma unroll
+                for (int q = 0; q < W; ++q)
+#pragma unroll
+                    for (int u = 0; u < kGradU; ++u) {
+                        const long long e = i + static_cast<long long>(u) * kGradT;
+                        if (e < c1) x[q][u] = ld_peer(s_ptr[q] + e);
+                    }
+#pragma unroll
+                for (int u = 0; u < kGradU; ++u) {
+                    acc[u] = x[0][u];
+#pragma unroll
+                    for (int q = 1; q < W; ++q) add4(acc[u], x[q][u]);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < kGradU; ++u) {
+                    const long long e = i + static_cast<long long>(u) * kGradT;
+                    if (e < c1) acc[u] = ld_peer(s_ptr[0] + e);
+                }
+                for (int q = 1; q < world; ++q)
+#pragma unroll
+                    for (int u = 0; u < kGradU; ++u) {
+                        const long long e = i + static_cast<long long>(u) * kGradT;
+                        if (e < c1) add4(acc[u], ld_peer(s_ptr[q] + e));
+                    }
+            }
+#pragma unroll
+            for (int u = 0; u < kGradU; ++u) {
+                acc[u].x = acc[u].x / wf;
+                acc[u].y = acc[u].y / wf;
+                acc[u].z = acc[u].z / wf;
+                acc[u].w = acc[u].w / wf;
+            }
+#pragma unroll 4
+            for (int q = 0; q < world; ++q)
+#pragma unroll
+                for (int u = 0; u < kGradU; ++u) {
+                    const long long e = i + static_cast<long long>(u) * kGradT;
+                    if (e < c1) s_ptr[q][e] = acc[u];
+                }
+        }
+    }
+    // a rank whose entry wait ran out skips the exit wait (its peers then time out too)
+    if (ok) rank_barrier(ex, 1, epoch, &s_ok);
+    finish_launch(ex, epoch);
+}
+
 }  // namespace syncbn
 }  // namespace rl2
 
@@ -339,4 +454,26 @@ extern "C" int rl2_peer_reduce(const rl2_peer_reduce_args* a, const rl2_syncbn_e
     }
     syncbn::small_reduce_kernel<<<1, 32, 0, as_stream(stream)>>>(*a, *ex);
     return launch_status("data-parallel scalar reduction");
+}
+
+extern "C" long long rl2_peer_mean_flag_bytes(int world) {
+    return 2LL * syncbn::kGradBlocks * world * 8;
+}
+
+extern "C" int rl2_peer_mean(long long count, const rl2_syncbn_exchange* ex, void* stream) {
+    clear_error();
+    if (count < 0 || count % 4 != 0 || !exchange_valid(ex)) {
+        set_error("peer mean: invalid arguments (count a multiple of 4 floats)");
+        return -1;
+    }
+    const long long n4 = count / 4;
+    const dim3 grid(syncbn::kGradBlocks), block(syncbn::kGradT);
+    cudaStream_t s = as_stream(stream);
+    switch (ex->world) {
+        case 2: syncbn::grad_mean_kernel<2><<<grid, block, 0, s>>>(n4, *ex); break;
+        case 4: syncbn::grad_mean_kernel<4><<<grid, block, 0, s>>>(n4, *ex); break;
+        case 8: syncbn::grad_mean_kernel<8><<<grid, block, 0, s>>>(n4, *ex); break;
+        default: syncbn::grad_mean_kernel<0><<<grid, block, 0, s>>>(n4, *ex); break;
+    }
+    return launch_status("data-parallel gradient mean");
 }

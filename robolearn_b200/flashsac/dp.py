@@ -10,9 +10,11 @@ src/robolearn/flashsac/updates.py):
   each rank's packed per-32-row-group partials of a layer are all-gathered in one call
   and merged in a fixed rank-major group order by the same kernels as on one GPU, so
   every rank computes bit-identical statistics;
-* the gradient arena of each optimised network is averaged (``all_reduce`` AVG) before
-  Adam; the fp16 recipe's overflow flags are combined with MAX so every rank skips the
-  same steps;
+* the gradient arena of each optimised network is averaged before Adam: on NVLink by one
+  peer-memory kernel per optimizer step over arenas held in symmetric memory
+  (``PeerGradients``: each rank sums its share of the arena over the ranks in rank order
+  and stores the mean into every rank's arena), otherwise by ``all_reduce`` AVG; the fp16
+  recipe's overflow flags are combined with MAX so every rank skips the same steps;
 * the actor entropy feeding the temperature step is averaged, and the reported metrics
   are averaged (``critic/max_entropy_bonus``: maximum); on NVLink these scalars and the
   overflow flags travel through one peer-memory kernel per sync point
@@ -52,6 +54,7 @@ class DataParallel:
         self.rank = dist.get_rank(group)
         self.nccl = dist.get_backend(group) == "nccl"
         self.peer: PeerExchange | None = None
+        self.peer_grads: PeerGradients | None = None
 
     def enable_peer(self, device, slots: int, max_cols: int, health_ptr: int, timeout_s: float = 10.0) -> bool:
         """Exchange batch-norm statistics through NVLink peer memory instead of NCCL all-gathers
@@ -63,6 +66,32 @@ class DataParallel:
             return False
         self.peer = PeerExchange(self, slots, max_cols, device, health_ptr=health_ptr, timeout_s=timeout_s)
         return True
+
+    def enable_peer_gradients(self, nets, device, health_ptr: int, timeout_s: float = 10.0) -> bool:
+        """Move the gradient arenas of ``nets`` into NVLink symmetric memory and average them
+        with one peer-memory kernel per optimizer step (``gradient_mean``) instead of NCCL
+        all-reduces. Collective; call before any launch list takes the arenas' addresses.
+        Needs the peer exchange; ``RL2_DP_PEER_GRAD=0`` keeps NCCL. Returns whether it is on."""
+        import os
+
+        if self.peer is None or os.environ.get("RL2_DP_PEER_GRAD", "1") == "0":
+            return False
+        self.peer_grads = PeerGradients(self, nets, device, health_ptr=health_ptr, timeout_s=timeout_s)
+        return True
+
+    def gradient_mean(self, net):
+        """A launch (callable, graph-capturable) that replaces ``net.grads`` by its mean over
+        the ranks: one peer-memory kernel (``rl2_peer_mean``) when the arenas are in symmetric
+        memory, else an NCCL / gloo all-reduce. ``launch.launches`` counts this library's kernels."""
+        pg = self.peer_grads
+        if pg is not None and pg.holds(net):
+            return pg.reducer(net)
+
+        def launch():
+            self.all_reduce_mean(net.grads)
+
+        launch.launches = 0
+        return launch
 
     # ---- reductions -------------------------------------------------------
     def all_reduce_mean(self, t: torch.Tensor) -> None:
@@ -198,3 +227,76 @@ class PeerExchange:
                               health=self.health_ptr, timeout_s=self.timeout_s)
         self._keep += [data, flags, ex]
         return ex
+
+
+class PeerGradients:
+    """Gradient arenas of the optimised networks in one NVLink symmetric buffer.
+
+    Layout of every rank's buffer: the networks' arenas (each padded to 64 floats), then
+    ``sites`` flag regions of ``rl2_peer_mean_flag_bytes(world)`` bytes, one per call site
+    of ``reducer`` (assigned in program-construction order, the same on every rank), each
+    with its own two-word epoch counter on this rank. ``net.grads`` becomes a view of the
+    buffer, so every launch list built afterwards addresses the shared arena.
+    """
+
+    def __init__(self, dp: DataParallel, nets, device, health_ptr: int = 0, timeout_s: float = 10.0,
+                 sites: int = 16):
+        import torch.distributed._symmetric_memory as symm
+
+        from .. import _native as N
+
+        lib = N.load()
+        W = dp.world
+        self.flag_bytes = (int(lib.rl2_peer_mean_flag_bytes(W)) + 255) // 256 * 256
+        self.offsets = {}
+        off = 0
+        for net in nets:
+            self.offsets[id(net)] = (off, net.size)
+            off += (net.size + 63) // 64 * 64
+        self.flag_base = 4 * off
+        self.sites = sites
+        self.buf = symm.empty(off + sites * self.flag_bytes // 4, dtype=torch.float32, device=device)
+        self.buf.zero_()
+        group = dp.group if dp.group is not None else dp.dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, group)
+        for net in nets:
+            o, n = self.offsets[id(net)]
+            self.buf[o:o + n].copy_(net.grads)
+            net.grads = self.buf[o:o + n]
+        torch.cuda.synchronize(device)
+        dp.dist.barrier(group=dp.group)
+        self.ptrs = list(self.handle.buffer_ptrs)
+        self.world, self.rank, self.device = W, dp.rank, device
+        self.epochs = torch.zeros(2 * sites, dtype=torch.int32, device=device)
+        self.health_ptr = health_ptr or None
+        self.timeout_s = timeout_s
+        self.next = 0
+        self._keep: list = []
+
+    def holds(self, net) -> bool:
+        return id(net) in self.offsets and net.grads.data_ptr() == self.buf.data_ptr() + 4 * self.offsets[id(net)][0]
+
+    def reducer(self, net):
+        """Launch averaging ``net.grads`` over the ranks (one ``rl2_peer_mean`` kernel)."""
+        from .. import _native as N
+
+        if self.next >= self.sites:
+            raise RuntimeError("peer gradients: all call sites are in use")
+        s = self.next
+        self.next += 1
+        o, n = self.offsets[id(net)]
+        data = torch.tensor([p + 4 * o for p in self.ptrs], dtype=torch.int64, device=self.device)
+        flags = torch.tensor([p + self.flag_base + s * self.flag_bytes for p in self.ptrs], dtype=torch.int64,
+                             device=self.device)
+        ex = N.SyncBNExchange(peer_data=data.data_ptr(), peer_flags=flags.data_ptr(),
+                              epoch=self.epochs.data_ptr() + 8 * s, world=self.world, rank=self.rank,
+                              health=self.health_ptr, timeout_s=self.timeout_s)
+        lib = N.load()
+        ref = ctypes.byref(ex)
+
+        def launch():
+            N.check(lib.rl2_peer_mean(n, ref, N.stream_ptr()), "data-parallel gradient mean")
+
+        launch.keep = (data, flags, ex)
+        launch.launches = 1
+        return launch

@@ -201,6 +201,8 @@ class Learner:
             la, lc = self.actor.bn_layers, self.critic.bn_layers
             self.dp.enable_peer(device, 2 * len(la) + 3 * len(lc) + 16, max([32] + [C for _, C in la + lc]),
                                 self.health.data_ptr())
+            # gradient arenas in symmetric memory: one peer-memory mean per optimizer step
+            self.dp.enable_peer_gradients([self.actor, self.critic], device, self.health.data_ptr())
         pa, pa_eval, pc, pc_eval = {}, {}, {}, {}
         sa, scc = self.scalers["actor"], self.scalers["critic"]
         self.actor_train = Run(self.actor, 2 * B, True, self.actor_x.data_ptr(), self.ldax, update_running=True,
@@ -232,7 +234,7 @@ class Learner:
         gradients below the prefix end are left to the optimizer launch."""
         prog = list(run.backward_program)
         dp = self.dp
-        if dp is None or not apply_optimizer or not dp.nccl or not run.grad_marks:
+        if dp is None or not apply_optimizer or not dp.nccl or not run.grad_marks or self._peer_mean(net):
             return prog, net.size
         side = self._grad_stream
         out, hi = [], net.size
@@ -251,6 +253,12 @@ class Learner:
                 out.append(bucket)
                 hi = lo
         return out, hi
+
+    def _peer_mean(self, net: Net) -> bool:
+        """Whether ``net``'s gradients are averaged by the peer-memory kernel (whole arena,
+        once, just before the optimizer step)."""
+        dp = self.dp
+        return dp is not None and dp.peer_grads is not None and dp.peer_grads.holds(net)
 
     def _optimizer(self, name: str, net: Net, target: Net | None = None, prefix: int | None = None):
         """Fused optimizer pass; under data parallelism the gradients are averaged first
@@ -277,9 +285,14 @@ class Learner:
         # skip the step on any rank's overflow
         flags = dp.scalar_reducer(max_int=sc.found_inf) if (
             dp is not None and sc.found_inf is not None and self.kind == FP16) else None
+        mean = dp.gradient_mean(net) if self._peer_mean(net) else None
 
         def launch():
-            if dp is not None:  # average the gradients of all ranks
+            if mean is not None:
+                mean()
+                if flags is not None:
+                    flags()
+            elif dp is not None:  # average the gradients of all ranks
                 if prefix is not None and prefix < net.size:
                     torch.cuda.current_stream().wait_stream(self._grad_stream)
                     if prefix > 0:
@@ -291,8 +304,8 @@ class Learner:
             N.check(lib.rl2_adam_prepare(pref, N.stream_ptr()), f"{name} adam prepare")
             N.check(lib.rl2_adam_step(sref, N.stream_ptr()), f"{name} adam step")
 
-        launch.keep = (prep, step, flags)
-        launch.launches = 2 + (flags.launches if flags is not None else 0)
+        launch.keep = (prep, step, flags, mean)
+        launch.launches = 2 + (flags.launches if flags is not None else 0) + (mean.launches if mean is not None else 0)
         return launch
 
     def _program(self, actor_phase: bool, apply_optimizer: bool = True):

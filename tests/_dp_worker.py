@@ -98,7 +98,8 @@ def main():
     single = make(rows * dp.world, None, device, precision, widths) if dp.rank == 0 else None
     torch.cuda.synchronize()
     dist.barrier()  # rank 0 built a second learner: start the updates together
-    report = {"world": dp.world, "precision": precision, "peer": dp.peer is not None, "updates": []}
+    report = {"world": dp.world, "precision": precision, "peer": dp.peer is not None,
+              "peer_grads": dp.peer_grads is not None, "updates": []}
     phases = (True, False)
     wide = widths == "wide"
     for phase in phases:

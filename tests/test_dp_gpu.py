@@ -15,8 +15,10 @@ way at a pre-activation within rounding of zero moves a 1024-wide layer's gradie
 about 1e-3 (measured: 5.9e-4 relative L2 and 1.1e-2 of the largest element on
 encoder.0.w2 after one phase). Parameters are not the measure there: Adam's first steps
 turn such differences of near-zero gradients into whole learning-rate steps. Both ranks must hold
-bit-identical parameters and report no health flag. Batch-norm statistics go through the NVLink peer-memory kernels
-(``RL2_DP_PEER=1``, the default) and, in one FP32 case, through NCCL all-gathers.
+bit-identical parameters and report no health flag. Batch-norm statistics and the gradient
+means go through the NVLink peer-memory kernels (``RL2_DP_PEER=1``, the default) and, in
+one FP32 case, through NCCL all-gathers and all-reduces. ``test_peer_mean_bit_exact``
+checks the gradient-mean kernel alone, bit for bit.
 Skipped with fewer than two GPUs.
 """
 
@@ -57,6 +59,7 @@ def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol,
     report = json.loads(out.read_text())
     assert report["ranks_identical"]
     assert report["peer"] == (peer == "1")
+    assert report["peer_grads"] == (peer == "1")
     assert report["health"] == 0
     for upd in report["updates"]:
         worst = max(upd["errors"].items(), key=lambda kv: kv[1][measure])
@@ -65,3 +68,19 @@ def test_two_rank_update_matches_global_batch(tmp_path, precision, measure, tol,
             for got, want in zip(upd["metrics_dp"], upd["metrics_single"]):
                 assert abs(got - want) <= 1e-2 * max(abs(want), 1e-2), (upd["phase"], upd["metrics_dp"],
                                                                          upd["metrics_single"])
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_mean_bit_exact(tmp_path):
+    """rl2_peer_mean over 2 ranks: bit-identical to the rank-order sum / world, eager and
+    from a captured graph, for arenas from one float4 to a few million floats."""
+    out = tmp_path / "mean.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           str(ROOT / "tests" / "_peer_mean_worker.py"), str(out)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    done = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert done.returncode == 0, done.stdout[-4000:] + done.stderr[-4000:]
+    report = json.loads(out.read_text())
+    assert report["health"] == 0
+    assert report["ok"]
