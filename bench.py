@@ -64,10 +64,11 @@ CFG5_BATCH = 32768
 CFG5_STEPS = 5  # timed cfg5 updates in the headline line's summary (about 1 s on one GPU)
 # DRAM traffic of the GEMM family over one cfg3 update pair: the per-launch
 # dram__bytes_read.sum + dram__bytes_write.sum of every product of one actor + critic
-# update pair, summed (ncu launch list with those metrics; see the profiles directory).
-# None until that capture exists.
-GEMM_TRAFFIC_PER_PAIR = None
-GEMM_TRAFFIC_SOURCE = "not captured"
+# update pair, summed (ncu launch list with those metrics, one pass, caches flushed before
+# each launch; profiles/gemm_family_dram_cfg3.md).
+GEMM_TRAFFIC_PER_PAIR = 3480483072
+GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum summed over the 94 GEMM launches of one "
+                       "update pair (2765.0 MB read + 715.4 MB written; caches flushed before each launch)")
 
 
 def parse():
@@ -243,7 +244,8 @@ def gemm_roofline(L, peak_tflops):
     return {"kernel": "rl2 tcgen05 GEMM (all products of one actor+critic update pair)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tflops, 4), "traffic": None, "launches": len(plans),
-            "flops_per_pair": flops, "ms_per_pair": round(sec * 1e3, 4)}
+            "flops_per_pair": flops, "algorithmic_bytes_per_pair": sum(p.bytes for p in plans),
+            "ms_per_pair": round(sec * 1e3, 4)}
 
 
 def cpu_threads() -> int:
