@@ -1,6 +1,7 @@
 """Host-side logic of data-parallel FlashSAC on CPU ranks (gloo, world size 2): the
-batch-norm partial all-gather layout, mean / max reductions, the scalar reducer's
-collective form (the peer-memory kernel's fallback) and row slicing."""
+batch-norm partial all-gather layout, mean / max reductions, the collective forms of the
+scalar reducer and of the gradient mean (the peer-memory kernels' fallbacks) and row
+slicing."""
 
 import os
 import socket
@@ -48,6 +49,17 @@ def _worker(rank: int, world: int, port: int, out):
         dp.scalar_reducer(max_int=flag)()
         ok &= torch.allclose(metrics, torch.tensor([0.5, 1.0, 6.0]))
         ok &= flag.item() == world - 1
+        # gradient mean without peer memory: the collective form, and no peer arenas on gloo
+
+        class Net:
+            grads = torch.tensor([1.0 + rank, -2.0 * rank, 4.0, 8.0 * rank])
+
+        net = Net()
+        ok &= dp.enable_peer_gradients([net], "cpu", 0) is False and dp.peer_grads is None
+        launch = dp.gradient_mean(net)
+        ok &= launch.launches == 0
+        launch()
+        ok &= torch.allclose(net.grads, torch.tensor([1.5, -1.0, 4.0, 4.0]))
         out[rank] = bool(ok)
     finally:
         dist.destroy_process_group()
