@@ -246,6 +246,10 @@ __device__ __forceinline__ float action_log_std(const rl2_ppo_loss_args& a, int 
     return a.std_type ? logf(fminf(fmaxf(p, a.std_min), a.std_max)) : p;
 }
 
+// MAXA: compile-time bound on the action count (16, or kMaxAct), so the per-action arrays
+// are indexed statically and stay in registers; the arithmetic and its order do not
+// depend on it.
+template <int MAXA>
 __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
     __shared__ double sh[kT / 32][loss_slots(kMaxAct)];
     const int row = blockIdx.x * kT + threadIdx.x;
@@ -255,21 +259,25 @@ __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
     const float sc = 1.0f / static_cast<float>(a.rows);
     const float eps = a.clip_ratio;
     float vals[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
-    float ds[kMaxAct], dm[kMaxAct];
-#pragma unroll 4
-    for (int j = 0; j < A; ++j) ds[j] = dm[j] = 0.0f;
+    float ds[MAXA], dm[MAXA];
+#pragma unroll
+    for (int j = 0; j < MAXA; ++j) ds[j] = dm[j] = 0.0f;
     PlaneWriter pw(dplane);
     if (live) {
         const float* mean = a.head + static_cast<long long>(row) * a.ld_head;
         const float value = a.head[a.head_twin_stride + static_cast<long long>(row) * a.ld_head];
         const float* act = a.actions + static_cast<long long>(row) * A;
         float logp = 0.0f, entropy = 0.0f;
-        float r[kMaxAct];
-        for (int j = 0; j < A; ++j) {
-            const float s = action_log_std(a, j);
-            r[j] = (act[j] - mean[j]) * expf(-s);
-            logp = logp - 0.5f * (r[j] * r[j] + 2.0f * s + kLog2Pi);
-            entropy = entropy + s + kHalfLog2PiE;
+        float r[MAXA];
+#pragma unroll
+        for (int j = 0; j < MAXA; ++j) {
+            r[j] = 0.0f;
+            if (j < A) {
+                const float s = action_log_std(a, j);
+                r[j] = (act[j] - mean[j]) * expf(-s);
+                logp = logp - 0.5f * (r[j] * r[j] + 2.0f * s + kLog2Pi);
+                entropy = entropy + s + kHalfLog2PiE;
+            }
         }
         const float adv = a.advantages[row];
         const float ratio = expf(logp - a.old_log_probs[row]);
@@ -297,39 +305,68 @@ __global__ void loss_kernel(const rl2_ppo_loss_args a, const Plane dplane) {
         vals[3] = sc * entropy;
         const bool inside = ratio >= 1.0f - eps && ratio <= 1.0f + eps;
         const float d_logp = ((first || inside) ? -adv * sc : 0.0f) * ratio;
-        for (int j = 0; j < A; ++j) {
-            const float s = action_log_std(a, j);
-            dm[j] = d_logp * r[j] * expf(-s);
-            ds[j] = d_logp * (r[j] * r[j] - 1.0f);
+#pragma unroll
+        for (int j = 0; j < MAXA; ++j) {
+            if (j < A) {
+                const float s = action_log_std(a, j);
+                dm[j] = d_logp * r[j] * expf(-s);
+                ds[j] = d_logp * (r[j] * r[j] - 1.0f);
+            }
         }
         const float dval = dv * a.value_loss_scale * a.value_coefficient * sc;
         vals[4] = dval;
         // d_head: actor twin = d mean (padding columns zero), critic twin = [dV, 0, ...]
         const long long ld = a.ld_d_head;
-        for (int j = 0; j < ld; ++j) {
-            const float g0 = j < A ? dm[j] : 0.0f;
-            const float g1 = j == 0 ? dval : 0.0f;
+        // tf32 planes with 16-byte rows: four columns per store (one 16-byte piece per
+        // plane instead of one scalar store per column and plane)
+        const bool vec4 = pw.active() && !pw.p.h16 && ld % 4 == 0 && pw.p.ld % 4 == 0 && pw.p.tstride % 4 == 0 &&
+                          (reinterpret_cast<uintptr_t>(pw.p.lo) & 15u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(pw.p.hi) & 15u) == 0;
+        auto put = [&](int j, float g0, float g1) {
             if (a.d_head) {
                 a.d_head[static_cast<long long>(row) * ld + j] = g0;
                 a.d_head[a.d_head_twin_stride + static_cast<long long>(row) * ld + j] = g1;
             }
-            if (pw.active()) {
+            if (pw.active() && !vec4) {
                 pw.store(0, row, j, g0);
                 pw.store(1, row, j, g1);
+            }
+        };
+#pragma unroll
+        for (int j = 0; j < MAXA; ++j)
+            if (j < ld) put(j, j < A ? dm[j] : 0.0f, j == 0 ? dval : 0.0f);
+        for (int j = MAXA; j < ld; ++j) put(j, 0.0f, 0.0f);
+        if (vec4) {
+#pragma unroll
+            for (int j = 0; j < MAXA; j += 4) {
+                if (j < ld) {
+                    pw.store4(0, row, j, make_float4(j < A ? dm[j] : 0.0f, j + 1 < A ? dm[j + 1] : 0.0f,
+                                                     j + 2 < A ? dm[j + 2] : 0.0f, j + 3 < A ? dm[j + 3] : 0.0f));
+                    pw.store4(1, row, j, make_float4(j == 0 ? dval : 0.0f, 0.0f, 0.0f, 0.0f));
+                }
+            }
+            for (int j = MAXA; j < ld; j += 4) {
+                pw.store4(0, row, j, make_float4(0.0f, 0.0f, 0.0f, 0.0f));
+                pw.store4(1, row, j, make_float4(0.0f, 0.0f, 0.0f, 0.0f));
             }
         }
     }
     pw.flush();
-    // block partials: warp sums then a fixed-order combine of the warps
+    // block partials: warp sums then a fixed-order combine of the warps (slots in the order
+    // loss, policy, value, entropy, d bias critic, d s[0 .. A), d bias actor[0 .. A))
     const int warp = threadIdx.x >> 5;
-    for (int v = 0; v < nslot; ++v) {
-        double x;
-        if (v < 5) x = vals[v];
-        else if (v < 5 + A) x = ds[v - 5];
-        else x = dm[v - 5 - A];
+    auto push = [&](int v, double x) {
         x = warp_sum_d(x);
         if ((threadIdx.x & 31) == 0) sh[warp][v] = x;
-    }
+    };
+#pragma unroll
+    for (int v = 0; v < 5; ++v) push(v, vals[v]);
+#pragma unroll
+    for (int j = 0; j < MAXA; ++j)
+        if (j < A) push(5 + j, ds[j]);
+#pragma unroll
+    for (int j = 0; j < MAXA; ++j)
+        if (j < A) push(5 + A + j, dm[j]);
     __syncthreads();
     for (int v = threadIdx.x; v < nslot; v += kT) {
         double s = 0.0;
@@ -576,7 +613,10 @@ extern "C" int rl2_ppo_loss(const rl2_ppo_loss_args* a, void* stream) {
         return -1;
     }
     const int blocks = (a->rows + ppo::kT - 1) / ppo::kT;
-    ppo::loss_kernel<<<blocks, ppo::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
+    if (a->act <= 16)
+        ppo::loss_kernel<16><<<blocks, ppo::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
+    else
+        ppo::loss_kernel<ppo::kMaxAct><<<blocks, ppo::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
     return launch_status("rl2_ppo_loss");
 }
 
