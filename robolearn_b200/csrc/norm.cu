@@ -417,11 +417,14 @@ __global__ void __launch_bounds__(kColsumThreads) colsum_finalize_kernel(const f
     float s = 0.0f;
     if (c < cols) {
         const float* src = part + static_cast<long long>(t) * groups * cols + c;
+        // eight groups' loads in flight before they are added (the sum stays sequential in g)
         int g = g0;
-        for (; g + 4 <= g1; g += 4) {
-            const float a = src[static_cast<long long>(g) * cols], b = src[static_cast<long long>(g + 1) * cols];
-            const float d = src[static_cast<long long>(g + 2) * cols], e = src[static_cast<long long>(g + 3) * cols];
-            s = (((s + a) + b) + d) + e;
+        for (; g + 8 <= g1; g += 8) {
+            float x[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = src[static_cast<long long>(g + k) * cols];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s = s + x[k];
         }
         for (; g < g1; ++g) s += src[static_cast<long long>(g) * cols];
     }

@@ -647,9 +647,11 @@ extern "C" int rl2_ppo_clip_gradients(float* grads, long long actor_count, long 
         return -1;
     }
     const int blocks = ppo::sum_blocks(n);
+    // the sums: two CTAs per SM at most (fewer partials for the last block's fixed-order merge)
+    const int sum_grid = blocks < 296 ? blocks : 296;
     cudaStream_t s = as_stream(stream);
-    ppo::sumsq_kernel<<<blocks, ppo::kT, 0, s>>>(grads, actor_count, critic_count, n, separate, max_norm, norms_out,
-                                                 partials, counter);
+    ppo::sumsq_kernel<<<sum_grid, ppo::kT, 0, s>>>(grads, actor_count, critic_count, n, separate, max_norm, norms_out,
+                                                   partials, counter);
     ppo::scale_kernel<<<blocks, ppo::kT, 0, s>>>(grads, actor_count, critic_count, n, norms_out);
     return launch_status("rl2_ppo_clip_gradients");
 }
