@@ -16,6 +16,7 @@ namespace rl2 {
 namespace norm {
 
 constexpr int kT = 256;
+constexpr int kRowRegs = 16;  // row values a lane keeps in registers (rows up to 512 columns)
 
 __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_a, float n_b, float mean_b,
                                            float m2_b) {
@@ -233,7 +234,29 @@ __global__ void bwd_reduce_kernel(const rl2_bn_backward_args a) {
     const int r0 = g * 32;
     const int n = min(32, a.rows - r0);
     float s1 = 0.0f, s2 = 0.0f;
-    for (int i = 0; i < n; ++i) {
+    int i = 0;
+    {  // eight rows' loads in flight before they are used (same per-row arithmetic and order)
+        const int tc = t * a.cols + c;
+        const float mu = a.mean[tc], is = a.invstd[tc], ga = a.gamma[tc], be = a.beta[tc];
+        for (; i + 8 <= n; i += 8) {
+            float xv[8], dv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const long long r = r0 + i + k;
+                xv[k] = a.x[t * a.x_twin_stride + r * a.ldx + c];
+                dv[k] = a.dy[t * a.dy_twin_stride + r * a.lddy + c];
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float xhat = (xv[k] - mu) * is;
+                float d = dv[k];
+                if (a.relu && !(xhat * ga + be > 0.0f)) d = 0.0f;
+                s1 += d;
+                s2 += d * xhat;
+            }
+        }
+    }
+    for (; i < n; ++i) {
         float xhat;
         const float d = masked_dbn(a, t, r0 + i, c, xhat);
         s1 += d;
@@ -371,11 +394,32 @@ __global__ void rms_backward_kernel(const float* __restrict__ du, long long lddu
         const float* x = h + t * ht + r * ldh;
         const float* g = gamma + t * cols;
         float s = 0.0f;
+        float* o = dh + t * dht + r * lddh;
+        if (cols <= 32 * kRowRegs) {
+            // the row's values loaded once, all in flight before the (sequential) sum
+            float gv[kRowRegs], dv[kRowRegs], xv[kRowRegs];
+#pragma unroll
+            for (int q = 0; q < kRowRegs; ++q) {
+                const int c = lane + 32 * q;
+                if (c < cols) gv[q] = g[c], dv[q] = d[c], xv[q] = x[c];
+            }
+#pragma unroll
+            for (int q = 0; q < kRowRegs; ++q)
+                if (lane + 32 * q < cols) s += gv[q] * dv[q] * xv[q];
+            s = warp_sum(s);
+            const float rr = rv[w];
+            const float k = rr * rr * rr * s / static_cast<float>(cols);
+#pragma unroll
+            for (int q = 0; q < kRowRegs; ++q) {
+                const int c = lane + 32 * q;
+                if (c < cols) o[c] = rr * gv[q] * dv[q] - xv[q] * k;
+            }
+            continue;
+        }
         for (int c = lane; c < cols; c += 32) s += g[c] * d[c] * x[c];
         s = warp_sum(s);
         const float rr = rv[w];
         const float k = rr * rr * rr * s / static_cast<float>(cols);
-        float* o = dh + t * dht + r * lddh;
         for (int c = lane; c < cols; c += 32) o[c] = rr * g[c] * d[c] - x[c] * k;
     }
 }
@@ -391,7 +435,20 @@ __global__ void rms_dgamma_kernel(const float* __restrict__ du, long long lddu, 
     const int r0 = g * 32;
     const int n = min(32, rows - r0);
     float s = 0.0f;
-    for (int i = 0; i < n; ++i) {
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {  // eight rows' loads in flight before they are added in order
+        float a[8], b[8], q[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const long long r = r0 + i + k;
+            a[k] = du[t * dut + r * lddu + c];
+            b[k] = h[t * ht + r * ldh + c];
+            q[k] = rv[static_cast<long long>(t) * rows + r];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += a[k] * b[k] * q[k];
+    }
+    for (; i < n; ++i) {
         const long long r = r0 + i;
         s += du[t * dut + r * lddu + c] * h[t * ht + r * ldh + c] * rv[static_cast<long long>(t) * rows + r];
     }
