@@ -73,57 +73,59 @@ __global__ void deterministic_kernel(const rl2_policy_args a) {
 }
 
 // one warp per row; dgrad columns [0,A) = d mean, [A,2A) = d pre-tanh log-std
-__global__ void backward_kernel(const rl2_policy_args a, const Plane plane) {
+// One CTA per 32-row column-sum group: the group's 32 x A elements are computed by all
+// threads at once (each element's arithmetic as in a per-row loop), their d(mean) and
+// d(log-std pre-activation) kept in shared memory, then thread c < 2A adds column c over
+// the group's rows in row order (the same sequential sum per group as one warp walking
+// the rows), so the bias-gradient partials do not depend on the thread layout.
+__global__ void __launch_bounds__(kT) backward_kernel(const rl2_policy_args a, const Plane plane) {
     PlaneWriter pw(plane);
-    __shared__ float part[kWarps][2 * 64];
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
+    __shared__ float dmean_s[32][64];
+    __shared__ float ds_s[32][64];
     const float dlp_val = a.d_log_pi_value ? *a.d_log_pi_value : 0.0f;
     const float bc = (a.bc_alpha > 0.0f && a.q_abs) ? a.bc_alpha * *a.q_abs : 0.0f;
     const int groups = (a.rows + 31) / 32;
-    // each warp handles 32 consecutive rows (one column-sum group) at a time
-    for (int g = blockIdx.x * kWarps + warp; g < groups; g += gridDim.x * kWarps) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};  // lanes own columns lane, lane+32, lane+64, lane+96 of 2A
-#pragma unroll 4
-        for (int rr = 0; rr < 32; ++rr) {
-            const long long row = static_cast<long long>(g) * 32 + rr;
-            if (row >= a.rows) continue;
+    const int A = a.act;
+    for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+        const long long r0 = static_cast<long long>(g) * 32;
+        const int nrows = static_cast<int>(min(32LL, static_cast<long long>(a.rows) - r0));
+        for (int e = threadIdx.x; e < nrows * A; e += kT) {
+            const int rr = e / A, j = e - rr * A;
+            const long long row = r0 + rr;
             const float* h = a.head + row * a.ld_head;
             const float* n = a.noise + row * a.ld_noise;
             const float dlp = row < a.grad_rows ? (a.d_log_pi ? a.d_log_pi[row] : dlp_val) : 0.0f;
-            for (int j = lane; j < a.act; j += 32) {
-                const Sample s = sample(h[j], h[a.act + j], n[j]);
-                float da = 0.0f;
-                if (row < a.grad_rows && a.d_action) da = a.d_action[row * a.ld_d_action + j];
-                if (bc != 0.0f && row < a.grad_rows)
-                    da += bc * 2.0f * (s.action - a.replay_action[row * a.ld_replay_action + j]) /
-                          (static_cast<float>(a.grad_rows) * a.act);
-                const float draw = da * (1.0f - s.action * s.action) + dlp * 2.0f * s.action;
-                const float dmean = draw;
-                const float dlogstd = draw * s.std * n[j] - dlp;
-                const float ds = dlogstd * (kLogStdMax - kLogStdMin) * 0.5f * (1.0f - s.ts * s.ts);
-                if (a.d_head) {
-                    a.d_head[row * a.ld_d_head + j] = dmean;
-                    a.d_head[row * a.ld_d_head + a.act + j] = ds;
-                }
-                if (pw.active()) {
-                    pw.store(0, row, j, dmean);
-                    pw.store(0, row, a.act + j, ds);
-                }
-                const int s0 = j / 32;
-                acc[s0] += dmean;
-                acc[s0 + 2] += ds;
+            const Sample smp = sample(h[j], h[A + j], n[j]);
+            float da = 0.0f;
+            if (row < a.grad_rows && a.d_action) da = a.d_action[row * a.ld_d_action + j];
+            if (bc != 0.0f && row < a.grad_rows)
+                da += bc * 2.0f * (smp.action - a.replay_action[row * a.ld_replay_action + j]) /
+                      (static_cast<float>(a.grad_rows) * A);
+            const float draw = da * (1.0f - smp.action * smp.action) + dlp * 2.0f * smp.action;
+            const float dmean = draw;
+            const float dlogstd = draw * smp.std * n[j] - dlp;
+            const float ds = dlogstd * (kLogStdMax - kLogStdMin) * 0.5f * (1.0f - smp.ts * smp.ts);
+            if (a.d_head) {
+                a.d_head[row * a.ld_d_head + j] = dmean;
+                a.d_head[row * a.ld_d_head + A + j] = ds;
             }
-        }
-        if (a.bias_part) {
-            for (int j = lane; j < a.act; j += 32) {
-                const int s0 = j / 32;
-                a.bias_part[static_cast<long long>(g) * 2 * a.act + j] = acc[s0];
-                a.bias_part[static_cast<long long>(g) * 2 * a.act + a.act + j] = acc[s0 + 2];
+            if (pw.active()) {
+                pw.store(0, row, j, dmean);
+                pw.store(0, row, A + j, ds);
             }
+            dmean_s[rr][j] = dmean;
+            ds_s[rr][j] = ds;
         }
+        __syncthreads();
+        if (a.bias_part && threadIdx.x < 2 * A) {
+            const int c = threadIdx.x < A ? threadIdx.x : threadIdx.x - A;
+            const float(*src)[64] = threadIdx.x < A ? dmean_s : ds_s;
+            float acc = 0.0f;
+            for (int rr = 0; rr < nrows; ++rr) acc += src[rr][c];
+            a.bias_part[static_cast<long long>(g) * 2 * A + threadIdx.x] = acc;
+        }
+        __syncthreads();  // the next group reuses the shared rows
     }
-    (void)part;
     pw.flush();
 }
 
@@ -336,7 +338,7 @@ extern "C" int rl2_policy_backward(const rl2_policy_args* a, void* stream) {
         return -1;
     }
     const int groups = (a->rows + 31) / 32;
-    const int blocks = std::min((groups + policy::kWarps - 1) / policy::kWarps, 148 * 8);
+    const int blocks = std::min(groups, 148 * 8);
     policy::backward_kernel<<<blocks, policy::kT, 0, as_stream(stream)>>>(*a, to_plane(&a->d_plane));
     return launch_status("policy backward");
 }
